@@ -1,0 +1,193 @@
+"""Generates the golden fixtures of tests/golden/ by running the REFERENCE implementation on CPU.
+
+Run in a container where the reference checkout is importable (default /root/reference, or REFERENCE_ROOT):
+
+    python tests/golden/make_golden.py
+
+For every case it builds the seeded synthetic weights (janus_b200.synthetic.make_weights), loads them into a
+transformers Qwen3_5TextModel / Qwen3_5MoeTextModel in fp32, wraps it in the reference's janus.hybrid.HybridBackbone
+(its plain CPU path: torch chunk/recurrent rules, dense-mask varlen attention), runs the reference's
+DecisionModel.forward readout (PointerHead for listwise, ScalarHead for tree) on the synthetic packed requests, and
+stores the logits and the temperature-1 probabilities. The int4 experts enter the reference as their dequantised
+bf16 values (HF experts hold dense stacks). It also stores per-op vectors of the reference's gated delta rule.
+
+The fixtures are written once and not edited afterwards; tests compare the CPU oracle and the CUDA path to them.
+"""
+
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parent.parent))
+REFERENCE = os.environ.get("REFERENCE_ROOT", "/root/reference")
+
+from janus_b200.config import SHAPES  # noqa: E402
+from janus_b200 import synthetic  # noqa: E402
+from janus_b200.packing import Question, pack_listwise, pack_tree  # noqa: E402
+
+# name: (shape, overrides of the shape, readout mode, seed, request factory)
+def _cases():
+    tiny = SHAPES["tiny"]
+    t4 = lambda seed: synthetic.tiny_request(vocab=4096, seed=seed, mode="tree")
+
+    def small_tree(vocab, seed, state=200, questions=3, block=12):
+        tok = synthetic.Tokens(vocab, seed)
+        qs = []
+        for qi in range(questions):
+            kind = ("choice", "score", "noul")[qi % 3]
+            header = tok(block)
+            if kind == "noul":
+                qs.append(Question(kind, header, (tok(3),)))
+            else:
+                qs.append(Question(kind, header, tuple(tok(int(tok.rng.integers(2, 5))) for _ in range(int(tok.rng.integers(2, 5))))))
+        return pack_tree(tok(state), qs)
+
+    def small_list(vocab, seed, state=192):
+        tok = synthetic.Tokens(vocab, seed)
+        return pack_listwise(tok(state), [Question("choice", tok(9), tuple(tok(4) for _ in range(3)), tok(3)),
+                                          Question("noul", tok(6), (tok(2), tok(2)), tok(3))])
+
+    return {
+        "tiny_listwise": (tiny, {}, "listwise", 0, lambda: [synthetic.tiny_request(vocab=4096, seed=0)]),
+        "tiny_tree": (tiny, {}, "tree", 1, lambda: [t4(1), t4(2)]),
+        "tiny_tree_long": (tiny, {}, "tree", 2, lambda: [small_tree(4096, 5, state=300), small_tree(4096, 6, state=77)]),
+        "tiny_moe_tree": (SHAPES["tiny-moe"], {}, "tree", 3, lambda: [small_tree(4096, 7), small_tree(4096, 8, state=90)]),
+        "w08b_listwise": (SHAPES["0.8b"], dict(layers=4, vocab=4096), "listwise", 4, lambda: [small_list(4096, 9)]),
+        "w4b_tree": (SHAPES["4b"], dict(layers=4, vocab=4096), "tree", 5,
+                     lambda: [small_tree(4096, 10, state=160), small_tree(4096, 11, state=100)]),
+        "wa3b_tree": (SHAPES["35b-a3b"], dict(layers=4, vocab=4096, experts=32), "tree", 6,
+                      lambda: [small_tree(4096, 12, state=96, questions=2)]),
+    }
+
+
+def shape_of(shape, overrides):
+    layers = overrides.pop("layers", shape.layers)
+    return shape.with_layers(layers, **overrides)
+
+
+def hf_model(shape, weights):
+    """A transformers text model of `shape` in fp32 holding `weights` (int4 experts dequantised)."""
+    from transformers import Qwen3_5MoeTextConfig, Qwen3_5TextConfig, Qwen3_5MoeTextModel, Qwen3_5TextModel
+    common = dict(vocab_size=shape.vocab, hidden_size=shape.hidden, num_hidden_layers=shape.layers,
+                  num_attention_heads=shape.heads, num_key_value_heads=shape.kv_heads, head_dim=shape.head_dim,
+                  linear_num_key_heads=shape.lin_k_heads, linear_num_value_heads=shape.lin_v_heads,
+                  linear_key_head_dim=shape.lin_k_dim, linear_value_head_dim=shape.lin_v_dim,
+                  linear_conv_kernel_dim=shape.conv_kernel, layer_types=list(shape.layer_types),
+                  max_position_embeddings=32768, attention_dropout=0.0, use_cache=False, tie_word_embeddings=False,
+                  rms_norm_eps=shape.rms_eps)
+    if shape.moe:
+        cfg = Qwen3_5MoeTextConfig(moe_intermediate_size=shape.moe_intermediate,
+                                   shared_expert_intermediate_size=shape.shared_intermediate,
+                                   num_experts=shape.experts, num_experts_per_tok=shape.top_k, **common)
+        cls = Qwen3_5MoeTextModel
+    else:
+        cfg = Qwen3_5TextConfig(intermediate_size=shape.intermediate, **common)
+        cls = Qwen3_5TextModel
+    cfg._attn_implementation = "sdpa"
+    torch.manual_seed(0)
+    lm = cls(cfg).float()
+    state = {}
+    for name, t in weights.items():
+        if name.startswith("head.") or name.endswith(".scales"):
+            continue
+        if name + ".scales" in weights:
+            t = synthetic.int4_dequantize(t, weights[name + ".scales"])
+        state[name] = t.float()
+    missing, unexpected = lm.load_state_dict(state, strict=False)
+    missing = [m for m in missing if "rotary" not in m]
+    if missing or unexpected:
+        raise RuntimeError(f"state dict mismatch: missing {missing[:5]} unexpected {unexpected[:5]}")
+    return lm.eval()
+
+
+def reference_logits(shape, weights, mode, packs):
+    sys.path.insert(0, REFERENCE)
+    from janus.hybrid import HybridBackbone
+    from janus.model import DecisionModel, ModelConfig, PointerHead, ScalarHead
+    from janus.packing import Branch as RefBranch, PackedRequest as RefPacked
+    lm = hf_model(shape, weights)
+    backbone = HybridBackbone(lm, tokenizer=None, attention="sdpa", state_chunk_tokens=4096)
+    model = DecisionModel.__new__(DecisionModel)
+    torch.nn.Module.__init__(model)
+    model.config = ModelConfig(backbone="tiny-qwen3_5", backbone_family="qwen3_5", mode=mode, adaptation="frozen",
+                               dtype="float32", attention="sdpa", tree_positions="continue")
+    model.backbone = backbone
+    if mode == "tree":
+        model.head = ScalarHead(shape.hidden)
+        model.head.out.weight.data = weights["head.out.weight"].float().clone()
+        model.head.out.bias.data = weights["head.out.bias"].float().clone()
+    else:
+        model.head = PointerHead(shape.hidden, shape.head_rank)
+        model.head.query.weight.data = weights["head.query.weight"].float().clone()
+        model.head.key.weight.data = weights["head.key.weight"].float().clone()
+    model.head.norm.weight.data = weights["head.norm.weight"].float().clone()
+    model.head.norm.bias.data = weights["head.norm.bias"].float().clone()
+    model.last_compute = None
+    refs = [RefPacked(p.input_ids, p.position_ids, p.segment_ids, p.parents,
+                      [RefBranch(b.start, b.end, b.question_index, b.option_indices, b.option_positions,
+                                 b.decision_position, b.kind, b.leaves) for b in p.branches],
+                      p.state_length, p.option_counts) for p in packs]
+    with torch.no_grad():
+        return model.forward_many(refs)
+
+
+def pack_to_dict(p):
+    return {"input_ids": p.input_ids[0].tolist(), "position_ids": p.position_ids[0].tolist(),
+            "segment_ids": p.segment_ids.tolist(), "parents": p.parents.tolist(), "state_length": p.state_length,
+            "option_counts": list(p.option_counts),
+            "branches": [dict(start=b.start, end=b.end, question_index=b.question_index,
+                              option_indices=list(b.option_indices), option_positions=list(b.option_positions),
+                              decision_position=b.decision_position, kind=b.kind,
+                              leaves=[list(x) for x in b.leaves]) for b in p.branches]}
+
+
+def delta_rule_vectors():
+    """Per-op vectors of the reference's gated delta rule (transformers torch_chunk_gated_delta_rule and
+    torch_recurrent_gated_delta_rule as janus.hybrid.chunk_rule returns them on CPU)."""
+    sys.path.insert(0, REFERENCE)
+    from janus.hybrid import chunk_rule
+    from transformers.models.qwen3_5.modeling_qwen3_5 import torch_recurrent_gated_delta_rule
+    g = torch.Generator().manual_seed(123)
+    B, T, Hk, Hv, D = 2, 150, 2, 4, 32
+    q = torch.randn(B, T, Hk, D, generator=g)
+    k = torch.randn(B, T, Hk, D, generator=g)
+    v = torch.randn(B, T, Hv, D, generator=g)
+    b = torch.randn(B, T, Hv, generator=g)
+    a = torch.randn(B, T, Hv, generator=g)
+    beta = torch.sigmoid(b)
+    g_ = -torch.rand(Hv, generator=g).mul(4).exp() * torch.nn.functional.softplus(a + 1.0)
+    s0 = torch.randn(B, Hv, D, D, generator=g) * 0.1
+    rep = lambda x: x.repeat_interleave(Hv // Hk, dim=2)
+    rule = chunk_rule("cpu")
+    o_c, s_c = rule(rep(q), rep(k), v, g=g_, beta=beta, initial_state=s0, output_final_state=True, use_qk_l2norm_in_kernel=True)
+    o_r, s_r = torch_recurrent_gated_delta_rule(rep(q[:, :9]), rep(k[:, :9]), v[:, :9], g=g_[:, :9], beta=beta[:, :9],
+                                                initial_state=s0, output_final_state=True, use_qk_l2norm_in_kernel=True)
+    return dict(q=q, k=k, v=v, g=g_, beta=beta, s0=s0, o_chunk=o_c, s_chunk=s_c, o_rec9=o_r, s_rec9=s_r)
+
+
+def main():
+    torch.set_num_threads(os.cpu_count() or 8)
+    manifest = {}
+    for name, (base, overrides, mode, seed, factory) in _cases().items():
+        shape = shape_of(base, dict(overrides))
+        packs = factory()
+        weights = synthetic.make_weights(shape, seed=seed, head="scalar" if mode == "tree" else "pointer")
+        logits = reference_logits(shape, weights, mode, packs)
+        probs = [[torch.softmax(z.float(), -1).tolist() for z in per] for per in logits]
+        manifest[name] = dict(shape=base.name, overrides=overrides, mode=mode, seed=seed,
+                              checksum=synthetic.weight_checksum(weights), packs=[pack_to_dict(p) for p in packs],
+                              logits=[[z.float().tolist() for z in per] for per in logits], probs=probs)
+        print(name, "questions", sum(len(p) for p in probs), flush=True)
+    (HERE / "readout_cases.json").write_text(json.dumps(manifest))
+    vec = delta_rule_vectors()
+    np.savez_compressed(HERE / "delta_rule.npz", **{k: v.numpy() for k, v in vec.items()})
+    print("wrote", HERE / "readout_cases.json", HERE / "delta_rule.npz")
+
+
+if __name__ == "__main__":
+    main()
