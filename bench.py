@@ -1,0 +1,336 @@
+"""Benchmark of the B200 decision readout (workload 3: the 4B shape, 16 requests of an 8192-token state and 8 tree
+questions per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One step is one forward readout of a batch of 16 requests (every level, every layer, heads): `value` is decision
+requests per second over all ranks with the level tables already on the device; `e2e` is the same metric through
+the public API (DecisionReadout.probabilities: host planning, one host-to-device copy, the device pass, one
+device-to-host copy of the logits and the softmax) per step. Weights are random (seeded) and generated on the
+device; requests are seeded synthetic token ids (no dataset). Multi-GPU: one process per GPU (torchrun), each rank a
+replica serving its own 16 requests (requests are independent: weak scaling, no collective on the data path); the
+step time is the max over ranks.
+
+`--impl reference` times the reference algorithm on the host cores instead: the CPU oracle (oracle/hybrid.py, a
+restatement of the reference's readout pinned to its golden outputs) on one request of the same workload through a
+2-layer slice of the model (one DeltaNet and one attention layer over every level), its per-layer times weighted by
+the model's 24 DeltaNet and 8 attention layers.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+WORKLOAD = 3
+REQUESTS_PER_GPU = 16
+METRIC = "decision requests/s (4B shape, 8K state, 8 questions)"
+UNIT = "requests/s"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class Clocks:
+    """nvidia-smi samples of SM clock and throttle reasons while running (start before, stop after the timed region)."""
+
+    def __init__(self, index, out):
+        self.out = out
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=open(out, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.out) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def attention_flops(levels, shape):
+    """4 * D * Hq * sum over query tokens of their visible keys (tree rule), per attention layer, per level."""
+    per = []
+    for lv in levels:
+        lengths = np.diff(lv.row_start.astype(np.int64))
+        own = float((lengths * (lengths + 1) // 2).sum())
+        anc = float(sum(((hi - lo).astype(np.int64) * lengths).sum() for lo, hi in zip(lv.anc_lo, lv.anc_hi)))
+        per.append(4.0 * shape.head_dim * shape.heads * (own + anc))
+    return per
+
+
+def chunk_algorithmic(levels, shape):
+    """DeltaNet chunk-scan FLOPs and bytes per launch (per DeltaNet layer) at each level: FLOPs per token per value
+    head 6*Dk*Dv + 2*C*(3*Dk + 2*Dv) (C = 64); bytes = q, k, v (bf16) + g, beta (fp32) in, o out (bf16), the final
+    fp32 state out when kept."""
+    Dk, Dv, Hk, Hv = shape.lin_k_dim, shape.lin_v_dim, shape.lin_k_heads, shape.lin_v_heads
+    out = []
+    for lv in levels:
+        T = lv.T
+        flops = T * Hv * (6 * Dk * Dv + 2 * 64 * (3 * Dk + 2 * Dv))
+        byts = T * (2 * Hk * Dk * 2 + Hv * Dv * 2 + Hv * 8 + Hv * Dv * 2) + (lv.B * Hv * Dk * Dv * 4 if lv.keep else 0)
+        out.append((flops, byts))
+    return out
+
+
+def run_reference(args):
+    """The reference arm: the CPU oracle on a bounded sample of the workload, all host threads."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    value, sample = cpu_reference_rate(args.steps, min(args.warmup, 1))
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 / value if value else None, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "4b-tree-8k-state-8q", "requests_per_gpu": 1, "sample": sample},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def cpu_reference_rate(steps=1, warmup=0):
+    """Seconds per request of the oracle for one full request of the workload (8192-token state, 8 questions)
+    through a 2-layer slice of the 4B shape (one DeltaNet and one attention layer, every level), weighted by the
+    model's layer counts (24 DeltaNet + 8 attention); returns (requests/s, description)."""
+    from janus_b200 import synthetic
+    from janus_b200.config import FULL, LINEAR, SHAPES
+    from oracle import hybrid as oracle
+    full = SHAPES["4b"]
+    shape = full.with_layers(2, vocab=4096)
+    shape = shape.__class__(**{**shape.__dict__, "layer_types": (LINEAR, FULL)})
+    weights = synthetic.make_weights(shape, seed=0, head="scalar", device="cpu")
+    model = oracle.Oracle(shape, weights)
+    pack = synthetic.q4b_request(vocab=4096, seed=0)
+    times = []
+    for i in range(max(0, warmup) + max(1, steps)):
+        model.layer_seconds = {}
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            oracle.probabilities(model.logits(pack, "tree"))
+        total = time.perf_counter() - t0
+        if i >= warmup:
+            rest = total - sum(model.layer_seconds.values())
+            n_lin = sum(1 for t in full.layer_types if t == LINEAR)
+            times.append(rest + n_lin * model.layer_seconds[LINEAR] + (full.layers - n_lin) * model.layer_seconds[FULL])
+    per_request = statistics.median(times)
+    sample = (f"one 4B-shape request ({pack.token_count} tokens: 8192-token state, 8 questions) through a 2-layer "
+              f"slice (1 DeltaNet + 1 attention layer) of the CPU oracle, fp32, {torch.get_num_threads()} threads, "
+              f"per-layer times weighted 24 DeltaNet + 8 attention, median of {len(times)}")
+    return 1.0 / per_request, sample
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--requests", type=int, default=REQUESTS_PER_GPU)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="debug: fewer layers (not a valid bench number)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+        pg = dist
+
+    from janus_b200 import ops, synthetic
+    from janus_b200.config import SHAPES
+    from janus_b200.model import DecisionReadout
+
+    shape = SHAPES["4b"]
+    if args.layers:
+        shape = shape.with_layers(args.layers)
+    weights = synthetic.make_weights(shape, seed=0, head="scalar", device=device)
+    model = DecisionReadout(shape, weights, "tree", device=device)
+    del weights
+    torch.cuda.empty_cache()
+    packs = [synthetic.q4b_request(seed=1000 * rank + j) for j in range(args.requests)]
+    tokens = sum(p.token_count for p in packs)
+    prepared = model.prepare(packs)
+    levels, readout, plan = prepared
+
+    def barrier():
+        if pg is not None:
+            pg.barrier(device_ids=[local])
+
+    def max_over_ranks(x):
+        if pg is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    # warm-up
+    for _ in range(args.warmup):
+        model.run(prepared)
+    torch.cuda.synchronize()
+
+    # timed device pass
+    attn_flops = attention_flops(levels, shape)
+    chunk_alg = chunk_algorithmic(levels, shape)
+    ops.TIMED.clear()
+    ops.TIMED["tree_attention"] = []
+    ops.TIMED["gdn_chunk_scan"] = []
+    ops.TIMED["gdn_fork_recurrent"] = []
+    clocks = Clocks(local, os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else ".",
+                                        f"clocks_rank{rank}.csv"))
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = ops.LAUNCHES[0]
+    step_events = []
+    for _ in range(args.steps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        model.run(prepared)
+        e.record()
+        step_events.append((s, e))
+    torch.cuda.synchronize()
+    barrier()
+    clock = clocks.stop()
+    launches = (ops.LAUNCHES[0] - launches0) // args.steps
+    step_ms = [s.elapsed_time(e) for s, e in step_events]
+    total_ms = max_over_ranks(sum(step_ms))
+    ms_per_step = total_ms / args.steps
+    value = world * args.requests / (ms_per_step / 1000.0)
+
+    # per-kernel device time inside the timed region
+    kernel_ms = {name: sum(s.elapsed_time(e) for s, e in rec) / args.steps for name, rec in ops.TIMED.items() if rec}
+    n_attn_layers = sum(1 for t in shape.layer_types if t != "linear_attention")
+    n_lin_layers = shape.layers - n_attn_layers
+    attn_launch = ops.TIMED["tree_attention"]
+    per_attn = [s.elapsed_time(e) for s, e in attn_launch]
+    ops.TIMED.clear()
+
+    # the roofline of the dominant kernel of the library
+    pk, pk_kind = peaks()
+    dominant = max(kernel_ms, key=kernel_ms.get) if kernel_ms else None
+    roof = None
+    if dominant == "tree_attention":
+        flops_step = n_attn_layers * sum(attn_flops)
+        launches_per_step = len(per_attn) // args.steps
+        achieved = flops_step / (kernel_ms[dominant] / 1000.0) / 1e12
+        peak = pk["bf16_tflops_sustained"]
+        roof = {"kernel": "tree_attention", "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "traffic": None, "peak_kind": f"{pk_kind} bf16 sustained",
+                "algorithmic_per_launch": flops_step / max(1, launches_per_step), "launches_per_step": launches_per_step,
+                "ms_per_step": kernel_ms[dominant]}
+    elif dominant in ("gdn_chunk_scan", "gdn_fork_recurrent"):
+        fl = sum(f for f, _ in chunk_alg) * n_lin_layers
+        by = sum(b for _, b in chunk_alg) * n_lin_layers
+        sec = kernel_ms[dominant] / 1000.0
+        t_peak = pk["bf16_tflops_sustained"] * 1e12
+        b_peak = pk["hbm_gbs"] * 1e9
+        bound = "tensor" if fl / t_peak > by / b_peak else "hbm"
+        if bound == "tensor":
+            roof = {"kernel": dominant, "bound": "tensor", "achieved": fl / sec / 1e12, "peak": t_peak / 1e12,
+                    "unit": "TFLOP/s", "frac": fl / sec / t_peak, "traffic": None}
+        else:
+            roof = {"kernel": dominant, "bound": "hbm", "achieved": by / sec / 1e9, "peak": b_peak / 1e9,
+                    "unit": "GB/s", "frac": by / sec / b_peak, "traffic": None}
+        roof["ms_per_step"] = kernel_ms[dominant]
+        roof["peak_kind"] = pk_kind
+
+    # end to end through the public API: host packing -> H2D -> device pass -> D2H -> softmax
+    e2e_ms = []
+    h2d = d2h = 0
+    barrier()
+    for _ in range(max(3, args.steps // 2)):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        lv, ro, pl = model.prepare(packs)
+        flat = model.run((lv, ro, pl))
+        host = flat.cpu()
+        probs = [torch.softmax(z, -1) for per in __import__("janus_b200.model", fromlist=["assemble"]).assemble(host, ro) for z in per]
+        e2e_ms.append((time.perf_counter() - t0) * 1000.0)
+        h2d, d2h = pl.h2d_bytes, flat.numel() * 4
+    e2e_step = max_over_ranks(statistics.median(e2e_ms))
+    e2e_value = world * args.requests / (e2e_step / 1000.0)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cores = os.cpu_count() or 1
+        torch.set_num_threads(cores)
+        v, sample = cpu_reference_rate(1, 0)
+        cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        lat = sorted(step_ms)
+        p = lambda q: lat[min(len(lat) - 1, max(0, int(np.ceil(q * len(lat))) - 1))]
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "4b-tree-8k-state-8q" + (f"-{args.layers}layers-INVALID" if args.layers else ""),
+                           "requests_per_gpu": args.requests, "tokens_per_gpu": tokens, "state_tokens": 8192,
+                           "questions": 8, "parallelism": f"dp{world} (replicas)",
+                           "l2": "inputs larger than L2 (activations of a level are GBs)"},
+                "latency_ms": {"p50": p(0.5), "p90": p(0.9), "per": "batch step (every request of the batch completes at its end)"},
+                "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                        "ms_per_step": e2e_step},
+                "gpu_launches": launches, "kernel_ms_per_step": kernel_ms, "roofline": roof, "cpu_baseline": cpu,
+                "clocks": clock}
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

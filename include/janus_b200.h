@@ -1,0 +1,143 @@
+/*
+ * janus_b200 — C ABI of the B200 (sm_100a) kernels of the Janus decision readout.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t passed as `void*`, launches asynchronously
+ * on that stream and returns 0 on success or a negative JANUS_* status (the text of the last error of the calling
+ * thread is available from janus_b200_last_error). No entry point allocates, frees, synchronises or keeps a pointer
+ * past the call; the caller owns every buffer, including workspaces. Kernels never trap: bad arguments are rejected
+ * on the host before any launch.
+ *
+ * Layouts: a "level" is a batch of rows (tree segments) packed back to back without padding: T tokens, B rows,
+ * row_start[B+1] the first token of each row (row_start[B] == T), row_of_token[T] the row of each token. Rows are
+ * ordered so that the children of one parent row are consecutive (tree order). bf16 is __nv_bfloat16.
+ *
+ * Each entry point names the reference interface it replaces (IcarusAICo/janus paths; transformers 5.5.0 for the
+ * modules the reference reuses).
+ */
+#ifndef JANUS_B200_H
+#define JANUS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define JANUS_OK 0
+#define JANUS_ERR_INVALID (-1)     /* null pointer, size or shape out of range */
+#define JANUS_ERR_ALIGNMENT (-2)   /* a pointer or stride breaks the kernel's vector alignment */
+#define JANUS_ERR_UNSUPPORTED (-3) /* a head dimension / configuration no kernel is compiled for */
+#define JANUS_ERR_WORKSPACE (-4)   /* workspace too small */
+#define JANUS_ERR_CUDA (-5)        /* a CUDA launch or runtime error */
+#define JANUS_ERR_TIMEOUT (-6)     /* a bounded device-side wait ran out */
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int janus_b200_version(void);
+
+/* Copies the calling thread's last error text into buf (always NUL-terminated); returns its full length. */
+int janus_b200_last_error(char* buf, size_t len);
+
+/* Token embedding gather and the first Qwen3_5RMSNorm of the decoder:
+ * x[t] = table[ids[t]] (fp32 residual stream), y[t] = x[t] * rsqrt(mean(x^2) + eps) * (1 + norm_w) in bf16.
+ * Replaces embed_tokens + layers[0].input_layernorm (janus/hybrid.py:1665-1676, 1081-1087). */
+int janus_b200_embed_rmsnorm(const void* table, int64_t vocab, int64_t hidden, const int32_t* ids, int64_t T,
+                             const void* norm_w, float eps, float* x, void* y, void* stream);
+
+/* Residual add and the next RMSNorm in one pass: x += delta (bf16 [T, hidden] rows of stride delta_stride, or
+ * NULL for no add), y = rmsnorm(x) * (1 + norm_w) in bf16. x is the fp32 residual stream.
+ * Replaces `_add_norm` / `_add_rmsnorm` (janus/hybrid.py:257-273) and Qwen3_5RMSNorm. */
+int janus_b200_add_rmsnorm(float* x, const void* delta, int64_t delta_stride, int64_t T, int64_t hidden,
+                           const void* norm_w, float eps, void* y, void* stream);
+
+/* SwiGLU gate: out[t, i] = silu(gu[t, i]) * gu[t, I + i] (gu bf16 [T, 2I], out bf16 [T, I]).
+ * Replaces `_silu_mul` (janus/hybrid.py:263-264) on the merged gate/up projection (janus/hybrid.py:1108-1133). */
+int janus_b200_silu_mul(const void* gu, int64_t T, int64_t inter, void* out, void* stream);
+
+/* Gated RMSNorm over each value head: out = rmsnorm(core) * w * silu(z) (core bf16 [T, Hv, Dv]; z bf16 rows of
+ * stride z_stride, head h at column h*Dv; out bf16 [T, Hv*Dv]).
+ * Replaces `_gate_norm` / Qwen3_5RMSNormGated (janus/hybrid.py:241-247). */
+int janus_b200_gated_rmsnorm(const void* core, const void* z, int64_t z_stride, int64_t T, int64_t Hv, int64_t Dv,
+                             const void* w, float eps, void* out, void* stream);
+
+/* DeltaNet prologue of one level: causal depthwise conv (K taps) over [parent tail || projections] in fp32,
+ * silu, l2-normalised q and k (eps 1e-6), v, beta = sigmoid(b), g = -exp(A_log) * softplus(a + dt_bias).
+ * proj: bf16 rows of stride proj_stride with columns [q Hk*Dk | k Hk*Dk | v Hv*Dv | z Hv*Dv | b Hv | a Hv].
+ * tail_in: bf16 [B_parent, K-1, C] conv inputs before each parent row's end, row parent[b] (NULL: zeros);
+ * tail_out: bf16 [B, K-1, C] the last K-1 conv inputs of each row (NULL: not kept).
+ * Outputs q, k bf16 [T, Hk, Dk], v bf16 [T, Hv, Dv], g, beta fp32 [T, Hv].
+ * Replaces `_delta_serve` / `_delta_mix` (janus/hybrid.py:220-238, 276-301). */
+int janus_b200_gdn_prologue(const void* proj, int64_t proj_stride, int64_t T, int64_t B, const int32_t* row_start,
+                            const int32_t* row_of_token, const int32_t* parent, const void* tail_in, void* tail_out,
+                            const void* conv_w, const void* A_log, const void* dt_bias, int64_t Hk, int64_t Dk,
+                            int64_t Hv, int64_t Dv, int64_t K, void* q, void* k, void* v, float* g, float* beta,
+                            void* stream);
+
+/* Gated delta rule, token by token, with the per-branch state fork read in place: the rows of a level are grouped
+ * under P parents (children of parent p are rows child_start[p] .. child_start[p+1]-1); every child starts from
+ * its parent's fp32 state state_in[p] ([P, Hv, Dk, Dv], NULL: zeros) without copying it, and runs
+ * S <- S*exp(g); S <- S + k (beta (v - S^T k))^T; o = scale * S^T q over its tokens (value head h reads qk head
+ * h / (Hv/Hk)). state_out [B, Hv, Dk, Dv] receives each row's final state (NULL: not kept). o bf16 [T, Hv, Dv].
+ * Replaces the `index_select` fork + fla fused_recurrent_gated_delta_rule (janus/hybrid.py:1082-1083,
+ * 1064-1065; transformers torch_recurrent_gated_delta_rule). */
+int janus_b200_gdn_fork_recurrent(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                                  int64_t T, int64_t B, const int32_t* row_start, const int32_t* child_start,
+                                  int64_t P, const float* state_in, float* state_out, int64_t Hk, int64_t Hv,
+                                  int64_t Dk, int64_t Dv, float scale, void* o, void* stream);
+
+/* Gated delta rule in 64-token chunks for long rows (the state level): per (row, value head) the intra-chunk WY
+ * form on the tensor cores and the fp32 state carried across chunks. Row b starts from state_in[state_row[b]]
+ * ([*, Hv, Dk, Dv] fp32, read in place; state_row NULL: row b; state_in NULL: zeros); state_out [B, Hv, Dk, Dv]
+ * (NULL: not kept). Dk = Dv = 128 only. Same results as janus_b200_gdn_fork_recurrent up to fp32/bf16
+ * accumulation order.
+ * Replaces fla chunk_gated_delta_rule (janus/hybrid.py:100-125, 1064-1069; transformers
+ * torch_chunk_gated_delta_rule). */
+int janus_b200_gdn_chunk_scan(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                              int64_t T, int64_t B, const int32_t* row_start, const float* state_in,
+                              const int32_t* state_row, float* state_out,
+                              int64_t Hk, int64_t Hv, int64_t Dk, int64_t Dv, float scale, void* o, void* stream);
+
+/* Attention q/k preparation: per head RMSNorm (1 + w) of q and k, rotary on the first `rot` dims (cos/sin of
+ * positions[t] * inv_freq[i], fp32), v copied. qkv: bf16 rows of stride qkv_stride with columns
+ * [per q head: query D | gate D] (Hq*2D) | k Hkv*D | v Hkv*D]. Outputs q bf16 [T, Hq, D], k, v bf16 [T, Hkv, D].
+ * Replaces `_attn_serve` / `_attn_qk` (janus/hybrid.py:304-329) and apply_rotary_pos_emb. */
+int janus_b200_attn_qk_prep(const void* qkv, int64_t qkv_stride, int64_t T, const int32_t* positions,
+                            const float* inv_freq, int64_t rot, const void* q_norm_w, const void* k_norm_w, float eps,
+                            int64_t Hq, int64_t Hkv, int64_t D, void* q, void* k, void* v, void* stream);
+
+/* Tree attention of one level with the output gate: every query token attends, in one online softmax, to the
+ * tokens of its row's ancestor at each earlier level (key range [anc_lo[l][row], anc_hi[l][row]) of level l's
+ * keys) and to its own row's tokens causally; out = softmax(q k^T * scale) v * sigmoid(gate). GQA folded: the
+ * Hq/Hkv query heads of a kv head share every K/V tile. n_levels = ancestors + 1; k_levels[n_levels-1] is the
+ * level's own keys ([T, Hkv, D]). tiles: [n_tiles, 2] query token ranges [start, end) chosen by the caller (each
+ * within one request; janus_b200 python builds them). gate: bf16, token t head h at gate[t*gate_stride +
+ * h*gate_head_stride + d]. out bf16 [T, Hq*D]. D in {32, 64, 128, 256}.
+ * Replaces branch_attention / state_attention / _piece / _merge_gate (janus/hybrid.py:806-855, 943-989) and the
+ * tree rule of janus/attention.py:10-23. */
+int janus_b200_tree_attention(const void* q, int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int32_t n_levels,
+                              const void* const* k_levels, const void* const* v_levels,
+                              const int32_t* const* anc_lo, const int32_t* const* anc_hi, const int32_t* row_start,
+                              const int32_t* row_of_token, const int32_t* tiles, int64_t n_tiles, const void* gate,
+                              int64_t gate_stride, int64_t gate_head_stride, float scale, void* out, void* stream);
+
+/* ScalarHead readout fused with the final norm: for each of n rows r = rows[i] of the fp32 residual x [*, H]:
+ * h = rmsnorm(x[r]) * (1 + final_w) (eps rms_eps), logits[i] = LayerNorm(h; ln_w, ln_b, ln_eps) . w_out + b_out[0].
+ * Replaces lm.norm + ScalarHead.forward (janus/model.py:85-92, 342-350). */
+int janus_b200_head_scalar(const float* x, int64_t H, const int32_t* rows, int64_t n, const void* final_w,
+                           float rms_eps, const float* ln_w, const float* ln_b, float ln_eps, const float* w_out,
+                           const float* b_out, float* logits, void* stream);
+
+/* PointerHead readout fused with the final norm: option i (row option_rows[i], question option_question[i])
+ * scores logits[i] = (LN(h_opt) Wk^T) . (LN(h_dec) Wq^T) / sqrt(R), h the final-normed rows, h_dec the row
+ * decision_rows[option_question[i]]. wq, wk fp32 [R, H]. workspace: fp32, at least (n + Q) * R floats.
+ * Replaces lm.norm + PointerHead.forward (janus/model.py:71-82, 361-365). */
+int janus_b200_head_pointer(const float* x, int64_t H, const int32_t* option_rows, const int32_t* option_question,
+                            int64_t n, const int32_t* decision_rows, int64_t Q, const void* final_w, float rms_eps,
+                            const float* ln_w, const float* ln_b, float ln_eps, const float* wq, const float* wk,
+                            int64_t R, float* workspace, size_t workspace_bytes, float* logits, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* JANUS_B200_H */

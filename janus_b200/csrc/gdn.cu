@@ -1,0 +1,239 @@
+// Gated DeltaNet: the prologue (conv + silu + l2 + gates) and the recurrent rule with the in-place state fork.
+//
+// Prologue: one CTA per token; every 16-byte vector of 8 channels reads its K conv taps (the previous tokens of
+// the row, or the parent row's conv tail for the first K-1 tokens), so the projection output is read ~K times
+// from L1/L2 and once from HBM. q and k are l2-normalised per head with a shuffle reduction over the lanes that
+// hold the head. Rounding follows the reference: the conv activation is rounded once to bf16, the l2 norm is
+// computed in fp32 from that value and rounded once more (janus/hybrid.py:276-301).
+//
+// Fork recurrent: grid (parent row, value head). A parent's fp32 state [Dk, Dv] is read in place by every child row
+// (no per-row copy); each thread holds Dk*Dv/256 state entries (one value column, a slice of the key rows), so the
+// two reductions over the key dimension per token are a register loop plus one shared-memory exchange.
+#include "common.cuh"
+
+namespace jb {
+
+constexpr int kProThreads = 256;
+constexpr int kMaxTaps = 8;
+
+__global__ void __launch_bounds__(kProThreads) gdn_prologue_kernel(
+    const __nv_bfloat16* __restrict__ proj, int64_t proj_stride, const int32_t* __restrict__ row_start,
+    const int32_t* __restrict__ row_of_token, const int32_t* __restrict__ parent,
+    const __nv_bfloat16* __restrict__ tail_in, __nv_bfloat16* __restrict__ tail_out,
+    const __nv_bfloat16* __restrict__ conv_w, const __nv_bfloat16* __restrict__ A_log,
+    const __nv_bfloat16* __restrict__ dt_bias, int Hk, int Dk, int Hv, int Dv, int K, __nv_bfloat16* __restrict__ q,
+    __nv_bfloat16* __restrict__ k, __nv_bfloat16* __restrict__ v, float* __restrict__ g, float* __restrict__ beta) {
+  const int64_t t = blockIdx.x;
+  const int row = row_of_token[t];
+  const int64_t r0 = row_start[row];
+  const int64_t L = row_start[row + 1] - r0;
+  const int64_t i = t - r0;  // local index in the row
+  const int key_dim = Hk * Dk;
+  const int C = 2 * key_dim + Hv * Dv;
+  const int nv = C >> 3;
+  const int lanes_per_head = Dk >> 3;  // vectors per q/k head (Dk in {32,64,128,256})
+  const __nv_bfloat16* tail = (tail_in && parent) ? tail_in + (int64_t)parent[row] * (K - 1) * C : nullptr;
+  for (int base = 0; base < nv; base += blockDim.x) {
+    const int vec = base + threadIdx.x;
+    const bool live = vec < nv;
+    const int c0 = vec * 8;
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    if (live) {
+      // conv weights of the 8 channels: K taps each, contiguous [8][K]
+      for (int j = 0; j < K; ++j) {
+        // ext index i + j; ext[e] = tail[e] for e < K-1, else proj[r0 + e - (K-1)]
+        const int64_t e = i + j;
+        float xin[8];
+        if (e >= K - 1) {
+          load8(proj + (r0 + e - (K - 1)) * proj_stride + c0, xin);
+        } else if (tail) {
+          load8(tail + e * C + c0, xin);
+        } else {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) xin[u] = 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc[u] += xin[u] * bf2f(conv_w[(int64_t)(c0 + u) * K + j]);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc[u] = bf2f(f2bf(silu(acc[u])));  // rounded once, as the reference does
+    }
+    // l2 norm over each q / k head: lanes_per_head consecutive lanes hold one head
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) ss += acc[u] * acc[u];
+    for (int o = lanes_per_head >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (live) {
+      if (c0 < 2 * key_dim) {
+        const float r = rsqrtf(ss + 1e-6f);
+        float o8[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) o8[u] = acc[u] * r;
+        if (c0 < key_dim)
+          store8(q + t * key_dim + c0, o8);
+        else
+          store8(k + t * key_dim + (c0 - key_dim), o8);
+      } else {
+        store8(v + t * (int64_t)(Hv * Dv) + (c0 - 2 * key_dim), acc);
+      }
+      // conv tail of the row: the last K-1 conv inputs, written by the CTA of the row's last token
+      if (tail_out && i == L - 1) {
+        for (int j = 0; j < K - 1; ++j) {
+          const int64_t e = L + j;  // ext index
+          float xin[8];
+          if (e >= K - 1) {
+            load8(proj + (r0 + e - (K - 1)) * proj_stride + c0, xin);
+          } else if (tail) {
+            load8(tail + e * C + c0, xin);
+          } else {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) xin[u] = 0.f;
+          }
+          store8(tail_out + ((int64_t)row * (K - 1) + j) * C + c0, xin);
+        }
+      }
+    }
+  }
+  // gates: b at column C + Hv*Dv + h, a at C + Hv*Dv + Hv + h
+  for (int h = threadIdx.x; h < Hv; h += blockDim.x) {
+    const float b = bf2f(proj[t * proj_stride + C + Hv * Dv + h]);
+    const float a = bf2f(proj[t * proj_stride + C + Hv * Dv + Hv + h]);
+    beta[t * Hv + h] = sigmoidf_(b);
+    g[t * Hv + h] = -expf(bf2f(A_log[h])) * softplus(a + bf2f(dt_bias[h]));
+  }
+}
+
+// ------------------------------------------------------------------------------------------- fork recurrent rule
+
+template <int DK, int DV>
+__global__ void __launch_bounds__(256) gdn_fork_recurrent_kernel(
+    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
+    const float* __restrict__ g, const float* __restrict__ beta, const int32_t* __restrict__ row_start,
+    const int32_t* __restrict__ child_start, const float* __restrict__ state_in, float* __restrict__ state_out,
+    int Hk, int Hv, float scale, __nv_bfloat16* __restrict__ o) {
+  constexpr int NT = 256;
+  constexpr int NRG = NT / DV;     // row groups
+  constexpr int ROWS = DK / NRG;   // key rows per thread
+  static_assert(NT % DV == 0 && DK % NRG == 0, "state tiling");
+  __shared__ float s_k[DK], s_q[DK], s_v[DV], s_red[NRG][DV], s_gb[2];
+  const int p = blockIdx.x, h = blockIdx.y;
+  const int hk = h / (Hv / Hk);
+  const int j = threadIdx.x % DV, rg = threadIdx.x / DV;
+  const int64_t sbase_in = ((int64_t)p * Hv + h) * DK * DV;
+  for (int c = child_start[p]; c < child_start[p + 1]; ++c) {
+    float S[ROWS];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) S[r] = state_in ? state_in[sbase_in + (int64_t)(rg * ROWS + r) * DV + j] : 0.f;
+    for (int64_t t = row_start[c]; t < row_start[c + 1]; ++t) {
+      __syncthreads();  // the previous token's readers of s_k/s_q/s_v are done
+      for (int x = threadIdx.x; x < DK; x += NT) {
+        s_k[x] = bf2f(k[(t * Hk + hk) * DK + x]);
+        s_q[x] = bf2f(q[(t * Hk + hk) * DK + x]) * scale;
+      }
+      for (int x = threadIdx.x; x < DV; x += NT) s_v[x] = bf2f(v[(t * Hv + h) * DV + x]);
+      if (threadIdx.x == 0) {
+        s_gb[0] = expf(g[t * Hv + h]);
+        s_gb[1] = beta[t * Hv + h];
+      }
+      __syncthreads();
+      const float decay = s_gb[0];
+      float kv = 0.f;
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) {
+        S[r] *= decay;
+        kv += S[r] * s_k[rg * ROWS + r];
+      }
+      s_red[rg][j] = kv;
+      __syncthreads();
+      kv = 0.f;
+#pragma unroll
+      for (int x = 0; x < NRG; ++x) kv += s_red[x][j];
+      const float delta = (s_v[j] - kv) * s_gb[1];
+      float ov = 0.f;
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) {
+        S[r] += s_k[rg * ROWS + r] * delta;
+        ov += S[r] * s_q[rg * ROWS + r];
+      }
+      __syncthreads();  // everyone has read s_red (kv) before it is reused for o
+      s_red[rg][j] = ov;
+      __syncthreads();
+      if (rg == 0) {
+        float acc = 0.f;
+#pragma unroll
+        for (int x = 0; x < NRG; ++x) acc += s_red[x][j];
+        o[(t * Hv + h) * DV + j] = f2bf(acc);
+      }
+    }
+    if (state_out) {
+      const int64_t sb = ((int64_t)c * Hv + h) * DK * DV;
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) state_out[sb + (int64_t)(rg * ROWS + r) * DV + j] = S[r];
+    }
+  }
+}
+
+}  // namespace jb
+
+using namespace jb;
+
+extern "C" int janus_b200_gdn_prologue(const void* proj, int64_t proj_stride, int64_t T, int64_t B,
+                                       const int32_t* row_start, const int32_t* row_of_token, const int32_t* parent,
+                                       const void* tail_in, void* tail_out, const void* conv_w, const void* A_log,
+                                       const void* dt_bias, int64_t Hk, int64_t Dk, int64_t Hv, int64_t Dv, int64_t K,
+                                       void* q, void* k, void* v, float* g, float* beta, void* stream) {
+  JB_REQUIRE(proj && row_start && row_of_token && conv_w && A_log && dt_bias && q && k && v && g && beta,
+             JANUS_ERR_INVALID, "gdn_prologue: null pointer");
+  JB_REQUIRE(T >= 0 && B >= 0 && Hk > 0 && Hv > 0 && Hv % Hk == 0 && K >= 2 && K <= kMaxTaps, JANUS_ERR_INVALID,
+             "gdn_prologue: bad head counts or K");
+  JB_REQUIRE(Dk == 32 || Dk == 64 || Dk == 128 || Dk == 256, JANUS_ERR_UNSUPPORTED, "gdn_prologue: Dk %lld",
+             (long long)Dk);
+  JB_REQUIRE(Dv % 8 == 0, JANUS_ERR_UNSUPPORTED, "gdn_prologue: Dv %lld", (long long)Dv);
+  const int64_t C = 2 * Hk * Dk + Hv * Dv;
+  JB_REQUIRE(proj_stride >= C + Hv * Dv + 2 * Hv && proj_stride % 8 == 0, JANUS_ERR_INVALID,
+             "gdn_prologue: proj stride %lld < %lld", (long long)proj_stride, (long long)(C + Hv * Dv + 2 * Hv));
+  JB_REQUIRE(JB_ALIGNED(proj, 16) && JB_ALIGNED(q, 16) && JB_ALIGNED(k, 16) && JB_ALIGNED(v, 16) &&
+                 (!tail_in || JB_ALIGNED(tail_in, 16)) && (!tail_out || JB_ALIGNED(tail_out, 16)),
+             JANUS_ERR_ALIGNMENT, "gdn_prologue: 16-byte alignment");
+  JB_REQUIRE(!tail_in || parent, JANUS_ERR_INVALID, "gdn_prologue: tail_in needs parent");
+  if (T == 0) return JANUS_OK;
+  gdn_prologue_kernel<<<(unsigned)T, kProThreads, 0, (cudaStream_t)stream>>>(
+      (const __nv_bfloat16*)proj, proj_stride, row_start, row_of_token, parent, (const __nv_bfloat16*)tail_in,
+      (__nv_bfloat16*)tail_out, (const __nv_bfloat16*)conv_w, (const __nv_bfloat16*)A_log,
+      (const __nv_bfloat16*)dt_bias, (int)Hk, (int)Dk, (int)Hv, (int)Dv, (int)K, (__nv_bfloat16*)q,
+      (__nv_bfloat16*)k, (__nv_bfloat16*)v, g, beta);
+  return launch_status("gdn_prologue");
+}
+
+extern "C" int janus_b200_gdn_fork_recurrent(const void* q, const void* k, const void* v, const float* g,
+                                             const float* beta, int64_t T, int64_t B, const int32_t* row_start,
+                                             const int32_t* child_start, int64_t P, const float* state_in,
+                                             float* state_out, int64_t Hk, int64_t Hv, int64_t Dk, int64_t Dv,
+                                             float scale, void* o, void* stream) {
+  JB_REQUIRE(q && k && v && g && beta && row_start && child_start && o, JANUS_ERR_INVALID,
+             "gdn_fork_recurrent: null pointer");
+  JB_REQUIRE(T >= 0 && B >= 0 && P >= 0 && Hk > 0 && Hv > 0 && Hv % Hk == 0, JANUS_ERR_INVALID,
+             "gdn_fork_recurrent: sizes");
+  if (P == 0 || T == 0) return JANUS_OK;
+  JB_REQUIRE(P <= 0x7fffffff && Hv <= 65535, JANUS_ERR_INVALID, "gdn_fork_recurrent: grid too large");
+  dim3 grid((unsigned)P, (unsigned)Hv);
+  cudaStream_t s = (cudaStream_t)stream;
+#define JB_FORK(DK_, DV_)                                                                                        \
+  gdn_fork_recurrent_kernel<DK_, DV_><<<grid, 256, 0, s>>>(                                                      \
+      (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, g, beta, row_start, child_start, \
+      state_in, state_out, (int)Hk, (int)Hv, scale, (__nv_bfloat16*)o)
+  if (Dk == 128 && Dv == 128) {
+    JB_FORK(128, 128);
+  } else if (Dk == 64 && Dv == 64) {
+    JB_FORK(64, 64);
+  } else if (Dk == 32 && Dv == 32) {
+    JB_FORK(32, 32);
+  } else {
+    set_error("gdn_fork_recurrent: (Dk, Dv) = (%lld, %lld) not compiled", (long long)Dk, (long long)Dv);
+    return JANUS_ERR_UNSUPPORTED;
+  }
+#undef JB_FORK
+  return launch_status("gdn_fork_recurrent");
+}

@@ -1,0 +1,134 @@
+// Readout heads fused with the decoder's final RMSNorm: a gather of the readout rows of the fp32 residual stream,
+// RMSNorm (1 + w), LayerNorm, and the Scalar / Pointer projections, all fp32. HBM/latency-bound: the gathered rows
+// are (options + decisions) * hidden * 4 bytes and the head weights are read once per CTA from L2.
+#include "common.cuh"
+
+namespace jb {
+
+constexpr int kHeadThreads = 256;
+constexpr int kHeadMaxH = 8192;
+
+// Final RMSNorm then LayerNorm of one row into shared memory `ln` (H floats); returns nothing, ln filled.
+__device__ void norm_row(const float* __restrict__ xr, int H, const __nv_bfloat16* __restrict__ final_w, float rms_eps,
+                         const float* __restrict__ ln_w, const float* __restrict__ ln_b, float ln_eps, float* ln,
+                         float* red) {
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float v = xr[i];
+    ln[i] = v;
+    ss += v * v;
+  }
+  ss = block_sum(ss, red);
+  const float r = rsqrtf(ss / (float)H + rms_eps);
+  float s = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float h = ln[i] * r * (1.f + bf2f(final_w[i]));
+    ln[i] = h;
+    s += h;
+  }
+  __syncthreads();
+  s = block_sum(s, red);
+  const float mean = s / (float)H;
+  float var = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float d = ln[i] - mean;
+    var += d * d;
+  }
+  __syncthreads();
+  var = block_sum(var, red);
+  const float inv = rsqrtf(var / (float)H + ln_eps);
+  for (int i = threadIdx.x; i < H; i += blockDim.x) ln[i] = (ln[i] - mean) * inv * ln_w[i] + ln_b[i];
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kHeadThreads) head_scalar_kernel(const float* __restrict__ x, int H,
+                                                                   const int32_t* __restrict__ rows,
+                                                                   const __nv_bfloat16* __restrict__ final_w,
+                                                                   float rms_eps, const float* __restrict__ ln_w,
+                                                                   const float* __restrict__ ln_b, float ln_eps,
+                                                                   const float* __restrict__ w_out,
+                                                                   const float* __restrict__ b_out,
+                                                                   float* __restrict__ logits) {
+  extern __shared__ float ln[];
+  __shared__ float red[32];
+  const int i = blockIdx.x;
+  norm_row(x + (int64_t)rows[i] * H, H, final_w, rms_eps, ln_w, ln_b, ln_eps, ln, red);
+  float d = 0.f;
+  for (int j = threadIdx.x; j < H; j += blockDim.x) d += ln[j] * w_out[j];
+  d = block_sum(d, red);
+  if (threadIdx.x == 0) logits[i] = d + b_out[0];
+}
+
+// Row i < n: option row (projected by wk); row n + q: the decision row of question q (projected by wq).
+__global__ void __launch_bounds__(kHeadThreads) head_project_kernel(
+    const float* __restrict__ x, int H, const int32_t* __restrict__ option_rows, int n,
+    const int32_t* __restrict__ decision_rows, const __nv_bfloat16* __restrict__ final_w, float rms_eps,
+    const float* __restrict__ ln_w, const float* __restrict__ ln_b, float ln_eps, const float* __restrict__ wq,
+    const float* __restrict__ wk, int R, float* __restrict__ proj) {
+  extern __shared__ float ln[];
+  __shared__ float red[32];
+  const int i = blockIdx.x;
+  const int row = i < n ? option_rows[i] : decision_rows[i - n];
+  const float* W = i < n ? wk : wq;
+  norm_row(x + (int64_t)row * H, H, final_w, rms_eps, ln_w, ln_b, ln_eps, ln, red);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int j = warp; j < R; j += nw) {
+    const float* wr = W + (int64_t)j * H;
+    float d = 0.f;
+    for (int c = lane; c < H; c += 32) d += ln[c] * wr[c];
+    d = warp_sum(d);
+    if (lane == 0) proj[(int64_t)i * R + j] = d;
+  }
+}
+
+__global__ void head_dot_kernel(const float* __restrict__ proj, int n, const int32_t* __restrict__ option_question,
+                                int R, float inv_scale, float* __restrict__ logits) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= n) return;
+  const float* a = proj + (int64_t)w * R;
+  const float* b = proj + (int64_t)(n + option_question[w]) * R;
+  float d = 0.f;
+  for (int j = lane; j < R; j += 32) d += a[j] * b[j];
+  d = warp_sum(d);
+  if (lane == 0) logits[w] = d * inv_scale;
+}
+
+}  // namespace jb
+
+using namespace jb;
+
+extern "C" int janus_b200_head_scalar(const float* x, int64_t H, const int32_t* rows, int64_t n, const void* final_w,
+                                      float rms_eps, const float* ln_w, const float* ln_b, float ln_eps,
+                                      const float* w_out, const float* b_out, float* logits, void* stream) {
+  JB_REQUIRE(x && rows && final_w && ln_w && ln_b && w_out && b_out && logits, JANUS_ERR_INVALID,
+             "head_scalar: null pointer");
+  JB_REQUIRE(H > 0 && H <= kHeadMaxH && n >= 0, JANUS_ERR_INVALID, "head_scalar: hidden %lld out of range", (long long)H);
+  if (n == 0) return JANUS_OK;
+  head_scalar_kernel<<<(unsigned)n, kHeadThreads, H * sizeof(float), (cudaStream_t)stream>>>(
+      x, (int)H, rows, (const __nv_bfloat16*)final_w, rms_eps, ln_w, ln_b, ln_eps, w_out, b_out, logits);
+  return launch_status("head_scalar");
+}
+
+extern "C" int janus_b200_head_pointer(const float* x, int64_t H, const int32_t* option_rows,
+                                       const int32_t* option_question, int64_t n, const int32_t* decision_rows,
+                                       int64_t Q, const void* final_w, float rms_eps, const float* ln_w,
+                                       const float* ln_b, float ln_eps, const float* wq, const float* wk, int64_t R,
+                                       float* workspace, size_t workspace_bytes, float* logits, void* stream) {
+  JB_REQUIRE(x && option_rows && option_question && decision_rows && final_w && ln_w && ln_b && wq && wk && logits,
+             JANUS_ERR_INVALID, "head_pointer: null pointer");
+  JB_REQUIRE(H > 0 && H <= kHeadMaxH && n >= 0 && Q >= 0 && R > 0, JANUS_ERR_INVALID, "head_pointer: sizes");
+  JB_REQUIRE(workspace && workspace_bytes >= (size_t)(n + Q) * R * sizeof(float), JANUS_ERR_WORKSPACE,
+             "head_pointer: workspace %zu bytes < %lld", workspace_bytes, (long long)((n + Q) * R * 4));
+  if (n == 0) return JANUS_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  head_project_kernel<<<(unsigned)(n + Q), kHeadThreads, H * sizeof(float), s>>>(
+      x, (int)H, option_rows, (int)n, decision_rows, (const __nv_bfloat16*)final_w, rms_eps, ln_w, ln_b, ln_eps, wq,
+      wk, (int)R, workspace);
+  int st = launch_status("head_pointer/project");
+  if (st) return st;
+  const int th = 256;
+  head_dot_kernel<<<(unsigned)((n * 32 + th - 1) / th), th, 0, s>>>(workspace, (int)n, option_question, (int)R,
+                                                                   1.f / sqrtf((float)R), logits);
+  return launch_status("head_pointer/dot");
+}

@@ -1,0 +1,195 @@
+// Row-wise glue between the GEMMs: embedding + RMSNorm, residual add + RMSNorm, SwiGLU gate, gated RMSNorm.
+// All HBM-bound: one CTA (or warp) per token row, 16-byte vector loads, one pass over the inputs, fp32 math and
+// a single rounding to bf16 at each output.
+#include "common.cuh"
+
+namespace jb {
+
+constexpr int kNormThreads = 128;
+constexpr int kNormVec = 4;  // vectors of 8 per thread kept in registers: hidden <= 8 * 4 * threads
+
+// y = x * rsqrt(mean(x^2) + eps) * (1 + w); x fp32 [H] already in registers as vals.
+template <bool kEmbed>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_kernel(const __nv_bfloat16* __restrict__ table,
+                                                                     const int32_t* __restrict__ ids,
+                                                                     const __nv_bfloat16* __restrict__ delta,
+                                                                     int64_t delta_stride, float* __restrict__ x,
+                                                                     int H, const __nv_bfloat16* __restrict__ w,
+                                                                     float eps, __nv_bfloat16* __restrict__ y) {
+  __shared__ float red[32];
+  const int64_t t = blockIdx.x;
+  const int nv = H >> 3;
+  float vals[kNormVec][8];
+  float ss = 0.f;
+  float* xr = x + t * (int64_t)H;
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    const int v = threadIdx.x + j * blockDim.x;
+    if (v < nv) {
+      if (kEmbed) {
+        load8(table + (int64_t)ids[t] * H + v * 8, vals[j]);
+      } else {
+        float4 a = reinterpret_cast<const float4*>(xr)[2 * v];
+        float4 b = reinterpret_cast<const float4*>(xr)[2 * v + 1];
+        vals[j][0] = a.x; vals[j][1] = a.y; vals[j][2] = a.z; vals[j][3] = a.w;
+        vals[j][4] = b.x; vals[j][5] = b.y; vals[j][6] = b.z; vals[j][7] = b.w;
+        if (delta) {
+          float d[8];
+          load8(delta + t * delta_stride + v * 8, d);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) vals[j][i] += d[i];
+        }
+      }
+      if (kEmbed || delta) {
+        reinterpret_cast<float4*>(xr)[2 * v] = make_float4(vals[j][0], vals[j][1], vals[j][2], vals[j][3]);
+        reinterpret_cast<float4*>(xr)[2 * v + 1] = make_float4(vals[j][4], vals[j][5], vals[j][6], vals[j][7]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += vals[j][i] * vals[j][i];
+    }
+  }
+  ss = block_sum(ss, red);
+  const float r = rsqrtf(ss / (float)H + eps);
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    const int v = threadIdx.x + j * blockDim.x;
+    if (v < nv) {
+      float wv[8], o[8];
+      load8(w + v * 8, wv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = vals[j][i] * r * (1.f + wv[i]);
+      store8(y + t * (int64_t)H + v * 8, o);
+    }
+  }
+}
+
+__global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int64_t T, int I, __nv_bfloat16* __restrict__ out) {
+  const int64_t n = T * (I >> 3);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / (I >> 3);
+    const int c = (int)(i - t * (I >> 3)) * 8;
+    float g[8], u[8], o[8];
+    load8(gu + t * 2 * I + c, g);
+    load8(gu + t * 2 * I + I + c, u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = silu(g[j]) * u[j];
+    store8(out + t * I + c, o);
+  }
+}
+
+// One warp per (token, value head); Dv / 32 elements per lane.
+template <int DV>
+__global__ void gated_rmsnorm_kernel(const __nv_bfloat16* __restrict__ core, const __nv_bfloat16* __restrict__ z,
+                                     int64_t z_stride, int64_t T, int Hv, const __nv_bfloat16* __restrict__ w,
+                                     float eps, __nv_bfloat16* __restrict__ out) {
+  constexpr int E = DV / 32;
+  const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= T * Hv) return;
+  const int64_t t = gw / Hv;
+  const int h = (int)(gw - t * Hv);
+  const __nv_bfloat16* c = core + gw * DV + lane * E;
+  const __nv_bfloat16* zz = z + t * z_stride + (int64_t)h * DV + lane * E;
+  float cv[E], ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < E; ++i) {
+    cv[i] = bf2f(c[i]);
+    ss += cv[i] * cv[i];
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)DV + eps);
+#pragma unroll
+  for (int i = 0; i < E; ++i) {
+    const float zv = bf2f(zz[i]);
+    out[gw * DV + lane * E + i] = f2bf(bf2f(w[lane * E + i]) * (cv[i] * r) * silu(zv));
+  }
+}
+
+static int check_norm_args(int64_t T, int64_t H, const void* y, const void* w) {
+  JB_REQUIRE(T >= 0 && H > 0 && H % 8 == 0 && H <= 8 * kNormVec * kNormThreads, JANUS_ERR_INVALID,
+             "rmsnorm: hidden %lld must be a positive multiple of 8 up to %d", (long long)H, 8 * kNormVec * kNormThreads);
+  JB_REQUIRE(y && w, JANUS_ERR_INVALID, "rmsnorm: null output or weight");
+  JB_REQUIRE(JB_ALIGNED(y, 16) && JB_ALIGNED(w, 16), JANUS_ERR_ALIGNMENT, "rmsnorm: output/weight not 16-byte aligned");
+  return JANUS_OK;
+}
+
+}  // namespace jb
+
+using namespace jb;
+
+extern "C" int janus_b200_embed_rmsnorm(const void* table, int64_t vocab, int64_t hidden, const int32_t* ids,
+                                        int64_t T, const void* norm_w, float eps, float* x, void* y, void* stream) {
+  int st = check_norm_args(T, hidden, y, norm_w);
+  if (st) return st;
+  JB_REQUIRE(table && ids && x && vocab > 0, JANUS_ERR_INVALID, "embed_rmsnorm: null table/ids/x");
+  JB_REQUIRE(JB_ALIGNED(table, 16) && JB_ALIGNED(x, 16), JANUS_ERR_ALIGNMENT, "embed_rmsnorm: table/x alignment");
+  if (T == 0) return JANUS_OK;
+  JB_REQUIRE((hidden / 8 + kNormThreads - 1) / kNormThreads <= kNormVec, JANUS_ERR_UNSUPPORTED,
+             "embed_rmsnorm: hidden %lld too large", (long long)hidden);
+  rmsnorm_rows_kernel<true><<<(unsigned)T, kNormThreads, 0, (cudaStream_t)stream>>>(
+      (const __nv_bfloat16*)table, ids, nullptr, 0, x, (int)hidden, (const __nv_bfloat16*)norm_w, eps,
+      (__nv_bfloat16*)y);
+  return launch_status("embed_rmsnorm");
+}
+
+extern "C" int janus_b200_add_rmsnorm(float* x, const void* delta, int64_t delta_stride, int64_t T, int64_t hidden,
+                                      const void* norm_w, float eps, void* y, void* stream) {
+  int st = check_norm_args(T, hidden, y, norm_w);
+  if (st) return st;
+  JB_REQUIRE(x, JANUS_ERR_INVALID, "add_rmsnorm: null x");
+  JB_REQUIRE(JB_ALIGNED(x, 16), JANUS_ERR_ALIGNMENT, "add_rmsnorm: x alignment");
+  if (delta) {
+    JB_REQUIRE(delta_stride >= hidden && delta_stride % 8 == 0 && JB_ALIGNED(delta, 16), JANUS_ERR_ALIGNMENT,
+               "add_rmsnorm: delta stride %lld / alignment", (long long)delta_stride);
+  }
+  if (T == 0) return JANUS_OK;
+  JB_REQUIRE((hidden / 8 + kNormThreads - 1) / kNormThreads <= kNormVec, JANUS_ERR_UNSUPPORTED,
+             "add_rmsnorm: hidden %lld too large", (long long)hidden);
+  rmsnorm_rows_kernel<false><<<(unsigned)T, kNormThreads, 0, (cudaStream_t)stream>>>(
+      nullptr, nullptr, (const __nv_bfloat16*)delta, delta_stride, x, (int)hidden, (const __nv_bfloat16*)norm_w,
+      eps, (__nv_bfloat16*)y);
+  return launch_status("add_rmsnorm");
+}
+
+extern "C" int janus_b200_silu_mul(const void* gu, int64_t T, int64_t inter, void* out, void* stream) {
+  JB_REQUIRE(gu && out && T >= 0 && inter > 0 && inter % 8 == 0, JANUS_ERR_INVALID,
+             "silu_mul: bad arguments (inter %lld must be a multiple of 8)", (long long)inter);
+  JB_REQUIRE(JB_ALIGNED(gu, 16) && JB_ALIGNED(out, 16), JANUS_ERR_ALIGNMENT, "silu_mul: alignment");
+  if (T == 0) return JANUS_OK;
+  const int64_t n = T * (inter / 8);
+  const int th = 256;
+  int blocks = (int)((n + th - 1) / th);
+  if (blocks > 148 * 64) blocks = 148 * 64;
+  silu_mul_kernel<<<blocks, th, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)gu, T, (int)inter,
+                                                          (__nv_bfloat16*)out);
+  return launch_status("silu_mul");
+}
+
+extern "C" int janus_b200_gated_rmsnorm(const void* core, const void* z, int64_t z_stride, int64_t T, int64_t Hv,
+                                        int64_t Dv, const void* w, float eps, void* out, void* stream) {
+  JB_REQUIRE(core && z && w && out && T >= 0 && Hv > 0 && z_stride >= Hv * Dv, JANUS_ERR_INVALID,
+             "gated_rmsnorm: bad arguments");
+  if (T == 0) return JANUS_OK;
+  const int64_t warps = T * Hv;
+  const int th = 256;
+  const unsigned blocks = (unsigned)((warps * 32 + th - 1) / th);
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (Dv) {
+    case 32:
+      gated_rmsnorm_kernel<32><<<blocks, th, 0, s>>>((const __nv_bfloat16*)core, (const __nv_bfloat16*)z, z_stride, T,
+                                                     (int)Hv, (const __nv_bfloat16*)w, eps, (__nv_bfloat16*)out);
+      break;
+    case 64:
+      gated_rmsnorm_kernel<64><<<blocks, th, 0, s>>>((const __nv_bfloat16*)core, (const __nv_bfloat16*)z, z_stride, T,
+                                                     (int)Hv, (const __nv_bfloat16*)w, eps, (__nv_bfloat16*)out);
+      break;
+    case 128:
+      gated_rmsnorm_kernel<128><<<blocks, th, 0, s>>>((const __nv_bfloat16*)core, (const __nv_bfloat16*)z, z_stride,
+                                                      T, (int)Hv, (const __nv_bfloat16*)w, eps, (__nv_bfloat16*)out);
+      break;
+    default:
+      set_error("gated_rmsnorm: Dv %lld not compiled (32, 64, 128)", (long long)Dv);
+      return JANUS_ERR_UNSUPPORTED;
+  }
+  return launch_status("gated_rmsnorm");
+}

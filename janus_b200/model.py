@@ -1,0 +1,201 @@
+"""The B200 decision readout: the hybrid backbone run level by level over packed tree levels, and the heads.
+
+This is the drop-in for `HybridBackbone.encode_many` + `DecisionModel.forward` + `Worker.probabilities`
+(janus/hybrid.py:1631-1807, janus/model.py:319-373, janus/server.py:277-282): the same packed requests in, the same
+per-question logits and probabilities out. Per level and layer the work is: the dense projections (cuBLAS bf16
+GEMMs on merged weights, as `_merge_projections` merges them, janus/hybrid.py:1108-1133) and every other op through
+libjanus_b200 (janus_b200.ops): embedding + RMSNorm, residual add + RMSNorm (fp32 residual stream), the DeltaNet
+prologue, the gated delta rule with the state fork read in place, the gated RMSNorm, attention q/k preparation,
+tree attention with the output gate, the SwiGLU gate and the heads fused with the final norm. Levels keep their
+DeltaNet states (conv tail, fp32 recurrent matrix) and attention keys/values only when a deeper level reads them.
+"""
+
+import math
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from . import ops
+from .config import LINEAR, ModelShape
+from .plan import DevicePlan, build_levels, build_readout
+
+
+class _Layer:
+    pass
+
+
+class DecisionReadout:
+    """One model on one CUDA device. `weights`: name -> tensor (janus_b200.synthetic.make_weights layout, HF names),
+    on any device; `mode`: "tree" (ScalarHead per leaf) or "listwise" (PointerHead)."""
+
+    def __init__(self, shape: ModelShape, weights, mode="tree", device="cuda"):
+        if mode not in ("tree", "listwise"):
+            raise ValueError("mode must be tree or listwise")
+        if shape.moe:
+            raise ValueError("MoE feed-forward not supported by this readout yet")
+        self.shape, self.mode = shape, mode
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("janus_b200 runs on CUDA devices only")
+        dev = self.device
+        w = lambda n, dt=torch.bfloat16: weights[n].to(dev, dt).contiguous()
+        self.embed = w("embed_tokens.weight")
+        self.final_norm = w("norm.weight")
+        self.layers = []
+        for i, kind in enumerate(shape.layer_types):
+            p = f"layers.{i}."
+            L = _Layer()
+            L.kind = kind
+            L.in_norm = w(p + "input_layernorm.weight")
+            L.post_norm = w(p + "post_attention_layernorm.weight")
+            if kind == LINEAR:
+                a = p + "linear_attn."
+                L.proj = torch.cat([w(a + n + ".weight") for n in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a")])
+                L.conv = w(a + "conv1d.weight").reshape(shape.conv_dim, shape.conv_kernel).contiguous()
+                L.A_log, L.dt_bias, L.gnorm = w(a + "A_log"), w(a + "dt_bias"), w(a + "norm.weight")
+                L.out = w(a + "out_proj.weight")
+            else:
+                a = p + "self_attn."
+                L.qkv = torch.cat([w(a + n + ".weight") for n in ("q_proj", "k_proj", "v_proj")])
+                L.q_norm, L.k_norm = w(a + "q_norm.weight"), w(a + "k_norm.weight")
+                L.o = w(a + "o_proj.weight")
+            m = p + "mlp."
+            L.gate_up = torch.cat([w(m + "gate_proj.weight"), w(m + "up_proj.weight")])
+            L.down = w(m + "down_proj.weight")
+            self.layers.append(L)
+        f32 = lambda n: w(n, torch.float32)
+        self.head = {k[5:]: f32(k) for k in weights if k.startswith("head.")}
+        r = shape.rotary_dim
+        # Qwen3_5TextRotaryEmbedding.compute_default_rope_parameters, fp32
+        self.inv_freq = (1.0 / (shape.rope_theta ** (torch.arange(0, r, 2, dtype=torch.int64).float() / r))).to(dev)
+        self.group = shape.heads // shape.kv_heads
+        self.last_plan = None
+
+    # ------------------------------------------------------------------------------------------------ level pass
+
+    def _level(self, lv, plan, history, logits):
+        s = self.shape
+        d, T = lv.depth, lv.T
+        eps = s.rms_eps
+        rs, rot = plan[(d, "row_start")], plan[(d, "row_of_token")]
+        x, y = ops.embed_rmsnorm(self.embed, plan[(d, "ids")], self.layers[0].in_norm, eps)
+        pending = None
+        kept = []
+        Vd, C = s.value_dim, s.conv_dim
+        for i, L in enumerate(self.layers):
+            if i > 0:
+                y = ops.add_rmsnorm(x, pending, L.in_norm, eps)
+            if L.kind == LINEAR:
+                proj = F.linear(y, L.proj)
+                parent_state = history[d - 1][i] if d > 0 else (None, None)
+                q, k, v, g, beta, tail = ops.gdn_prologue(
+                    proj, rs, rot, plan[(d, "parent")] if d > 0 else None, parent_state[0], lv.keep, L.conv, L.A_log,
+                    L.dt_bias, s.lin_k_heads, s.lin_k_dim, s.lin_v_heads, s.lin_v_dim)
+                if self._chunked(lv):
+                    o, S = ops.gdn_chunk_scan(q, k, v, g, beta, rs, parent_state[1],
+                                              plan[(d, "parent")] if d > 0 else None, lv.keep, 1.0 / math.sqrt(s.lin_k_dim))
+                else:
+                    o, S = ops.gdn_fork_recurrent(q, k, v, g, beta, rs, plan[(d, "child_start")], parent_state[1],
+                                                  lv.keep, 1.0 / math.sqrt(s.lin_k_dim))
+                core = ops.gated_rmsnorm(o, proj[:, C:C + Vd], L.gnorm, eps)
+                h = F.linear(core, L.out)
+                kept.append((tail, S) if lv.keep else None)
+            else:
+                qkv = F.linear(y, L.qkv)
+                D, Hq, Hkv = s.head_dim, s.heads, s.kv_heads
+                q, kk, vv = ops.attn_qk_prep(qkv, plan[(d, "pos")], self.inv_freq, L.q_norm, L.k_norm, eps, Hq, Hkv, D)
+                keys = [history[l][i][0] for l in range(d)] + [kk]
+                values = [history[l][i][1] for l in range(d)] + [vv]
+                gate = qkv[:, :Hq * 2 * D].view(T, Hq, 2 * D)[:, :, D:]
+                o = ops.tree_attention(q, keys, values, [plan[(d, "lo", l)] for l in range(d)],
+                                       [plan[(d, "hi", l)] for l in range(d)], rs, rot,
+                                       plan[(d, "tiles", self.group)].view(-1, 2), gate, D ** -0.5)
+                h = F.linear(o, L.o)
+                kept.append((kk, vv) if lv.keep else None)
+            y = ops.add_rmsnorm(x, h, L.post_norm, eps)
+            pending = F.linear(ops.silu_mul(F.linear(y, L.gate_up)), L.down)
+        ops.add_rmsnorm(x, pending, self.final_norm, eps)  # the last residual add (its normed output is unused)
+        self._heads(d, x, plan, logits)
+        return kept
+
+    CHUNK_MIN_TOKENS = 32  # mean row length from which a level runs the chunked rule (rows are read once per chunk)
+
+    def _chunked(self, lv):
+        """The chunked rule for levels of long rows (tensor-core WY form), the fork-recurrent rule for short ones
+        (the reference's split at janus/hybrid.py:115-118, RECURRENT_TOKENS = 16)."""
+        s = self.shape
+        return s.lin_k_dim == 128 and s.lin_v_dim == 128 and lv.T >= self.CHUNK_MIN_TOKENS * lv.B
+
+    def _heads(self, d, x, plan, logits):
+        ro = self._readout
+        hd, s = self.head, self.shape
+        if d in ro.scalar:
+            _, slots = ro.scalar[d]
+            z = ops.head_scalar(x, plan[(d, "scalar_rows")], self.final_norm, s.rms_eps, hd["norm.weight"],
+                                hd["norm.bias"], 1e-5, hd["out.weight"].reshape(-1), hd["out.bias"])
+            logits[torch.as_tensor(slots, device=x.device)] = z
+        if d in ro.pointer:
+            slots = ro.pointer[d][3]
+            z = ops.head_pointer(x, plan[(d, "opt_rows")], plan[(d, "opt_q")], plan[(d, "dec_rows")], self.final_norm,
+                                 s.rms_eps, hd["norm.weight"], hd["norm.bias"], 1e-5, hd["query.weight"],
+                                 hd["key.weight"])
+            logits[torch.as_tensor(slots, device=x.device)] = z
+
+    # ------------------------------------------------------------------------------------------------ public API
+
+    def plan(self, packs):
+        for p in packs:
+            ids = p.input_ids
+            if ids.numel() and (int(ids.min()) < 0 or int(ids.max()) >= self.shape.vocab):
+                raise ValueError(f"token ids must lie in [0, {self.shape.vocab})")
+        levels, index = build_levels(packs)
+        readout = build_readout(packs, levels, index, self.mode)
+        return levels, readout
+
+    def prepare(self, packs):
+        """Host planning plus the one host-to-device copy of the level tables: (levels, readout, device plan)."""
+        levels, readout = self.plan(packs)
+        return levels, readout, DevicePlan(levels, readout, self.device, groups=(self.group,))
+
+    def run(self, prepared):
+        """The device pass over prepared levels: all option logits as one fp32 device tensor [slots]."""
+        levels, readout, plan = prepared
+        self._readout = readout
+        self.last_plan = plan
+        logits = torch.zeros(readout.n_slots, dtype=torch.float32, device=self.device)
+        history = []
+        for lv in levels:
+            history.append(self._level(lv, plan, history, logits))
+        return logits
+
+    def logits_flat(self, packs):
+        """All option logits of a batch as one fp32 device tensor [slots] (order: pack, question, option; the
+        constant false option of a tree-mode noul has no slot) plus the host readout layout."""
+        prepared = self.prepare(packs)
+        return self.run(prepared), prepared[1]
+
+    def forward_many(self, packs):
+        """Per pack, per question, the logits as fp32 CPU tensors (janus/model.py:368-373 + :319-366)."""
+        flat, readout = self.logits_flat(packs)
+        host = flat.cpu()
+        return assemble(host, readout)
+
+    def probabilities(self, packs, temperatures=None):
+        """Worker.probabilities (janus/server.py:277-282): softmax(logits / T) per question, T = 1 by default."""
+        out = []
+        for i, per in enumerate(self.forward_many(packs)):
+            ts = (temperatures[i] if temperatures else None) or [1.0] * len(per)
+            out.append([torch.softmax(z / t, dim=-1) for z, t in zip(per, ts)])
+        return out
+
+
+def assemble(host_logits, readout):
+    """Per pack, per question logits from the flat host tensor and the readout layout."""
+    res = []
+    for layout in readout.layout:
+        per = []
+        for slots in layout:
+            per.append(torch.stack([host_logits[s] if s is not None else torch.zeros(()) for s in slots]))
+        res.append(per)
+    return res

@@ -1,0 +1,245 @@
+"""torch-tensor wrappers over the C ABI (include/janus_b200.h). Each op checks dtypes/devices/contiguity, launches
+on the current CUDA stream of the tensors' device and returns the output tensors; errors raise (ValueError for bad
+arguments, janus_b200._lib.JanusError for CUDA failures). There is no CPU path."""
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+BF16, F32, I32 = torch.bfloat16, torch.float32, torch.int32
+
+# Instrumentation for the benchmark: LAUNCHES counts the kernels launched through this module; for op names in
+# TIMED, every call records a CUDA event pair on the launching stream into TIMED[name] (start, end, call kwargs
+# summary) so kernel durations can be read after a synchronize.
+LAUNCHES = [0]
+TIMED = {}
+
+
+def _instrument(name, kernels=1):
+    def wrap(fn):
+        def inner(*args, **kwargs):
+            LAUNCHES[0] += kernels
+            rec = TIMED.get(name)
+            if rec is None:
+                return fn(*args, **kwargs)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            out = fn(*args, **kwargs)
+            e.record()
+            rec.append((s, e))
+            return out
+        inner.__name__, inner.__doc__ = fn.__name__, fn.__doc__
+        return inner
+    return wrap
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _need(t, dtype, name, contiguous=True):
+    if t is None:
+        raise ValueError(f"{name} is required")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (janus_b200 has no CPU path)")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if contiguous and not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t
+
+
+@_instrument("embed_rmsnorm", 1)
+def embed_rmsnorm(table, ids, norm_w, eps, x=None, y=None):
+    _need(table, BF16, "table"); _need(ids, I32, "ids"); _need(norm_w, BF16, "norm_w")
+    T, H = ids.shape[0], table.shape[1]
+    x = torch.empty(T, H, dtype=F32, device=ids.device) if x is None else x
+    y = torch.empty(T, H, dtype=BF16, device=ids.device) if y is None else y
+    _lib.check(_lib.load().janus_b200_embed_rmsnorm(_ptr(table), table.shape[0], H, _ptr(ids), T, _ptr(norm_w), eps,
+                                                    _ptr(x), _ptr(y), _stream(ids)), "embed_rmsnorm")
+    return x, y
+
+
+@_instrument("add_rmsnorm", 1)
+def add_rmsnorm(x, delta, norm_w, eps, y=None):
+    """x += delta (in place; delta may be None or a row-strided bf16 view), returns y = rmsnorm(x) * (1 + w)."""
+    _need(x, F32, "x"); _need(norm_w, BF16, "norm_w")
+    T, H = x.shape
+    if delta is not None:
+        _need(delta, BF16, "delta", contiguous=False)
+        if delta.stride(1) != 1 or delta.shape != (T, H):
+            raise ValueError("delta must be [T, H] with unit column stride")
+    y = torch.empty(T, H, dtype=BF16, device=x.device) if y is None else y
+    _lib.check(_lib.load().janus_b200_add_rmsnorm(_ptr(x), _ptr(delta), 0 if delta is None else delta.stride(0), T, H,
+                                                  _ptr(norm_w), eps, _ptr(y), _stream(x)), "add_rmsnorm")
+    return y
+
+
+@_instrument("silu_mul", 1)
+def silu_mul(gu, out=None):
+    _need(gu, BF16, "gu")
+    T, two_i = gu.shape
+    out = torch.empty(T, two_i // 2, dtype=BF16, device=gu.device) if out is None else out
+    _lib.check(_lib.load().janus_b200_silu_mul(_ptr(gu), T, two_i // 2, _ptr(out), _stream(gu)), "silu_mul")
+    return out
+
+
+@_instrument("gated_rmsnorm", 1)
+def gated_rmsnorm(core, z, w, eps, out=None):
+    """core bf16 [T, Hv, Dv]; z bf16 [T, Hv*Dv] view with unit column stride."""
+    _need(core, BF16, "core"); _need(z, BF16, "z", contiguous=False); _need(w, BF16, "w")
+    T, Hv, Dv = core.shape
+    if z.stride(1) != 1 or z.shape != (T, Hv * Dv):
+        raise ValueError("z must be [T, Hv*Dv] with unit column stride")
+    out = torch.empty(T, Hv * Dv, dtype=BF16, device=core.device) if out is None else out
+    _lib.check(_lib.load().janus_b200_gated_rmsnorm(_ptr(core), _ptr(z), z.stride(0), T, Hv, Dv, _ptr(w), eps, _ptr(out),
+                                                    _stream(core)), "gated_rmsnorm")
+    return out
+
+
+@_instrument("gdn_prologue", 1)
+def gdn_prologue(proj, row_start, row_of_token, parent, tail_in, keep_tail, conv_w, A_log, dt_bias, Hk, Dk, Hv, Dv):
+    """proj bf16 [T, >= C + Hv*Dv + 2Hv] (unit column stride). Returns q, k, v, g, beta, tail_out (or None)."""
+    _need(proj, BF16, "proj", contiguous=False)
+    if proj.stride(1) != 1:
+        raise ValueError("proj must have unit column stride")
+    T = proj.shape[0]
+    B = row_start.shape[0] - 1
+    C = 2 * Hk * Dk + Hv * Dv
+    K = conv_w.shape[-1]
+    dev = proj.device
+    q = torch.empty(T, Hk, Dk, dtype=BF16, device=dev)
+    k = torch.empty(T, Hk, Dk, dtype=BF16, device=dev)
+    v = torch.empty(T, Hv, Dv, dtype=BF16, device=dev)
+    g = torch.empty(T, Hv, dtype=F32, device=dev)
+    beta = torch.empty(T, Hv, dtype=F32, device=dev)
+    tail_out = torch.empty(B, K - 1, C, dtype=BF16, device=dev) if keep_tail else None
+    if tail_in is not None:
+        _need(tail_in, BF16, "tail_in")
+    _lib.check(_lib.load().janus_b200_gdn_prologue(
+        _ptr(proj), proj.stride(0), T, B, _ptr(_need(row_start, I32, "row_start")),
+        _ptr(_need(row_of_token, I32, "row_of_token")), _ptr(parent), _ptr(tail_in), _ptr(tail_out),
+        _ptr(_need(conv_w, BF16, "conv_w")), _ptr(_need(A_log, BF16, "A_log")), _ptr(_need(dt_bias, BF16, "dt_bias")),
+        Hk, Dk, Hv, Dv, K, _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _stream(proj)), "gdn_prologue")
+    return q, k, v, g, beta, tail_out
+
+
+@_instrument("gdn_fork_recurrent", 1)
+def gdn_fork_recurrent(q, k, v, g, beta, row_start, child_start, state_in, keep_state, scale):
+    """Rows grouped under P = len(child_start) - 1 parents; state_in [P, Hv, Dk, Dv] fp32 or None."""
+    T, Hk, Dk = q.shape
+    Hv, Dv = v.shape[1], v.shape[2]
+    B = row_start.shape[0] - 1
+    P = child_start.shape[0] - 1
+    o = torch.empty(T, Hv, Dv, dtype=BF16, device=q.device)
+    state_out = torch.empty(B, Hv, Dk, Dv, dtype=F32, device=q.device) if keep_state else None
+    if state_in is not None:
+        _need(state_in, F32, "state_in")
+        if state_in.shape[0] != P:
+            raise ValueError(f"state_in has {state_in.shape[0]} rows for {P} parents")
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _need(t, BF16, n)
+    _lib.check(_lib.load().janus_b200_gdn_fork_recurrent(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(_need(g, F32, "g")), _ptr(_need(beta, F32, "beta")), T, B,
+        _ptr(_need(row_start, I32, "row_start")), _ptr(_need(child_start, I32, "child_start")), P, _ptr(state_in),
+        _ptr(state_out), Hk, Hv, Dk, Dv, scale, _ptr(o), _stream(q)), "gdn_fork_recurrent")
+    return o, state_out
+
+
+@_instrument("gdn_chunk_scan", 1)
+def gdn_chunk_scan(q, k, v, g, beta, row_start, state_in, state_row, keep_state, scale):
+    """Long rows in 64-token chunks; row b starts from state_in[state_row[b]] (None: zeros / identity map)."""
+    T, Hk, Dk = q.shape
+    Hv, Dv = v.shape[1], v.shape[2]
+    B = row_start.shape[0] - 1
+    o = torch.empty(T, Hv, Dv, dtype=BF16, device=q.device)
+    state_out = torch.empty(B, Hv, Dk, Dv, dtype=F32, device=q.device) if keep_state else None
+    if state_in is not None:
+        _need(state_in, F32, "state_in")
+    if state_row is not None:
+        _need(state_row, I32, "state_row")
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _need(t, BF16, n)
+    _lib.check(_lib.load().janus_b200_gdn_chunk_scan(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(_need(g, F32, "g")), _ptr(_need(beta, F32, "beta")), T, B,
+        _ptr(_need(row_start, I32, "row_start")), _ptr(state_in), _ptr(state_row), _ptr(state_out), Hk, Hv, Dk, Dv,
+        scale, _ptr(o), _stream(q)), "gdn_chunk_scan")
+    return o, state_out
+
+
+@_instrument("attn_qk_prep", 1)
+def attn_qk_prep(qkv, positions, inv_freq, q_norm_w, k_norm_w, eps, Hq, Hkv, D, k_out=None, v_out=None):
+    _need(qkv, BF16, "qkv", contiguous=False)
+    if qkv.stride(1) != 1:
+        raise ValueError("qkv must have unit column stride")
+    T = qkv.shape[0]
+    dev = qkv.device
+    q = torch.empty(T, Hq, D, dtype=BF16, device=dev)
+    k = torch.empty(T, Hkv, D, dtype=BF16, device=dev) if k_out is None else k_out
+    v = torch.empty(T, Hkv, D, dtype=BF16, device=dev) if v_out is None else v_out
+    _lib.check(_lib.load().janus_b200_attn_qk_prep(
+        _ptr(qkv), qkv.stride(0), T, _ptr(_need(positions, I32, "positions")), _ptr(_need(inv_freq, F32, "inv_freq")),
+        inv_freq.shape[0] * 2, _ptr(_need(q_norm_w, BF16, "q_norm_w")), _ptr(_need(k_norm_w, BF16, "k_norm_w")), eps,
+        Hq, Hkv, D, _ptr(q), _ptr(k), _ptr(v), _stream(qkv)), "attn_qk_prep")
+    return q, k, v
+
+
+@_instrument("tree_attention", 1)
+def tree_attention(q, keys, values, anc_lo, anc_hi, row_start, row_of_token, tiles, gate, scale, out=None):
+    """q bf16 [T, Hq, D]; keys/values: per level [T_l, Hkv, D] (last = own); anc_lo/anc_hi: per ancestor level
+    int32 [B]; tiles int32 [n, 2]; gate: bf16 view [T, Hq, D] (any strides with unit last stride)."""
+    _need(q, BF16, "q")
+    T, Hq, D = q.shape
+    Hkv = keys[-1].shape[1]
+    n = len(keys)
+    if len(values) != n or len(anc_lo) != n - 1 or len(anc_hi) != n - 1:
+        raise ValueError("tree_attention: one key/value array per level and one range pair per ancestor level")
+    for t in (*keys, *values):
+        _need(t, BF16, "keys/values")
+    for t in (*anc_lo, *anc_hi):
+        _need(t, I32, "ancestor ranges")
+    _need(gate, BF16, "gate", contiguous=False)
+    if gate.stride(2) != 1:
+        raise ValueError("gate must have unit last stride")
+    out = torch.empty(T, Hq * D, dtype=BF16, device=q.device) if out is None else out
+    arr = lambda ts: (ctypes.c_void_p * max(1, len(ts)))(*[t.data_ptr() for t in ts])
+    karr, varr, larr, harr = arr(keys), arr(values), arr(anc_lo), arr(anc_hi)
+    _lib.check(_lib.load().janus_b200_tree_attention(
+        _ptr(q), T, Hq, Hkv, D, n, ctypes.cast(karr, ctypes.c_void_p), ctypes.cast(varr, ctypes.c_void_p),
+        ctypes.cast(larr, ctypes.c_void_p), ctypes.cast(harr, ctypes.c_void_p), _ptr(_need(row_start, I32, "row_start")),
+        _ptr(_need(row_of_token, I32, "row_of_token")), _ptr(_need(tiles, I32, "tiles")), tiles.shape[0], _ptr(gate),
+        gate.stride(0), gate.stride(1), scale, _ptr(out), _stream(q)), "tree_attention")
+    return out
+
+
+@_instrument("head_scalar", 1)
+def head_scalar(x, rows, final_w, rms_eps, ln_w, ln_b, ln_eps, w_out, b_out, logits=None):
+    _need(x, F32, "x"); _need(rows, I32, "rows")
+    n = rows.shape[0]
+    logits = torch.empty(n, dtype=F32, device=x.device) if logits is None else logits
+    _lib.check(_lib.load().janus_b200_head_scalar(_ptr(x), x.shape[1], _ptr(rows), n, _ptr(_need(final_w, BF16, "final_w")),
+                                                  rms_eps, _ptr(_need(ln_w, F32, "ln_w")), _ptr(_need(ln_b, F32, "ln_b")),
+                                                  ln_eps, _ptr(_need(w_out, F32, "w_out")), _ptr(_need(b_out, F32, "b_out")),
+                                                  _ptr(logits), _stream(x)), "head_scalar")
+    return logits
+
+
+@_instrument("head_pointer", 2)
+def head_pointer(x, option_rows, option_question, decision_rows, final_w, rms_eps, ln_w, ln_b, ln_eps, wq, wk,
+                 logits=None, workspace=None):
+    _need(x, F32, "x")
+    n, Q, R = option_rows.shape[0], decision_rows.shape[0], wq.shape[0]
+    logits = torch.empty(n, dtype=F32, device=x.device) if logits is None else logits
+    workspace = torch.empty((n + Q) * R, dtype=F32, device=x.device) if workspace is None else workspace
+    _lib.check(_lib.load().janus_b200_head_pointer(
+        _ptr(x), x.shape[1], _ptr(_need(option_rows, I32, "option_rows")), _ptr(_need(option_question, I32, "option_question")),
+        n, _ptr(_need(decision_rows, I32, "decision_rows")), Q, _ptr(_need(final_w, BF16, "final_w")), rms_eps,
+        _ptr(_need(ln_w, F32, "ln_w")), _ptr(_need(ln_b, F32, "ln_b")), ln_eps, _ptr(_need(wq, F32, "wq")),
+        _ptr(_need(wk, F32, "wk")), R, _ptr(workspace), workspace.numel() * 4, _ptr(logits), _stream(x)), "head_pointer")
+    return logits

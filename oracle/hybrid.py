@@ -18,6 +18,7 @@ module against them.
 """
 
 import math
+import time
 
 import torch
 import torch.nn.functional as F
@@ -149,23 +150,25 @@ def apply_rope(x, cos, sin):
 def attention(q, k_all, v_all, n_prefix, scale):
     """Softmax attention of the L own queries q [L, Hq, D] over keys [n_prefix + L, Hkv, D]: every prefix (ancestor)
     key and the own keys causally, the tree rule along one root-to-leaf path (janus/attention.py:10-23). GQA: query
-    head h reads kv head h // (Hq / Hkv). Query chunks bound the score matrix. Returns [L, Hq, D]."""
+    head h reads kv head h // (Hq / Hkv), folded without repeating the keys. Query chunks bound the score matrix.
+    Returns [L, Hq, D]."""
     L, Hq, D = q.shape
     T, Hkv, _ = k_all.shape
     grp = Hq // Hkv
-    kr = k_all.float().repeat_interleave(grp, dim=1).transpose(0, 1)  # [Hq, T, D]
-    vr = v_all.float().repeat_interleave(grp, dim=1).transpose(0, 1)
-    qt = q.float().transpose(0, 1)
-    out = torch.empty(Hq, L, D)
+    kt = k_all.float().permute(1, 2, 0)            # [Hkv, D, T]
+    vt = v_all.float().transpose(0, 1)             # [Hkv, T, D]
+    qt = q.float().view(L, Hkv, grp, D).permute(1, 2, 0, 3)  # [Hkv, G, L, D]
+    out = torch.empty(Hkv, grp, L, D)
     step = max(1, (256 << 20) // (4 * Hq * max(T, 1)))
     keys = torch.arange(T)
     for a in range(0, L, step):
         b = min(L, a + step)
-        s = qt[:, a:b] @ kr.transpose(1, 2) * scale
+        s = torch.matmul(qt[:, :, a:b].reshape(Hkv, grp * (b - a), D), kt).view(Hkv, grp, b - a, T) * scale
         allowed = keys[None, :] <= (n_prefix + torch.arange(a, b))[:, None]
-        s = s.masked_fill(~allowed[None], float("-inf"))
-        out[:, a:b] = torch.softmax(s, dim=-1) @ vr
-    return out.transpose(0, 1)
+        s = s.masked_fill(~allowed, float("-inf"))
+        p = torch.softmax(s, dim=-1).view(Hkv, grp * (b - a), T)
+        out[:, :, a:b] = torch.matmul(p, vt).view(Hkv, grp, b - a, D)
+    return out.permute(2, 0, 1, 3).reshape(L, Hq, D)
 
 
 def moe_block(x, p, shape):
@@ -260,6 +263,7 @@ class Oracle:
             w[name] = t.float()
         self.w = w
         self.chunk_threshold = chunk_threshold
+        self.layer_seconds = {}  # wall seconds spent per layer kind (the CPU baseline scales a slice by these)
 
     def _p(self, prefix):
         n = len(prefix)
@@ -276,6 +280,7 @@ class Oracle:
         cos, sin = rope_tables(positions, s.rotary_dim, s.rope_theta)
         states = []
         for i, kind in enumerate(s.layer_types):
+            t0 = time.perf_counter()
             p = self._p(f"layers.{i}.")
             h = rmsnorm(x, p["input_layernorm.weight"], s.rms_eps)
             if kind == LINEAR:
@@ -311,6 +316,7 @@ class Oracle:
             x = x + h
             h = rmsnorm(x, p["post_attention_layernorm.weight"], s.rms_eps)
             x = x + (moe_block(h, self._p(f"layers.{i}.mlp."), s) if s.moe else mlp(h, self._p(f"layers.{i}.mlp.")))
+            self.layer_seconds[kind] = self.layer_seconds.get(kind, 0.0) + time.perf_counter() - t0
         return rmsnorm(x, self.w["norm.weight"], s.rms_eps), states
 
     def encode(self, packed):

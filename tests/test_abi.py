@@ -1,0 +1,31 @@
+"""The C ABI library (no GPU needed): it loads, and it exports every function include/janus_b200.h declares."""
+
+import ctypes
+import re
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared():
+    text = (ROOT / "include" / "janus_b200.h").read_text()
+    return sorted(set(re.findall(r"\bint\s+(janus_b200_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    from janus_b200 import _lib
+    lib = _lib.load()
+    names = declared()
+    assert len(names) >= 10
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(_lib.SIGNATURES) == set(names), set(names) ^ set(_lib.SIGNATURES)
+    assert lib.janus_b200_version() >= 100
+
+
+def test_argument_errors_need_no_gpu():
+    from janus_b200 import _lib
+    lib = _lib.load()
+    st = lib.janus_b200_silu_mul(None, 4, 8, None, None)
+    assert st == -1
+    assert "silu_mul" in _lib.last_error()

@@ -1,0 +1,253 @@
+"""Each libjanus_b200 op on the GPU against the CPU oracle's fp32 restatement (seeded inputs, small sizes).
+
+bf16 outputs are compared with a tolerance of 2e-2 absolute + 2e-2 relative on O(1) values (one bf16 rounding of
+the output plus bf16 operands inside the kernels); fp32 outputs (states, logits) with 2e-3."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import hybrid as oracle
+
+pytestmark = pytest.mark.gpu
+BF = torch.bfloat16
+
+
+def _ops():
+    from janus_b200 import ops
+    return ops
+
+
+def close(a, b, atol=2e-2, rtol=2e-2):
+    np.testing.assert_allclose(a.detach().float().cpu().numpy(), b.detach().float().cpu().numpy(), atol=atol, rtol=rtol)
+
+
+def test_embed_and_add_rmsnorm():
+    ops = _ops()
+    g = torch.Generator().manual_seed(0)
+    V, H, T = 50, 2560, 33
+    table = (torch.randn(V, H, generator=g)).to(BF)
+    ids = torch.randint(0, V, (T,), generator=g, dtype=torch.int32)
+    w = (torch.randn(H, generator=g) * 0.1).to(BF)
+    x, y = ops.embed_rmsnorm(table.cuda(), ids.cuda(), w.cuda(), 1e-6)
+    ref_x = table.float()[ids.long()]
+    close(x, ref_x, atol=0, rtol=0)
+    close(y, oracle.rmsnorm(ref_x, w, 1e-6))
+    delta = torch.randn(T, H, generator=g).to(BF)
+    w2 = (torch.randn(H, generator=g) * 0.1).to(BF)
+    y2 = ops.add_rmsnorm(x, delta.cuda(), w2.cuda(), 1e-6)
+    close(x, ref_x + delta.float(), atol=1e-6, rtol=1e-6)
+    close(y2, oracle.rmsnorm(ref_x + delta.float(), w2, 1e-6))
+
+
+def test_silu_mul_and_gated_rmsnorm():
+    ops = _ops()
+    g = torch.Generator().manual_seed(1)
+    gu = torch.randn(17, 2 * 96, generator=g).to(BF)
+    out = ops.silu_mul(gu.cuda())
+    close(out, torch.nn.functional.silu(gu.float()[:, :96]) * gu.float()[:, 96:])
+    for Dv in (32, 128):
+        T, Hv = 9, 4
+        core = torch.randn(T, Hv, Dv, generator=g).to(BF)
+        zbuf = torch.randn(T, Hv * Dv + 40, generator=g).to(BF)
+        w = (1 + 0.1 * torch.randn(Dv, generator=g)).to(BF)
+        out = ops.gated_rmsnorm(core.cuda(), zbuf.cuda()[:, 8:8 + Hv * Dv], w.cuda(), 1e-6)
+        ref = oracle.gated_rmsnorm(core.float(), zbuf.float()[:, 8:8 + Hv * Dv].reshape(T, Hv, Dv), w, 1e-6)
+        close(out, ref.reshape(T, -1))
+
+
+def _level(lengths):
+    rs = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    rot = np.repeat(np.arange(len(lengths)), lengths).astype(np.int32)
+    return torch.from_numpy(rs), torch.from_numpy(rot)
+
+
+@pytest.mark.parametrize("dims", [(2, 32, 4, 32), (16, 128, 32, 128)])
+def test_gdn_prologue_with_parent_tails(dims):
+    ops = _ops()
+    Hk, Dk, Hv, Dv = dims
+    K = 4
+    C = 2 * Hk * Dk + Hv * Dv
+    g = torch.Generator().manual_seed(2)
+    lengths = [5, 1, 2, 70]
+    parent = torch.tensor([1, 0, 1, 2], dtype=torch.int32)
+    rs, rot = _level(lengths)
+    T = int(rs[-1])
+    stride = C + Hv * Dv + 2 * Hv + 8
+    proj = torch.randn(T, stride, generator=g).to(BF)
+    tails = torch.randn(3, K - 1, C, generator=g).to(BF)
+    conv = (torch.randn(C, K, generator=g) * 0.3).to(BF)
+    A_log = torch.log(torch.rand(Hv, generator=g) * 16).to(BF)
+    dt = torch.ones(Hv).to(BF)
+    q, k, v, gg, beta, tail_out = ops.gdn_prologue(proj.cuda(), rs.cuda(), rot.cuda(), parent.cuda(), tails.cuda(), True,
+                                                    conv.cuda(), A_log.cuda(), dt.cuda(), Hk, Dk, Hv, Dv)
+    for r, L in enumerate(lengths):
+        a, b = int(rs[r]), int(rs[r + 1])
+        mixed = proj.float()[a:b, :C]
+        bb = proj.float()[a:b, C + Hv * Dv:C + Hv * Dv + Hv]
+        aa = proj.float()[a:b, C + Hv * Dv + Hv:C + Hv * Dv + 2 * Hv]
+        tail = tails.float()[int(parent[r])].t()  # [C, K-1]
+        rq, rk, rv, rg, rb, rt = oracle.delta_prologue(mixed, bb, aa, tail, conv.float(), A_log, dt, Hk * Dk, Dk, Dv)
+        close(q[a:b], rq)
+        close(k[a:b], rk)
+        close(v[a:b], rv)
+        close(gg[a:b], rg, atol=1e-4, rtol=1e-4)
+        close(beta[a:b], rb, atol=1e-5, rtol=1e-5)
+        close(tail_out[r].float().t(), rt, atol=0, rtol=0)
+
+
+@pytest.mark.parametrize("dims", [(2, 32, 4, 32), (16, 128, 32, 128)])
+def test_gdn_fork_recurrent_reads_parent_states(dims):
+    ops = _ops()
+    Hk, Dk, Hv, Dv = dims
+    g = torch.Generator().manual_seed(3)
+    lengths = [3, 6, 1, 4, 2]
+    child_start = torch.tensor([0, 2, 2, 5], dtype=torch.int32)  # parent 0: rows 0-1, parent 1: none, parent 2: rows 2-4
+    rs, _ = _level(lengths)
+    T = int(rs[-1])
+    q = oracle.l2norm(torch.randn(T, Hk, Dk, generator=g)).to(BF)
+    k = oracle.l2norm(torch.randn(T, Hk, Dk, generator=g)).to(BF)
+    v = torch.randn(T, Hv, Dv, generator=g).to(BF)
+    gg = -torch.rand(T, Hv, generator=g) * 0.5
+    beta = torch.rand(T, Hv, generator=g)
+    S0 = torch.randn(3, Hv, Dk, Dv, generator=g) * 0.2
+    scale = 1 / math.sqrt(Dk)
+    o, S = ops.gdn_fork_recurrent(q.cuda(), k.cuda(), v.cuda(), gg.cuda(), beta.cuda(), rs.cuda(), child_start.cuda(),
+                                  S0.cuda(), True, scale)
+    parent_of = [0, 0, 2, 2, 2]
+    for r in range(5):
+        a, b = int(rs[r]), int(rs[r + 1])
+        ro, rS = oracle.delta_recurrent(q[a:b].float(), k[a:b].float(), v[a:b].float(), gg[a:b], beta[a:b], S0[parent_of[r]])
+        close(o[a:b], ro)
+        close(S[r], rS, atol=2e-4, rtol=2e-4)
+    # no parent state: zeros
+    o2, _ = ops.gdn_fork_recurrent(q.cuda(), k.cuda(), v.cuda(), gg.cuda(), beta.cuda(), rs.cuda(),
+                                   torch.arange(6, dtype=torch.int32).cuda(), None, False, scale)
+    ro, _ = oracle.delta_recurrent(q[3:9].float(), k[3:9].float(), v[3:9].float(), gg[3:9], beta[3:9], None)
+    close(o2[3:9], ro)
+
+
+@pytest.mark.parametrize("shape", [(4, 2, 32, 8), (16, 4, 256, 64), (8, 2, 256, 64), (16, 2, 128, 32)])
+def test_attn_qk_prep(shape):
+    ops = _ops()
+    Hq, Hkv, D, rot = shape
+    g = torch.Generator().manual_seed(4)
+    T = 21
+    stride = Hq * 2 * D + 2 * Hkv * D
+    qkv = torch.randn(T, stride, generator=g).to(BF)
+    pos = torch.randint(0, 9000, (T,), generator=g, dtype=torch.int32)
+    qw = (0.1 * torch.randn(D, generator=g)).to(BF)
+    kw = (0.1 * torch.randn(D, generator=g)).to(BF)
+    inv = 1.0 / (10000.0 ** (torch.arange(0, rot, 2, dtype=torch.int64).float() / rot))
+    q, k, v = ops.attn_qk_prep(qkv.cuda(), pos.cuda(), inv.cuda(), qw.cuda(), kw.cuda(), 1e-6, Hq, Hkv, D)
+    cos, sin = oracle.rope_tables(pos.long(), rot, 10000.0)
+    f = qkv.float()
+    rq = oracle.apply_rope(oracle.rmsnorm(f[:, :Hq * 2 * D].view(T, Hq, 2 * D)[..., :D], qw, 1e-6), cos, sin)
+    rk = oracle.apply_rope(oracle.rmsnorm(f[:, Hq * 2 * D:Hq * 2 * D + Hkv * D].view(T, Hkv, D), kw, 1e-6), cos, sin)
+    close(q, rq)
+    close(k, rk)
+    close(v, f[:, Hq * 2 * D + Hkv * D:].view(T, Hkv, D), atol=0, rtol=0)
+
+
+@pytest.mark.parametrize("heads", [(4, 2, 32), (16, 4, 256), (8, 2, 256), (16, 2, 256), (4, 4, 128)])
+def test_tree_attention_three_levels(heads):
+    """A state level (2 requests), a block level and a leaf level; every query of the leaf level sees its state,
+    its block and its own leaf causally (janus/attention.py:10-23 along the path)."""
+    ops = _ops()
+    from janus_b200.plan import build_levels
+    from janus_b200 import synthetic
+    Hq, Hkv, D = heads
+    G = Hq // Hkv
+    packs = [synthetic.q4b_request(vocab=4096, seed=s, state_tokens=n, questions=3, block_tokens=9)
+             for s, n in ((0, 150), (1, 70))]
+    levels, _ = build_levels(packs)
+    g = torch.Generator().manual_seed(5)
+    K = [torch.randn(lv.T, Hkv, D, generator=g).to(BF) for lv in levels]
+    V = [torch.randn(lv.T, Hkv, D, generator=g).to(BF) for lv in levels]
+    for d, lv in enumerate(levels):
+        T = lv.T
+        q = torch.randn(T, Hq, D, generator=g).to(BF)
+        gate_buf = torch.randn(T, Hq, 2 * D, generator=g).to(BF)
+        gate = gate_buf[:, :, D:]
+        cuda = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        out = ops.tree_attention(q.cuda(), [k.cuda() for k in K[:d + 1]], [v.cuda() for v in V[:d + 1]],
+                                 [cuda(x) for x in lv.anc_lo], [cuda(x) for x in lv.anc_hi], cuda(lv.row_start),
+                                 cuda(lv.row_of_token), cuda(lv.attention_tiles(G)), gate_buf.cuda()[:, :, D:], D ** -0.5)
+        out = out.view(T, Hq, D).float().cpu()
+        for r in range(lv.B):
+            a, b = int(lv.row_start[r]), int(lv.row_start[r + 1])
+            pk = [K[l][int(lv.anc_lo[l][r]):int(lv.anc_hi[l][r])] for l in range(d)]
+            pv = [V[l][int(lv.anc_lo[l][r]):int(lv.anc_hi[l][r])] for l in range(d)]
+            k_all = torch.cat(pk + [K[d][a:b]]).float()
+            v_all = torch.cat(pv + [V[d][a:b]]).float()
+            ref = oracle.attention(q[a:b].float(), k_all, v_all, k_all.shape[0] - (b - a), D ** -0.5)
+            ref = ref * torch.sigmoid(gate[a:b].float())
+            close(out[a:b], ref)
+
+
+def test_heads_match_oracle():
+    ops = _ops()
+    g = torch.Generator().manual_seed(6)
+    T, H, R = 40, 1024, 128
+    x = torch.randn(T, H, generator=g) * 3
+    fw = (0.1 * torch.randn(H, generator=g)).to(BF)
+    lw, lb = 1 + 0.1 * torch.randn(H, generator=g), 0.1 * torch.randn(H, generator=g)
+    w_out, b_out = 0.02 * torch.randn(1, H, generator=g), torch.tensor([0.3])
+    rows = torch.tensor([3, 7, 39, 0], dtype=torch.int32)
+    z = ops.head_scalar(x.cuda(), rows.cuda(), fw.cuda(), 1e-6, lw.cuda(), lb.cuda(), 1e-5, w_out.reshape(-1).cuda(),
+                        b_out.cuda())
+    hidden = oracle.rmsnorm(x, fw, 1e-6)
+    p = {"head.norm.weight": lw, "head.norm.bias": lb, "head.out.weight": w_out, "head.out.bias": b_out}
+    close(z, oracle.scalar_head(hidden[rows.long()], p), atol=2e-4, rtol=2e-4)
+    wq, wk = 0.02 * torch.randn(R, H, generator=g), 0.02 * torch.randn(R, H, generator=g)
+    orows = torch.tensor([1, 2, 3, 10, 11], dtype=torch.int32)
+    oq = torch.tensor([0, 0, 0, 1, 1], dtype=torch.int32)
+    drows = torch.tensor([5, 12], dtype=torch.int32)
+    z = ops.head_pointer(x.cuda(), orows.cuda(), oq.cuda(), drows.cuda(), fw.cuda(), 1e-6, lw.cuda(), lb.cuda(), 1e-5,
+                         wq.cuda(), wk.cuda())
+    p = {"head.norm.weight": lw, "head.norm.bias": lb, "head.query.weight": wq, "head.key.weight": wk}
+    ref = torch.cat([oracle.pointer_head(hidden[5], hidden[[1, 2, 3]], p), oracle.pointer_head(hidden[12], hidden[[10, 11]], p)])
+    close(z, ref, atol=2e-4, rtol=2e-4)
+
+
+def test_bad_arguments_raise_before_launch():
+    ops = _ops()
+    x = torch.zeros(4, 12, device="cuda")
+    with pytest.raises(ValueError):
+        ops.add_rmsnorm(x, None, torch.zeros(12, dtype=BF, device="cuda"), 1e-6)  # hidden not a multiple of 8
+    with pytest.raises(ValueError):
+        ops.silu_mul(torch.zeros(3, 10, dtype=BF, device="cuda"))
+
+
+def test_gdn_chunk_scan_matches_recurrent_oracle():
+    """Rows of 1, 63, 64, 65 and 300 tokens (ragged last chunks), GQA 32:16, an initial state per row read through
+    state_row; outputs and final states against the oracle's token-by-token rule."""
+    ops = _ops()
+    Hk, Hv, D = 16, 32, 128
+    g = torch.Generator().manual_seed(7)
+    lengths = [1, 63, 64, 65, 300]
+    rs, _ = _level(lengths)
+    T = int(rs[-1])
+    q = oracle.l2norm(torch.randn(T, Hk, D, generator=g)).to(BF)
+    k = oracle.l2norm(torch.randn(T, Hk, D, generator=g)).to(BF)
+    v = torch.randn(T, Hv, D, generator=g).to(BF)
+    A = torch.rand(Hv, generator=g) * 8
+    gg = -A * torch.nn.functional.softplus(torch.randn(T, Hv, generator=g) + 1.0) * 0.1
+    beta = torch.sigmoid(torch.randn(T, Hv, generator=g))
+    S0 = torch.randn(2, Hv, D, D, generator=g) * 0.1
+    state_row = torch.tensor([1, 0, 1, 1, 0], dtype=torch.int32)
+    scale = D ** -0.5
+    o, S = ops.gdn_chunk_scan(q.cuda(), k.cuda(), v.cuda(), gg.cuda(), beta.cuda(), rs.cuda(), S0.cuda(),
+                              state_row.cuda(), True, scale)
+    for r in range(len(lengths)):
+        a, b = int(rs[r]), int(rs[r + 1])
+        ro, rS = oracle.delta_recurrent(q[a:b].float(), k[a:b].float(), v[a:b].float(), gg[a:b], beta[a:b],
+                                        S0[int(state_row[r])])
+        close(o[a:b], ro, atol=3e-2, rtol=3e-2)
+        close(S[r], rS, atol=3e-2, rtol=3e-2)
+    o2, _ = ops.gdn_chunk_scan(q.cuda(), k.cuda(), v.cuda(), gg.cuda(), beta.cuda(), rs.cuda(), None, None, False, scale)
+    a, b = int(rs[4]), int(rs[5])
+    ro, _ = oracle.delta_chunked(q[a:b].float(), k[a:b].float(), v[a:b].float(), gg[a:b], beta[a:b], None)
+    close(o2[a:b], ro, atol=3e-2, rtol=3e-2)

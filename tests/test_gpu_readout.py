@@ -1,0 +1,47 @@
+"""The full B200 readout against the reference's own probabilities (golden fixtures) and the CPU oracle.
+
+Tolerance (the bar of the benchmark): option probabilities within 2e-3 absolute of the reference's fp32 CPU
+readout on the same seeded weights and requests; the argmax agrees wherever the reference's top-2 margin exceeds
+4e-3 (twice the tolerance)."""
+
+import numpy as np
+import pytest
+import torch
+
+from tests.golden_cases import case_model, load_cases
+
+pytestmark = pytest.mark.gpu
+CASES = load_cases()
+DENSE = sorted(n for n, c in CASES.items() if "moe" not in c["shape"] and "a3b" not in c["shape"])
+PROB_ATOL = 2e-3
+
+
+@pytest.mark.parametrize("name", DENSE)
+def test_readout_matches_reference_probabilities(name):
+    from janus_b200.model import DecisionReadout
+    case = CASES[name]
+    shape, weights, mode, packs = case_model(case)
+    model = DecisionReadout(shape, weights, mode)
+    probs = model.probabilities(packs)
+    worst = 0.0
+    for got_pack, ref_pack in zip(probs, case["probs"]):
+        for got, ref in zip(got_pack, ref_pack):
+            ref = np.array(ref)
+            got = got.numpy()
+            worst = max(worst, float(np.abs(got - ref).max()))
+            top = np.sort(ref)[-2:] if ref.size > 1 else ref
+            if ref.size > 1 and top[1] - top[0] > 2 * PROB_ATOL:
+                assert got.argmax() == ref.argmax()
+    assert worst <= PROB_ATOL, f"{name}: max |p - p_ref| = {worst:.2e}"
+
+
+def test_batch_composition_does_not_change_results():
+    """A request's probabilities do not depend on the other requests of its batch (rows are independent)."""
+    from janus_b200.model import DecisionReadout
+    case = CASES["tiny_tree"]
+    shape, weights, mode, packs = case_model(case)
+    model = DecisionReadout(shape, weights, mode)
+    both = model.probabilities(packs)
+    alone = model.probabilities(packs[1:])
+    for a, b in zip(both[1], alone[0]):
+        np.testing.assert_allclose(a.numpy(), b.numpy(), atol=1e-6)

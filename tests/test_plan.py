@@ -1,0 +1,63 @@
+"""Host-side level planning (no GPU): level tables, ancestor ranges, tiles, readout layout."""
+
+import numpy as np
+
+from janus_b200 import synthetic
+from janus_b200.plan import build_levels, build_readout
+
+
+def test_tree_levels_and_ranges():
+    packs = [synthetic.tiny_request(seed=s, mode="tree") for s in (1, 2)]
+    levels, index = build_levels(packs)
+    assert [lv.depth for lv in levels] == [0, 1, 2]
+    l0, l1, l2 = levels
+    assert l0.B == 2 and l0.T == 512
+    assert l1.B == 6 and l2.B == 2 * (4 + 3 + 1)
+    # children of one parent are consecutive and child_start covers every row
+    assert l2.child_start[0] == 0 and l2.child_start[-1] == l2.B
+    assert (np.diff(l2.parent) >= 0).all()
+    # every leaf sees its request's state and its block
+    for r in range(l2.B):
+        b = l2.parent[r]
+        assert l2.anc_lo[1][r] == l1.row_start[b] and l2.anc_hi[1][r] == l1.row_start[b + 1]
+        st = l1.parent[b]
+        assert l2.anc_lo[0][r] == l0.row_start[st] and l2.anc_hi[0][r] == l0.row_start[st + 1]
+    assert l0.keep and l1.keep and not l2.keep
+    # token content matches the packs
+    i, seg, a = l2.rows[3]
+    n = l2.row_start[4] - l2.row_start[3]
+    assert (l2.ids[l2.row_start[3]:l2.row_start[4]] == packs[i].input_ids[0, a:a + n].numpy()).all()
+
+
+def test_tiles_cover_every_token_once_and_stay_in_one_request():
+    packs = [synthetic.q4b_request(vocab=4096, seed=s, state_tokens=300, questions=3) for s in range(3)]
+    levels, _ = build_levels(packs)
+    for lv in levels:
+        for g in (1, 2, 4, 8):
+            tiles = lv.attention_tiles(g)
+            cover = np.zeros(lv.T, dtype=int)
+            for a, b in tiles:
+                assert 0 < b - a <= 64 // g
+                cover[a:b] += 1
+                if lv.depth > 0:  # one state per tile
+                    rows = lv.row_of_token[a:b]
+                    assert len(set(lv.anc_lo[0][rows].tolist())) == 1
+                else:
+                    assert len(set(lv.row_of_token[a:b].tolist())) == 1
+            assert (cover == 1).all()
+
+
+def test_readout_layout_tree_and_listwise():
+    packs = [synthetic.tiny_request(seed=0, mode="tree")]
+    levels, index = build_levels(packs)
+    ro = build_readout(packs, levels, index, "tree")
+    layout = ro.layout[0]
+    assert [len(q) for q in layout] == [4, 3, 2]
+    assert layout[2][0] is None and layout[2][1] is not None  # noul: [0, z]
+    assert ro.n_slots == 4 + 3 + 1
+    packs = [synthetic.tiny_request(seed=0, mode="listwise")]
+    levels, index = build_levels(packs)
+    ro = build_readout(packs, levels, index, "listwise")
+    assert ro.n_slots == 4 + 3 + 2
+    orows, oq, drows, slots = ro.pointer[1]
+    assert len(drows) == 3 and oq.tolist() == [0] * 4 + [1] * 3 + [2] * 2
