@@ -8,7 +8,8 @@ For every case it builds the seeded synthetic weights (janus_b200.synthetic.make
 transformers Qwen3_5TextModel / Qwen3_5MoeTextModel in fp32, wraps it in the reference's janus.hybrid.HybridBackbone
 (its plain CPU path: torch chunk/recurrent rules, dense-mask varlen attention), runs the reference's
 DecisionModel.forward readout (PointerHead for listwise, ScalarHead for tree) on the synthetic packed requests, and
-stores the logits and the temperature-1 probabilities. The int4 experts enter the reference as their dequantised
+stores the logits and the temperature-1 probabilities, plus the probabilities of the same reference readout with
+the backbone cast to bf16 and their largest deviation from the fp32 ones (the precision noise floor of the case). The int4 experts enter the reference as their dequantised
 bf16 values (HF experts hold dense stacks). It also stores per-op vectors of the reference's gated delta rule.
 
 The fixtures are written once and not edited afterwards; tests compare the CPU oracle and the CUDA path to them.
@@ -105,12 +106,12 @@ def hf_model(shape, weights):
     return lm.eval()
 
 
-def reference_logits(shape, weights, mode, packs):
+def reference_logits(shape, weights, mode, packs, dtype=torch.float32):
     sys.path.insert(0, REFERENCE)
     from janus.hybrid import HybridBackbone
     from janus.model import DecisionModel, ModelConfig, PointerHead, ScalarHead
     from janus.packing import Branch as RefBranch, PackedRequest as RefPacked
-    lm = hf_model(shape, weights)
+    lm = hf_model(shape, weights).to(dtype)
     backbone = HybridBackbone(lm, tokenizer=None, attention="sdpa", state_chunk_tokens=4096)
     model = DecisionModel.__new__(DecisionModel)
     torch.nn.Module.__init__(model)
@@ -179,10 +180,15 @@ def main():
         weights = synthetic.make_weights(shape, seed=seed, head="scalar" if mode == "tree" else "pointer")
         logits = reference_logits(shape, weights, mode, packs)
         probs = [[torch.softmax(z.float(), -1).tolist() for z in per] for per in logits]
+        # the same reference readout with the backbone in bf16 (its plain CPU path): the precision noise floor
+        logits16 = reference_logits(shape, weights, mode, packs, torch.bfloat16)
+        probs16 = [[torch.softmax(z.float(), -1).tolist() for z in per] for per in logits16]
+        dev16 = max(abs(a - b) for pp, qq in zip(probs, probs16) for p, q in zip(pp, qq) for a, b in zip(p, q))
         manifest[name] = dict(shape=base.name, overrides=overrides, mode=mode, seed=seed,
                               checksum=synthetic.weight_checksum(weights), packs=[pack_to_dict(p) for p in packs],
-                              logits=[[z.float().tolist() for z in per] for per in logits], probs=probs)
-        print(name, "questions", sum(len(p) for p in probs), flush=True)
+                              logits=[[z.float().tolist() for z in per] for per in logits], probs=probs,
+                              probs_bf16=probs16, bf16_max_dev=dev16)
+        print(name, "questions", sum(len(p) for p in probs), "reference bf16 vs fp32 max |dp|", dev16, flush=True)
     (HERE / "readout_cases.json").write_text(json.dumps(manifest))
     vec = delta_rule_vectors()
     np.savez_compressed(HERE / "delta_rule.npz", **{k: v.numpy() for k, v in vec.items()})
