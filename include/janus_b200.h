@@ -136,6 +136,19 @@ int janus_b200_head_pointer(const float* x, int64_t H, const int32_t* option_row
                             const float* ln_w, const float* ln_b, float ln_eps, const float* wq, const float* wk,
                             int64_t R, float* workspace, size_t workspace_bytes, float* logits, void* stream);
 
+/* The PointerHead readout of janus_b200_head_pointer for callers that cannot allocate device memory: it takes no
+ * workspace and allocates nothing; the projected rows go to a static 1 MiB device array inside this library
+ * (kept by every GPU that loads the library until the process exits). Limit: (n + Q) * R <= 262144 floats (2048
+ * rows at rank 128); larger calls return JANUS_ERR_WORKSPACE without launching. The first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress) with that device current; make that first call before any
+ * stream capture. All calls on a device share the array, so calls that overlap on the GPU race: serialise them.
+ * This entry point has no counterpart in the reference (its heads run in torch with the caching allocator). */
+int janus_b200_head_pointer_noalloc(const float* x, int64_t H, const int32_t* option_rows,
+                                    const int32_t* option_question, int64_t n, const int32_t* decision_rows, int64_t Q,
+                                    const void* final_w, float rms_eps, const float* ln_w, const float* ln_b,
+                                    float ln_eps, const float* wq, const float* wk, int64_t R, float* logits,
+                                    void* stream);
+
 #ifdef __cplusplus
 }
 #endif

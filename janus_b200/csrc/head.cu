@@ -1,6 +1,8 @@
 // Readout heads fused with the decoder's final RMSNorm: a gather of the readout rows of the fp32 residual stream,
 // RMSNorm (1 + w), LayerNorm, and the Scalar / Pointer projections, all fp32. HBM/latency-bound: the gathered rows
 // are (options + decisions) * hidden * 4 bytes and the head weights are read once per CTA from L2.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace jb {
@@ -131,4 +133,75 @@ extern "C" int janus_b200_head_pointer(const float* x, int64_t H, const int32_t*
   head_dot_kernel<<<(unsigned)((n * 32 + th - 1) / th), th, 0, s>>>(workspace, (int)n, option_question, (int)R,
                                                                    1.f / sqrtf((float)R), logits);
   return launch_status("head_pointer/dot");
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// PointerHead without a caller workspace. The projected rows live in a static device array of this library
+// (kPointerScratchFloats fp32 = 1 MiB, held by every GPU that loads the library until the process exits). Host code
+// cannot pass the array's name to a kernel (on the host it names a stand-in, not device memory), so the device address
+// is looked up once per device with cudaGetSymbolAddress, with that device current, on the first call there; that
+// first call on a device should come before any stream capture. Every call on a device shares the array: calls that
+// overlap on the GPU (other streams, or other threads) race on it and must be serialised by the caller. The
+// projection kernel writes every element it later reads, so nothing needs clearing between calls.
+
+namespace jb {
+
+constexpr size_t kPointerScratchFloats = size_t(1) << 18;
+constexpr int kMaxDevices = 64;
+static __device__ __align__(256) float g_pointer_scratch[kPointerScratchFloats];
+static float* g_pointer_scratch_addr[kMaxDevices] = {};
+static std::mutex g_pointer_scratch_mutex;
+
+static int pointer_scratch(float** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_error("head_pointer_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    return JANUS_ERR_CUDA;
+  }
+  JB_REQUIRE(dev >= 0 && dev < kMaxDevices, JANUS_ERR_UNSUPPORTED, "head_pointer_noalloc: device %d >= %d", dev,
+             kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_pointer_scratch_mutex);
+  if (!g_pointer_scratch_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_pointer_scratch);
+    if (e != cudaSuccess || !p) {
+      set_error("head_pointer_noalloc: cudaGetSymbolAddress on device %d: %s", dev, cudaGetErrorString(e));
+      return JANUS_ERR_CUDA;
+    }
+    g_pointer_scratch_addr[dev] = static_cast<float*>(p);
+  }
+  *out = g_pointer_scratch_addr[dev];
+  return JANUS_OK;
+}
+
+}  // namespace jb
+
+extern "C" int janus_b200_head_pointer_noalloc(const float* x, int64_t H, const int32_t* option_rows,
+                                               const int32_t* option_question, int64_t n,
+                                               const int32_t* decision_rows, int64_t Q, const void* final_w,
+                                               float rms_eps, const float* ln_w, const float* ln_b, float ln_eps,
+                                               const float* wq, const float* wk, int64_t R, float* logits,
+                                               void* stream) {
+  JB_REQUIRE(x && option_rows && option_question && decision_rows && final_w && ln_w && ln_b && wq && wk && logits,
+             JANUS_ERR_INVALID, "head_pointer_noalloc: null pointer");
+  JB_REQUIRE(H > 0 && H <= kHeadMaxH && n >= 0 && Q >= 0 && R > 0, JANUS_ERR_INVALID, "head_pointer_noalloc: sizes");
+  JB_REQUIRE((size_t)(n + Q) * (size_t)R <= kPointerScratchFloats, JANUS_ERR_WORKSPACE,
+             "head_pointer_noalloc: (options %lld + decisions %lld) x rank %lld = %lld floats exceed the static "
+             "scratch of %zu floats; split the call or use janus_b200_head_pointer with a workspace",
+             (long long)n, (long long)Q, (long long)R, (long long)((n + Q) * R), kPointerScratchFloats);
+  if (n == 0) return JANUS_OK;
+  float* scratch = nullptr;
+  int st = pointer_scratch(&scratch);
+  if (st) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  head_project_kernel<<<(unsigned)(n + Q), kHeadThreads, H * sizeof(float), s>>>(
+      x, (int)H, option_rows, (int)n, decision_rows, (const __nv_bfloat16*)final_w, rms_eps, ln_w, ln_b, ln_eps, wq,
+      wk, (int)R, scratch);
+  st = launch_status("head_pointer_noalloc/project");
+  if (st) return st;
+  const int th = 256;
+  head_dot_kernel<<<(unsigned)((n * 32 + th - 1) / th), th, 0, s>>>(scratch, (int)n, option_question, (int)R,
+                                                                   1.f / sqrtf((float)R), logits);
+  return launch_status("head_pointer_noalloc/dot");
 }
