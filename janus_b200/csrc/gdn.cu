@@ -1,9 +1,9 @@
 // Gated DeltaNet: the prologue (conv + silu + l2 + gates) and the recurrent rule with the in-place state fork.
 //
-// Prologue: one CTA per token; every 16-byte vector of 8 channels reads its K conv taps (the previous tokens of
-// the row, or the parent row's conv tail for the first K-1 tokens), so the projection output is read ~K times
-// from L1/L2 and once from HBM. q and k are l2-normalised per head with a shuffle reduction over the lanes that
-// hold the head. Rounding follows the reference: the conv activation is rounded once to bf16, the l2 norm is
+// Prologue: a CTA covers 32 consecutive tokens x 2048 channels; each thread owns 8 channels and slides the causal
+// conv window over the tokens (registers), restarting it at a row boundary from the row's earlier tokens or the
+// parent row's conv tail, so the projection output is read once. q and k are l2-normalised per head with a shuffle
+// reduction over the lanes that hold the head. Rounding follows the reference: the conv activation is rounded once to bf16, the l2 norm is
 // computed in fp32 from that value and rounded once more (janus/hybrid.py:276-301).
 //
 // Fork recurrent: grid (parent row, value head). A parent's fp32 state [Dk, Dv] is read in place by every child row
@@ -15,51 +15,81 @@ namespace jb {
 
 constexpr int kProThreads = 256;
 constexpr int kMaxTaps = 8;
+constexpr int kProTokens = 32;  // tokens per CTA: each thread slides its conv window over them
 
+// grid (token tiles of kProTokens, channel blocks of 8 * kProThreads). Thread = 8 consecutive channels; it keeps the
+// last K-1 conv inputs of its channels in registers while it walks the tile's tokens, so every projection element is
+// read once (plus K-1 halo rows at a tile or row start, from the previous tokens or the parent's conv tail).
+template <int K>
 __global__ void __launch_bounds__(kProThreads) gdn_prologue_kernel(
-    const __nv_bfloat16* __restrict__ proj, int64_t proj_stride, const int32_t* __restrict__ row_start,
+    const __nv_bfloat16* __restrict__ proj, int64_t proj_stride, int64_t T, const int32_t* __restrict__ row_start,
     const int32_t* __restrict__ row_of_token, const int32_t* __restrict__ parent,
     const __nv_bfloat16* __restrict__ tail_in, __nv_bfloat16* __restrict__ tail_out,
     const __nv_bfloat16* __restrict__ conv_w, const __nv_bfloat16* __restrict__ A_log,
-    const __nv_bfloat16* __restrict__ dt_bias, int Hk, int Dk, int Hv, int Dv, int K, __nv_bfloat16* __restrict__ q,
+    const __nv_bfloat16* __restrict__ dt_bias, int Hk, int Dk, int Hv, int Dv, __nv_bfloat16* __restrict__ q,
     __nv_bfloat16* __restrict__ k, __nv_bfloat16* __restrict__ v, float* __restrict__ g, float* __restrict__ beta) {
-  const int64_t t = blockIdx.x;
-  const int row = row_of_token[t];
-  const int64_t r0 = row_start[row];
-  const int64_t L = row_start[row + 1] - r0;
-  const int64_t i = t - r0;  // local index in the row
+  const int64_t t0 = (int64_t)blockIdx.x * kProTokens;
+  const int64_t t1 = t0 + kProTokens < T ? t0 + kProTokens : T;
   const int key_dim = Hk * Dk;
   const int C = 2 * key_dim + Hv * Dv;
-  const int nv = C >> 3;
-  const int lanes_per_head = Dk >> 3;  // vectors per q/k head (Dk in {32,64,128,256})
-  const __nv_bfloat16* tail = (tail_in && parent) ? tail_in + (int64_t)parent[row] * (K - 1) * C : nullptr;
-  for (int base = 0; base < nv; base += blockDim.x) {
-    const int vec = base + threadIdx.x;
-    const bool live = vec < nv;
-    const int c0 = vec * 8;
-    float acc[8];
+  const int vec = blockIdx.y * kProThreads + threadIdx.x;
+  const bool live = vec * 8 < C;
+  const int c0 = live ? vec * 8 : 0;
+  const int lanes_per_head = Dk >> 3;
+  float w[8][K];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-    if (live) {
-      // conv weights of the 8 channels: K taps each, contiguous [8][K]
-      for (int j = 0; j < K; ++j) {
-        // ext index i + j; ext[e] = tail[e] for e < K-1, else proj[r0 + e - (K-1)]
-        const int64_t e = i + j;
-        float xin[8];
-        if (e >= K - 1) {
-          load8(proj + (r0 + e - (K - 1)) * proj_stride + c0, xin);
+  for (int u = 0; u < 8; ++u)
+#pragma unroll
+    for (int j = 0; j < K; ++j) w[u][j] = live ? bf2f(conv_w[(int64_t)(c0 + u) * K + j]) : 0.f;
+  float hist[K - 1][8];  // hist[j]: conv input at relative position j - (K-1) before the current token
+  int cur_row = -1;
+  int64_t r0 = 0, L = 0;
+  const __nv_bfloat16* tail = nullptr;
+  for (int64_t t = t0; t < t1; ++t) {
+    const int row = row_of_token[t];
+    if (row != cur_row) {  // (re)fill the window from the row's earlier tokens or the parent's conv tail
+      cur_row = row;
+      r0 = row_start[row];
+      L = row_start[row + 1] - r0;
+      tail = (tail_in && parent) ? tail_in + (int64_t)parent[row] * (K - 1) * C : nullptr;
+      const int64_t i = t - r0;
+#pragma unroll
+      for (int j = 0; j < K - 1; ++j) {
+        const int64_t e = i + j;  // ext index of relative position j - (K-1)
+        if (!live) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) hist[j][u] = 0.f;
+        } else if (e >= K - 1) {
+          load8(proj + (r0 + e - (K - 1)) * proj_stride + c0, hist[j]);
         } else if (tail) {
-          load8(tail + e * C + c0, xin);
+          load8(tail + e * C + c0, hist[j]);
         } else {
 #pragma unroll
-          for (int u = 0; u < 8; ++u) xin[u] = 0.f;
+          for (int u = 0; u < 8; ++u) hist[j][u] = 0.f;
         }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) acc[u] += xin[u] * bf2f(conv_w[(int64_t)(c0 + u) * K + j]);
       }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) acc[u] = bf2f(f2bf(silu(acc[u])));  // rounded once, as the reference does
     }
+    float x[8], acc[8];
+    if (live) {
+      load8(proj + t * proj_stride + c0, x);
+    } else {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) x[u] = 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      float a = x[u] * w[u][K - 1];
+#pragma unroll
+      for (int j = 0; j < K - 1; ++j) a += hist[j][u] * w[u][j];
+      acc[u] = bf2f(f2bf(silu(a)));  // rounded once, as the reference does
+    }
+    // slide the window
+#pragma unroll
+    for (int j = 0; j < K - 2; ++j)
+#pragma unroll
+      for (int u = 0; u < 8; ++u) hist[j][u] = hist[j + 1][u];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) hist[K - 2][u] = x[u];
     // l2 norm over each q / k head: lanes_per_head consecutive lanes hold one head
     float ss = 0.f;
 #pragma unroll
@@ -78,30 +108,22 @@ __global__ void __launch_bounds__(kProThreads) gdn_prologue_kernel(
       } else {
         store8(v + t * (int64_t)(Hv * Dv) + (c0 - 2 * key_dim), acc);
       }
-      // conv tail of the row: the last K-1 conv inputs, written by the CTA of the row's last token
-      if (tail_out && i == L - 1) {
-        for (int j = 0; j < K - 1; ++j) {
-          const int64_t e = L + j;  // ext index
-          float xin[8];
-          if (e >= K - 1) {
-            load8(proj + (r0 + e - (K - 1)) * proj_stride + c0, xin);
-          } else if (tail) {
-            load8(tail + e * C + c0, xin);
-          } else {
+      if (tail_out && t == r0 + L - 1) {  // the row's last K-1 conv inputs are the window now
 #pragma unroll
-            for (int u = 0; u < 8; ++u) xin[u] = 0.f;
-          }
-          store8(tail_out + ((int64_t)row * (K - 1) + j) * C + c0, xin);
-        }
+        for (int j = 0; j < K - 1; ++j) store8(tail_out + ((int64_t)row * (K - 1) + j) * C + c0, hist[j]);
       }
     }
   }
-  // gates: b at column C + Hv*Dv + h, a at C + Hv*Dv + Hv + h
-  for (int h = threadIdx.x; h < Hv; h += blockDim.x) {
-    const float b = bf2f(proj[t * proj_stride + C + Hv * Dv + h]);
-    const float a = bf2f(proj[t * proj_stride + C + Hv * Dv + Hv + h]);
-    beta[t * Hv + h] = sigmoidf_(b);
-    g[t * Hv + h] = -expf(bf2f(A_log[h])) * softplus(a + bf2f(dt_bias[h]));
+  // gates, by the first channel block: b at column C + Hv*Dv + h, a at C + Hv*Dv + Hv + h
+  if (blockIdx.y == 0) {
+    for (int x = threadIdx.x; x < (int)(t1 - t0) * Hv; x += blockDim.x) {
+      const int64_t t = t0 + x / Hv;
+      const int h = x % Hv;
+      const float b = bf2f(proj[t * proj_stride + C + Hv * Dv + h]);
+      const float a = bf2f(proj[t * proj_stride + C + Hv * Dv + Hv + h]);
+      beta[t * Hv + h] = sigmoidf_(b);
+      g[t * Hv + h] = -expf(bf2f(A_log[h])) * softplus(a + bf2f(dt_bias[h]));
+    }
   }
 }
 
@@ -199,11 +221,24 @@ extern "C" int janus_b200_gdn_prologue(const void* proj, int64_t proj_stride, in
              JANUS_ERR_ALIGNMENT, "gdn_prologue: 16-byte alignment");
   JB_REQUIRE(!tail_in || parent, JANUS_ERR_INVALID, "gdn_prologue: tail_in needs parent");
   if (T == 0) return JANUS_OK;
-  gdn_prologue_kernel<<<(unsigned)T, kProThreads, 0, (cudaStream_t)stream>>>(
-      (const __nv_bfloat16*)proj, proj_stride, row_start, row_of_token, parent, (const __nv_bfloat16*)tail_in,
-      (__nv_bfloat16*)tail_out, (const __nv_bfloat16*)conv_w, (const __nv_bfloat16*)A_log,
-      (const __nv_bfloat16*)dt_bias, (int)Hk, (int)Dk, (int)Hv, (int)Dv, (int)K, (__nv_bfloat16*)q,
-      (__nv_bfloat16*)k, (__nv_bfloat16*)v, g, beta);
+  dim3 grid((unsigned)((T + kProTokens - 1) / kProTokens), (unsigned)((C / 8 + kProThreads - 1) / kProThreads));
+  cudaStream_t s = (cudaStream_t)stream;
+#define JB_PRO(K_)                                                                                                  \
+  gdn_prologue_kernel<K_><<<grid, kProThreads, 0, s>>>(                                                             \
+      (const __nv_bfloat16*)proj, proj_stride, T, row_start, row_of_token, parent, (const __nv_bfloat16*)tail_in,   \
+      (__nv_bfloat16*)tail_out, (const __nv_bfloat16*)conv_w, (const __nv_bfloat16*)A_log,                          \
+      (const __nv_bfloat16*)dt_bias, (int)Hk, (int)Dk, (int)Hv, (int)Dv, (__nv_bfloat16*)q, (__nv_bfloat16*)k,      \
+      (__nv_bfloat16*)v, g, beta)
+  switch (K) {
+    case 2: JB_PRO(2); break;
+    case 3: JB_PRO(3); break;
+    case 4: JB_PRO(4); break;
+    case 5: JB_PRO(5); break;
+    default:
+      set_error("gdn_prologue: conv kernel size %lld not compiled (2..5)", (long long)K);
+      return JANUS_ERR_UNSUPPORTED;
+  }
+#undef JB_PRO
   return launch_status("gdn_prologue");
 }
 
