@@ -136,6 +136,37 @@ int janus_b200_head_pointer(const float* x, int64_t H, const int32_t* option_row
                             const float* ln_w, const float* ln_b, float ln_eps, const float* wq, const float* wk,
                             int64_t R, float* workspace, size_t workspace_bytes, float* logits, void* stream);
 
+/* MoE routing and tile plan, sync-free: softmax over fp32 router logits [S, E] (E <= 512), top-k (k <= 16),
+ * renormalised weights (topk_idx int32 / topk_w fp32 [S, k]); assignments a = t*k + j sorted by expert into
+ * sorted_ids [max_tiles * tile_rows] (-1 pads each expert to a multiple of tile_rows, which must be 64),
+ * tile_expert [max_tiles], the tile count in n_tiles[0] on the device. max_tiles >= ceil((S*k + E*63) / 64).
+ * workspace: int32, at least 3*E.
+ * Replaces Qwen3_5MoeTopKRouter.forward (transformers qwen3_5_moe :754-770) and `align`
+ * (janus/moe_w4a16.py:89-106). */
+int janus_b200_moe_route(const float* logits, int64_t S, int64_t E, int64_t k, int64_t tile_rows, int32_t* topk_idx,
+                         float* topk_w, int32_t* sorted_ids, int32_t* tile_expert, int64_t max_tiles,
+                         int32_t* n_tiles, int32_t* workspace, size_t workspace_bytes, void* stream);
+
+/* W4A16 grouped GEMM over the expert-sorted tiles of janus_b200_moe_route. Weights: codes uint8 [E, rows, K/2]
+ * (two int4 per byte, even element in the low nibble, two's complement) and bf16 scales [E, rows, K/128]; the
+ * value fed to the tensor cores is code * scale computed in fp32 and rounded once to bf16.
+ * gated = 1 (gate_up, rows = 2N): x rows are tokens (assignment / topk), out[sorted row, n] =
+ * silu(x W_gate^T) * (x W_up^T) in bf16, out rows = max_tiles*64 sorted rows.
+ * gated = 0 (down, rows = N): x rows are the sorted rows of the first GEMM's output, out[assignment, n] =
+ * topk_w[assignment] * x W^T in bf16. N % 64 == 0, K % 128 == 0.
+ * Replaces _w4a16_moe_kernel / fused_moe (janus/moe_w4a16.py:37-86, 122-140) for the int4-g128 format. */
+int janus_b200_moe_grouped_w4a16(const void* x, int64_t ldx, const uint8_t* codes, const void* scales, int64_t E,
+                                 int64_t N, int64_t K, int32_t gated, const int32_t* sorted_ids,
+                                 const int32_t* tile_expert, const int32_t* n_tiles, int64_t max_tiles, int64_t topk,
+                                 const float* topk_w, void* out, int64_t ldo, void* stream);
+
+/* MoE output: out[t] = sum_j y[t*k + j] (fp32 sum of the weighted expert rows) + sigmoid(shared_gate_logit[t]) *
+ * shared[t] (shared NULL: none), bf16 [S, H].
+ * Replaces the per-token sum and the gated shared expert of Qwen3_5MoeSparseMoeBlock.forward
+ * (transformers qwen3_5_moe :778-791, janus/moe_w4a16.py:140). */
+int janus_b200_moe_combine(const void* y, int64_t k, const void* shared, const float* shared_gate_logit, int64_t S,
+                           int64_t H, void* out, void* stream);
+
 /* The PointerHead readout of janus_b200_head_pointer for callers that cannot allocate device memory: it takes no
  * workspace and allocates nothing; the projected rows go to a static 1 MiB device array inside this library
  * (kept by every GPU that loads the library until the process exits). Limit: (n + Q) * R <= 262144 floats (2048

@@ -32,8 +32,6 @@ class DecisionReadout:
     def __init__(self, shape: ModelShape, weights, mode="tree", device="cuda"):
         if mode not in ("tree", "listwise"):
             raise ValueError("mode must be tree or listwise")
-        if shape.moe:
-            raise ValueError("MoE feed-forward not supported by this readout yet")
         self.shape, self.mode = shape, mode
         self.device = torch.device(device)
         if self.device.type != "cuda":
@@ -61,8 +59,17 @@ class DecisionReadout:
                 L.q_norm, L.k_norm = w(a + "q_norm.weight"), w(a + "k_norm.weight")
                 L.o = w(a + "o_proj.weight")
             m = p + "mlp."
-            L.gate_up = torch.cat([w(m + "gate_proj.weight"), w(m + "up_proj.weight")])
-            L.down = w(m + "down_proj.weight")
+            if shape.moe:
+                L.router = w(m + "gate.weight")
+                u8 = lambda n: weights[n].to(dev).contiguous()
+                L.gu_codes, L.gu_scales = u8(m + "experts.gate_up_proj"), w(m + "experts.gate_up_proj.scales")
+                L.dn_codes, L.dn_scales = u8(m + "experts.down_proj"), w(m + "experts.down_proj.scales")
+                L.shared_gate_up = torch.cat([w(m + "shared_expert.gate_proj.weight"), w(m + "shared_expert.up_proj.weight")])
+                L.shared_down = w(m + "shared_expert.down_proj.weight")
+                L.shared_gate = w(m + "shared_expert_gate.weight")
+            else:
+                L.gate_up = torch.cat([w(m + "gate_proj.weight"), w(m + "up_proj.weight")])
+                L.down = w(m + "down_proj.weight")
             self.layers.append(L)
         f32 = lambda n: w(n, torch.float32)
         self.head = {k[5:]: f32(k) for k in weights if k.startswith("head.")}
@@ -114,10 +121,23 @@ class DecisionReadout:
                 h = F.linear(o, L.o)
                 kept.append((kk, vv) if lv.keep else None)
             y = ops.add_rmsnorm(x, h, L.post_norm, eps)
-            pending = F.linear(ops.silu_mul(F.linear(y, L.gate_up)), L.down)
+            pending = self._moe(y, L) if s.moe else F.linear(ops.silu_mul(F.linear(y, L.gate_up)), L.down)
         ops.add_rmsnorm(x, pending, self.final_norm, eps)  # the last residual add (its normed output is unused)
         self._heads(d, x, plan, logits)
         return kept
+
+    def _moe(self, y, L):
+        """Qwen3_5MoeSparseMoeBlock (transformers qwen3_5_moe :773-791) on the W4A16 experts: router logits in fp32
+        (bf16 GEMM, fp32 output) -> routing plan -> gate_up grouped GEMM (silu(gate) * up) -> down grouped GEMM times
+        the routing weight -> per-token sum plus the sigmoid-gated shared expert."""
+        k = self.shape.top_k
+        logits = torch.mm(y, L.router.t(), out_dtype=torch.float32)
+        plan = ops.moe_route(logits, k)
+        h = ops.moe_grouped_w4a16(y, L.gu_codes, L.gu_scales, plan, True, k)
+        y2 = ops.moe_grouped_w4a16(h, L.dn_codes, L.dn_scales, plan, False, k, topk_w=plan[1])
+        shared = F.linear(ops.silu_mul(F.linear(y, L.shared_gate_up)), L.shared_down)
+        sg = torch.mm(y, L.shared_gate.t(), out_dtype=torch.float32)
+        return ops.moe_combine(y2, k, shared, sg.reshape(-1))
 
     CHUNK_MIN_TOKENS = 32  # mean row length from which a level runs the chunked rule (rows are read once per chunk)
 

@@ -243,3 +243,64 @@ def head_pointer(x, option_rows, option_question, decision_rows, final_w, rms_ep
         _ptr(_need(ln_w, F32, "ln_w")), _ptr(_need(ln_b, F32, "ln_b")), ln_eps, _ptr(_need(wq, F32, "wq")),
         _ptr(_need(wk, F32, "wk")), R, _ptr(workspace), workspace.numel() * 4, _ptr(logits), _stream(x)), "head_pointer")
     return logits
+
+
+MOE_TILE = 64
+
+
+def moe_max_tiles(S, E, k):
+    return (S * k + E * (MOE_TILE - 1) + MOE_TILE - 1) // MOE_TILE
+
+
+@_instrument("moe_route", 4)
+def moe_route(logits, k):
+    """fp32 router logits [S, E] -> (topk_idx, topk_w, sorted_ids, tile_expert, n_tiles) on the device."""
+    _need(logits, F32, "logits")
+    S, E = logits.shape
+    dev = logits.device
+    mt = moe_max_tiles(S, E, k)
+    topk_idx = torch.empty(S, k, dtype=I32, device=dev)
+    topk_w = torch.empty(S, k, dtype=F32, device=dev)
+    sorted_ids = torch.empty(mt * MOE_TILE, dtype=I32, device=dev)
+    tile_expert = torch.empty(mt, dtype=I32, device=dev)
+    n_tiles = torch.empty(1, dtype=I32, device=dev)
+    ws = torch.empty(3 * E, dtype=I32, device=dev)
+    _lib.check(_lib.load().janus_b200_moe_route(_ptr(logits), S, E, k, MOE_TILE, _ptr(topk_idx), _ptr(topk_w),
+                                                _ptr(sorted_ids), _ptr(tile_expert), mt, _ptr(n_tiles), _ptr(ws),
+                                                ws.numel() * 4, _stream(logits)), "moe_route")
+    return topk_idx, topk_w, sorted_ids, tile_expert, n_tiles
+
+
+@_instrument("moe_grouped_w4a16", 1)
+def moe_grouped_w4a16(x, codes, scales, plan, gated, k, topk_w=None, out=None):
+    """x bf16 [rows, K] (unit column stride); codes uint8 [E, NW, K/2], scales bf16 [E, NW, K/128] (NW = 2N gated)."""
+    _need(x, BF16, "x", contiguous=False)
+    if x.stride(1) != 1:
+        raise ValueError("x must have unit column stride")
+    _need(codes, torch.uint8, "codes"); _need(scales, BF16, "scales")
+    E, NW, half_k = codes.shape
+    K = 2 * half_k
+    N = NW // 2 if gated else NW
+    topk_idx, _, sorted_ids, tile_expert, n_tiles = plan
+    mt = tile_expert.shape[0]
+    S = topk_idx.shape[0]
+    if out is None:
+        out = torch.empty((mt * MOE_TILE if gated else S * k), N, dtype=BF16, device=x.device)
+    _lib.check(_lib.load().janus_b200_moe_grouped_w4a16(
+        _ptr(x), x.stride(0), _ptr(codes), _ptr(scales), E, N, K, 1 if gated else 0, _ptr(sorted_ids),
+        _ptr(tile_expert), _ptr(n_tiles), mt, k, _ptr(topk_w), _ptr(out), out.stride(0), _stream(x)),
+        "moe_grouped_w4a16")
+    return out
+
+
+@_instrument("moe_combine", 1)
+def moe_combine(y, k, shared, shared_gate_logit, out=None):
+    _need(y, BF16, "y")
+    S = y.shape[0] // k
+    H = y.shape[1]
+    out = torch.empty(S, H, dtype=BF16, device=y.device) if out is None else out
+    if shared is not None:
+        _need(shared, BF16, "shared"); _need(shared_gate_logit, F32, "shared_gate_logit")
+    _lib.check(_lib.load().janus_b200_moe_combine(_ptr(y), k, _ptr(shared), _ptr(shared_gate_logit), S, H, _ptr(out),
+                                                  _stream(y)), "moe_combine")
+    return out

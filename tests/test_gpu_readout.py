@@ -14,7 +14,7 @@ from tests.golden_cases import case_model, load_cases
 
 pytestmark = pytest.mark.gpu
 CASES = load_cases()
-DENSE = sorted(n for n, c in CASES.items() if "moe" not in c["shape"] and "a3b" not in c["shape"])
+DENSE = sorted(CASES)
 PROB_ATOL = 2e-3
 
 
