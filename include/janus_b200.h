@@ -109,16 +109,24 @@ int janus_b200_attn_qk_prep(const void* qkv, int64_t qkv_stride, int64_t T, cons
  * tokens of its row's ancestor at each earlier level (key range [anc_lo[l][row], anc_hi[l][row]) of level l's
  * keys) and to its own row's tokens causally; out = softmax(q k^T * scale) v * sigmoid(gate). GQA folded: the
  * Hq/Hkv query heads of a kv head share every K/V tile. n_levels = ancestors + 1; k_levels[n_levels-1] is the
- * level's own keys ([T, Hkv, D]). tiles: [n_tiles, 2] query token ranges [start, end) chosen by the caller (each
- * within one request; janus_b200 python builds them). gate: bf16, token t head h at gate[t*gate_stride +
- * h*gate_head_stride + d]. out bf16 [T, Hq*D]. D in {32, 64, 128, 256}.
+ * level's own keys ([T, Hkv, D]). tiles: [n_tiles, 2] query token ranges [start, end) of at most
+ * janus_b200_tree_attention_tile_tokens(D, Hq, Hkv) tokens, each within one request (janus_b200 python builds them).
+ * gate: bf16, token t head h at gate[t*gate_stride + h*gate_head_stride + d]. out bf16 [T, Hq*D]. D in
+ * {32, 64, 128, 256}; 128 and 256 run on tcgen05 with TMEM accumulators, 32 and 64 on mma.sync. status: optional
+ * device int32, set to 1 if a bounded device-side wait ran out (the output is then invalid); NULL: not reported.
  * Replaces branch_attention / state_attention / _piece / _merge_gate (janus/hybrid.py:806-855, 943-989) and the
  * tree rule of janus/attention.py:10-23. */
 int janus_b200_tree_attention(const void* q, int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int32_t n_levels,
                               const void* const* k_levels, const void* const* v_levels,
                               const int32_t* const* anc_lo, const int32_t* const* anc_hi, const int32_t* row_start,
                               const int32_t* row_of_token, const int32_t* tiles, int64_t n_tiles, const void* gate,
-                              int64_t gate_stride, int64_t gate_head_stride, float scale, void* out, void* stream);
+                              int64_t gate_stride, int64_t gate_head_stride, float scale, void* out, int32_t* status,
+                              void* stream);
+
+/* The largest number of query tokens per tile janus_b200_tree_attention accepts for this head dim and GQA layout
+ * (128 rows of the tensor-core tile, or 64, divided by Hq/Hkv); 0 for an unsupported layout.
+ * The tiling of the query axis that `_piece` bounds by PIECE_BYTES (janus/hybrid.py:407-420). */
+int janus_b200_tree_attention_tile_tokens(int64_t D, int64_t Hq, int64_t Hkv);
 
 /* ScalarHead readout fused with the final norm: for each of n rows r = rows[i] of the fp32 residual x [*, H]:
  * h = rmsnorm(x[r]) * (1 + final_w) (eps rms_eps), logits[i] = LayerNorm(h; ln_w, ln_b, ln_eps) . w_out + b_out[0].

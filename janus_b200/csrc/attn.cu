@@ -141,9 +141,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) tree_attention_kernel(TreeAtt
   constexpr int CH = D / 8;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int hkv = blockIdx.y;
-  const int q0 = p.tiles[2 * blockIdx.x], q1 = p.tiles[2 * blockIdx.x + 1];
-  const int ntok = q1 - q0;
   const int G = p.G, TQ = kBM / G;
+  const int q0 = p.tiles[2 * blockIdx.x];
+  const int ntok = min(p.tiles[2 * blockIdx.x + 1] - q0, TQ);  // longer tiles are truncated (the host never makes them)
+  const int q1 = q0 + ntok;
   const int L = p.n_levels;
 
   // per-token metadata and the CTA's key range per level
@@ -386,9 +387,22 @@ static int launch_tree(const TreeAttnParams& p, int64_t n_tiles, cudaStream_t s)
   return launch_status("tree_attention");
 }
 
+int tree_attention_tc(const void* q, int64_t Hq, int64_t Hkv, int64_t D, int32_t n_levels, const void* const* k_levels,
+                      const void* const* v_levels, const int32_t* const* anc_lo, const int32_t* const* anc_hi,
+                      const int32_t* row_start, const int32_t* row_of_token, const int32_t* tiles, int64_t n_tiles,
+                      const void* gate, int64_t gate_stride, int64_t gate_head_stride, float scale, void* out,
+                      int32_t* err, cudaStream_t stream);
+
 }  // namespace jb
 
 using namespace jb;
+
+extern "C" int janus_b200_tree_attention_tile_tokens(int64_t D, int64_t Hq, int64_t Hkv) {
+  if (Hq <= 0 || Hkv <= 0 || Hq % Hkv) return 0;
+  const int64_t G = Hq / Hkv;
+  const int64_t rows = (D == 128 || D == 256) ? 128 : kBM;
+  return G <= rows && rows % G == 0 ? (int)(rows / G) : 0;
+}
 
 extern "C" int janus_b200_attn_qk_prep(const void* qkv, int64_t qkv_stride, int64_t T, const int32_t* positions,
                                        const float* inv_freq, int64_t rot, const void* q_norm_w, const void* k_norm_w,
@@ -415,7 +429,8 @@ extern "C" int janus_b200_tree_attention(const void* q, int64_t T, int64_t Hq, i
                                          const int32_t* const* anc_lo, const int32_t* const* anc_hi,
                                          const int32_t* row_start, const int32_t* row_of_token, const int32_t* tiles,
                                          int64_t n_tiles, const void* gate, int64_t gate_stride,
-                                         int64_t gate_head_stride, float scale, void* out, void* stream) {
+                                         int64_t gate_head_stride, float scale, void* out, int32_t* status,
+                                         void* stream) {
   JB_REQUIRE(q && k_levels && v_levels && row_start && row_of_token && tiles && gate && out, JANUS_ERR_INVALID,
              "tree_attention: null pointer");
   JB_REQUIRE(n_levels >= 1 && n_levels <= kMaxLevels, JANUS_ERR_UNSUPPORTED, "tree_attention: %d levels (1..%d)",
@@ -456,6 +471,9 @@ extern "C" int janus_b200_tree_attention(const void* q, int64_t T, int64_t Hq, i
   p.scale_log2 = scale * 1.4426950408889634f;
   if (n_tiles == 0 || T == 0) return JANUS_OK;
   cudaStream_t s = (cudaStream_t)stream;
+  if ((D == 128 || D == 256) && 128 % G == 0)
+    return tree_attention_tc(q, Hq, Hkv, D, n_levels, k_levels, v_levels, anc_lo, anc_hi, row_start, row_of_token,
+                             tiles, n_tiles, gate, gate_stride, gate_head_stride, scale, out, status, s);
   switch (D) {
     case 32: return launch_tree<32>(p, n_tiles, s);
     case 64: return launch_tree<64>(p, n_tiles, s);

@@ -77,6 +77,7 @@ class DecisionReadout:
         # Qwen3_5TextRotaryEmbedding.compute_default_rope_parameters, fp32
         self.inv_freq = (1.0 / (shape.rope_theta ** (torch.arange(0, r, 2, dtype=torch.int64).float() / r))).to(dev)
         self.group = shape.heads // shape.kv_heads
+        self.tile_tokens = ops.tree_attention_tile_tokens(shape.head_dim, shape.heads, shape.kv_heads)
         self.last_plan = None
 
     # ------------------------------------------------------------------------------------------------ level pass
@@ -117,7 +118,7 @@ class DecisionReadout:
                 gate = qkv[:, :Hq * 2 * D].view(T, Hq, 2 * D)[:, :, D:]
                 o = ops.tree_attention(q, keys, values, [plan[(d, "lo", l)] for l in range(d)],
                                        [plan[(d, "hi", l)] for l in range(d)], rs, rot,
-                                       plan[(d, "tiles", self.group)].view(-1, 2), gate, D ** -0.5)
+                                       plan[(d, "tiles", self.tile_tokens)].view(-1, 2), gate, D ** -0.5)
                 h = F.linear(o, L.o)
                 kept.append((kk, vv) if lv.keep else None)
             y = ops.add_rmsnorm(x, h, L.post_norm, eps)
@@ -176,7 +177,7 @@ class DecisionReadout:
     def prepare(self, packs):
         """Host planning plus the one host-to-device copy of the level tables: (levels, readout, device plan)."""
         levels, readout = self.plan(packs)
-        return levels, readout, DevicePlan(levels, readout, self.device, groups=(self.group,))
+        return levels, readout, DevicePlan(levels, readout, self.device, tile_tokens=(self.tile_tokens,))
 
     def run(self, prepared):
         """The device pass over prepared levels: all option logits as one fp32 device tensor [slots]."""

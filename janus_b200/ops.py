@@ -191,7 +191,16 @@ def attn_qk_prep(qkv, positions, inv_freq, q_norm_w, k_norm_w, eps, Hq, Hkv, D, 
 
 
 @_instrument("tree_attention", 1)
-def tree_attention(q, keys, values, anc_lo, anc_hi, row_start, row_of_token, tiles, gate, scale, out=None):
+def tree_attention_tile_tokens(D, Hq, Hkv):
+    """Query tokens per attention tile the library accepts for this layout."""
+    n = _lib.load().janus_b200_tree_attention_tile_tokens(D, Hq, Hkv)
+    if n <= 0:
+        raise ValueError(f"tree_attention: no kernel for D={D}, Hq={Hq}, Hkv={Hkv}")
+    return n
+
+
+def tree_attention(q, keys, values, anc_lo, anc_hi, row_start, row_of_token, tiles, gate, scale, out=None,
+                   status=None):
     """q bf16 [T, Hq, D]; keys/values: per level [T_l, Hkv, D] (last = own); anc_lo/anc_hi: per ancestor level
     int32 [B]; tiles int32 [n, 2]; gate: bf16 view [T, Hq, D] (any strides with unit last stride)."""
     _need(q, BF16, "q")
@@ -214,7 +223,7 @@ def tree_attention(q, keys, values, anc_lo, anc_hi, row_start, row_of_token, til
         _ptr(q), T, Hq, Hkv, D, n, ctypes.cast(karr, ctypes.c_void_p), ctypes.cast(varr, ctypes.c_void_p),
         ctypes.cast(larr, ctypes.c_void_p), ctypes.cast(harr, ctypes.c_void_p), _ptr(_need(row_start, I32, "row_start")),
         _ptr(_need(row_of_token, I32, "row_of_token")), _ptr(_need(tiles, I32, "tiles")), tiles.shape[0], _ptr(gate),
-        gate.stride(0), gate.stride(1), scale, _ptr(out), _stream(q)), "tree_attention")
+        gate.stride(0), gate.stride(1), scale, _ptr(out), _ptr(status), _stream(q)), "tree_attention")
     return out
 
 

@@ -5,8 +5,9 @@ Level d holds every segment at depth d of every pack, in (pack, parent row, segm
 T_d tokens, B_d rows. Because rows are sorted by parent, the children of one parent row are consecutive, which is
 what the fork kernel (a parent's state read in place by its children) and the tree attention tiles rely on. For
 every row the plan records its parent row in level d-1 and its ancestor row's token range at every earlier level
-(the keys it may attend to). Attention tiles are runs of at most 64/G query tokens that never cross a change of
-long ancestor (so a tile reads one state, not two) nor leave a long row of their own level.
+(the keys it may attend to). Attention tiles are runs of at most `tokens` query tokens (the attention kernel's
+tile: 128 or 64 rows over the GQA group) that never cross a change of long ancestor (so a tile reads one state,
+not two) nor leave a long row of their own level.
 
 Everything here is numpy on the host; `DevicePlan` moves the int32 tables to the GPU in one copy.
 """
@@ -35,7 +36,7 @@ class Level:
     child_start: np.ndarray    # [P+1] int32, P = rows of level depth-1 (depth 0: [0..B], each row its own group)
     rows: list                 # (pack, segment, first packed position) per row
     keep: bool = False         # a deeper level reads this level's states
-    tiles: dict = field(default_factory=dict)  # G -> [n, 2] int32
+    tiles: dict = field(default_factory=dict)  # tokens per tile -> [n, 2] int32
 
     @property
     def T(self):
@@ -45,11 +46,11 @@ class Level:
     def B(self):
         return int(self.row_start.shape[0] - 1)
 
-    def attention_tiles(self, group):
-        """Query tiles for a GQA group size `group` (64 // group tokens each)."""
-        if group in self.tiles:
-            return self.tiles[group]
-        tq = max(1, 64 // group)
+    def attention_tiles(self, tokens):
+        """Query tiles of at most `tokens` tokens (janus_b200_tree_attention_tile_tokens)."""
+        if tokens in self.tiles:
+            return self.tiles[tokens]
+        tq = max(1, int(tokens))
         out = []
         start = None
         count = 0
@@ -75,7 +76,7 @@ class Level:
         if start is not None:
             out.append((start, start + count))
         arr = np.asarray(out, dtype=np.int32).reshape(-1, 2)
-        self.tiles[group] = arr
+        self.tiles[tokens] = arr
         return arr
 
 
@@ -189,7 +190,7 @@ def build_readout(packs, levels, row_index, mode):
 class DevicePlan:
     """The int32 tables of every level on one device, moved with a single host-to-device copy."""
 
-    def __init__(self, levels, readout, device, groups=()):
+    def __init__(self, levels, readout, device, tile_tokens=()):
         chunks, index = [], {}
 
         def add(key, arr):
@@ -208,8 +209,8 @@ class DevicePlan:
             for l, (lo, hi) in enumerate(zip(lv.anc_lo, lv.anc_hi)):
                 add((d, "lo", l), lo)
                 add((d, "hi", l), hi)
-            for g in groups:
-                add((d, "tiles", g), lv.attention_tiles(g))
+            for n in tile_tokens:
+                add((d, "tiles", n), lv.attention_tiles(n))
         for d, (rows, _) in readout.scalar.items():
             add((d, "scalar_rows"), rows)
         for d, (orows, oq, drows, _) in readout.pointer.items():

@@ -151,7 +151,8 @@ def test_attn_qk_prep(shape):
     close(v, f[:, Hq * 2 * D + Hkv * D:].view(T, Hkv, D), atol=0, rtol=0)
 
 
-@pytest.mark.parametrize("heads", [(4, 2, 32), (16, 4, 256), (8, 2, 256), (16, 2, 256), (4, 4, 128)])
+@pytest.mark.parametrize("heads", [(4, 2, 32), (16, 4, 256), (8, 2, 256), (16, 2, 256), (4, 4, 128), (8, 8, 256),
+                                   (2, 1, 64)])
 def test_tree_attention_three_levels(heads):
     """A state level (2 requests), a block level and a leaf level; every query of the leaf level sees its state,
     its block and its own leaf causally (janus/attention.py:10-23 along the path)."""
@@ -172,9 +173,13 @@ def test_tree_attention_three_levels(heads):
         gate_buf = torch.randn(T, Hq, 2 * D, generator=g).to(BF)
         gate = gate_buf[:, :, D:]
         cuda = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        tiles = lv.attention_tiles(ops.tree_attention_tile_tokens(D, Hq, Hkv))
         out = ops.tree_attention(q.cuda(), [k.cuda() for k in K[:d + 1]], [v.cuda() for v in V[:d + 1]],
                                  [cuda(x) for x in lv.anc_lo], [cuda(x) for x in lv.anc_hi], cuda(lv.row_start),
-                                 cuda(lv.row_of_token), cuda(lv.attention_tiles(G)), gate_buf.cuda()[:, :, D:], D ** -0.5)
+                                 cuda(lv.row_of_token), cuda(tiles), gate_buf.cuda()[:, :, D:], D ** -0.5,
+                                 status=status)
+        assert int(status.item()) == 0
         out = out.view(T, Hq, D).float().cpu()
         for r in range(lv.B):
             a, b = int(lv.row_start[r]), int(lv.row_start[r + 1])

@@ -33,11 +33,11 @@ def test_tiles_cover_every_token_once_and_stay_in_one_request():
     packs = [synthetic.q4b_request(vocab=4096, seed=s, state_tokens=300, questions=3) for s in range(3)]
     levels, _ = build_levels(packs)
     for lv in levels:
-        for g in (1, 2, 4, 8):
-            tiles = lv.attention_tiles(g)
+        for n in (1, 8, 16, 32, 64, 128):
+            tiles = lv.attention_tiles(n)
             cover = np.zeros(lv.T, dtype=int)
             for a, b in tiles:
-                assert 0 < b - a <= 64 // g
+                assert 0 < b - a <= n
                 cover[a:b] += 1
                 if lv.depth > 0:  # one state per tile
                     rows = lv.row_of_token[a:b]
