@@ -103,13 +103,15 @@ def attention_flops(levels, shape):
     return per
 
 
-def chunk_algorithmic(levels, shape):
-    """DeltaNet chunk-scan FLOPs and bytes per launch (per DeltaNet layer) at each level: FLOPs per token per value
-    head 6*Dk*Dv + 2*C*(3*Dk + 2*Dv) (C = 64); bytes = q, k, v (bf16) + g, beta (fp32) in, o out (bf16), the final
-    fp32 state out when kept."""
+def chunk_algorithmic(levels, shape, which):
+    """DeltaNet rule FLOPs and bytes per launch (per DeltaNet layer) at each level the kernel `which` runs (a
+    bool per level): FLOPs per token per value head 6*Dk*Dv + 2*C*(3*Dk + 2*Dv) (C = 64); bytes = q, k, v (bf16) +
+    g, beta (fp32) in, o out (bf16), the final fp32 state out when kept."""
     Dk, Dv, Hk, Hv = shape.lin_k_dim, shape.lin_v_dim, shape.lin_k_heads, shape.lin_v_heads
     out = []
-    for lv in levels:
+    for lv, use in zip(levels, which):
+        if not use:
+            continue
         T = lv.T
         flops = T * Hv * (6 * Dk * Dv + 2 * 64 * (3 * Dk + 2 * Dv))
         byts = T * (2 * Hk * Dk * 2 + Hv * Dv * 2 + Hv * 8 + Hv * Dv * 2) + (lv.B * Hv * Dk * Dv * 4 if lv.keep else 0)
@@ -226,7 +228,7 @@ def main():
 
     # timed device pass
     attn_flops = attention_flops(levels, shape)
-    chunk_alg = chunk_algorithmic(levels, shape)
+    chunked = [model._chunked(lv) for lv in levels]
     ops.TIMED.clear()
     ops.TIMED["tree_attention"] = []
     ops.TIMED["gdn_chunk_scan"] = []
@@ -274,8 +276,9 @@ def main():
                 "algorithmic_per_launch": flops_step / max(1, launches_per_step), "launches_per_step": launches_per_step,
                 "ms_per_step": kernel_ms[dominant]}
     elif dominant in ("gdn_chunk_scan", "gdn_fork_recurrent"):
-        fl = sum(f for f, _ in chunk_alg) * n_lin_layers
-        by = sum(b for _, b in chunk_alg) * n_lin_layers
+        alg = chunk_algorithmic(levels, shape, chunked if dominant == "gdn_chunk_scan" else [not c for c in chunked])
+        fl = sum(f for f, _ in alg) * n_lin_layers
+        by = sum(b for _, b in alg) * n_lin_layers
         sec = kernel_ms[dominant] / 1000.0
         t_peak = pk["bf16_tflops_sustained"] * 1e12
         b_peak = pk["hbm_gbs"] * 1e9

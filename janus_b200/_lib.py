@@ -24,8 +24,9 @@ SIGNATURES = {
                                       c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
                                       c_float, c_void_p, c_void_p],
     "janus_b200_gdn_chunk_scan": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
-                                  c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_float, c_void_p,
-                                  c_void_p],
+                                  c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
+                                  c_float, c_void_p, c_size_t, c_void_p, c_void_p],
+    "janus_b200_gdn_chunk_scan_workspace": [c_int64, c_int64, c_int64],
     "janus_b200_attn_qk_prep": [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float,
                                 c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p],
     "janus_b200_tree_attention": [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p,
@@ -48,6 +49,8 @@ SIGNATURES = {
                                         c_void_p],
 }
 
+SIZE_RESULTS = {"janus_b200_gdn_chunk_scan_workspace"}  # entry points returning size_t
+
 _LIB = None
 
 
@@ -63,7 +66,7 @@ def load(path=None):
     for name, args in SIGNATURES.items():
         fn = getattr(lib, name)
         fn.argtypes = args
-        fn.restype = c_int32
+        fn.restype = c_size_t if name in SIZE_RESULTS else c_int32
     if path is None:
         _LIB = lib
     return lib

@@ -95,6 +95,12 @@ __device__ __forceinline__ void tst16(uint32_t addr, const float* f) {
       "r"(__float_as_uint(f[14])), "r"(__float_as_uint(f[15])));
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
+// 2^x on the MUFU unit, flush-to-zero (results below 2^-126 are 0: irrelevant for softmax weights)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -212,6 +218,7 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(Params p) {
     cpa16(sbase + Lay::Q + swz(r, d, BM), p.q + ((int64_t)(ok ? q0 + tq : q0) * p.Hq + hkv * G + g) * D + d, ok);
   }
   load_kv(0, 0, false);
+  load_kv(0, 0, true);
   if (total > 1) load_kv(1, 1, false);
   asm volatile("cp.async.commit_group;\n" ::);
   asm volatile("cp.async.wait_group 0;\n" ::);
@@ -243,9 +250,7 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(Params p) {
     if (tid == 0 && j + 1 < total) issue_s(j + 1);
     ok = wait_bar(&bar_s[sb], (j >> 1) & 1, p.err);
     fence_after();
-    if (j + 2 < total) load_kv(j + 2, sb, false);
-    load_kv(j, sb, true);
-    asm volatile("cp.async.commit_group;\n" ::);
+    if (j + 2 < total) load_kv(j + 2, sb, false);  // K_j's stage: S_j is complete
     int lvl, ks;
     block_of(j, lvl, ks);
     int lo, hi;
@@ -263,14 +268,23 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(Params p) {
 #pragma unroll
     for (int c = 0; c < BN; c += 16) tld16(lane_addr + sb * BN + c, s + c);
     float mx = -INFINITY;
+    if (ks >= lo && ks + BN <= hi) {  // the whole block is visible to this row
 #pragma unroll
-    for (int c = 0; c < BN; ++c) {
-      const int kk = ks + c;
-      s[c] = (kk >= lo && kk < hi) ? s[c] * p.scale_log2 : -INFINITY;
-      mx = fmaxf(mx, s[c]);
+      for (int c = 0; c < BN; ++c) mx = fmaxf(mx, s[c]);
+    } else {
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        const int kk = ks + c;
+        s[c] = (kk >= lo && kk < hi) ? s[c] : -INFINITY;
+        mx = fmaxf(mx, s[c]);
+      }
     }
+    mx *= p.scale_log2;  // scale > 0: the max of the scaled scores
     if (j > 0) ok = ok && wait_bar(&bar_pv, (j - 1) & 1, p.err);
     fence_after();
+    // V_{j+1} into the stage PV_{j-1} has finished reading; it lands while this block and the next are processed
+    if (j + 1 < total) load_kv(j + 1, sb ^ 1, true);
+    asm volatile("cp.async.commit_group;\n" ::);
     // lazy max: refresh when the row's max grows by more than 2^8; rescale O then (warp-collective TMEM access)
     const bool grow = mx > m_used + 8.f;
     const float m_new = grow ? mx : m_used;
@@ -289,13 +303,14 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(Params p) {
     l_sum *= alpha;
     m_used = m_new;
     const float mref = m_used == -INFINITY ? 0.f : m_used;
+    const float sc = p.scale_log2;
     unsigned char* prow = base + Lay::P + r * 128;
 #pragma unroll
     for (int c = 0; c < BN; c += 8) {
       float e[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        e[i] = exp2f(s[c + i] - mref);
+        e[i] = ex2(fmaf(s[c + i], sc, -mref));
         l_sum += e[i];
       }
       uint4 v;
@@ -307,7 +322,7 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(Params p) {
       v.w = *reinterpret_cast<uint32_t*>(&h3);
       *reinterpret_cast<uint4*>(prow + ((((c >> 3) ^ (r & 7))) << 4)) = v;
     }
-    asm volatile("cp.async.wait_group 0;\n" ::);
+    asm volatile("cp.async.wait_group 1;\n" ::);  // the previous iteration's group: K_{j+1}, V_j
     fence_async_smem();
     fence_before();
     ok = __syncthreads_and(ok);  // CTA-uniform: a timed-out wait anywhere stops every thread at the loop head
@@ -321,6 +336,7 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(Params p) {
       commit(&bar_pv);
     }
   }
+  asm volatile("cp.async.wait_group 0;\n" ::);
   if (total > 0 && ok) ok = wait_bar(&bar_pv, (total - 1) & 1, p.err);
   fence_before();
   ok = __syncthreads_and(ok);

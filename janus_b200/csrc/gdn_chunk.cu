@@ -1,19 +1,19 @@
-// Gated delta rule over long rows in 64-token chunks (the state level), one CTA per (row, value head).
+// Gated delta rule over long rows in 64-token chunks (the state level), in two launches.
 //
-// Per chunk (G = in-chunk cumulative g, all exponentials of differences of G, so nothing overflows):
-//   N = -tril_strict(diag(beta) K K^T * e^(G_i - G_j))          (tensor cores, fp32 accumulate)
-//   T = (I - N)^-1                                               (fp32: 16x16 diagonal blocks by substitution, then
-//                                                                 two doubling stages 16 -> 32 -> 64)
-//   U = T (V * beta),  W = T (K * beta * e^G)                    (bf16 operands, fp32 accumulate)
-//   V' = U - W S                                                 (S rounded to bf16 for the product)
-//   O = scale (Q * e^G) S + tril(scale Q K^T * e^(G_i - G_j)) V'
-//   S = e^(G_last) S + (K * e^(G_last - G))^T V'                 (S kept in fp32 registers across chunks)
-// the WY form of transformers' torch_chunk_gated_delta_rule (the reference's CPU rule) and of fla's chunk kernels
-// (its GPU rule), with fla's rounding points (bf16 operands for every product, fp32 state). Rows end in a ragged
-// chunk: the missing tokens are loaded as zeros with g = beta = 0, which leaves the state untouched.
-//
-// Warp tiling (8 warps, mma.sync m16n8k16 bf16): 64x64 products as 4 m-tiles x 2 column halves; 64x128 products
-// likewise with 64-column halves; the 128x128 state update with one 16-row slice of S per warp.
+// 1. gdn_chunk_prep: one CTA per (chunk, value head), all chunks of all rows in parallel. With G the in-chunk
+//    cumulative g (every exponential is of a difference of G, so nothing overflows):
+//      N  = -tril_strict(diag(beta) K K^T * e^(G_i - G_j))          tensor cores, fp32 accumulate
+//      T  = (I - N)^-1                                               fp32: 16x16 diagonal blocks by substitution,
+//                                                                    then doubling stages 16 -> 32 -> 64
+//      U  = T (V * beta),  W = T (K * beta * e^G)                    bf16 operands, fp32 accumulate, stored bf16
+//      QK = tril(scale Q K^T * e^(G_i - G_j))                        stored bf16, plus G itself
+// 2. gdn_chunk_state: one CTA per (row, value head, 32 of the 128 value columns) — the columns of the state evolve
+//    independently — walking the row's chunks in order with its fp32 slice of S in registers:
+//      V' = U - W S;   O = scale (Q * e^G) S + QK V';   S = e^(G_last) S + (K * e^(G_last - G))^T V'
+//    (S rounded to bf16 for the products, as fla's chunk kernels do). The WY form of transformers'
+//    torch_chunk_gated_delta_rule (the reference's CPU rule) and of fla's chunk kernels (its GPU rule). A row's last
+//    chunk is ragged: the missing tokens are zeros with g = beta = 0, which leaves the state untouched.
+// Both kernels use mma.sync m16n8k16 (bf16, fp32 accumulate) on XOR-swizzled shared tiles.
 #include "common.cuh"
 
 namespace jb {
@@ -21,12 +21,16 @@ namespace {
 
 constexpr int CT = 64;   // chunk tokens
 constexpr int DH = 128;  // Dk = Dv
-constexpr int NT = 256;
+constexpr int DB = 32;   // value columns per state CTA
 constexpr int PADF = 65; // fp32 [64][65] tiles
 
 __device__ __forceinline__ uint32_t s32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 __device__ __forceinline__ void cpa16(void* dst, const void* src, bool ok) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s32(dst)), "l"(src), "r"(ok ? 16 : 0));
+}
+__device__ __forceinline__ void cp_commit_wait() {
+  asm volatile("cp.async.commit_group;\n" ::);
+  asm volatile("cp.async.wait_group 0;\n" ::);
 }
 __device__ __forceinline__ void ldx4(uint32_t* r, const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
@@ -43,285 +47,352 @@ __device__ __forceinline__ void mma(float* c, const uint32_t* a, uint32_t b0, ui
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// swizzled bf16 tile [rows][COLS]: 16-byte chunk c of row r at chunk c ^ (r & 7)
+// swizzled bf16 tiles [rows][COLS]: COLS >= 64 XOR the 16-byte chunk with row & 7; COLS == 32 (64-byte rows) with
+// (row >> 1) & 3, so the 8 rows of an ldmatrix hit 8 distinct bank groups either way
 template <int COLS>
-__device__ __forceinline__ int sw(int r, int c) { return r * COLS + (((c >> 3) ^ (r & 7)) << 3) + (c & 7); }
-
-// A fragment (16x16) at (m0, k0) of a row-major swizzled tile [m][k]
+__device__ __forceinline__ int sw(int r, int c) {
+  if constexpr (COLS == 32) return r * 32 + (((c >> 3) ^ ((r >> 1) & 3)) << 3) + (c & 7);
+  else return r * COLS + (((c >> 3) ^ (r & 7)) << 3) + (c & 7);
+}
+// A fragment (16x16) at (m0, k0) of a row-major tile [m][k]
 template <int COLS>
 __device__ __forceinline__ void lda(uint32_t* a, const __nv_bfloat16* t, int m0, int k0, int lane) {
   ldx4(a, t + sw<COLS>(m0 + (lane & 15), k0 + ((lane >> 4) << 3)));
 }
-// A fragment (16x16) at (m0, k0) of A = X^T where X is a row-major swizzled tile [k][m]
+// A fragment (16x16) at (m0, k0) of A = X^T, X row-major [k][m]
 template <int COLS>
 __device__ __forceinline__ void lda_t(uint32_t* a, const __nv_bfloat16* t, int m0, int k0, int lane) {
   ldx4t(a, t + sw<COLS>(k0 + (lane & 7) + ((lane >> 4) << 3), m0 + (((lane >> 3) & 1) << 3)));
 }
-// B fragments of two n-tiles (n0, n0+8) x k16 at k0, B[k][n] = X[n][k] with X row-major [n][k]
+// B fragments of n-tiles n0, n0+8 at k0 with B[k][n] = X[n][k], X row-major [n][k]
 template <int COLS>
 __device__ __forceinline__ void ldb_nk(uint32_t* b, const __nv_bfloat16* t, int n0, int k0, int lane) {
   ldx4(b, t + sw<COLS>(n0 + (lane & 7) + ((lane >> 4) << 3), k0 + (((lane >> 3) & 1) << 3)));
 }
-// B fragments of two n-tiles (n0, n0+8) x k16 at k0, B[k][n] = X[k][n] with X row-major [k][n]
+// B fragments of n-tiles n0, n0+8 at k0 with B[k][n] = X[k][n], X row-major [k][n]
 template <int COLS>
 __device__ __forceinline__ void ldb_kn(uint32_t* b, const __nv_bfloat16* t, int n0, int k0, int lane) {
   ldx4t(b, t + sw<COLS>(k0 + (lane & 7) + (((lane >> 3) & 1) << 3), n0 + ((lane >> 4) << 3)));
 }
 
-struct Smem {
-  __nv_bfloat16 q[CT * DH];    // Q, then Q * e^G * scale
-  __nv_bfloat16 k[CT * DH];    // K, then K * e^(G_last - G)
-  __nv_bfloat16 v[CT * DH];    // V, then V * beta
-  __nv_bfloat16 kb[CT * DH];   // K * beta * e^G, then W
-  __nv_bfloat16 vn[CT * DH];   // V'
-  __nv_bfloat16 s[DH * DH];    // S (bf16 copy)
-  __nv_bfloat16 qk[CT * CT];   // masked decayed scale * Q K^T
-  __nv_bfloat16 t[CT * CT];    // T (bf16)
-  float n[CT * PADF];          // N
-  float tf[CT * PADF];         // T (fp32)
-  float m[32 * 33];            // stage-2 product
-  float G[CT], eG[CT], eGl[CT], beta[CT], graw[CT];
+// the row of global chunk c (chunk_start: prefix sum of the rows' chunk counts, rows with no chunk skipped over)
+__device__ __forceinline__ int chunk_row(const int32_t* chunk_start, int B, int c) {
+  int lo = 0, hi = B;  // invariant: chunk_start[lo] <= c < chunk_start[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (chunk_start[mid] <= c) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+// ------------------------------------------------------------------------------------------------ chunk prep
+
+struct PrepSmem {
+  __nv_bfloat16 q[CT * DH];  // Q, then K * beta * e^G
+  __nv_bfloat16 k[CT * DH];
+  __nv_bfloat16 v[CT * DH];  // V, then V * beta
+  __nv_bfloat16 t[CT * CT];  // T (bf16)
+  float n[CT * PADF];
+  float tf[CT * PADF];
+  float m[32 * 33];
+  float G[CT], eG[CT], beta[CT], graw[CT];
 };
 
-__global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const __nv_bfloat16* __restrict__ q,
-                                                          const __nv_bfloat16* __restrict__ k,
-                                                          const __nv_bfloat16* __restrict__ v,
-                                                          const float* __restrict__ g, const float* __restrict__ beta,
-                                                          const int32_t* __restrict__ row_start,
-                                                          const float* __restrict__ state_in,
-                                                          const int32_t* __restrict__ state_row,
-                                                          float* __restrict__ state_out, int Hk, int Hv, float scale,
-                                                          __nv_bfloat16* __restrict__ o) {
+__global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
+    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
+    const float* __restrict__ g, const float* __restrict__ beta, const int32_t* __restrict__ row_start,
+    const int32_t* __restrict__ chunk_start, int B, int Hk, int Hv, float scale, __nv_bfloat16* __restrict__ Wg,
+    __nv_bfloat16* __restrict__ Ug, __nv_bfloat16* __restrict__ QKg, float* __restrict__ Gg) {
   extern __shared__ __align__(16) unsigned char raw[];
-  Smem& sm = *reinterpret_cast<Smem*>(raw);
-  const int row = blockIdx.x, h = blockIdx.y;
+  PrepSmem& sm = *reinterpret_cast<PrepSmem*>(raw);
+  const int c = blockIdx.x, h = blockIdx.y;
   const int hk = h / (Hv / Hk);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t r0 = row_start[row], r1 = row_start[row + 1];
-
-  // S accumulator: warp w owns key rows 16w..16w+15, all 128 value columns (16 n-tiles)
-  float S[16][4];
-  {
-    const int64_t sb = ((int64_t)(state_row ? state_row[row] : row) * Hv + h) * DH * DH;
-#pragma unroll
-    for (int n = 0; n < 16; ++n)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int rr = warp * 16 + (lane >> 2) + (e >> 1) * 8, cc = n * 8 + (lane & 3) * 2 + (e & 1);
-        S[n][e] = state_in ? state_in[sb + rr * DH + cc] : 0.f;
-      }
+  const int row = chunk_row(chunk_start, B, c);
+  const int64_t t0 = row_start[row] + (int64_t)(c - chunk_start[row]) * CT;
+  const int64_t rend = row_start[row + 1];
+  const int nt = (rend - t0) < CT ? (int)(rend - t0) : CT;
+  for (int x = tid; x < CT * (DH / 8); x += 256) {
+    const int r = x / (DH / 8), ch = (x % (DH / 8)) * 8;
+    const bool ok = r < nt;
+    const int64_t t = ok ? t0 + r : t0;
+    cpa16(&sm.q[sw<DH>(r, ch)], q + (t * Hk + hk) * DH + ch, ok);
+    cpa16(&sm.k[sw<DH>(r, ch)], k + (t * Hk + hk) * DH + ch, ok);
+    cpa16(&sm.v[sw<DH>(r, ch)], v + (t * Hv + h) * DH + ch, ok);
   }
-
-  for (int64_t c0 = r0; c0 < r1; c0 += CT) {
-    const int nt = (r1 - c0) < CT ? (int)(r1 - c0) : CT;
-    // ---- bf16 copy of S for this chunk's products
+  if (tid < CT) {
+    const bool ok = tid < nt;
+    sm.graw[tid] = ok ? g[(t0 + tid) * Hv + h] : 0.f;
+    sm.beta[tid] = ok ? beta[(t0 + tid) * Hv + h] : 0.f;
+  }
+  cp_commit_wait();
+  __syncthreads();
+  if (warp == 0) {  // in-chunk cumulative sum of g (two values per lane)
+    const float a = sm.graw[2 * lane], b = a + sm.graw[2 * lane + 1];
+    float inc = b;
 #pragma unroll
-    for (int n = 0; n < 16; ++n)
+    for (int off = 1; off < 32; off <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, inc, off);
+      if (lane >= off) inc += y;
+    }
+    const float excl = inc - b;
+    sm.G[2 * lane] = excl + a;
+    sm.G[2 * lane + 1] = excl + b;
+  }
+  __syncthreads();
+  if (tid < CT) {
+    sm.eG[tid] = expf(sm.G[tid]);
+    if (tid < nt) Gg[(t0 + tid) * Hv + h] = sm.G[tid];
+  }
+  // K K^T -> N (fp32, smem), Q K^T -> QK (bf16, global); warp: m-tile w>>1, n-tiles (w&1)*4 .. +3
+  {
+    const int mt = warp >> 1, nb = (warp & 1) * 32;
+    float kk[4][4] = {}, qk[4][4] = {};
+#pragma unroll
+    for (int ks = 0; ks < DH; ks += 16) {
+      uint32_t ak[4], aq[4], b[4];
+      lda<DH>(ak, sm.k, mt * 16, ks, lane);
+      lda<DH>(aq, sm.q, mt * 16, ks, lane);
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        ldb_nk<DH>(b, sm.k, nb + np * 16, ks, lane);
+        mma(kk[2 * np], ak, b[0], b[1]);
+        mma(kk[2 * np + 1], ak, b[2], b[3]);
+        mma(qk[2 * np], aq, b[0], b[1]);
+        mma(qk[2 * np + 1], aq, b[2], b[3]);
+      }
+    }
+    __nv_bfloat16* qkc = QKg + ((int64_t)c * Hv + h) * CT * CT;
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
 #pragma unroll
       for (int e = 0; e < 4; e += 2) {
-        const int rr = warp * 16 + (lane >> 2) + (e >> 1) * 8, cc = n * 8 + (lane & 3) * 2;
-        *reinterpret_cast<__nv_bfloat162*>(&sm.s[sw<DH>(rr, cc)]) = __floats2bfloat162_rn(S[n][e], S[n][e + 1]);
-      }
-    // ---- load the chunk
-    for (int x = tid; x < CT * (DH / 8); x += NT) {
-      const int r = x / (DH / 8), ch = (x % (DH / 8)) * 8;
-      const bool ok = r < nt;
-      const int64_t t = ok ? c0 + r : r0;
-      cpa16(&sm.q[sw<DH>(r, ch)], q + (t * Hk + hk) * DH + ch, ok);
-      cpa16(&sm.k[sw<DH>(r, ch)], k + (t * Hk + hk) * DH + ch, ok);
-      cpa16(&sm.v[sw<DH>(r, ch)], v + (t * Hv + h) * DH + ch, ok);
-    }
-    asm volatile("cp.async.commit_group;\n" ::);
-    if (tid < CT) {
-      const bool ok = tid < nt;
-      sm.graw[tid] = ok ? g[(c0 + tid) * Hv + h] : 0.f;
-      sm.beta[tid] = ok ? beta[(c0 + tid) * Hv + h] : 0.f;
-    }
-    asm volatile("cp.async.wait_group 0;\n" ::);
-    __syncthreads();
-    if (warp == 0) {  // in-chunk cumulative sum of g (two values per lane)
-      float a = sm.graw[2 * lane], b = a + sm.graw[2 * lane + 1];
-      float inc = b;
+        const int i = mt * 16 + (lane >> 2) + (e >> 1) * 8, j = nb + n * 8 + (lane & 3) * 2;
+        float qv[2];
 #pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, inc, off);
-        if (lane >= off) inc += y;
-      }
-      const float excl = inc - b;
-      sm.G[2 * lane] = excl + a;
-      sm.G[2 * lane + 1] = excl + b;
-    }
-    __syncthreads();
-    const float Gl = sm.G[CT - 1];
-    if (tid < CT) {
-      sm.eG[tid] = expf(sm.G[tid]);
-      sm.eGl[tid] = expf(Gl - sm.G[tid]);
-    }
-    // ---- phase A: K K^T -> N (fp32), Q K^T -> qk (bf16); warp: m-tile w>>1, n-tiles (w&1)*4 .. +3
-    {
-      const int mt = warp >> 1, nb = (warp & 1) * 32;
-      float kk[4][4] = {}, qk[4][4] = {};
-#pragma unroll
-      for (int ks = 0; ks < DH; ks += 16) {
-        uint32_t ak[4], aq[4], b[4];
-        lda<DH>(ak, sm.k, mt * 16, ks, lane);
-        lda<DH>(aq, sm.q, mt * 16, ks, lane);
-#pragma unroll
-        for (int np = 0; np < 2; ++np) {
-          ldb_nk<DH>(b, sm.k, nb + np * 16, ks, lane);
-          mma(kk[2 * np], ak, b[0], b[1]);
-          mma(kk[2 * np + 1], ak, b[2], b[3]);
-          mma(qk[2 * np], aq, b[0], b[1]);
-          mma(qk[2 * np + 1], aq, b[2], b[3]);
+        for (int u = 0; u < 2; ++u) {
+          const float dec = (j + u <= i) ? expf(sm.G[i] - sm.G[j + u]) : 0.f;
+          sm.n[i * PADF + j + u] = (j + u < i) ? -sm.beta[i] * kk[n][e + u] * dec : 0.f;
+          qv[u] = (j + u <= i) ? qk[n][e + u] * dec * scale : 0.f;
         }
+        *reinterpret_cast<__nv_bfloat162*>(qkc + i * CT + j) = __floats2bfloat162_rn(qv[0], qv[1]);
       }
-      __syncthreads();  // eG / eGl visible (written above by threads < 64)
+  }
+  __syncthreads();  // every warp is done reading sm.q as Q
+  for (int x = tid; x < CT * DH / 2; x += 256) {  // q <- K beta e^G, v <- V beta
+    const int r = x / (DH / 2), cc = (x % (DH / 2)) * 2;
+    const int off = sw<DH>(r, cc);
+    const float2 kf = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&sm.k[off]));
+    const float2 vf = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&sm.v[off]));
+    const float b = sm.beta[r], eg = sm.eG[r];
+    *reinterpret_cast<__nv_bfloat162*>(&sm.q[off]) = __floats2bfloat162_rn(kf.x * b * eg, kf.y * b * eg);
+    *reinterpret_cast<__nv_bfloat162*>(&sm.v[off]) = __floats2bfloat162_rn(vf.x * b, vf.y * b);
+  }
+  // T = (I - N)^-1: diagonal 16x16 blocks (warps 0-3, lane c < 16 owns column c)
+  if (warp < 4) {
+    const int base = warp * 16;
+    const int cc = lane & 15;
+    float col[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) col[r] = (r == cc) ? 1.f : 0.f;
+#pragma unroll
+    for (int r = 1; r < 16; ++r) {
+      float acc = 0.f;
+#pragma unroll
+      for (int m = 0; m < 16; ++m)
+        if (m < r && m >= cc) acc += sm.n[(base + r) * PADF + base + m] * col[m];
+      if (cc < r) col[r] = acc;
+    }
+    if (lane < 16) {
+#pragma unroll
+      for (int r = 0; r < 16; ++r) sm.tf[(base + r) * PADF + base + cc] = col[r];
+    }
+  }
+  __syncthreads();
+  // stage 1: T[2h+1, 2h] = T[2h+1, 2h+1] N[2h+1, 2h] T[2h, 2h] (16x16 blocks), h = 0, 1
+  for (int x = tid; x < 512; x += 256) {
+    const int hb = x >> 8, i = (x >> 4) & 15, j = x & 15;
+    const int bi = (2 * hb + 1) * 16, bj = 2 * hb * 16;
+    float acc = 0.f;
+    for (int m = j; m < 16; ++m) acc += sm.n[(bi + i) * PADF + bj + m] * sm.tf[(bj + m) * PADF + bj + j];
+    sm.m[(hb * 16 + i) * 33 + j] = acc;
+  }
+  __syncthreads();
+  for (int x = tid; x < 512; x += 256) {
+    const int hb = x >> 8, i = (x >> 4) & 15, j = x & 15;
+    const int bi = (2 * hb + 1) * 16, bj = 2 * hb * 16;
+    float acc = 0.f;
+    for (int m = 0; m <= i; ++m) acc += sm.tf[(bi + i) * PADF + bi + m] * sm.m[(hb * 16 + m) * 33 + j];
+    sm.tf[(bi + i) * PADF + bj + j] = acc;
+  }
+  __syncthreads();
+  // stage 2: T[32:, :32] = T[32:, 32:] N[32:, :32] T[:32, :32]
+  for (int x = tid; x < 1024; x += 256) {
+    const int i = x >> 5, j = x & 31;
+    float acc = 0.f;
+    for (int m = j; m < 32; ++m) acc += sm.n[(32 + i) * PADF + m] * sm.tf[m * PADF + j];
+    sm.m[i * 33 + j] = acc;
+  }
+  __syncthreads();
+  for (int x = tid; x < 1024; x += 256) {
+    const int i = x >> 5, j = x & 31;
+    float acc = 0.f;
+    for (int m = 0; m <= i; ++m) acc += sm.tf[(32 + i) * PADF + 32 + m] * sm.m[m * 33 + j];
+    sm.tf[(32 + i) * PADF + j] = acc;
+  }
+  __syncthreads();
+  for (int x = tid; x < CT * CT; x += 256) {
+    const int i = x >> 6, j = x & 63;
+    sm.t[sw<CT>(i, j)] = __float2bfloat16_rn(j <= i ? sm.tf[i * PADF + j] : 0.f);
+  }
+  __syncthreads();
+  // U = T vb, W = T kb (64 x 128; warp: m-tile w>>1, columns (w&1)*64 .. +63), stored bf16 per token
+  const int mt = warp >> 1, cb = (warp & 1) * 64;
+  float U[8][4] = {}, Wacc[8][4] = {};
+#pragma unroll
+  for (int ks = 0; ks < CT; ks += 16) {
+    uint32_t a[4], b[4];
+    lda<CT>(a, sm.t, mt * 16, ks, lane);
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+      ldb_kn<DH>(b, sm.v, cb + np * 16, ks, lane);
+      mma(U[2 * np], a, b[0], b[1]);
+      mma(U[2 * np + 1], a, b[2], b[3]);
+      ldb_kn<DH>(b, sm.q, cb + np * 16, ks, lane);
+      mma(Wacc[2 * np], a, b[0], b[1]);
+      mma(Wacc[2 * np + 1], a, b[2], b[3]);
+    }
+  }
+#pragma unroll
+  for (int n = 0; n < 8; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      const int i = mt * 16 + (lane >> 2) + (e >> 1) * 8, j = cb + n * 8 + (lane & 3) * 2;
+      if (i < nt) {
+        const int64_t off = ((t0 + i) * Hv + h) * DH + j;
+        *reinterpret_cast<__nv_bfloat162*>(Ug + off) = __floats2bfloat162_rn(U[n][e], U[n][e + 1]);
+        *reinterpret_cast<__nv_bfloat162*>(Wg + off) = __floats2bfloat162_rn(Wacc[n][e], Wacc[n][e + 1]);
+      }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ state pass
+
+struct StateSmem {
+  __nv_bfloat16 w[CT * DH];   // W
+  __nv_bfloat16 q[CT * DH];   // Q, then Q e^G scale
+  __nv_bfloat16 k[CT * DH];   // K, then K e^(G_last - G)
+  __nv_bfloat16 qk[CT * CT];  // masked decayed scale Q K^T
+  __nv_bfloat16 s[DH * DB];   // S slice (bf16) [dk][dv]
+  __nv_bfloat16 vn[CT * DB];  // V' slice [tok][dv]
+  float G[CT];
+};
+
+__global__ void __launch_bounds__(128, 3) gdn_chunk_state_kernel(
+    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const int32_t* __restrict__ row_start,
+    const int32_t* __restrict__ chunk_start, const float* __restrict__ state_in, const int32_t* __restrict__ state_row,
+    float* __restrict__ state_out, int Hk, int Hv, float scale, const __nv_bfloat16* __restrict__ Wg,
+    const __nv_bfloat16* __restrict__ Ug, const __nv_bfloat16* __restrict__ QKg, const float* __restrict__ Gg,
+    __nv_bfloat16* __restrict__ o) {
+  extern __shared__ __align__(16) unsigned char raw[];
+  StateSmem& sm = *reinterpret_cast<StateSmem*>(raw);
+  const int row = blockIdx.x, h = blockIdx.y, c0 = blockIdx.z * DB;
+  const int hk = h / (Hv / Hk);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // S slice: warp w owns key rows 32w..32w+31 (2 m-tiles) x DB columns (4 n-tiles)
+  float S[2][4][4];
+  {
+    const float* s0 =
+        state_in ? state_in + ((int64_t)(state_row ? state_row[row] : row) * Hv + h) * DH * DH : nullptr;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
       for (int n = 0; n < 4; ++n)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int i = mt * 16 + (lane >> 2) + (e >> 1) * 8, j = nb + n * 8 + (lane & 3) * 2 + (e & 1);
-          const float dec = (j <= i) ? expf(sm.G[i] - sm.G[j]) : 0.f;
-          sm.n[i * PADF + j] = (j < i) ? -sm.beta[i] * kk[n][e] * dec : 0.f;
-          sm.qk[sw<CT>(i, j)] = __float2bfloat16_rn((j <= i) ? qk[n][e] * dec * scale : 0.f);
+          const int rr = warp * 32 + mt * 16 + (lane >> 2) + (e >> 1) * 8, cc = c0 + n * 8 + (lane & 3) * 2 + (e & 1);
+          S[mt][n][e] = s0 ? s0[rr * DH + cc] : 0.f;
         }
+  }
+  const int64_t r0 = row_start[row], r1 = row_start[row + 1];
+  for (int c = chunk_start[row]; c < chunk_start[row + 1]; ++c) {
+    const int64_t t0 = r0 + (int64_t)(c - chunk_start[row]) * CT;
+    const int nt = (r1 - t0) < CT ? (int)(r1 - t0) : CT;
+    for (int x = tid; x < CT * (DH / 8); x += 128) {
+      const int r = x / (DH / 8), ch = (x % (DH / 8)) * 8;
+      const bool ok = r < nt;
+      const int64_t t = ok ? t0 + r : t0;
+      cpa16(&sm.w[sw<DH>(r, ch)], Wg + (t * Hv + h) * DH + ch, ok);
+      cpa16(&sm.q[sw<DH>(r, ch)], q + (t * Hk + hk) * DH + ch, ok);
+      cpa16(&sm.k[sw<DH>(r, ch)], k + (t * Hk + hk) * DH + ch, ok);
     }
+    const __nv_bfloat16* qkc = QKg + ((int64_t)c * Hv + h) * CT * CT;
+    for (int x = tid; x < CT * (CT / 8); x += 128) {
+      const int r = x / (CT / 8), ch = (x % (CT / 8)) * 8;
+      cpa16(&sm.qk[sw<CT>(r, ch)], qkc + r * CT + ch, true);
+    }
+    if (tid < CT) sm.G[tid] = tid < nt ? Gg[(t0 + tid) * Hv + h] : 0.f;
+    // bf16 copy of the state slice (rows of this warp)
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          const int rr = warp * 32 + mt * 16 + (lane >> 2) + (e >> 1) * 8, cc = n * 8 + (lane & 3) * 2;
+          *reinterpret_cast<__nv_bfloat162*>(&sm.s[sw<DB>(rr, cc)]) =
+              __floats2bfloat162_rn(S[mt][n][e], S[mt][n][e + 1]);
+        }
+    cp_commit_wait();
     __syncthreads();
-    // ---- elementwise: kb = K beta e^G, k <- K e^(Gl - G), v <- V beta, q <- Q e^G scale
-    for (int x = tid; x < CT * DH / 2; x += NT) {
+    const float Gl = sm.G[nt - 1];  // padded tokens carry g = 0: the cumulative sum stays at its last value
+    for (int x = tid; x < CT * DH / 2; x += 128) {  // q <- Q e^G scale, k <- K e^(Gl - G)
       const int r = x / (DH / 2), cc = (x % (DH / 2)) * 2;
       const int off = sw<DH>(r, cc);
-      const float2 kf = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&sm.k[off]));
-      const float2 vf = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&sm.v[off]));
+      const float Gr = r < nt ? sm.G[r] : Gl;
+      const float eq = expf(Gr) * scale, ek = expf(Gl - Gr);
       const float2 qf = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&sm.q[off]));
-      const float b = sm.beta[r], eg = sm.eG[r], egl = sm.eGl[r];
-      *reinterpret_cast<__nv_bfloat162*>(&sm.kb[off]) = __floats2bfloat162_rn(kf.x * b * eg, kf.y * b * eg);
-      *reinterpret_cast<__nv_bfloat162*>(&sm.k[off]) = __floats2bfloat162_rn(kf.x * egl, kf.y * egl);
-      *reinterpret_cast<__nv_bfloat162*>(&sm.v[off]) = __floats2bfloat162_rn(vf.x * b, vf.y * b);
-      *reinterpret_cast<__nv_bfloat162*>(&sm.q[off]) = __floats2bfloat162_rn(qf.x * eg * scale, qf.y * eg * scale);
+      const float2 kf = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&sm.k[off]));
+      *reinterpret_cast<__nv_bfloat162*>(&sm.q[off]) = __floats2bfloat162_rn(qf.x * eq, qf.y * eq);
+      *reinterpret_cast<__nv_bfloat162*>(&sm.k[off]) = __floats2bfloat162_rn(kf.x * ek, kf.y * ek);
     }
-    // ---- T = (I - N)^-1: diagonal 16x16 blocks (warps 0-3, lane c < 16 owns column c)
-    if (warp < 4) {
-      const int base = warp * 16;
-      const int c = lane & 15;
-      float col[16];
-#pragma unroll
-      for (int r = 0; r < 16; ++r) col[r] = (r == c) ? 1.f : 0.f;
-#pragma unroll
-      for (int r = 1; r < 16; ++r) {
-        float acc = 0.f;
-#pragma unroll
-        for (int m = 0; m < 16; ++m)
-          if (m < r && m >= c) acc += sm.n[(base + r) * PADF + base + m] * col[m];
-        if (c < r) col[r] = acc;
-      }
-      if (lane < 16) {
-#pragma unroll
-        for (int r = 0; r < 16; ++r) sm.tf[(base + r) * PADF + base + c] = col[r];
-      }
-    }
-    __syncthreads();
-    // stage 1: T[2h+1, 2h] = T[2h+1,2h+1] N[2h+1,2h] T[2h,2h] (16x16 blocks), h = 0, 1
+    // V' = U - W S  (warp w: m-tile w, 4 n-tiles)
     {
-      // M = N[2h+1,2h] T[2h,2h]: 2 x 256 outputs
-      for (int x = tid; x < 512; x += NT) {
-        const int hb = x >> 8, i = (x >> 4) & 15, j = x & 15;
-        const int bi = (2 * hb + 1) * 16, bj = 2 * hb * 16;
-        float acc = 0.f;
-        for (int m = j; m < 16; ++m) acc += sm.n[(bi + i) * PADF + bj + m] * sm.tf[(bj + m) * PADF + bj + j];
-        sm.m[(hb * 16 + i) * 33 + j] = acc;
-      }
-      __syncthreads();
-      for (int x = tid; x < 512; x += NT) {
-        const int hb = x >> 8, i = (x >> 4) & 15, j = x & 15;
-        const int bi = (2 * hb + 1) * 16, bj = 2 * hb * 16;
-        float acc = 0.f;
-        for (int m = 0; m <= i; ++m) acc += sm.tf[(bi + i) * PADF + bi + m] * sm.m[(hb * 16 + m) * 33 + j];
-        sm.tf[(bi + i) * PADF + bj + j] = acc;
-      }
-    }
-    __syncthreads();
-    // stage 2: T[32:, :32] = T[32:,32:] N[32:, :32] T[:32, :32]
-    for (int x = tid; x < 1024; x += NT) {
-      const int i = x >> 5, j = x & 31;
-      float acc = 0.f;
-      for (int m = j; m < 32; ++m) acc += sm.n[(32 + i) * PADF + m] * sm.tf[m * PADF + j];
-      sm.m[i * 33 + j] = acc;
-    }
-    __syncthreads();
-    for (int x = tid; x < 1024; x += NT) {
-      const int i = x >> 5, j = x & 31;
-      float acc = 0.f;
-      for (int m = 0; m <= i; ++m) acc += sm.tf[(32 + i) * PADF + 32 + m] * sm.m[m * 33 + j];
-      sm.tf[(32 + i) * PADF + j] = acc;
-    }
-    __syncthreads();
-    // T to bf16 (lower triangle incl. diagonal; zeros above)
-    for (int x = tid; x < CT * CT; x += NT) {
-      const int i = x >> 6, j = x & 63;
-      sm.t[sw<CT>(i, j)] = __float2bfloat16_rn(j <= i ? sm.tf[i * PADF + j] : 0.f);
-    }
-    __syncthreads();
-    // ---- phase B: U = T vb, W = T kb  (64 x 128; warp: m-tile w>>1, columns (w&1)*64 .. +63)
-    const int mt = warp >> 1, cb = (warp & 1) * 64;
-    float U[8][4] = {}, Wacc[8][4] = {};
-#pragma unroll
-    for (int ks = 0; ks < CT; ks += 16) {
-      uint32_t a[4], b[4];
-      lda<CT>(a, sm.t, mt * 16, ks, lane);
-#pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        ldb_kn<DH>(b, sm.v, cb + np * 16, ks, lane);
-        mma(U[2 * np], a, b[0], b[1]);
-        mma(U[2 * np + 1], a, b[2], b[3]);
-        ldb_kn<DH>(b, sm.kb, cb + np * 16, ks, lane);
-        mma(Wacc[2 * np], a, b[0], b[1]);
-        mma(Wacc[2 * np + 1], a, b[2], b[3]);
-      }
-    }
-    __syncthreads();  // every warp is done reading kb
-#pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        const int i = mt * 16 + (lane >> 2) + (e >> 1) * 8, j = cb + n * 8 + (lane & 3) * 2;
-        *reinterpret_cast<__nv_bfloat162*>(&sm.kb[sw<DH>(i, j)]) = __floats2bfloat162_rn(Wacc[n][e], Wacc[n][e + 1]);
-      }
-    __syncthreads();
-    // ---- phase C: V' = U - W S
-    {
-      float P[8][4] = {};
+      float P[4][4] = {};
 #pragma unroll
       for (int ks = 0; ks < DH; ks += 16) {
         uint32_t a[4], b[4];
-        lda<DH>(a, sm.kb, mt * 16, ks, lane);
+        lda<DH>(a, sm.w, warp * 16, ks, lane);
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
-          ldb_kn<DH>(b, sm.s, cb + np * 16, ks, lane);
+        for (int np = 0; np < 2; ++np) {
+          ldb_kn<DB>(b, sm.s, np * 16, ks, lane);
           mma(P[2 * np], a, b[0], b[1]);
           mma(P[2 * np + 1], a, b[2], b[3]);
         }
       }
 #pragma unroll
-      for (int n = 0; n < 8; ++n)
+      for (int n = 0; n < 4; ++n)
 #pragma unroll
         for (int e = 0; e < 4; e += 2) {
-          const int i = mt * 16 + (lane >> 2) + (e >> 1) * 8, j = cb + n * 8 + (lane & 3) * 2;
-          *reinterpret_cast<__nv_bfloat162*>(&sm.vn[sw<DH>(i, j)]) =
-              __floats2bfloat162_rn(U[n][e] - P[n][e], U[n][e + 1] - P[n][e + 1]);
+          const int i = warp * 16 + (lane >> 2) + (e >> 1) * 8, j = n * 8 + (lane & 3) * 2;
+          float2 u = make_float2(0.f, 0.f);
+          if (i < nt)
+            u = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(Ug + ((t0 + i) * Hv + h) * DH + c0 + j));
+          *reinterpret_cast<__nv_bfloat162*>(&sm.vn[sw<DB>(i, j)]) =
+              __floats2bfloat162_rn(u.x - P[n][e], u.y - P[n][e + 1]);
         }
     }
-    __syncthreads();
-    // ---- phase D: O = q S + qk V'
+    __syncthreads();  // V' and the scaled q / k are visible
+    // O = (Q e^G scale) S + QK V'
     {
-      float O[8][4] = {};
+      float O[4][4] = {};
 #pragma unroll
       for (int ks = 0; ks < DH; ks += 16) {
         uint32_t a[4], b[4];
-        lda<DH>(a, sm.q, mt * 16, ks, lane);
+        lda<DH>(a, sm.q, warp * 16, ks, lane);
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
-          ldb_kn<DH>(b, sm.s, cb + np * 16, ks, lane);
+        for (int np = 0; np < 2; ++np) {
+          ldb_kn<DB>(b, sm.s, np * 16, ks, lane);
           mma(O[2 * np], a, b[0], b[1]);
           mma(O[2 * np + 1], a, b[2], b[3]);
         }
@@ -329,83 +400,124 @@ __global__ void __launch_bounds__(NT, 1) gdn_chunk_kernel(const __nv_bfloat16* _
 #pragma unroll
       for (int ks = 0; ks < CT; ks += 16) {
         uint32_t a[4], b[4];
-        lda<CT>(a, sm.qk, mt * 16, ks, lane);
+        lda<CT>(a, sm.qk, warp * 16, ks, lane);
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
-          ldb_kn<DH>(b, sm.vn, cb + np * 16, ks, lane);
+        for (int np = 0; np < 2; ++np) {
+          ldb_kn<DB>(b, sm.vn, np * 16, ks, lane);
           mma(O[2 * np], a, b[0], b[1]);
           mma(O[2 * np + 1], a, b[2], b[3]);
         }
       }
 #pragma unroll
-      for (int n = 0; n < 8; ++n)
+      for (int n = 0; n < 4; ++n)
 #pragma unroll
         for (int e = 0; e < 4; e += 2) {
-          const int i = mt * 16 + (lane >> 2) + (e >> 1) * 8, j = cb + n * 8 + (lane & 3) * 2;
+          const int i = warp * 16 + (lane >> 2) + (e >> 1) * 8, j = n * 8 + (lane & 3) * 2;
           if (i < nt)
-            *reinterpret_cast<__nv_bfloat162*>(o + ((c0 + i) * Hv + h) * DH + j) =
+            *reinterpret_cast<__nv_bfloat162*>(o + ((t0 + i) * Hv + h) * DH + c0 + j) =
                 __floats2bfloat162_rn(O[n][e], O[n][e + 1]);
         }
     }
-    // ---- phase E: S = e^(G_last) S + (K e^(Gl - G))^T V'   (warp: key rows 16w..16w+15)
+    // S = e^(G_last) S + (K e^(Gl - G))^T V'
     {
       const float dl = expf(Gl);
 #pragma unroll
-      for (int n = 0; n < 16; ++n)
+      for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) S[n][e] *= dl;
+        for (int n = 0; n < 4; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) S[mt][n][e] *= dl;
 #pragma unroll
       for (int ks = 0; ks < CT; ks += 16) {
-        uint32_t a[4], b[4];
-        lda_t<DH>(a, sm.k, warp * 16, ks, lane);
+        uint32_t b[2][4];
 #pragma unroll
-        for (int np = 0; np < 8; ++np) {
-          ldb_kn<DH>(b, sm.vn, np * 16, ks, lane);
-          mma(S[2 * np], a, b[0], b[1]);
-          mma(S[2 * np + 1], a, b[2], b[3]);
+        for (int np = 0; np < 2; ++np) ldb_kn<DB>(b[np], sm.vn, np * 16, ks, lane);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          uint32_t a[4];
+          lda_t<DH>(a, sm.k, warp * 32 + mt * 16, ks, lane);
+#pragma unroll
+          for (int np = 0; np < 2; ++np) {
+            mma(S[mt][2 * np], a, b[np][0], b[np][1]);
+            mma(S[mt][2 * np + 1], a, b[np][2], b[np][3]);
+          }
         }
       }
     }
-    __syncthreads();  // all reads of this chunk's tiles (and of sm.s) are done before the next chunk overwrites them
+    __syncthreads();  // this chunk's tiles are free for the next one
   }
   if (state_out) {
-    const int64_t sb = ((int64_t)row * Hv + h) * DH * DH;
+    float* so = state_out + ((int64_t)row * Hv + h) * DH * DH;
 #pragma unroll
-    for (int n = 0; n < 16; ++n)
+    for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int rr = warp * 16 + (lane >> 2) + (e >> 1) * 8, cc = n * 8 + (lane & 3) * 2 + (e & 1);
-        state_out[sb + rr * DH + cc] = S[n][e];
-      }
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int rr = warp * 32 + mt * 16 + (lane >> 2) + (e >> 1) * 8, cc = c0 + n * 8 + (lane & 3) * 2 + (e & 1);
+          so[rr * DH + cc] = S[mt][n][e];
+        }
   }
 }
+
+size_t align_up(size_t x) { return (x + 255) & ~(size_t)255; }
 
 }  // namespace
 }  // namespace jb
 
 using namespace jb;
 
+extern "C" size_t janus_b200_gdn_chunk_scan_workspace(int64_t T, int64_t n_chunks, int64_t Hv) {
+  const size_t tok = (size_t)T * Hv;
+  return 2 * align_up(tok * DH * sizeof(__nv_bfloat16)) + align_up((size_t)n_chunks * Hv * CT * CT * 2) +
+         align_up(tok * sizeof(float));
+}
+
 extern "C" int janus_b200_gdn_chunk_scan(const void* q, const void* k, const void* v, const float* g,
                                          const float* beta, int64_t T, int64_t B, const int32_t* row_start,
-                                         const float* state_in, const int32_t* state_row, float* state_out, int64_t Hk, int64_t Hv, int64_t Dk,
-                                         int64_t Dv, float scale, void* o, void* stream) {
-  JB_REQUIRE(q && k && v && g && beta && row_start && o, JANUS_ERR_INVALID, "gdn_chunk_scan: null pointer");
+                                         const int32_t* chunk_start, int64_t n_chunks, const float* state_in,
+                                         const int32_t* state_row, float* state_out, int64_t Hk, int64_t Hv,
+                                         int64_t Dk, int64_t Dv, float scale, void* workspace, size_t workspace_bytes,
+                                         void* o, void* stream) {
+  JB_REQUIRE(q && k && v && g && beta && row_start && chunk_start && o, JANUS_ERR_INVALID,
+             "gdn_chunk_scan: null pointer");
   JB_REQUIRE(Dk == DH && Dv == DH, JANUS_ERR_UNSUPPORTED, "gdn_chunk_scan: Dk = Dv = 128 only (got %lld, %lld)",
              (long long)Dk, (long long)Dv);
-  JB_REQUIRE(T >= 0 && B >= 0 && Hk > 0 && Hv > 0 && Hv % Hk == 0 && Hv <= 65535, JANUS_ERR_INVALID,
-             "gdn_chunk_scan: sizes");
+  JB_REQUIRE(T >= 0 && B >= 0 && n_chunks >= 0 && Hk > 0 && Hv > 0 && Hv % Hk == 0 && Hv <= 65535 &&
+                 n_chunks <= 0x7fffffff,
+             JANUS_ERR_INVALID, "gdn_chunk_scan: sizes");
   JB_REQUIRE(JB_ALIGNED(q, 16) && JB_ALIGNED(k, 16) && JB_ALIGNED(v, 16) && JB_ALIGNED(o, 4), JANUS_ERR_ALIGNMENT,
              "gdn_chunk_scan: alignment");
+  const size_t need = janus_b200_gdn_chunk_scan_workspace(T, n_chunks, Hv);
+  JB_REQUIRE(workspace && workspace_bytes >= need && JB_ALIGNED(workspace, 256), JANUS_ERR_WORKSPACE,
+             "gdn_chunk_scan: workspace %zu bytes (256-aligned) < %zu", workspace_bytes, need);
   if (B == 0 || T == 0) return JANUS_OK;
-  const size_t smem = sizeof(Smem);
-  cudaError_t e = cudaFuncSetAttribute(gdn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const size_t tok = (size_t)T * Hv;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  __nv_bfloat16* Wg = reinterpret_cast<__nv_bfloat16*>(ws);
+  __nv_bfloat16* Ug = reinterpret_cast<__nv_bfloat16*>(ws + align_up(tok * DH * 2));
+  __nv_bfloat16* QKg = reinterpret_cast<__nv_bfloat16*>(ws + 2 * align_up(tok * DH * 2));
+  float* Gg =
+      reinterpret_cast<float*>(ws + 2 * align_up(tok * DH * 2) + align_up((size_t)n_chunks * Hv * CT * CT * 2));
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sizeof(PrepSmem));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gdn_chunk_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(StateSmem));
   if (e != cudaSuccess) {
-    set_error("gdn_chunk_scan: smem attribute (%zu bytes): %s", smem, cudaGetErrorString(e));
+    set_error("gdn_chunk_scan: smem attribute: %s", cudaGetErrorString(e));
     return JANUS_ERR_CUDA;
   }
-  dim3 grid((unsigned)B, (unsigned)Hv);
-  gdn_chunk_kernel<<<grid, NT, smem, (cudaStream_t)stream>>>(
-      (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, g, beta, row_start, state_in,
-      state_row, state_out, (int)Hk, (int)Hv, scale, (__nv_bfloat16*)o);
-  return launch_status("gdn_chunk_scan");
+  if (n_chunks > 0) {
+    gdn_chunk_prep_kernel<<<dim3((unsigned)n_chunks, (unsigned)Hv), 256, sizeof(PrepSmem), s>>>(
+        (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, g, beta, row_start, chunk_start,
+        (int)B, (int)Hk, (int)Hv, scale, Wg, Ug, QKg, Gg);
+    int st = launch_status("gdn_chunk_scan/prep");
+    if (st) return st;
+  }
+  gdn_chunk_state_kernel<<<dim3((unsigned)B, (unsigned)Hv, DH / DB), 128, sizeof(StateSmem), s>>>(
+      (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, row_start, chunk_start, state_in, state_row, state_out,
+      (int)Hk, (int)Hv, scale, Wg, Ug, QKg, Gg, (__nv_bfloat16*)o);
+  return launch_status("gdn_chunk_scan/state");
 }

@@ -101,8 +101,9 @@ class DecisionReadout:
                     proj, rs, rot, plan[(d, "parent")] if d > 0 else None, parent_state[0], lv.keep, L.conv, L.A_log,
                     L.dt_bias, s.lin_k_heads, s.lin_k_dim, s.lin_v_heads, s.lin_v_dim)
                 if self._chunked(lv):
-                    o, S = ops.gdn_chunk_scan(q, k, v, g, beta, rs, parent_state[1],
-                                              plan[(d, "parent")] if d > 0 else None, lv.keep, 1.0 / math.sqrt(s.lin_k_dim))
+                    o, S = ops.gdn_chunk_scan(q, k, v, g, beta, rs, plan[(d, "chunk_start")], int(lv.chunk_start[-1]),
+                                              parent_state[1], plan[(d, "parent")] if d > 0 else None, lv.keep,
+                                              1.0 / math.sqrt(s.lin_k_dim))
                 else:
                     o, S = ops.gdn_fork_recurrent(q, k, v, g, beta, rs, plan[(d, "child_start")], parent_state[1],
                                                   lv.keep, 1.0 / math.sqrt(s.lin_k_dim))

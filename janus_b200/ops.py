@@ -152,9 +152,10 @@ def gdn_fork_recurrent(q, k, v, g, beta, row_start, child_start, state_in, keep_
     return o, state_out
 
 
-@_instrument("gdn_chunk_scan", 1)
-def gdn_chunk_scan(q, k, v, g, beta, row_start, state_in, state_row, keep_state, scale):
-    """Long rows in 64-token chunks; row b starts from state_in[state_row[b]] (None: zeros / identity map)."""
+@_instrument("gdn_chunk_scan", 2)
+def gdn_chunk_scan(q, k, v, g, beta, row_start, chunk_start, n_chunks, state_in, state_row, keep_state, scale):
+    """Long rows in 64-token chunks; row b starts from state_in[state_row[b]] (None: zeros / identity map).
+    chunk_start int32 [B+1] (first chunk of each row), n_chunks = chunk_start[B]."""
     T, Hk, Dk = q.shape
     Hv, Dv = v.shape[1], v.shape[2]
     B = row_start.shape[0] - 1
@@ -166,31 +167,17 @@ def gdn_chunk_scan(q, k, v, g, beta, row_start, state_in, state_row, keep_state,
         _need(state_row, I32, "state_row")
     for t, n in ((q, "q"), (k, "k"), (v, "v")):
         _need(t, BF16, n)
-    _lib.check(_lib.load().janus_b200_gdn_chunk_scan(
+    lib = _lib.load()
+    nbytes = lib.janus_b200_gdn_chunk_scan_workspace(T, n_chunks, Hv)
+    ws = torch.empty(max(1, nbytes), dtype=torch.uint8, device=q.device)
+    _lib.check(lib.janus_b200_gdn_chunk_scan(
         _ptr(q), _ptr(k), _ptr(v), _ptr(_need(g, F32, "g")), _ptr(_need(beta, F32, "beta")), T, B,
-        _ptr(_need(row_start, I32, "row_start")), _ptr(state_in), _ptr(state_row), _ptr(state_out), Hk, Hv, Dk, Dv,
-        scale, _ptr(o), _stream(q)), "gdn_chunk_scan")
+        _ptr(_need(row_start, I32, "row_start")), _ptr(_need(chunk_start, I32, "chunk_start")), n_chunks,
+        _ptr(state_in), _ptr(state_row), _ptr(state_out), Hk, Hv, Dk, Dv, scale, _ptr(ws), ws.numel(), _ptr(o),
+        _stream(q)), "gdn_chunk_scan")
     return o, state_out
 
 
-@_instrument("attn_qk_prep", 1)
-def attn_qk_prep(qkv, positions, inv_freq, q_norm_w, k_norm_w, eps, Hq, Hkv, D, k_out=None, v_out=None):
-    _need(qkv, BF16, "qkv", contiguous=False)
-    if qkv.stride(1) != 1:
-        raise ValueError("qkv must have unit column stride")
-    T = qkv.shape[0]
-    dev = qkv.device
-    q = torch.empty(T, Hq, D, dtype=BF16, device=dev)
-    k = torch.empty(T, Hkv, D, dtype=BF16, device=dev) if k_out is None else k_out
-    v = torch.empty(T, Hkv, D, dtype=BF16, device=dev) if v_out is None else v_out
-    _lib.check(_lib.load().janus_b200_attn_qk_prep(
-        _ptr(qkv), qkv.stride(0), T, _ptr(_need(positions, I32, "positions")), _ptr(_need(inv_freq, F32, "inv_freq")),
-        inv_freq.shape[0] * 2, _ptr(_need(q_norm_w, BF16, "q_norm_w")), _ptr(_need(k_norm_w, BF16, "k_norm_w")), eps,
-        Hq, Hkv, D, _ptr(q), _ptr(k), _ptr(v), _stream(qkv)), "attn_qk_prep")
-    return q, k, v
-
-
-@_instrument("tree_attention", 1)
 def tree_attention_tile_tokens(D, Hq, Hkv):
     """Query tokens per attention tile the library accepts for this layout."""
     n = _lib.load().janus_b200_tree_attention_tile_tokens(D, Hq, Hkv)
@@ -199,6 +186,7 @@ def tree_attention_tile_tokens(D, Hq, Hkv):
     return n
 
 
+@_instrument("tree_attention", 1)
 def tree_attention(q, keys, values, anc_lo, anc_hi, row_start, row_of_token, tiles, gate, scale, out=None,
                    status=None):
     """q bf16 [T, Hq, D]; keys/values: per level [T_l, Hkv, D] (last = own); anc_lo/anc_hi: per ancestor level

@@ -34,6 +34,7 @@ class Level:
     anc_lo: list               # per ancestor level l < depth: [B] int32 first key (token of level l)
     anc_hi: list               # per ancestor level: [B] int32 end key
     child_start: np.ndarray    # [P+1] int32, P = rows of level depth-1 (depth 0: [0..B], each row its own group)
+    chunk_start: np.ndarray    # [B+1] int32, first 64-token chunk of each row (the chunked delta rule)
     rows: list                 # (pack, segment, first packed position) per row
     keep: bool = False         # a deeper level reads this level's states
     tiles: dict = field(default_factory=dict)  # tokens per tile -> [n, 2] int32
@@ -138,8 +139,10 @@ def build_levels(packs):
             prev.keep = True
             anc_lo = [lo[parent] for lo in prev.anc_lo] + [prev.row_start[:-1][parent].astype(np.int32)]
             anc_hi = [hi[parent] for hi in prev.anc_hi] + [prev.row_start[1:][parent].astype(np.int32)]
+        chunk_start = np.zeros(B + 1, dtype=np.int64)
+        np.cumsum((lengths + 63) // 64, out=chunk_start[1:])
         levels.append(Level(d, ids, pos, row_start.astype(np.int32), rot, parent, anc_lo, anc_hi,
-                            child_start.astype(np.int32), rows))
+                            child_start.astype(np.int32), chunk_start.astype(np.int32), rows))
     return levels, row_index
 
 
@@ -206,6 +209,7 @@ class DevicePlan:
             add((d, "row_of_token"), lv.row_of_token)
             add((d, "parent"), np.maximum(lv.parent, 0))
             add((d, "child_start"), lv.child_start)
+            add((d, "chunk_start"), lv.chunk_start)
             for l, (lo, hi) in enumerate(zip(lv.anc_lo, lv.anc_hi)):
                 add((d, "lo", l), lo)
                 add((d, "hi", l), hi)

@@ -9,7 +9,7 @@ ROOT = Path(__file__).resolve().parent.parent
 
 def declared():
     text = (ROOT / "include" / "janus_b200.h").read_text()
-    return sorted(set(re.findall(r"\bint\s+(janus_b200_\w+)\s*\(", text)))
+    return sorted(set(re.findall(r"\b(?:int|size_t)\s+(janus_b200_\w+)\s*\(", text)))
 
 
 def test_library_exports_every_declared_symbol():

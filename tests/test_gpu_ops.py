@@ -244,15 +244,18 @@ def test_gdn_chunk_scan_matches_recurrent_oracle():
     S0 = torch.randn(2, Hv, D, D, generator=g) * 0.1
     state_row = torch.tensor([1, 0, 1, 1, 0], dtype=torch.int32)
     scale = D ** -0.5
-    o, S = ops.gdn_chunk_scan(q.cuda(), k.cuda(), v.cuda(), gg.cuda(), beta.cuda(), rs.cuda(), S0.cuda(),
-                              state_row.cuda(), True, scale)
+    cs = torch.from_numpy(np.concatenate([[0], np.cumsum([(n + 63) // 64 for n in lengths])]).astype(np.int32))
+    nc = int(cs[-1])
+    o, S = ops.gdn_chunk_scan(q.cuda(), k.cuda(), v.cuda(), gg.cuda(), beta.cuda(), rs.cuda(), cs.cuda(), nc,
+                              S0.cuda(), state_row.cuda(), True, scale)
     for r in range(len(lengths)):
         a, b = int(rs[r]), int(rs[r + 1])
         ro, rS = oracle.delta_recurrent(q[a:b].float(), k[a:b].float(), v[a:b].float(), gg[a:b], beta[a:b],
                                         S0[int(state_row[r])])
         close(o[a:b], ro, atol=3e-2, rtol=3e-2)
         close(S[r], rS, atol=3e-2, rtol=3e-2)
-    o2, _ = ops.gdn_chunk_scan(q.cuda(), k.cuda(), v.cuda(), gg.cuda(), beta.cuda(), rs.cuda(), None, None, False, scale)
+    o2, _ = ops.gdn_chunk_scan(q.cuda(), k.cuda(), v.cuda(), gg.cuda(), beta.cuda(), rs.cuda(), cs.cuda(), nc, None,
+                               None, False, scale)
     a, b = int(rs[4]), int(rs[5])
     ro, _ = oracle.delta_chunked(q[a:b].float(), k[a:b].float(), v[a:b].float(), gg[a:b], beta[a:b], None)
     close(o2[a:b], ro, atol=3e-2, rtol=3e-2)
