@@ -178,6 +178,23 @@ def gdn_chunk_scan(q, k, v, g, beta, row_start, chunk_start, n_chunks, state_in,
     return o, state_out
 
 
+@_instrument("attn_qk_prep", 1)
+def attn_qk_prep(qkv, positions, inv_freq, q_norm_w, k_norm_w, eps, Hq, Hkv, D, k_out=None, v_out=None):
+    _need(qkv, BF16, "qkv", contiguous=False)
+    if qkv.stride(1) != 1:
+        raise ValueError("qkv must have unit column stride")
+    T = qkv.shape[0]
+    dev = qkv.device
+    q = torch.empty(T, Hq, D, dtype=BF16, device=dev)
+    k = torch.empty(T, Hkv, D, dtype=BF16, device=dev) if k_out is None else k_out
+    v = torch.empty(T, Hkv, D, dtype=BF16, device=dev) if v_out is None else v_out
+    _lib.check(_lib.load().janus_b200_attn_qk_prep(
+        _ptr(qkv), qkv.stride(0), T, _ptr(_need(positions, I32, "positions")), _ptr(_need(inv_freq, F32, "inv_freq")),
+        inv_freq.shape[0] * 2, _ptr(_need(q_norm_w, BF16, "q_norm_w")), _ptr(_need(k_norm_w, BF16, "k_norm_w")), eps,
+        Hq, Hkv, D, _ptr(q), _ptr(k), _ptr(v), _stream(qkv)), "attn_qk_prep")
+    return q, k, v
+
+
 def tree_attention_tile_tokens(D, Hq, Hkv):
     """Query tokens per attention tile the library accepts for this layout."""
     n = _lib.load().janus_b200_tree_attention_tile_tokens(D, Hq, Hkv)

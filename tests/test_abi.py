@@ -29,3 +29,10 @@ def test_argument_errors_need_no_gpu():
     st = lib.janus_b200_silu_mul(None, 4, 8, None, None)
     assert st == -1
     assert "silu_mul" in _lib.last_error()
+
+
+def test_every_op_the_readout_calls_is_wrapped():
+    """janus_b200.model only calls ops that janus_b200.ops defines (a CPU check of the host path's wiring)."""
+    from janus_b200 import ops
+    used = set(re.findall(r"\bops\.(\w+)\(", (ROOT / "janus_b200" / "model.py").read_text()))
+    assert used and all(callable(getattr(ops, n, None)) for n in used), used - set(dir(ops))
