@@ -9,8 +9,10 @@
 //      QK = tril(scale Q K^T * e^(G_i - G_j))                        stored bf16, plus G itself
 // 2. gdn_chunk_state: one CTA per (row, value head, 32 of the 128 value columns) — the columns of the state evolve
 //    independently — walking the row's chunks in order with its fp32 slice of S in registers:
-//      V' = U - W S;   O = scale (Q * e^G) S + QK V';   S = e^(G_last) S + (K * e^(G_last - G))^T V'
-//    (S rounded to bf16 for the products, as fla's chunk kernels do). The WY form of transformers'
+//      V' = U - W S;   O = scale e^G (Q S) + QK V';   S = e^(G_last) S + K^T (V' * e^(G_last - G))
+//    (S rounded to bf16 for the products, as fla's chunk kernels do; the e^G factors scale rows of fp32 results
+//    instead of the bf16 operands, so q and k are used as loaded). The next chunk's W is loaded while the output
+//    and the state update of this one run. The WY form of transformers'
 //    torch_chunk_gated_delta_rule (the reference's CPU rule) and of fla's chunk kernels (its GPU rule). A row's last
 //    chunk is ragged: the missing tokens are zeros with g = beta = 0, which leaves the state untouched.
 // Both kernels use mma.sync m16n8k16 (bf16, fp32 accumulate) on XOR-swizzled shared tiles.
@@ -105,7 +107,7 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
     __nv_bfloat16* __restrict__ Ug, __nv_bfloat16* __restrict__ QKg, float* __restrict__ Gg) {
   extern __shared__ __align__(16) unsigned char raw[];
   PrepSmem& sm = *reinterpret_cast<PrepSmem*>(raw);
-  const int c = blockIdx.x, h = blockIdx.y;
+  const int h = blockIdx.x, c = blockIdx.y;  // heads fastest: the Hv/Hk heads sharing q and k run together
   const int hk = h / (Hv / Hk);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = chunk_row(chunk_start, B, c);
@@ -179,14 +181,22 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
       }
   }
   __syncthreads();  // every warp is done reading sm.q as Q
-  for (int x = tid; x < CT * DH / 2; x += 256) {  // q <- K beta e^G, v <- V beta
-    const int r = x / (DH / 2), cc = (x % (DH / 2)) * 2;
+  if (tid < CT) sm.eG[tid] = sm.beta[tid] * sm.eG[tid];  // row factor of K: beta e^G (beta alone for V below)
+  __syncthreads();
+  for (int x = tid; x < CT * DH / 8; x += 256) {  // q <- K beta e^G, v <- V beta, 8 elements per step
+    const int r = x / (DH / 8), cc = (x % (DH / 8)) * 8;
     const int off = sw<DH>(r, cc);
-    const float2 kf = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&sm.k[off]));
-    const float2 vf = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&sm.v[off]));
-    const float b = sm.beta[r], eg = sm.eG[r];
-    *reinterpret_cast<__nv_bfloat162*>(&sm.q[off]) = __floats2bfloat162_rn(kf.x * b * eg, kf.y * b * eg);
-    *reinterpret_cast<__nv_bfloat162*>(&sm.v[off]) = __floats2bfloat162_rn(vf.x * b, vf.y * b);
+    float kf[8], vf[8];
+    load8(&sm.k[off], kf);
+    load8(&sm.v[off], vf);
+    const float fk = sm.eG[r], fv = sm.beta[r];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      kf[u] *= fk;
+      vf[u] *= fv;
+    }
+    store8(&sm.q[off], kf);
+    store8(&sm.v[off], vf);
   }
   // T = (I - N)^-1: diagonal 16x16 blocks (warps 0-3, lane c < 16 owns column c)
   if (warp < 4) {
@@ -207,38 +217,62 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
 #pragma unroll
       for (int r = 0; r < 16; ++r) sm.tf[(base + r) * PADF + base + cc] = col[r];
     }
+  } else {  // zeros above the block diagonal that the full-length sums below read: T[0:16, 16:32], T[32:48, 48:64]
+    for (int x = tid - 128; x < 512; x += 128) {
+      const int blk = x >> 8, r = (x >> 4) & 15, cc = x & 15;
+      sm.tf[(blk * 32 + r) * PADF + blk * 32 + 16 + cc] = 0.f;
+    }
   }
   __syncthreads();
-  // stage 1: T[2h+1, 2h] = T[2h+1, 2h+1] N[2h+1, 2h] T[2h, 2h] (16x16 blocks), h = 0, 1
-  for (int x = tid; x < 512; x += 256) {
-    const int hb = x >> 8, i = (x >> 4) & 15, j = x & 15;
+  // stage 1: T[2h+1, 2h] = T[2h+1, 2h+1] N[2h+1, 2h] T[2h, 2h] (16x16 blocks), h = 0, 1. Thread: column j, two rows.
+  // The triangular zeros of N and T make the full-length sums exact, so every loop has a fixed trip count.
+  {
+    const int hb = tid >> 7, j = tid & 15, i0 = (tid >> 4) & 7;  // rows i0 and i0 + 8
     const int bi = (2 * hb + 1) * 16, bj = 2 * hb * 16;
-    float acc = 0.f;
-    for (int m = j; m < 16; ++m) acc += sm.n[(bi + i) * PADF + bj + m] * sm.tf[(bj + m) * PADF + bj + j];
-    sm.m[(hb * 16 + i) * 33 + j] = acc;
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      const float t = sm.tf[(bj + m) * PADF + bj + j];
+      a0 += sm.n[(bi + i0) * PADF + bj + m] * t;
+      a1 += sm.n[(bi + i0 + 8) * PADF + bj + m] * t;
+    }
+    sm.m[(hb * 16 + i0) * 33 + j] = a0;
+    sm.m[(hb * 16 + i0 + 8) * 33 + j] = a1;
+    __syncthreads();
+    a0 = a1 = 0.f;
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      const float mm = sm.m[(hb * 16 + m) * 33 + j];
+      a0 += sm.tf[(bi + i0) * PADF + bi + m] * mm;
+      a1 += sm.tf[(bi + i0 + 8) * PADF + bi + m] * mm;
+    }
+    sm.tf[(bi + i0) * PADF + bj + j] = a0;
+    sm.tf[(bi + i0 + 8) * PADF + bj + j] = a1;
   }
   __syncthreads();
-  for (int x = tid; x < 512; x += 256) {
-    const int hb = x >> 8, i = (x >> 4) & 15, j = x & 15;
-    const int bi = (2 * hb + 1) * 16, bj = 2 * hb * 16;
-    float acc = 0.f;
-    for (int m = 0; m <= i; ++m) acc += sm.tf[(bi + i) * PADF + bi + m] * sm.m[(hb * 16 + m) * 33 + j];
-    sm.tf[(bi + i) * PADF + bj + j] = acc;
-  }
-  __syncthreads();
-  // stage 2: T[32:, :32] = T[32:, 32:] N[32:, :32] T[:32, :32]
-  for (int x = tid; x < 1024; x += 256) {
-    const int i = x >> 5, j = x & 31;
-    float acc = 0.f;
-    for (int m = j; m < 32; ++m) acc += sm.n[(32 + i) * PADF + m] * sm.tf[m * PADF + j];
-    sm.m[i * 33 + j] = acc;
-  }
-  __syncthreads();
-  for (int x = tid; x < 1024; x += 256) {
-    const int i = x >> 5, j = x & 31;
-    float acc = 0.f;
-    for (int m = 0; m <= i; ++m) acc += sm.tf[(32 + i) * PADF + 32 + m] * sm.m[m * 33 + j];
-    sm.tf[(32 + i) * PADF + j] = acc;
+  // stage 2: T[32:, :32] = T[32:, 32:] N[32:, :32] T[:32, :32]. Thread: column j, rows i0, i0+8, i0+16, i0+24.
+  {
+    const int j = tid & 31, i0 = tid >> 5;
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int m = 0; m < 32; ++m) {
+      const float t = sm.tf[m * PADF + j];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] += sm.n[(32 + i0 + 8 * u) * PADF + m] * t;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) sm.m[(i0 + 8 * u) * 33 + j] = a[u];
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < 4; ++u) a[u] = 0.f;
+#pragma unroll
+    for (int m = 0; m < 32; ++m) {
+      const float mm = sm.m[m * 33 + j];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] += sm.tf[(32 + i0 + 8 * u) * PADF + 32 + m] * mm;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) sm.tf[(32 + i0 + 8 * u) * PADF + j] = a[u];
   }
   __syncthreads();
   for (int x = tid; x < CT * CT; x += 256) {
@@ -279,12 +313,13 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
 // ------------------------------------------------------------------------------------------------ state pass
 
 struct StateSmem {
-  __nv_bfloat16 w[CT * DH];   // W
-  __nv_bfloat16 q[CT * DH];   // Q, then Q e^G scale
-  __nv_bfloat16 k[CT * DH];   // K, then K e^(G_last - G)
-  __nv_bfloat16 qk[CT * CT];  // masked decayed scale Q K^T
-  __nv_bfloat16 s[DH * DB];   // S slice (bf16) [dk][dv]
-  __nv_bfloat16 vn[CT * DB];  // V' slice [tok][dv]
+  __nv_bfloat16 w[CT * DH];    // W
+  __nv_bfloat16 q[CT * DH];    // Q
+  __nv_bfloat16 k[CT * DH];    // K
+  __nv_bfloat16 qk[CT * CT];   // masked decayed scale Q K^T
+  __nv_bfloat16 s[DH * DB];    // S slice (bf16) [dk][dv]
+  __nv_bfloat16 vn[CT * DB];   // V' slice [tok][dv]
+  __nv_bfloat16 vnd[CT * DB];  // V' e^(G_last - G)
   float G[CT];
 };
 
@@ -296,7 +331,8 @@ __global__ void __launch_bounds__(128, 3) gdn_chunk_state_kernel(
     __nv_bfloat16* __restrict__ o) {
   extern __shared__ __align__(16) unsigned char raw[];
   StateSmem& sm = *reinterpret_cast<StateSmem*>(raw);
-  const int row = blockIdx.x, h = blockIdx.y, c0 = blockIdx.z * DB;
+  // slices fastest: the DH / DB CTAs of one (row, head) read the same W, q, k, QK tiles and run together (L2 hits)
+  const int c0 = blockIdx.x * DB, h = blockIdx.y, row = blockIdx.z;
   const int hk = h / (Hv / Hk);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // S slice: warp w owns key rows 32w..32w+31 (2 m-tiles) x DB columns (4 n-tiles)
@@ -315,14 +351,25 @@ __global__ void __launch_bounds__(128, 3) gdn_chunk_state_kernel(
         }
   }
   const int64_t r0 = row_start[row], r1 = row_start[row + 1];
-  for (int c = chunk_start[row]; c < chunk_start[row + 1]; ++c) {
-    const int64_t t0 = r0 + (int64_t)(c - chunk_start[row]) * CT;
-    const int nt = (r1 - t0) < CT ? (int)(r1 - t0) : CT;
+  const int cbeg = chunk_start[row], cend = chunk_start[row + 1];
+  auto chunk_t0 = [&](int c) { return r0 + (int64_t)(c - cbeg) * CT; };
+  auto chunk_nt = [&](int c) { const int64_t t0 = chunk_t0(c); return (r1 - t0) < CT ? (int)(r1 - t0) : CT; };
+  auto load_w = [&](int c) {
+    const int64_t t0 = chunk_t0(c);
+    const int nt = chunk_nt(c);
+    for (int x = tid; x < CT * (DH / 8); x += 128) {
+      const int r = x / (DH / 8), ch = (x % (DH / 8)) * 8;
+      const bool ok = r < nt;
+      cpa16(&sm.w[sw<DH>(r, ch)], Wg + ((ok ? t0 + r : t0) * Hv + h) * DH + ch, ok);
+    }
+  };
+  auto load_qk = [&](int c) {
+    const int64_t t0 = chunk_t0(c);
+    const int nt = chunk_nt(c);
     for (int x = tid; x < CT * (DH / 8); x += 128) {
       const int r = x / (DH / 8), ch = (x % (DH / 8)) * 8;
       const bool ok = r < nt;
       const int64_t t = ok ? t0 + r : t0;
-      cpa16(&sm.w[sw<DH>(r, ch)], Wg + (t * Hv + h) * DH + ch, ok);
       cpa16(&sm.q[sw<DH>(r, ch)], q + (t * Hk + hk) * DH + ch, ok);
       cpa16(&sm.k[sw<DH>(r, ch)], k + (t * Hk + hk) * DH + ch, ok);
     }
@@ -331,6 +378,15 @@ __global__ void __launch_bounds__(128, 3) gdn_chunk_state_kernel(
       const int r = x / (CT / 8), ch = (x % (CT / 8)) * 8;
       cpa16(&sm.qk[sw<CT>(r, ch)], qkc + r * CT + ch, true);
     }
+  };
+  if (cbeg < cend) {
+    load_w(cbeg);
+    load_qk(cbeg);
+    asm volatile("cp.async.commit_group;\n" ::);
+  }
+  for (int c = cbeg; c < cend; ++c) {
+    const int64_t t0 = chunk_t0(c);
+    const int nt = chunk_nt(c);
     if (tid < CT) sm.G[tid] = tid < nt ? Gg[(t0 + tid) * Hv + h] : 0.f;
     // bf16 copy of the state slice (rows of this warp)
 #pragma unroll
@@ -343,20 +399,14 @@ __global__ void __launch_bounds__(128, 3) gdn_chunk_state_kernel(
           *reinterpret_cast<__nv_bfloat162*>(&sm.s[sw<DB>(rr, cc)]) =
               __floats2bfloat162_rn(S[mt][n][e], S[mt][n][e + 1]);
         }
-    cp_commit_wait();
+    asm volatile("cp.async.wait_group 0;\n" ::);
     __syncthreads();
     const float Gl = sm.G[nt - 1];  // padded tokens carry g = 0: the cumulative sum stays at its last value
-    for (int x = tid; x < CT * DH / 2; x += 128) {  // q <- Q e^G scale, k <- K e^(Gl - G)
-      const int r = x / (DH / 2), cc = (x % (DH / 2)) * 2;
-      const int off = sw<DH>(r, cc);
-      const float Gr = r < nt ? sm.G[r] : Gl;
-      const float eq = expf(Gr) * scale, ek = expf(Gl - Gr);
-      const float2 qf = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&sm.q[off]));
-      const float2 kf = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&sm.k[off]));
-      *reinterpret_cast<__nv_bfloat162*>(&sm.q[off]) = __floats2bfloat162_rn(qf.x * eq, qf.y * eq);
-      *reinterpret_cast<__nv_bfloat162*>(&sm.k[off]) = __floats2bfloat162_rn(kf.x * ek, kf.y * ek);
-    }
-    // V' = U - W S  (warp w: m-tile w, 4 n-tiles)
+    // this thread's two fragment rows: e^G scale for O, e^(Gl - G) for the state update
+    const int ra = warp * 16 + (lane >> 2), rb = ra + 8;
+    const float Ga = ra < nt ? sm.G[ra] : Gl, Gb = rb < nt ? sm.G[rb] : Gl;
+    const float fqa = expf(Ga) * scale, fqb = expf(Gb) * scale, fka = expf(Gl - Ga), fkb = expf(Gl - Gb);
+    // V' = U - W S (warp w: m-tile w, 4 n-tiles); V' and V' e^(Gl - G) to shared memory
     {
       float P[4][4] = {};
 #pragma unroll
@@ -374,16 +424,22 @@ __global__ void __launch_bounds__(128, 3) gdn_chunk_state_kernel(
       for (int n = 0; n < 4; ++n)
 #pragma unroll
         for (int e = 0; e < 4; e += 2) {
-          const int i = warp * 16 + (lane >> 2) + (e >> 1) * 8, j = n * 8 + (lane & 3) * 2;
+          const int i = e ? rb : ra, j = n * 8 + (lane & 3) * 2;
           float2 u = make_float2(0.f, 0.f);
           if (i < nt)
             u = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(Ug + ((t0 + i) * Hv + h) * DH + c0 + j));
-          *reinterpret_cast<__nv_bfloat162*>(&sm.vn[sw<DB>(i, j)]) =
-              __floats2bfloat162_rn(u.x - P[n][e], u.y - P[n][e + 1]);
+          const float v0 = u.x - P[n][e], v1 = u.y - P[n][e + 1];
+          const float fk = e ? fkb : fka;
+          *reinterpret_cast<__nv_bfloat162*>(&sm.vn[sw<DB>(i, j)]) = __floats2bfloat162_rn(v0, v1);
+          *reinterpret_cast<__nv_bfloat162*>(&sm.vnd[sw<DB>(i, j)]) = __floats2bfloat162_rn(v0 * fk, v1 * fk);
         }
     }
-    __syncthreads();  // V' and the scaled q / k are visible
-    // O = (Q e^G scale) S + QK V'
+    __syncthreads();  // V' visible; sm.w is free
+    if (c + 1 < cend) {
+      load_w(c + 1);
+      asm volatile("cp.async.commit_group;\n" ::);
+    }
+    // O = ((Q S) * e^G scale) + QK V'
     {
       float O[4][4] = {};
 #pragma unroll
@@ -396,6 +452,13 @@ __global__ void __launch_bounds__(128, 3) gdn_chunk_state_kernel(
           mma(O[2 * np], a, b[0], b[1]);
           mma(O[2 * np + 1], a, b[2], b[3]);
         }
+      }
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        O[n][0] *= fqa;
+        O[n][1] *= fqa;
+        O[n][2] *= fqb;
+        O[n][3] *= fqb;
       }
 #pragma unroll
       for (int ks = 0; ks < CT; ks += 16) {
@@ -412,13 +475,13 @@ __global__ void __launch_bounds__(128, 3) gdn_chunk_state_kernel(
       for (int n = 0; n < 4; ++n)
 #pragma unroll
         for (int e = 0; e < 4; e += 2) {
-          const int i = warp * 16 + (lane >> 2) + (e >> 1) * 8, j = n * 8 + (lane & 3) * 2;
+          const int i = e ? rb : ra, j = n * 8 + (lane & 3) * 2;
           if (i < nt)
             *reinterpret_cast<__nv_bfloat162*>(o + ((t0 + i) * Hv + h) * DH + c0 + j) =
                 __floats2bfloat162_rn(O[n][e], O[n][e + 1]);
         }
     }
-    // S = e^(G_last) S + (K e^(Gl - G))^T V'
+    // S = e^(G_last) S + K^T (V' e^(Gl - G))
     {
       const float dl = expf(Gl);
 #pragma unroll
@@ -431,7 +494,7 @@ __global__ void __launch_bounds__(128, 3) gdn_chunk_state_kernel(
       for (int ks = 0; ks < CT; ks += 16) {
         uint32_t b[2][4];
 #pragma unroll
-        for (int np = 0; np < 2; ++np) ldb_kn<DB>(b[np], sm.vn, np * 16, ks, lane);
+        for (int np = 0; np < 2; ++np) ldb_kn<DB>(b[np], sm.vnd, np * 16, ks, lane);
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt) {
           uint32_t a[4];
@@ -444,7 +507,11 @@ __global__ void __launch_bounds__(128, 3) gdn_chunk_state_kernel(
         }
       }
     }
-    __syncthreads();  // this chunk's tiles are free for the next one
+    __syncthreads();  // q, k, QK, S and V' tiles are free for the next chunk
+    if (c + 1 < cend) {
+      load_qk(c + 1);
+      asm volatile("cp.async.commit_group;\n" ::);
+    }
   }
   if (state_out) {
     float* so = state_out + ((int64_t)row * Hv + h) * DH * DH;
@@ -483,8 +550,8 @@ extern "C" int janus_b200_gdn_chunk_scan(const void* q, const void* k, const voi
              "gdn_chunk_scan: null pointer");
   JB_REQUIRE(Dk == DH && Dv == DH, JANUS_ERR_UNSUPPORTED, "gdn_chunk_scan: Dk = Dv = 128 only (got %lld, %lld)",
              (long long)Dk, (long long)Dv);
-  JB_REQUIRE(T >= 0 && B >= 0 && n_chunks >= 0 && Hk > 0 && Hv > 0 && Hv % Hk == 0 && Hv <= 65535 &&
-                 n_chunks <= 0x7fffffff,
+  JB_REQUIRE(T >= 0 && B >= 0 && B <= 65535 && n_chunks >= 0 && n_chunks <= 65535 && Hk > 0 && Hv > 0 &&
+                 Hv % Hk == 0 && Hv <= 65535,
              JANUS_ERR_INVALID, "gdn_chunk_scan: sizes");
   JB_REQUIRE(JB_ALIGNED(q, 16) && JB_ALIGNED(k, 16) && JB_ALIGNED(v, 16) && JB_ALIGNED(o, 4), JANUS_ERR_ALIGNMENT,
              "gdn_chunk_scan: alignment");
@@ -510,13 +577,13 @@ extern "C" int janus_b200_gdn_chunk_scan(const void* q, const void* k, const voi
     return JANUS_ERR_CUDA;
   }
   if (n_chunks > 0) {
-    gdn_chunk_prep_kernel<<<dim3((unsigned)n_chunks, (unsigned)Hv), 256, sizeof(PrepSmem), s>>>(
+    gdn_chunk_prep_kernel<<<dim3((unsigned)Hv, (unsigned)n_chunks), 256, sizeof(PrepSmem), s>>>(
         (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, g, beta, row_start, chunk_start,
         (int)B, (int)Hk, (int)Hv, scale, Wg, Ug, QKg, Gg);
     int st = launch_status("gdn_chunk_scan/prep");
     if (st) return st;
   }
-  gdn_chunk_state_kernel<<<dim3((unsigned)B, (unsigned)Hv, DH / DB), 128, sizeof(StateSmem), s>>>(
+  gdn_chunk_state_kernel<<<dim3(DH / DB, (unsigned)Hv, (unsigned)B), 128, sizeof(StateSmem), s>>>(
       (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, row_start, chunk_start, state_in, state_row, state_out,
       (int)Hk, (int)Hv, scale, Wg, Ug, QKg, Gg, (__nv_bfloat16*)o);
   return launch_status("gdn_chunk_scan/state");
