@@ -116,8 +116,9 @@ int janus_b200_attn_qk_prep(const void* qkv, int64_t qkv_stride, int64_t T, cons
 /* Tree attention of one level with the output gate: every query token attends, in one online softmax, to the
  * tokens of its row's ancestor at each earlier level (key range [anc_lo[l][row], anc_hi[l][row]) of level l's
  * keys) and to its own row's tokens causally; out = softmax(q k^T * scale) v * sigmoid(gate). GQA folded: the
- * Hq/Hkv query heads of a kv head share every K/V tile. n_levels = ancestors + 1; k_levels[n_levels-1] is the
- * level's own keys ([T, Hkv, D]). tiles: [n_tiles, 2] query token ranges [start, end) of at most
+ * Hq/Hkv query heads of a kv head share every K/V tile. n_levels = ancestors + 1; k_levels[l], v_levels[l] are
+ * contiguous [level_tokens[l], Hkv, D] (host array of n_levels counts); k_levels[n_levels-1] is the level's own keys
+ * (level_tokens[n_levels-1] == T). tiles: [n_tiles, 2] query token ranges [start, end) of at most
  * janus_b200_tree_attention_tile_tokens(D, Hq, Hkv) tokens, each within one request (janus_b200 python builds them).
  * gate: bf16, token t head h at gate[t*gate_stride + h*gate_head_stride + d]. out bf16 [T, Hq*D]. D in
  * {32, 64, 128, 256}; 128 and 256 run on tcgen05 with TMEM accumulators, 32 and 64 on mma.sync. status: optional
@@ -125,7 +126,7 @@ int janus_b200_attn_qk_prep(const void* qkv, int64_t qkv_stride, int64_t T, cons
  * Replaces branch_attention / state_attention / _piece / _merge_gate (janus/hybrid.py:806-855, 943-989) and the
  * tree rule of janus/attention.py:10-23. */
 int janus_b200_tree_attention(const void* q, int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int32_t n_levels,
-                              const void* const* k_levels, const void* const* v_levels,
+                              const void* const* k_levels, const void* const* v_levels, const int64_t* level_tokens,
                               const int32_t* const* anc_lo, const int32_t* const* anc_hi, const int32_t* row_start,
                               const int32_t* row_of_token, const int32_t* tiles, int64_t n_tiles, const void* gate,
                               int64_t gate_stride, int64_t gate_head_stride, float scale, void* out, int32_t* status,

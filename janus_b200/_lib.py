@@ -30,7 +30,7 @@ SIGNATURES = {
     "janus_b200_attn_qk_prep": [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float,
                                 c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p],
     "janus_b200_tree_attention": [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p,
-                                  c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_float,
+                                  c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_float,
                                   c_void_p, c_void_p, c_void_p],
     "janus_b200_tree_attention_tile_tokens": [c_int64, c_int64, c_int64],
     "janus_b200_head_scalar": [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_float, c_void_p, c_void_p, c_float,

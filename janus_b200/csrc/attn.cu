@@ -388,7 +388,8 @@ static int launch_tree(const TreeAttnParams& p, int64_t n_tiles, cudaStream_t s)
 }
 
 int tree_attention_tc(const void* q, int64_t Hq, int64_t Hkv, int64_t D, int32_t n_levels, const void* const* k_levels,
-                      const void* const* v_levels, const int32_t* const* anc_lo, const int32_t* const* anc_hi,
+                      const void* const* v_levels, const int64_t* level_tokens, const int32_t* const* anc_lo,
+                      const int32_t* const* anc_hi,
                       const int32_t* row_start, const int32_t* row_of_token, const int32_t* tiles, int64_t n_tiles,
                       const void* gate, int64_t gate_stride, int64_t gate_head_stride, float scale, void* out,
                       int32_t* err, cudaStream_t stream);
@@ -426,13 +427,13 @@ extern "C" int janus_b200_attn_qk_prep(const void* qkv, int64_t qkv_stride, int6
 
 extern "C" int janus_b200_tree_attention(const void* q, int64_t T, int64_t Hq, int64_t Hkv, int64_t D,
                                          int32_t n_levels, const void* const* k_levels, const void* const* v_levels,
-                                         const int32_t* const* anc_lo, const int32_t* const* anc_hi,
-                                         const int32_t* row_start, const int32_t* row_of_token, const int32_t* tiles,
+                                         const int64_t* level_tokens, const int32_t* const* anc_lo,
+                                         const int32_t* const* anc_hi, const int32_t* row_start, const int32_t* row_of_token, const int32_t* tiles,
                                          int64_t n_tiles, const void* gate, int64_t gate_stride,
                                          int64_t gate_head_stride, float scale, void* out, int32_t* status,
                                          void* stream) {
-  JB_REQUIRE(q && k_levels && v_levels && row_start && row_of_token && tiles && gate && out, JANUS_ERR_INVALID,
-             "tree_attention: null pointer");
+  JB_REQUIRE(q && k_levels && v_levels && level_tokens && row_start && row_of_token && tiles && gate && out,
+             JANUS_ERR_INVALID, "tree_attention: null pointer");
   JB_REQUIRE(n_levels >= 1 && n_levels <= kMaxLevels, JANUS_ERR_UNSUPPORTED, "tree_attention: %d levels (1..%d)",
              n_levels, kMaxLevels);
   JB_REQUIRE(Hq > 0 && Hkv > 0 && Hq % Hkv == 0, JANUS_ERR_INVALID, "tree_attention: heads %lld/%lld",
@@ -441,13 +442,18 @@ extern "C" int janus_b200_tree_attention(const void* q, int64_t T, int64_t Hq, i
   JB_REQUIRE(G <= kBM && kBM % G == 0, JANUS_ERR_UNSUPPORTED, "tree_attention: GQA group %lld must divide %d",
              (long long)G, kBM);
   JB_REQUIRE(n_tiles >= 0 && n_tiles <= 0x7fffffff && Hkv <= 65535, JANUS_ERR_INVALID, "tree_attention: grid");
+  JB_REQUIRE(level_tokens[n_levels - 1] == T, JANUS_ERR_INVALID, "tree_attention: own level has %lld tokens, T=%lld",
+             (long long)level_tokens[n_levels - 1], (long long)T);
   JB_REQUIRE(JB_ALIGNED(q, 16) && JB_ALIGNED(out, 4) && JB_ALIGNED(gate, 4) && gate_stride % 2 == 0 &&
                  gate_head_stride % 2 == 0,
              JANUS_ERR_ALIGNMENT, "tree_attention: alignment");
   TreeAttnParams p{};
   p.q = (const __nv_bfloat16*)q;
   for (int l = 0; l < n_levels; ++l) {
-    JB_REQUIRE(k_levels[l] && v_levels[l] && JB_ALIGNED(k_levels[l], 16) && JB_ALIGNED(v_levels[l], 16),
+    JB_REQUIRE(level_tokens[l] >= 0 && level_tokens[l] <= 0x7fffffff, JANUS_ERR_INVALID,
+               "tree_attention: level %d token count", l);
+    JB_REQUIRE(level_tokens[l] == 0 || (k_levels[l] && v_levels[l] && JB_ALIGNED(k_levels[l], 16) &&
+                                        JB_ALIGNED(v_levels[l], 16)),
                JANUS_ERR_ALIGNMENT, "tree_attention: level %d keys/values null or unaligned", l);
     p.k[l] = (const __nv_bfloat16*)k_levels[l];
     p.v[l] = (const __nv_bfloat16*)v_levels[l];
@@ -472,8 +478,8 @@ extern "C" int janus_b200_tree_attention(const void* q, int64_t T, int64_t Hq, i
   if (n_tiles == 0 || T == 0) return JANUS_OK;
   cudaStream_t s = (cudaStream_t)stream;
   if ((D == 128 || D == 256) && 128 % G == 0)
-    return tree_attention_tc(q, Hq, Hkv, D, n_levels, k_levels, v_levels, anc_lo, anc_hi, row_start, row_of_token,
-                             tiles, n_tiles, gate, gate_stride, gate_head_stride, scale, out, status, s);
+    return tree_attention_tc(q, Hq, Hkv, D, n_levels, k_levels, v_levels, level_tokens, anc_lo, anc_hi, row_start,
+                             row_of_token, tiles, n_tiles, gate, gate_stride, gate_head_stride, scale, out, status, s);
   switch (D) {
     case 32: return launch_tree<32>(p, n_tiles, s);
     case 64: return launch_tree<64>(p, n_tiles, s);

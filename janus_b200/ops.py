@@ -223,10 +223,17 @@ def tree_attention(q, keys, values, anc_lo, anc_hi, row_start, row_of_token, til
         raise ValueError("gate must have unit last stride")
     out = torch.empty(T, Hq * D, dtype=BF16, device=q.device) if out is None else out
     arr = lambda ts: (ctypes.c_void_p * max(1, len(ts)))(*[t.data_ptr() for t in ts])
+    for t in (*keys, *values):
+        if t.dim() != 3 or t.shape[1:] != (Hkv, D) or not t.is_contiguous():
+            raise ValueError("tree_attention: keys/values must be contiguous [T_l, Hkv, D]")
+    if any(k.shape[0] != v.shape[0] for k, v in zip(keys, values)) or keys[-1].shape[0] != T:
+        raise ValueError("tree_attention: per-level key and value counts differ, or the own level is not T tokens")
     karr, varr, larr, harr = arr(keys), arr(values), arr(anc_lo), arr(anc_hi)
+    counts = (ctypes.c_int64 * n)(*[k.shape[0] for k in keys])
     _lib.check(_lib.load().janus_b200_tree_attention(
         _ptr(q), T, Hq, Hkv, D, n, ctypes.cast(karr, ctypes.c_void_p), ctypes.cast(varr, ctypes.c_void_p),
-        ctypes.cast(larr, ctypes.c_void_p), ctypes.cast(harr, ctypes.c_void_p), _ptr(_need(row_start, I32, "row_start")),
+        ctypes.cast(counts, ctypes.c_void_p), ctypes.cast(larr, ctypes.c_void_p), ctypes.cast(harr, ctypes.c_void_p),
+        _ptr(_need(row_start, I32, "row_start")),
         _ptr(_need(row_of_token, I32, "row_of_token")), _ptr(_need(tiles, I32, "tiles")), tiles.shape[0], _ptr(gate),
         gate.stride(0), gate.stride(1), scale, _ptr(out), _ptr(status), _stream(q)), "tree_attention")
     return out
