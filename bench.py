@@ -262,6 +262,14 @@ def main():
     per_attn = [s.elapsed_time(e) for s, e in attn_launch]
     ops.TIMED.clear()
 
+    # where one (extra, untimed) step's device time goes, per library op; the rest is cuBLAS GEMMs and torch glue
+    ops.TIMED.clear()
+    ops.TIMED.update({name: [] for name in ops.OPS})
+    model.run(prepared)
+    torch.cuda.synchronize()
+    op_ms = {name: round(sum(s.elapsed_time(e) for s, e in rec), 2) for name, rec in ops.TIMED.items() if rec}
+    ops.TIMED.clear()
+
     # the roofline of the dominant kernel of the library
     pk, pk_kind = peaks()
     dominant = max(kernel_ms, key=kernel_ms.get) if kernel_ms else None
@@ -328,7 +336,7 @@ def main():
                 "latency_ms": {"p50": p(0.5), "p90": p(0.9), "per": "batch step (every request of the batch completes at its end)"},
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "ms_per_step": e2e_step},
-                "gpu_launches": launches, "kernel_ms_per_step": kernel_ms, "roofline": roof, "cpu_baseline": cpu,
+                "gpu_launches": launches, "kernel_ms_per_step": kernel_ms, "op_ms_one_step": op_ms, "roofline": roof, "cpu_baseline": cpu,
                 "clocks": clock}
         print(json.dumps(line), flush=True)
     if pg is not None:

@@ -55,7 +55,8 @@ int janus_b200_add_rmsnorm(float* x, const void* delta, int64_t delta_stride, in
 int janus_b200_silu_mul(const void* gu, int64_t T, int64_t inter, void* out, void* stream);
 
 /* Gated RMSNorm over each value head: out = rmsnorm(core) * w * silu(z) (core bf16 [T, Hv, Dv]; z bf16 rows of
- * stride z_stride, head h at column h*Dv; out bf16 [T, Hv*Dv]).
+ * stride z_stride, head h at column h*Dv; out bf16 [T, Hv*Dv]; Dv in {32, 64, 128}; core, z, w, out 16-byte aligned
+ * and z_stride a multiple of 8).
  * Replaces `_gate_norm` / Qwen3_5RMSNormGated (janus/hybrid.py:241-247). */
 int janus_b200_gated_rmsnorm(const void* core, const void* z, int64_t z_stride, int64_t T, int64_t Hv, int64_t Dv,
                              const void* w, float eps, void* out, void* stream);

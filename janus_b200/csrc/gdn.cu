@@ -15,13 +15,14 @@ namespace jb {
 
 constexpr int kProThreads = 256;
 constexpr int kMaxTaps = 8;
-constexpr int kProTokens = 32;  // tokens per CTA: each thread slides its conv window over them
+constexpr int kProTokens = 96;  // tokens per CTA: each thread slides its conv window over them
+constexpr int kProBatch = 6;    // token loads a thread has in flight at once
 
 // grid (token tiles of kProTokens, channel blocks of 8 * kProThreads). Thread = 8 consecutive channels; it keeps the
 // last K-1 conv inputs of its channels in registers while it walks the tile's tokens, so every projection element is
 // read once (plus K-1 halo rows at a tile or row start, from the previous tokens or the parent's conv tail).
 template <int K>
-__global__ void __launch_bounds__(kProThreads) gdn_prologue_kernel(
+__global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
     const __nv_bfloat16* __restrict__ proj, int64_t proj_stride, int64_t T, const int32_t* __restrict__ row_start,
     const int32_t* __restrict__ row_of_token, const int32_t* __restrict__ parent,
     const __nv_bfloat16* __restrict__ tail_in, __nv_bfloat16* __restrict__ tail_out,
@@ -36,81 +37,110 @@ __global__ void __launch_bounds__(kProThreads) gdn_prologue_kernel(
   const bool live = vec * 8 < C;
   const int c0 = live ? vec * 8 : 0;
   const int lanes_per_head = Dk >> 3;
-  float w[8][K];
+  __nv_bfloat162 wp[4][K];  // conv taps of channel pairs (2u, 2u+1), kept packed to save registers
 #pragma unroll
-  for (int u = 0; u < 8; ++u)
+  for (int u = 0; u < 4; ++u)
 #pragma unroll
-    for (int j = 0; j < K; ++j) w[u][j] = live ? bf2f(conv_w[(int64_t)(c0 + u) * K + j]) : 0.f;
+    for (int j = 0; j < K; ++j) {
+      const __nv_bfloat16 zero = __float2bfloat16(0.f);
+      wp[u][j] = live ? __halves2bfloat162(conv_w[(int64_t)(c0 + 2 * u) * K + j], conv_w[(int64_t)(c0 + 2 * u + 1) * K + j])
+                      : __halves2bfloat162(zero, zero);
+    }
   float hist[K - 1][8];  // hist[j]: conv input at relative position j - (K-1) before the current token
   int cur_row = -1;
   int64_t r0 = 0, L = 0;
   const __nv_bfloat16* tail = nullptr;
-  for (int64_t t = t0; t < t1; ++t) {
-    const int row = row_of_token[t];
-    if (row != cur_row) {  // (re)fill the window from the row's earlier tokens or the parent's conv tail
-      cur_row = row;
-      r0 = row_start[row];
-      L = row_start[row + 1] - r0;
-      tail = (tail_in && parent) ? tail_in + (int64_t)parent[row] * (K - 1) * C : nullptr;
-      const int64_t i = t - r0;
+  for (int64_t tb = t0; tb < t1; tb += kProBatch) {
+    // the batch's loads go out together (memory-level parallelism), then the tokens are processed in order
+    bf16x8 xr[kProBatch];
+    int rows[kProBatch];
 #pragma unroll
-      for (int j = 0; j < K - 1; ++j) {
-        const int64_t e = i + j;  // ext index of relative position j - (K-1)
-        if (!live) {
+    for (int b = 0; b < kProBatch; ++b) {
+      const int64_t t = tb + b < t1 ? tb + b : t1 - 1;
+      rows[b] = row_of_token[t];
+      if (live) xr[b] = *reinterpret_cast<const bf16x8*>(proj + t * proj_stride + c0);
+    }
 #pragma unroll
-          for (int u = 0; u < 8; ++u) hist[j][u] = 0.f;
-        } else if (e >= K - 1) {
-          load8(proj + (r0 + e - (K - 1)) * proj_stride + c0, hist[j]);
-        } else if (tail) {
-          load8(tail + e * C + c0, hist[j]);
-        } else {
+    for (int b = 0; b < kProBatch; ++b) {
+      const int64_t t = tb + b;
+      if (t >= t1) break;
+      const int row = rows[b];
+      if (row != cur_row) {  // (re)fill the window from the row's earlier tokens or the parent's conv tail
+        cur_row = row;
+        r0 = row_start[row];
+        L = row_start[row + 1] - r0;
+        tail = (tail_in && parent) ? tail_in + (int64_t)parent[row] * (K - 1) * C : nullptr;
+        const int64_t i = t - r0;
 #pragma unroll
-          for (int u = 0; u < 8; ++u) hist[j][u] = 0.f;
+        for (int j = 0; j < K - 1; ++j) {
+          const int64_t e = i + j;  // ext index of relative position j - (K-1)
+          if (!live) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) hist[j][u] = 0.f;
+          } else if (e >= K - 1) {
+            load8(proj + (r0 + e - (K - 1)) * proj_stride + c0, hist[j]);
+          } else if (tail) {
+            load8(tail + e * C + c0, hist[j]);
+          } else {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) hist[j][u] = 0.f;
+          }
         }
       }
-    }
-    float x[8], acc[8];
-    if (live) {
-      load8(proj + t * proj_stride + c0, x);
-    } else {
+      float x[8], acc[8];
+      if (live) {
 #pragma unroll
-      for (int u = 0; u < 8; ++u) x[u] = 0.f;
-    }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      float a = x[u] * w[u][K - 1];
-#pragma unroll
-      for (int j = 0; j < K - 1; ++j) a += hist[j][u] * w[u][j];
-      acc[u] = bf2f(f2bf(silu(a)));  // rounded once, as the reference does
-    }
-    // slide the window
-#pragma unroll
-    for (int j = 0; j < K - 2; ++j)
-#pragma unroll
-      for (int u = 0; u < 8; ++u) hist[j][u] = hist[j + 1][u];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) hist[K - 2][u] = x[u];
-    // l2 norm over each q / k head: lanes_per_head consecutive lanes hold one head
-    float ss = 0.f;
-#pragma unroll
-    for (int u = 0; u < 8; ++u) ss += acc[u] * acc[u];
-    for (int o = lanes_per_head >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (live) {
-      if (c0 < 2 * key_dim) {
-        const float r = rsqrtf(ss + 1e-6f);
-        float o8[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) o8[u] = acc[u] * r;
-        if (c0 < key_dim)
-          store8(q + t * key_dim + c0, o8);
-        else
-          store8(k + t * key_dim + (c0 - key_dim), o8);
+        for (int u = 0; u < 4; ++u) {
+          const float2 f = __bfloat1622float2(xr[b].h[u]);
+          x[2 * u] = f.x;
+          x[2 * u + 1] = f.y;
+        }
       } else {
-        store8(v + t * (int64_t)(Hv * Dv) + (c0 - 2 * key_dim), acc);
-      }
-      if (tail_out && t == r0 + L - 1) {  // the row's last K-1 conv inputs are the window now
 #pragma unroll
-        for (int j = 0; j < K - 1; ++j) store8(tail_out + ((int64_t)row * (K - 1) + j) * C + c0, hist[j]);
+        for (int u = 0; u < 8; ++u) x[u] = 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float2 wl = __bfloat1622float2(wp[u][K - 1]);
+        float a0 = x[2 * u] * wl.x, a1 = x[2 * u + 1] * wl.y;
+#pragma unroll
+        for (int j = 0; j < K - 1; ++j) {
+          const float2 wj = __bfloat1622float2(wp[u][j]);
+          a0 += hist[j][2 * u] * wj.x;
+          a1 += hist[j][2 * u + 1] * wj.y;
+        }
+        acc[2 * u] = bf2f(f2bf(silu(a0)));  // rounded once, as the reference does
+        acc[2 * u + 1] = bf2f(f2bf(silu(a1)));
+      }
+      // slide the window
+#pragma unroll
+      for (int j = 0; j < K - 2; ++j)
+#pragma unroll
+        for (int u = 0; u < 8; ++u) hist[j][u] = hist[j + 1][u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) hist[K - 2][u] = x[u];
+      // l2 norm over each q / k head: lanes_per_head consecutive lanes hold one head
+      float ss = 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) ss += acc[u] * acc[u];
+      for (int o = lanes_per_head >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (live) {
+        if (c0 < 2 * key_dim) {
+          const float r = rsqrtf(ss + 1e-6f);
+          float o8[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) o8[u] = acc[u] * r;
+          if (c0 < key_dim)
+            store8(q + t * key_dim + c0, o8);
+          else
+            store8(k + t * key_dim + (c0 - key_dim), o8);
+        } else {
+          store8(v + t * (int64_t)(Hv * Dv) + (c0 - 2 * key_dim), acc);
+        }
+        if (tail_out && t == r0 + L - 1) {  // the row's last K-1 conv inputs are the window now
+#pragma unroll
+          for (int j = 0; j < K - 1; ++j) store8(tail_out + ((int64_t)row * (K - 1) + j) * C + c0, hist[j]);
+        }
       }
     }
   }

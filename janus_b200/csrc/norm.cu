@@ -63,45 +63,71 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_kernel(const __nv_b
   }
 }
 
-__global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int64_t T, int I, __nv_bfloat16* __restrict__ out) {
-  const int64_t n = T * (I >> 3);
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = i / (I >> 3);
-    const int c = (int)(i - t * (I >> 3)) * 8;
-    float g[8], u[8], o[8];
-    load8(gu + t * 2 * I + c, g);
-    load8(gu + t * 2 * I + I + c, u);
+// CTA per token (grid-stride over tokens), thread per 8 columns; kSiluUnroll column vectors in flight per thread.
+constexpr int kSiluThreads = 128, kSiluUnroll = 4;
+__global__ void __launch_bounds__(kSiluThreads) silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int64_t T, int I,
+                                                                __nv_bfloat16* __restrict__ out) {
+  const int nv = I >> 3;
+  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+    const __nv_bfloat16* gr = gu + t * 2 * I;
+    __nv_bfloat16* orow = out + t * I;
+    for (int c0 = threadIdx.x; c0 < nv; c0 += kSiluThreads * kSiluUnroll) {
+      bf16x8 g[kSiluUnroll], u[kSiluUnroll];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = silu(g[j]) * u[j];
-    store8(out + t * I + c, o);
+      for (int j = 0; j < kSiluUnroll; ++j) {
+        const int c = c0 + j * kSiluThreads;
+        if (c < nv) {
+          g[j] = *reinterpret_cast<const bf16x8*>(gr + c * 8);
+          u[j] = *reinterpret_cast<const bf16x8*>(gr + I + c * 8);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kSiluUnroll; ++j) {
+        const int c = c0 + j * kSiluThreads;
+        if (c < nv) {
+          bf16x8 o;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 a = __bfloat1622float2(g[j].h[i]), b = __bfloat1622float2(u[j].h[i]);
+            o.h[i] = __floats2bfloat162_rn(silu(a.x) * b.x, silu(a.y) * b.y);
+          }
+          *reinterpret_cast<bf16x8*>(orow + c * 8) = o;
+        }
+      }
+    }
   }
 }
 
-// One warp per (token, value head); Dv / 32 elements per lane.
+// Thread per 8 consecutive elements of one (token, value head); the DV / 8 threads of a head are consecutive lanes
+// of one warp and reduce the sum of squares with shuffles.
 template <int DV>
 __global__ void gated_rmsnorm_kernel(const __nv_bfloat16* __restrict__ core, const __nv_bfloat16* __restrict__ z,
                                      int64_t z_stride, int64_t T, int Hv, const __nv_bfloat16* __restrict__ w,
                                      float eps, __nv_bfloat16* __restrict__ out) {
-  constexpr int E = DV / 32;
-  const int64_t gw = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (gw >= T * Hv) return;
-  const int64_t t = gw / Hv;
-  const int h = (int)(gw - t * Hv);
-  const __nv_bfloat16* c = core + gw * DV + lane * E;
-  const __nv_bfloat16* zz = z + t * z_stride + (int64_t)h * DV + lane * E;
-  float cv[E], ss = 0.f;
+  constexpr int LPH = DV / 8;
+  static_assert(LPH >= 1 && LPH <= 32 && (32 % LPH) == 0, "head must span a power-of-two lane group");
+  const int64_t gi = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const bool live = gi < T * Hv * LPH;
+  const int64_t head = live ? gi / LPH : 0;
+  const int sub = (int)(gi % LPH);
+  const int64_t t = head / Hv;
+  const int h = (int)(head - t * Hv);
+  float cv[8], zv[8], wv[8], ss = 0.f;
+  if (live) {
+    load8(core + head * DV + sub * 8, cv);
+    load8(z + t * z_stride + (int64_t)h * DV + sub * 8, zv);
+    load8(w + sub * 8, wv);
 #pragma unroll
-  for (int i = 0; i < E; ++i) {
-    cv[i] = bf2f(c[i]);
-    ss += cv[i] * cv[i];
+    for (int i = 0; i < 8; ++i) ss += cv[i] * cv[i];
   }
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / (float)DV + eps);
 #pragma unroll
-  for (int i = 0; i < E; ++i) {
-    const float zv = bf2f(zz[i]);
-    out[gw * DV + lane * E + i] = f2bf(bf2f(w[lane * E + i]) * (cv[i] * r) * silu(zv));
+  for (int o = LPH >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (live) {
+    const float r = rsqrtf(ss / (float)DV + eps);
+    float res[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) res[i] = wv[i] * (cv[i] * r) * silu(zv[i]);
+    store8(out + head * DV + sub * 8, res);
   }
 }
 
@@ -156,12 +182,9 @@ extern "C" int janus_b200_silu_mul(const void* gu, int64_t T, int64_t inter, voi
              "silu_mul: bad arguments (inter %lld must be a multiple of 8)", (long long)inter);
   JB_REQUIRE(JB_ALIGNED(gu, 16) && JB_ALIGNED(out, 16), JANUS_ERR_ALIGNMENT, "silu_mul: alignment");
   if (T == 0) return JANUS_OK;
-  const int64_t n = T * (inter / 8);
-  const int th = 256;
-  int blocks = (int)((n + th - 1) / th);
-  if (blocks > 148 * 64) blocks = 148 * 64;
-  silu_mul_kernel<<<blocks, th, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)gu, T, (int)inter,
-                                                          (__nv_bfloat16*)out);
+  const int64_t blocks = T < 148 * 16 ? T : 148 * 16;
+  silu_mul_kernel<<<(unsigned)blocks, kSiluThreads, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)gu, T,
+                                                                                (int)inter, (__nv_bfloat16*)out);
   return launch_status("silu_mul");
 }
 
@@ -169,10 +192,11 @@ extern "C" int janus_b200_gated_rmsnorm(const void* core, const void* z, int64_t
                                         int64_t Dv, const void* w, float eps, void* out, void* stream) {
   JB_REQUIRE(core && z && w && out && T >= 0 && Hv > 0 && z_stride >= Hv * Dv, JANUS_ERR_INVALID,
              "gated_rmsnorm: bad arguments");
+  JB_REQUIRE(JB_ALIGNED(core, 16) && JB_ALIGNED(z, 16) && JB_ALIGNED(w, 16) && JB_ALIGNED(out, 16) && z_stride % 8 == 0,
+             JANUS_ERR_ALIGNMENT, "gated_rmsnorm: 16-byte alignment of core/z/w/out and z_stride % 8");
   if (T == 0) return JANUS_OK;
-  const int64_t warps = T * Hv;
   const int th = 256;
-  const unsigned blocks = (unsigned)((warps * 32 + th - 1) / th);
+  const unsigned blocks = (unsigned)((T * Hv * (Dv / 8) + th - 1) / th);
   cudaStream_t s = (cudaStream_t)stream;
   switch (Dv) {
     case 32:

@@ -15,9 +15,12 @@ BF16, F32, I32 = torch.bfloat16, torch.float32, torch.int32
 # summary) so kernel durations can be read after a synchronize.
 LAUNCHES = [0]
 TIMED = {}
+OPS = []  # names of the instrumented ops
 
 
 def _instrument(name, kernels=1):
+    OPS.append(name)
+
     def wrap(fn):
         def inner(*args, **kwargs):
             LAUNCHES[0] += kernels
