@@ -246,6 +246,7 @@ def main():
         e.record()
         step_events.append((s, e))
     torch.cuda.synchronize()
+    model.check_status()
     barrier()
     clock = clocks.stop()
     launches = (ops.LAUNCHES[0] - launches0) // args.steps
@@ -307,12 +308,9 @@ def main():
     for _ in range(max(3, args.steps // 2)):
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        lv, ro, pl = model.prepare(packs)
-        flat = model.run((lv, ro, pl))
-        host = flat.cpu()
-        probs = [torch.softmax(z, -1) for per in __import__("janus_b200.model", fromlist=["assemble"]).assemble(host, ro) for z in per]
+        probs = model.probabilities(packs)  # pack -> H2D -> device pass -> D2H of logits + status -> softmax
         e2e_ms.append((time.perf_counter() - t0) * 1000.0)
-        h2d, d2h = pl.h2d_bytes, flat.numel() * 4
+        h2d, d2h = model.last_plan.h2d_bytes, model._readout.n_slots * 4 + model.status.numel() * 4
     e2e_step = max_over_ranks(statistics.median(e2e_ms))
     e2e_value = world * args.requests / (e2e_step / 1000.0)
 

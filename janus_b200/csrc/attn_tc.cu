@@ -1,17 +1,23 @@
 // Tree attention on the 5th-generation tensor cores (tcgen05, accumulators in TMEM) for head dims 128 and 256.
 //
-// A CTA owns one kv head and 128 query rows = (128 / G) tokens x G query heads (GQA folded into M), one row per
-// softmax thread: row r lives in TMEM lane r, so the softmax of a row is thread-local. Three roles, six warps:
-//   warps 0-3  softmax: read S_j from TMEM, mask it by the tree rule (ancestor key ranges, own row causal),
-//              compute P_j = exp2(S_j*c - m) in registers, then (once O_{j-1} is final) rescale O when needed and
-//              write P_j to shared memory (bf16, K-major, 128B-swizzled); at the end normalise, gate and store O;
-//   warp 4     producer: TMA loads of the K_j and V_j tiles (64 keys x D, 128B swizzle, zero fill past the level's
-//              end) into two-stage rings;
-//   warp 5     MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM S buffers (M=128, N=64), and
-//              O += P_j V_j (M=128, N=D, V as the MN-major operand) into the D TMEM columns of O.
-// Hand-offs are mbarriers: TMA completion (expect-tx), tcgen05.commit for MMA completion, thread arrivals for the
-// softmax. The MMA thread issues S_{j+1} before it waits for P_j, so the tensor core computes the next scores while
-// the softmax warps work on the current ones, and the exponentials of block j overlap P_{j-1} V_{j-1}.
+// A CTA owns one kv head and 128 query rows = (128 / G) tokens x G query heads (GQA folded into M): row r lives in
+// TMEM lane r. Keys go in blocks of 128 (the MMA shape M=128 x N=128 runs at the full tensor rate; N=64 at half).
+// TMEM (512 columns): O [0, D) fp32, S [256, 384) fp32 (one block of scores), Q [384, 384 + D/2) bf16 pairs; Q is
+// the A operand of S = Q K^T straight from TMEM, so shared memory holds only K/V and P. Three roles, ten warps:
+//   warps 0-7  softmax, two warps per TMEM lane quarter (warp w: rows 32*(w%4).., key half w/4 of every S block and
+//              column half w/4 of O): write the Q rows into TMEM; per block read S_j, mask it by the tree rule
+//              (ancestor key ranges, own row causal), agree with the partner warp on the row max (shared memory + a
+//              64-thread named barrier), compute P_j = exp2(S_j*c - m) in registers, then (once P_{j-1} V_{j-1} is
+//              done) rescale O when needed and write P_j to shared memory (bf16, K-major, 128B-swizzled); at the end
+//              normalise, gate and store O;
+//   warp 8     producer: TMA loads (no multicast) of K/V into a ring of 5 slots of 128 keys x 128 head dims
+//              (128B swizzle, zero fill past the level's end), in the order the MMAs consume them:
+//              K_0, K_1, V_0, K_2, V_1, ..., V_{n-1} (a K or V block is D/128 slots);
+//   warp 9     MMA issuer (one thread): S_{j+1} = Q K_{j+1}^T (as soon as S_j has been read) before
+//              O += P_j V_j (two N=128 halves, V as the MN-major operand), so the tensor core alternates the two
+//              while the softmax warps work on block j. Each slot is released by a tcgen05.commit after the MMAs
+//              that read it. Any mbarrier wait of this thread idles the tensor pipe for a few hundred cycles, so it
+//              waits on one barrier per K/V item (all its slots) and at two points per block.
 // The running max m is refreshed only when a row's max grows by more than 2^8 (the row's O is then rescaled in
 // TMEM), so P stays <= 256 and the normaliser l uses the same m: the exact softmax. Every mbarrier wait is bounded;
 // a wait that runs out sets the status word and the CTA winds down (its TMA loads and MMAs drained first).
@@ -24,14 +30,22 @@
 namespace jb {
 namespace tc {
 
-constexpr int BM = 128, BN = 64;
-constexpr int NT = 192;  // 4 softmax warps, 1 producer warp, 1 MMA warp
+constexpr int BM = 128, BN = 128;
+constexpr int kSoftmaxThreads = 256;              // 8 softmax warps: two per TMEM lane quarter
+constexpr int kProducerWarp = 8, kMmaWarp = 9;
+constexpr int NT = kSoftmaxThreads + 64;          // + 1 producer warp + 1 MMA warp
 constexpr int kMaxLevels = 4;
-constexpr long kSpinLimit = 1L << 24;
+constexpr int kSlots = 5;                         // K/V ring slots
+constexpr uint32_t kSlotBytes = BN * 128 * 2;     // 128 keys x 128 head dims (two [128 keys][64 dims] TMA boxes)
+constexpr uint32_t kBoxBytes = BN * 128;          // one [128 keys][64 dims] box: 16 KB
+constexpr int kItemBars = 6;                      // > the K/V items in flight (at most kSlots)
+constexpr uint32_t kColO = 0, kColS = 256, kColQ = 384, kTmemCols = 512;
+constexpr long kSpinLimit = 1L << 30;         // a backstop; the wall-time limit ends waits first
+constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s: no legitimate hand-off here takes a millisecond
 constexpr unsigned kFull = 0xffffffffu;
 
 struct Params {
-  CUtensorMap kmap[kMaxLevels], vmap[kMaxLevels];  // [T_l keys][Hkv][D] bf16, box 64 keys x 1 head x 64 elements
+  CUtensorMap kmap[kMaxLevels], vmap[kMaxLevels];  // [T_l keys][Hkv][D] bf16, box 64 dims x 1 head x 128 keys
   const __nv_bfloat16* q;
   const int32_t* lo[kMaxLevels];
   const int32_t* hi[kMaxLevels];
@@ -47,9 +61,6 @@ struct Params {
 };
 
 __device__ __forceinline__ uint32_t s32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-__device__ __forceinline__ void cpa16(uint32_t dst, const void* src, bool ok) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0));
-}
 // UMMA shared-memory descriptor, 128B swizzle, sm_100 version bits
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
@@ -81,15 +92,29 @@ __device__ __forceinline__ void bar_expect_tx(uint64_t* bar, uint32_t bytes) {
                "r"(bytes)
                : "memory");
 }
-// bounded wait for the completion of the mbarrier phase of this parity; false (and the status word set) when the
-// limit ran out
+// bounded wait for the completion of the mbarrier phase of this parity. Gives up (returns false and sets the status
+// word) after kWaitNs of wall time, or as soon as any CTA of the grid has set the status word, so a grid that cannot
+// make progress ends within about one limit instead of one limit per wave.
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int32_t* err) {
   uint32_t done = 0;
-  for (long it = 0; it < kSpinLimit && !done; ++it)
+  uint64_t t0 = 0;
+  for (long it = 0; !done; ++it) {
     asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
                  : "=r"(done)
                  : "r"(s32(bar)), "r"(parity)
                  : "memory");
+    if (!done && (it & 1023) == 1023) {
+      const uint64_t now = global_ns();
+      if (t0 == 0) t0 = now;
+      const bool other = err && *reinterpret_cast<volatile int32_t*>(err) != 0;
+      if (other || now - t0 > kWaitNs || it > kSpinLimit) break;
+    }
+  }
   if (!done && err) atomicExch(err, 1);
   return done != 0;
 }
@@ -114,25 +139,20 @@ __device__ __forceinline__ void tld16(uint32_t addr, float* f) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) f[i] = __uint_as_float(v[i]);
 }
-// 64 consecutive fp32 TMEM columns of this thread's lane, waited for inside the same statement so no use of the
-// registers can be scheduled before the load has completed
-__device__ __forceinline__ void tld64(uint32_t addr, float* f) {
-  uint32_t v[64];
+// 32 consecutive fp32 TMEM columns of this thread's lane, waited for inside the same statement
+__device__ __forceinline__ void tld32(uint32_t addr, float* f) {
+  uint32_t v[32];
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
       "tcgen05.wait::ld.sync.aligned;\n"
       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
         "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
         "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-        "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31]),
-        "=r"(v[32]), "=r"(v[33]), "=r"(v[34]), "=r"(v[35]), "=r"(v[36]), "=r"(v[37]), "=r"(v[38]), "=r"(v[39]),
-        "=r"(v[40]), "=r"(v[41]), "=r"(v[42]), "=r"(v[43]), "=r"(v[44]), "=r"(v[45]), "=r"(v[46]), "=r"(v[47]),
-        "=r"(v[48]), "=r"(v[49]), "=r"(v[50]), "=r"(v[51]), "=r"(v[52]), "=r"(v[53]), "=r"(v[54]), "=r"(v[55]),
-        "=r"(v[56]), "=r"(v[57]), "=r"(v[58]), "=r"(v[59]), "=r"(v[60]), "=r"(v[61]), "=r"(v[62]), "=r"(v[63])
+        "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(addr)
       : "memory");
 #pragma unroll
-  for (int i = 0; i < 64; ++i) f[i] = __uint_as_float(v[i]);
+  for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
 }
 __device__ __forceinline__ void tst16(uint32_t addr, const float* f) {
   asm volatile(
@@ -158,30 +178,53 @@ __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::be
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// byte offset of (row, element d) in a K-major 128B-swizzled tile of `rows` rows: atoms of 64 elements (the layout
-// TMA writes with CU_TENSOR_MAP_SWIZZLE_128B into a 1024-byte aligned destination)
-__device__ __forceinline__ uint32_t swz(int row, int d, int rows) {
-  return (uint32_t)((d >> 6) * rows * 128 + row * 128 + ((((d & 63) >> 3) ^ (row & 7)) << 4));
+__device__ __forceinline__ void mma_ts(uint32_t tm, uint32_t ta, uint64_t db, uint32_t id, uint32_t acc) {
+  asm volatile(  // A from TMEM
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tm),
+      "r"(ta), "l"(db), "r"(id), "r"(acc));
+}
+__device__ __forceinline__ void tst16u(uint32_t addr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
+          addr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]));
+}
+__device__ __forceinline__ void tst_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// named barrier of the two softmax warps that share a TMEM lane quarter
+__device__ __forceinline__ void pair_sync(int quarter) {
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
 }
 
 template <int D>
 struct Layout {
-  static constexpr uint32_t Q = 0;                   // 128 rows x D
-  static constexpr uint32_t K = Q + BM * D * 2;      // 2 stages of 64 keys x D
-  static constexpr uint32_t V = K + 2 * BN * D * 2;  // 2 stages of 64 keys x D
-  static constexpr uint32_t P = V + 2 * BN * D * 2;  // 128 rows x 64 keys
+  static constexpr int SPT = D / 128;                      // ring slots per K or V block
+  static constexpr uint32_t RING = 0;                      // kSlots x 32 KB
+  static constexpr uint32_t P = RING + kSlots * kSlotBytes;  // 128 rows x 128 keys: two [128 rows][64 keys] atoms
   static constexpr uint32_t BYTES = P + BM * BN * 2;
-  static constexpr uint32_t STAGE = BN * D * 2;
-  static constexpr uint32_t TMEM_COLS = 512;  // S0 [0,64) S1 [64,128) O [128, 128+D)
 };
 
+// full[i % kItemBars]: K/V item i (all its slots) has landed; empty[slot]: the MMAs reading a ring slot are done
 struct Bars {
-  uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_empty[2], p_full, pv_done, q_full, drain;
+  uint64_t full[kItemBars], empty[kSlots], s_full, s_empty, p_full, pv_done, q_full, drain;
 };
+
+// The ring position sequence shared by the producer and the MMA issuer: block item i (0-based) of
+// K_0, K_1, V_0, K_2, V_1, ..., K_{n-1}, V_{n-2}, V_{n-1} is K_{kv_block(i)} when is_k(i); each item is SPT slots.
+__device__ __forceinline__ bool item_is_k(int i, int n) { return i == 0 || (i % 2 == 1 && (i + 1) / 2 < n); }
+__device__ __forceinline__ int item_block(int i, int n) {
+  if (i == 0) return 0;
+  if (i % 2 == 1 && (i + 1) / 2 < n) return (i + 1) / 2;  // K_{(i+1)/2}
+  // V blocks: V_j follows K_{j+1} (item 2j+2) while there is a K_{j+1}; after the last K they run in order
+  return i % 2 == 0 ? i / 2 - 1 : (i - 1) / 2;
+}
 
 template <int D>
 __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_constant__ Params p) {
   using Lay = Layout<D>;
+  constexpr int SPT = Lay::SPT;
   extern __shared__ unsigned char raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~(uintptr_t)1023);
   const uint32_t sbase = s32(base);
@@ -190,6 +233,9 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
   __shared__ int s_tok[BM], s_own[BM];
   __shared__ int s_lo[kMaxLevels - 1][BM], s_hi[kMaxLevels - 1][BM];
   __shared__ int s_klo[kMaxLevels], s_nblk[kMaxLevels];
+  __shared__ float s_red[2][2][BM];  // [block parity][key half][row]: partial row maxima
+  __shared__ float s_sum[2][BM];     // [key half][row]: partial row sums
+  __shared__ int s_ok[2][2][4];      // [block parity][key half][lane quarter]: the warp is still on track
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int hkv = blockIdx.y;
@@ -212,21 +258,17 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s32(&tmem_base)),
-                 "r"(Lay::TMEM_COLS));
+                 "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
-  if (tid == 160) {
-    for (int s = 0; s < 2; ++s) {
-      bar_init(&bars.k_full[s], 1);
-      bar_init(&bars.k_empty[s], 1);
-      bar_init(&bars.v_full[s], 1);
-      bar_init(&bars.v_empty[s], 1);
-      bar_init(&bars.s_full[s], 1);
-      bar_init(&bars.s_empty[s], 128);
-    }
-    bar_init(&bars.p_full, 128);
+  if (tid == 32 * kProducerWarp) {
+    for (int s = 0; s < kItemBars; ++s) bar_init(&bars.full[s], 1);
+    for (int s = 0; s < kSlots; ++s) bar_init(&bars.empty[s], 1);
+    bar_init(&bars.s_full, 1);
+    bar_init(&bars.s_empty, kSoftmaxThreads);
+    bar_init(&bars.p_full, kSoftmaxThreads);
     bar_init(&bars.pv_done, 1);
-    bar_init(&bars.q_full, 128);
+    bar_init(&bars.q_full, kSoftmaxThreads);
     bar_init(&bars.drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -250,109 +292,129 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
   const uint32_t tm = tmem_base;
   int total = 0;
   for (int l = 0; l < L; ++l) total += s_nblk[l];
+  const int n_items = 2 * total;
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       bool ok = true;
-      int issued = 0;  // K/V tiles issued: each has a pending or consumed full-barrier phase
-      int lvl = 0, b = 0;
-      for (int j = 0; j < total && ok; ++j, ++b) {
-        while (b >= s_nblk[lvl]) {
-          b = 0;
+      int issued = 0;  // items whose loads went out
+      for (int i = 0; i < n_items && ok; ++i) {
+        const bool is_k = item_is_k(i, total);
+        int blk = item_block(i, total), lvl = 0;
+        while (blk >= s_nblk[lvl]) {
+          blk -= s_nblk[lvl];
           ++lvl;
         }
-        const int st = j & 1, ks = s_klo[lvl] + b * BN;
-        if (j >= 2) ok = wait_bar(&bars.k_empty[st], ((j >> 1) - 1) & 1, p.err);
+        const int ks = s_klo[lvl] + blk * BN;
+        const CUtensorMap* map = is_k ? &p.kmap[lvl] : &p.vmap[lvl];
+        for (int h = 0; h < SPT && ok; ++h) {  // every slot of the item is free
+          const int pos = i * SPT + h;
+          if (pos >= kSlots) ok = wait_bar(&bars.empty[pos % kSlots], (pos / kSlots - 1) & 1, p.err);
+        }
         if (!ok) break;
-        bar_expect_tx(&bars.k_full[st], Lay::STAGE);
-#pragma unroll
-        for (int c = 0; c < D / 64; ++c)
-          tma_load3(sbase + Lay::K + st * Lay::STAGE + c * BN * 128, &p.kmap[lvl], c * 64, hkv, ks, &bars.k_full[st]);
-        if (j >= 2) ok = wait_bar(&bars.v_empty[st], ((j >> 1) - 1) & 1, p.err);
-        if (ok) {
-          bar_expect_tx(&bars.v_full[st], Lay::STAGE);
-#pragma unroll
-          for (int c = 0; c < D / 64; ++c)
-            tma_load3(sbase + Lay::V + st * Lay::STAGE + c * BN * 128, &p.vmap[lvl], c * 64, hkv, ks,
-                      &bars.v_full[st]);
+        uint64_t* fb = &bars.full[i % kItemBars];
+        bar_expect_tx(fb, SPT * kSlotBytes);
+        for (int h = 0; h < SPT; ++h) {
+          const uint32_t dst = sbase + Lay::RING + ((i * SPT + h) % kSlots) * kSlotBytes;
+          tma_load3(dst, map, h * 128, hkv, ks, fb);
+          tma_load3(dst + kBoxBytes, map, h * 128 + 64, hkv, ks, fb);
         }
-        issued = j + 1;
-        if (!ok) {  // K_j went out without V_j: wait for K_j alone below
-          wait_bar(&bars.k_full[st], (j >> 1) & 1, p.err);
-          issued = j;
-        }
+        issued = i + 1;
       }
-      // the last tile of each stage has landed before the CTA may leave (no-ops on the normal path: consumed)
-      for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; ++j) {
-        wait_bar(&bars.k_full[j & 1], (j >> 1) & 1, p.err);
-        wait_bar(&bars.v_full[j & 1], (j >> 1) & 1, p.err);
-      }
+      // every issued load has landed before the CTA may leave (no-ops on the normal path: all consumed)
+      for (int i = issued - kItemBars < 0 ? 0 : issued - kItemBars; i < issued; ++i)
+        wait_bar(&bars.full[i % kItemBars], (i / kItemBars) & 1, p.err);
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t ID_QK = idesc(BM, BN, 0, 0);
-      constexpr uint32_t ID_PV = idesc(BM, D, 0, 1);
-      auto issue_s = [&](int j) -> bool {  // S_j = Q K_j^T into S buffer j & 1
-        const int st = j & 1;
-        if (!wait_bar(&bars.k_full[st], (j >> 1) & 1, p.err)) return false;
-        if (j >= 2 && !wait_bar(&bars.s_empty[st], ((j >> 1) - 1) & 1, p.err)) return false;
+      constexpr uint32_t ID_PV = idesc(BM, 128, 0, 1);
+      // Every mbarrier wait of this thread idles the tensor pipe for a few hundred cycles (the wait resolves only
+      // after the MMAs issued before it), so each block waits twice: before S (scores read, K landed) and before
+      // PV (P written, V landed), on one barrier per K/V item.
+      int item = 0;  // K/V items consumed, in the producer's order
+      auto issue_s = [&]() -> bool {  // S = Q K^T over the next K item (SPT slots)
+        if (!wait_bar(&bars.full[item % kItemBars], (item / kItemBars) & 1, p.err)) return false;
         fence_after();
-        const uint32_t kb = sbase + Lay::K + st * Lay::STAGE;
+        for (int h = 0; h < SPT; ++h) {
+          const int slot = (item * SPT + h) % kSlots;
+          const uint32_t kb = sbase + Lay::RING + slot * kSlotBytes;
 #pragma unroll
-        for (int s = 0; s < D / 16; ++s)
-          mma(tm + st * BN, sdesc(sbase + Lay::Q + (s >> 2) * BM * 128 + (s & 3) * 32, 16, 1024),
-              sdesc(kb + (s >> 2) * BN * 128 + (s & 3) * 32, 16, 1024), ID_QK, s > 0);
-        commit(&bars.s_full[st]);
-        commit(&bars.k_empty[st]);
+          for (int s = 0; s < 8; ++s)  // 16 head dims per step: dims h*128 + 16 s
+            mma_ts(tm + kColS, tm + kColQ + (h * 8 + s) * 8, sdesc(kb + (s >> 2) * kBoxBytes + (s & 3) * 32, 16, 1024),
+                   ID_QK, (h | s) ? 1u : 0u);
+          commit(&bars.empty[slot]);
+        }
+        commit(&bars.s_full);
+        ++item;
         return true;
       };
       bool ok = wait_bar(&bars.q_full, 0, p.err);
-      if (ok && total > 0) ok = issue_s(0);
+      fence_after();
+      if (ok && total > 0) ok = issue_s();
       for (int j = 0; j < total && ok; ++j) {
-        if (j + 1 < total) ok = issue_s(j + 1);
-        if (!ok) break;
-        const int st = j & 1;
-        ok = wait_bar(&bars.p_full, j & 1, p.err) && wait_bar(&bars.v_full[st], (j >> 1) & 1, p.err);
-        if (!ok) break;
+        if (j + 1 < total) {  // S_{j+1} once the softmax has read S_j
+          ok = wait_bar(&bars.s_empty, j & 1, p.err);
+          fence_after();
+          if (ok) ok = issue_s();
+        }
+        if (ok)
+          ok = wait_bar(&bars.p_full, j & 1, p.err) &&
+               wait_bar(&bars.full[item % kItemBars], (item / kItemBars) & 1, p.err);
         fence_after();
-        const uint32_t vb = sbase + Lay::V + st * Lay::STAGE;
+        for (int h = 0; h < SPT && ok; ++h) {  // O[:, h*128 ..] += P_j V_j[:, h*128 ..]
+          const int slot = (item * SPT + h) % kSlots;
+          const uint32_t vb = sbase + Lay::RING + slot * kSlotBytes;
 #pragma unroll
-        for (int s = 0; s < BN / 16; ++s)
-          mma(tm + 2 * BN, sdesc(sbase + Lay::P + s * 32, 16, 1024), sdesc(vb + s * 16 * 128, BN * 128, 1024), ID_PV,
-              (j > 0 || s > 0) ? 1u : 0u);
-        commit(&bars.pv_done);
-        commit(&bars.v_empty[st]);
+          for (int s = 0; s < BN / 16; ++s)  // 16 keys per step
+            mma(tm + kColO + h * 128, sdesc(sbase + Lay::P + (s >> 2) * (BM * 128) + (s & 3) * 32, 16, 1024),
+                sdesc(vb + s * 16 * 128, kBoxBytes, 1024), ID_PV, (j > 0 || s > 0) ? 1u : 0u);
+          commit(&bars.empty[slot]);
+        }
+        ++item;
+        if (ok) commit(&bars.pv_done);
       }
       commit(&bars.drain);  // completes once every MMA issued above has finished
     }
   } else {
     // ------------------------------------------------------------------------------------------ softmax warps
-    const int r = tid;  // query row = TMEM lane
+    constexpr int HC = BN / 2, HD = D / 2;
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = 32 * quarter + lane;  // query row = TMEM lane
     const int tq = r / G;
-    const uint32_t lane_addr = tm + ((uint32_t)(32 * warp) << 16);
-    for (int c = tid; c < BM * (D / 8); c += 128) {  // Q tile: row rr = tq * G + g
-      const int rr = c / (D / 8), d = (c % (D / 8)) * 8;
-      const int tqq = rr / G, g = rr % G;
-      const bool live = tqq < ntok;
-      cpa16(sbase + Lay::Q + swz(rr, d, BM), p.q + ((int64_t)(live ? q0 + tqq : q0) * p.Hq + hkv * G + g) * D + d,
-            live);
+    const uint32_t lane_addr = tm + ((uint32_t)(32 * quarter) << 16);
+    {  // this warp's half of the Q row into TMEM (bf16 pairs, even dim in the low half)
+      const bool live = tq < ntok;
+      const __nv_bfloat16* qr = p.q + ((int64_t)(live ? q0 + tq : q0) * p.Hq + hkv * G + r % G) * D + half * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 2; c += 16) {
+        uint32_t v[16];
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const uint4 x = live ? *reinterpret_cast<const uint4*>(qr + 2 * (c + i)) : make_uint4(0, 0, 0, 0);
+          v[i] = x.x;
+          v[i + 1] = x.y;
+          v[i + 2] = x.z;
+          v[i + 3] = x.w;
+        }
+        tst16u(lane_addr + kColQ + half * (HD / 2) + c, v);
+      }
+      tst_wait();
+      fence_before();
+      bar_arrive(&bars.q_full);
     }
-    asm volatile("cp.async.commit_group;\n" ::);
-    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
-    fence_async_smem();
-    bar_arrive(&bars.q_full);
     const float sc = p.scale_log2;
     float m_used = -INFINITY, l_sum = 0.f;
-    bool ok = true;
+    bool ok = true;  // warp-uniform; the two warps of a pair agree on it at every pair barrier
     int lvl = 0, b = 0;
-    for (int j = 0; j < total && ok; ++j, ++b) {
+    for (int j = 0; j < total; ++j, ++b) {
       while (b >= s_nblk[lvl]) {
         b = 0;
         ++lvl;
       }
-      const int sb = j & 1, ks = s_klo[lvl] + b * BN;
+      const int ks = s_klo[lvl] + b * BN + half * HC;  // first key of this warp's columns
       int lo, hi;
       if (tq >= ntok) {
         lo = 0;
@@ -364,26 +426,36 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
         lo = s_lo[lvl][tq];
         hi = s_hi[lvl][tq];
       }
-      ok = __all_sync(kFull, wait_bar(&bars.s_full[sb], (j >> 1) & 1, p.err));
-      if (!ok) break;
-      fence_after();
-      float s[BN];
-      tld64(lane_addr + sb * BN, s);
-      fence_before();
-      bar_arrive(&bars.s_empty[sb]);  // the S buffer may be overwritten
-      float mx = -INFINITY;
-      if (ks >= lo && ks + BN <= hi) {  // the whole block is visible to this row
+      const bool mine = ok && __all_sync(kFull, wait_bar(&bars.s_full, j & 1, p.err));
+      float s[HC], mx = -INFINITY;
+      if (mine) {
+        fence_after();
+        tld32(lane_addr + kColS + half * HC, s);
+        tld32(lane_addr + kColS + half * HC + 32, s + 32);
+        fence_before();
+        bar_arrive(&bars.s_empty);  // S may be overwritten by the next block's scores
+        if (!(ks >= lo && ks + HC <= hi)) {  // not every column of this half is visible to this row
 #pragma unroll
-        for (int c = 0; c < BN; ++c) mx = fmaxf(mx, s[c]);
-      } else {
-#pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          const int kk = ks + c;
-          s[c] = (kk >= lo && kk < hi) ? s[c] : -INFINITY;
-          mx = fmaxf(mx, s[c]);
+          for (int c = 0; c < HC; ++c) {
+            const int kk = ks + c;
+            s[c] = (kk >= lo && kk < hi) ? s[c] : -INFINITY;
+          }
         }
+        float mx4[4] = {s[0], s[1], s[2], s[3]};
+#pragma unroll
+        for (int c = 4; c < HC; c += 4)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) mx4[i] = fmaxf(mx4[i], s[c + i]);
+        mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       }
-      mx *= sc;
+      // exchange the half-row maxima (and whether both warps are still on track) with the partner warp
+      const int par = j & 1;
+      s_red[par][half][r] = mx;
+      if (lane == 0) s_ok[par][half][quarter] = mine;
+      pair_sync(quarter);
+      ok = mine && s_ok[par][half ^ 1][quarter];
+      if (!ok) break;
+      mx = fmaxf(mx, s_red[par][half ^ 1][r]) * sc;
       const bool grow = mx > m_used + 8.f;
       const float m_new = grow ? mx : m_used;
       const bool rescale = grow && m_used != -INFINITY;
@@ -391,50 +463,57 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
       l_sum *= alpha;
       m_used = m_new;
       const float mref = m_used == -INFINITY ? 0.f : m_used;
-      uint32_t pk[BN / 2];
+      uint32_t pk[HC / 2];
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < BN; c += 2) {
+      for (int c = 0; c < HC; c += 2) {
         const float e0 = ex2(fmaf(s[c], sc, -mref)), e1 = ex2(fmaf(s[c + 1], sc, -mref));
-        l_sum += e0 + e1;
+        ls[(c >> 1) & 3] += e0 + e1;
         pk[c / 2] = pack_bf16(e0, e1);
       }
+      l_sum += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       if (j > 0) ok = __all_sync(kFull, wait_bar(&bars.pv_done, (j - 1) & 1, p.err));  // P free, O final
-      if (!ok) break;
-      fence_after();
-      if (__any_sync(kFull, rescale)) {
+      if (ok) {  // (a wait that ran out is handed to the partner at the next pair barrier)
+        fence_after();
+        if (__any_sync(kFull, rescale)) {
 #pragma unroll 1
-        for (int c = 0; c < D; c += 16) {
-          float o[16];
-          tld16(lane_addr + 2 * BN + c, o);
+          for (int c = 0; c < HD; c += 16) {
+            float o[16];
+            tld16(lane_addr + kColO + half * HD + c, o);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] *= alpha;
-          tst16(lane_addr + 2 * BN + c, o);
+            for (int i = 0; i < 16; ++i) o[i] *= alpha;
+            tst16(lane_addr + kColO + half * HD + c, o);
+          }
         }
-      }
-      unsigned char* prow = base + Lay::P + r * 128;
+        unsigned char* prow = base + Lay::P + half * (BM * 128) + r * 128;  // atom `half`: keys half*64 ..
 #pragma unroll
-      for (int c = 0; c < BN / 8; ++c)
-        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
-            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-      fence_async_smem();
-      fence_before();
-      bar_arrive(&bars.p_full);
+        for (int c = 0; c < HC / 8; ++c)
+          *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        fence_async_smem();
+        fence_before();
+        bar_arrive(&bars.p_full);
+      }
     }
     if (total > 0 && ok) ok = __all_sync(kFull, wait_bar(&bars.pv_done, (total - 1) & 1, p.err));
     fence_after();
-    // epilogue: warp-collective TMEM loads by every softmax thread, stores by the live rows
-    if (ok) {
+    // the row's normaliser: this half's sum plus the partner's (both warps reach this barrier exactly once)
+    s_sum[half][r] = l_sum;
+    pair_sync(quarter);
+    l_sum += s_sum[half ^ 1][r];
+    // epilogue: warp-collective TMEM loads of this warp's half of O, stores by the live rows
+    if (__all_sync(kFull, ok)) {
       const bool live = tq < ntok;
       const int g = r % G;
       const int64_t t = q0 + (live ? tq : 0);
       const int h = hkv * G + g;
       const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
-      const __nv_bfloat16* gr = p.gate + t * p.gate_stride + (int64_t)h * p.gate_head_stride;
-      __nv_bfloat16* orow = p.out + (t * p.Hq + h) * D;
+      const __nv_bfloat16* gr = p.gate + t * p.gate_stride + (int64_t)h * p.gate_head_stride + half * HD;
+      __nv_bfloat16* orow = p.out + (t * p.Hq + h) * D + half * HD;
 #pragma unroll 1
-      for (int c = 0; c < D; c += 16) {
+      for (int c = 0; c < HD; c += 16) {
         float o[16];
-        tld16(lane_addr + 2 * BN + c, o);
+        tld16(lane_addr + kColO + half * HD + c, o);
         if (live) {
           float gv[16], res[16];
 #pragma unroll
@@ -454,7 +533,7 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
   wait_bar(&bars.drain, 0, p.err);
   fence_before();
   __syncthreads();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(Lay::TMEM_COLS));
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(kTmemCols));
 }
 
 // ------------------------------------------------------------------------------------------------ host side
@@ -476,7 +555,7 @@ static EncodeTiled encode_fn() {
   return fn;
 }
 
-// K or V of one level: [T keys][Hkv][D] bf16, boxes of 64 keys x 1 head x 64 elements, 128B swizzle; keys past T
+// K or V of one level: [T keys][Hkv][D] bf16, boxes of 64 dims x 1 head x 128 keys, 128B swizzle; keys past T
 // read as zeros (and are masked)
 static int make_kv_map(CUtensorMap* map, const void* ptr, int64_t T, int64_t Hkv, int64_t D) {
   EncodeTiled enc = encode_fn();
@@ -486,7 +565,7 @@ static int make_kv_map(CUtensorMap* map, const void* ptr, int64_t T, int64_t Hkv
   }
   const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)Hkv, (cuuint64_t)T};
   const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)(Hkv * D * 2)};
-  const cuuint32_t box[3] = {64, 1, (cuuint32_t)BN};
+  const cuuint32_t box[3] = {64, 1, (cuuint32_t)BN};  // 64 dims x 1 head x 128 keys
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

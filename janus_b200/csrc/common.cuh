@@ -54,6 +54,9 @@ __device__ __forceinline__ float block_sum(float v, float* scratch) {
 }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + expf(-x)); }
+// silu with the hardware approximations of exp and division (relative error ~1e-7, far below the bf16 rounding
+// every caller applies to the result)
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + expf(-x)); }
 __device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1pf(expf(x)); }
 

@@ -109,8 +109,8 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
           a0 += hist[j][2 * u] * wj.x;
           a1 += hist[j][2 * u + 1] * wj.y;
         }
-        acc[2 * u] = bf2f(f2bf(silu(a0)));  // rounded once, as the reference does
-        acc[2 * u + 1] = bf2f(f2bf(silu(a1)));
+        acc[2 * u] = bf2f(f2bf(silu_fast(a0)));  // rounded once, as the reference does
+        acc[2 * u + 1] = bf2f(f2bf(silu_fast(a1)));
       }
       // slide the window
 #pragma unroll

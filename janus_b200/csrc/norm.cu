@@ -89,7 +89,7 @@ __global__ void __launch_bounds__(kSiluThreads) silu_mul_kernel(const __nv_bfloa
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const float2 a = __bfloat1622float2(g[j].h[i]), b = __bfloat1622float2(u[j].h[i]);
-            o.h[i] = __floats2bfloat162_rn(silu(a.x) * b.x, silu(a.y) * b.y);
+            o.h[i] = __floats2bfloat162_rn(silu_fast(a.x) * b.x, silu_fast(a.y) * b.y);
           }
           *reinterpret_cast<bf16x8*>(orow + c * 8) = o;
         }
@@ -126,7 +126,7 @@ __global__ void gated_rmsnorm_kernel(const __nv_bfloat16* __restrict__ core, con
     const float r = rsqrtf(ss / (float)DV + eps);
     float res[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) res[i] = wv[i] * (cv[i] * r) * silu(zv[i]);
+    for (int i = 0; i < 8; ++i) res[i] = wv[i] * (cv[i] * r) * silu_fast(zv[i]);
     store8(out + head * DV + sub * 8, res);
   }
 }

@@ -16,7 +16,7 @@ import numpy as np
 import torch
 import torch.nn.functional as F
 
-from . import ops
+from . import _lib, ops
 from .config import LINEAR, ModelShape
 from .plan import DevicePlan, build_levels, build_readout
 
@@ -79,6 +79,7 @@ class DecisionReadout:
         self.group = shape.heads // shape.kv_heads
         self.tile_tokens = ops.tree_attention_tile_tokens(shape.head_dim, shape.heads, shape.kv_heads)
         self.last_plan = None
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)  # set by a device-side wait that ran out
 
     # ------------------------------------------------------------------------------------------------ level pass
 
@@ -119,7 +120,8 @@ class DecisionReadout:
                 gate = qkv[:, :Hq * 2 * D].view(T, Hq, 2 * D)[:, :, D:]
                 o = ops.tree_attention(q, keys, values, [plan[(d, "lo", l)] for l in range(d)],
                                        [plan[(d, "hi", l)] for l in range(d)], rs, rot,
-                                       plan[(d, "tiles", self.tile_tokens)].view(-1, 2), gate, D ** -0.5)
+                                       plan[(d, "tiles", self.tile_tokens)].view(-1, 2), gate, D ** -0.5,
+                                       status=self.status)
                 h = F.linear(o, L.o)
                 kept.append((kk, vv) if lv.keep else None)
             y = ops.add_rmsnorm(x, h, L.post_norm, eps)
@@ -186,6 +188,7 @@ class DecisionReadout:
         self._readout = readout
         self.last_plan = plan
         logits = torch.zeros(readout.n_slots, dtype=torch.float32, device=self.device)
+        self.status.zero_()
         history = []
         for lv in levels:
             history.append(self._level(lv, plan, history, logits))
@@ -197,10 +200,16 @@ class DecisionReadout:
         prepared = self.prepare(packs)
         return self.run(prepared), prepared[1]
 
+    def check_status(self):
+        """Raise if a bounded device-side wait of the last run ran out (its results are then invalid)."""
+        if int(self.status.item()) != 0:
+            raise _lib.JanusError("tree_attention: a device-side wait ran out; the results of this run are invalid")
+
     def forward_many(self, packs):
         """Per pack, per question, the logits as fp32 CPU tensors (janus/model.py:368-373 + :319-366)."""
         flat, readout = self.logits_flat(packs)
         host = flat.cpu()
+        self.check_status()
         return assemble(host, readout)
 
     def probabilities(self, packs, temperatures=None):
