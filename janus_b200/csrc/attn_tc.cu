@@ -3,7 +3,7 @@
 // A CTA owns one kv head and 128 query rows = (128 / G) tokens x G query heads (GQA folded into M): row r lives in
 // TMEM lane r. Keys go in blocks of 128 (the MMA shape M=128 x N=128 runs at the full tensor rate; N=64 at half).
 // TMEM (512 columns): O [0, D) fp32, S [256, 384) fp32 (one block of scores), Q [384, 384 + D/2) bf16 pairs; Q is
-// the A operand of S = Q K^T straight from TMEM, so shared memory holds only K/V and P. Three roles, ten warps:
+// the A operand of S = Q K^T straight from TMEM, so shared memory holds only K/V and P. Four roles, eleven warps:
 //   warps 0-7  softmax, two warps per TMEM lane quarter (warp w: rows 32*(w%4).., key half w/4 of every S block and
 //              column half w/4 of O): write the Q rows into TMEM; per block read S_j, mask it by the tree rule
 //              (ancestor key ranges, own row causal), agree with the partner warp on the row max (shared memory + a
@@ -13,11 +13,12 @@
 //   warp 8     producer: TMA loads (no multicast) of K/V into a ring of 5 slots of 128 keys x 128 head dims
 //              (128B swizzle, zero fill past the level's end), in the order the MMAs consume them:
 //              K_0, K_1, V_0, K_2, V_1, ..., V_{n-1} (a K or V block is D/128 slots);
-//   warp 9     MMA issuer (one thread): S_{j+1} = Q K_{j+1}^T (as soon as S_j has been read) before
-//              O += P_j V_j (two N=128 halves, V as the MN-major operand), so the tensor core alternates the two
-//              while the softmax warps work on block j. Each slot is released by a tcgen05.commit after the MMAs
-//              that read it. Any mbarrier wait of this thread idles the tensor pipe for a few hundred cycles, so it
-//              waits on one barrier per K/V item (all its slots) and at two points per block.
+//   warp 9     S issuer (one thread): S_{j+1} = Q K_{j+1}^T as soon as S_j has been read and K_{j+1} landed;
+//   warp 10    PV issuer (one thread): O += P_j V_j (two N=128 halves, V as the MN-major operand) once P_j is
+//              written and V_j landed. An mbarrier wait idles its issuing thread for a few hundred cycles; with two
+//              issuers the tensor pipe runs one's MMAs while the other waits, and it computes S_{j+1} while the
+//              softmax warps work on block j. Each ring slot is released by a tcgen05.commit after the MMAs that
+//              read it; one full barrier covers all slots of a K/V item.
 // The running max m is refreshed only when a row's max grows by more than 2^8 (the row's O is then rescaled in
 // TMEM), so P stays <= 256 and the normaliser l uses the same m: the exact softmax. Every mbarrier wait is bounded;
 // a wait that runs out sets the status word and the CTA winds down (its TMA loads and MMAs drained first).
@@ -32,8 +33,8 @@ namespace tc {
 
 constexpr int BM = 128, BN = 128;
 constexpr int kSoftmaxThreads = 256;              // 8 softmax warps: two per TMEM lane quarter
-constexpr int kProducerWarp = 8, kMmaWarp = 9;
-constexpr int NT = kSoftmaxThreads + 64;          // + 1 producer warp + 1 MMA warp
+constexpr int kProducerWarp = 8, kMmaSWarp = 9, kMmaPvWarp = 10;
+constexpr int NT = kSoftmaxThreads + 96;          // + 1 producer warp + 2 MMA-issuing warps
 constexpr int kMaxLevels = 4;
 constexpr int kSlots = 5;                         // K/V ring slots
 constexpr uint32_t kSlotBytes = BN * 128 * 2;     // 128 keys x 128 head dims (two [128 keys][64 dims] TMA boxes)
@@ -221,6 +222,10 @@ __device__ __forceinline__ int item_block(int i, int n) {
   return i % 2 == 0 ? i / 2 - 1 : (i - 1) / 2;
 }
 
+// the item indices of K_j and V_j in that sequence
+__device__ __forceinline__ int k_item(int j) { return j == 0 ? 0 : 2 * j - 1; }
+__device__ __forceinline__ int v_item(int j, int n) { return j + 1 < n ? 2 * j + 2 : 2 * n - 1; }
+
 template <int D>
 __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_constant__ Params p) {
   using Lay = Layout<D>;
@@ -269,7 +274,7 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
     bar_init(&bars.p_full, kSoftmaxThreads);
     bar_init(&bars.pv_done, 1);
     bar_init(&bars.q_full, kSoftmaxThreads);
-    bar_init(&bars.drain, 1);
+    bar_init(&bars.drain, 2);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -326,17 +331,18 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
       for (int i = issued - kItemBars < 0 ? 0 : issued - kItemBars; i < issued; ++i)
         wait_bar(&bars.full[i % kItemBars], (i / kItemBars) & 1, p.err);
     }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------------------------------------ MMA issuer
+  } else if (warp == kMmaSWarp) {
+    // ------------------------------------------------------------------------------------------ S issuer
+    // Two issuing threads, one for S and one for PV: any mbarrier wait of an issuing thread idles it for a few
+    // hundred cycles, and with two of them the tensor pipe runs one's MMAs while the other waits.
     if (lane == 0) {
       constexpr uint32_t ID_QK = idesc(BM, BN, 0, 0);
-      constexpr uint32_t ID_PV = idesc(BM, 128, 0, 1);
-      // Every mbarrier wait of this thread idles the tensor pipe for a few hundred cycles (the wait resolves only
-      // after the MMAs issued before it), so each block waits twice: before S (scores read, K landed) and before
-      // PV (P written, V landed), on one barrier per K/V item.
-      int item = 0;  // K/V items consumed, in the producer's order
-      auto issue_s = [&]() -> bool {  // S = Q K^T over the next K item (SPT slots)
-        if (!wait_bar(&bars.full[item % kItemBars], (item / kItemBars) & 1, p.err)) return false;
+      bool ok = wait_bar(&bars.q_full, 0, p.err);
+      for (int j = 0; j < total && ok; ++j) {
+        const int item = k_item(j);
+        if (j > 0) ok = wait_bar(&bars.s_empty, (j - 1) & 1, p.err);  // S_{j-1} has been read
+        ok = ok && wait_bar(&bars.full[item % kItemBars], (item / kItemBars) & 1, p.err);
+        if (!ok) break;
         fence_after();
         for (int h = 0; h < SPT; ++h) {
           const int slot = (item * SPT + h) % kSlots;
@@ -348,23 +354,21 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
           commit(&bars.empty[slot]);
         }
         commit(&bars.s_full);
-        ++item;
-        return true;
-      };
-      bool ok = wait_bar(&bars.q_full, 0, p.err);
-      fence_after();
-      if (ok && total > 0) ok = issue_s();
+      }
+      commit(&bars.drain);  // completes once every MMA issued by this thread has finished
+    }
+  } else if (warp == kMmaPvWarp) {
+    // ------------------------------------------------------------------------------------------ PV issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_PV = idesc(BM, 128, 0, 1);
+      bool ok = true;
       for (int j = 0; j < total && ok; ++j) {
-        if (j + 1 < total) {  // S_{j+1} once the softmax has read S_j
-          ok = wait_bar(&bars.s_empty, j & 1, p.err);
-          fence_after();
-          if (ok) ok = issue_s();
-        }
-        if (ok)
-          ok = wait_bar(&bars.p_full, j & 1, p.err) &&
-               wait_bar(&bars.full[item % kItemBars], (item / kItemBars) & 1, p.err);
+        const int item = v_item(j, total);
+        ok = wait_bar(&bars.p_full, j & 1, p.err) &&
+             wait_bar(&bars.full[item % kItemBars], (item / kItemBars) & 1, p.err);
+        if (!ok) break;
         fence_after();
-        for (int h = 0; h < SPT && ok; ++h) {  // O[:, h*128 ..] += P_j V_j[:, h*128 ..]
+        for (int h = 0; h < SPT; ++h) {  // O[:, h*128 ..] += P_j V_j[:, h*128 ..]
           const int slot = (item * SPT + h) % kSlots;
           const uint32_t vb = sbase + Lay::RING + slot * kSlotBytes;
 #pragma unroll
@@ -373,10 +377,9 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
                 sdesc(vb + s * 16 * 128, kBoxBytes, 1024), ID_PV, (j > 0 || s > 0) ? 1u : 0u);
           commit(&bars.empty[slot]);
         }
-        ++item;
-        if (ok) commit(&bars.pv_done);
+        commit(&bars.pv_done);
       }
-      commit(&bars.drain);  // completes once every MMA issued above has finished
+      commit(&bars.drain);
     }
   } else {
     // ------------------------------------------------------------------------------------------ softmax warps
