@@ -186,6 +186,27 @@ int janus_b200_moe_grouped_w4a16(const void* x, int64_t ldx, const uint8_t* code
 int janus_b200_moe_combine(const void* y, int64_t k, const void* shared, const float* shared_gate_logit, int64_t S,
                            int64_t H, void* out, void* stream);
 
+/* Expert-parallel MoE (no counterpart in the reference, which runs on one device): the tile plan of
+ * janus_b200_moe_route built from explicit slot -> expert ids instead of router logits. expert_ids int32 [n]
+ * (slot a = row * k + j; an id < 0 or >= E means the slot has no expert here and is skipped); outputs as
+ * janus_b200_moe_route (sorted_ids hold slot indices, -1 padding; the tile count stays on the device).
+ * Used by the receiving rank of an expert-parallel dispatch, whose rows carry their local expert ids. */
+int janus_b200_moe_plan(const int32_t* expert_ids, int64_t n, int64_t E, int64_t tile_rows, int32_t* sorted_ids,
+                        int32_t* tile_expert, int64_t max_tiles, int32_t* n_tiles, int32_t* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/* out[r] = sum over the slots j of row r with slot_expert[r*k + j] >= 0 (all slots when slot_expert is NULL) of
+ * y[r*k + j], in fp32 and slot order (y bf16 [R*k, H], out fp32 [R, H]): the per-rank partial of the expert sum
+ * that an expert-parallel combine sends back. No counterpart in the reference. */
+int janus_b200_moe_reduce_slots(const void* y, int64_t k, const int32_t* slot_expert, int64_t R, int64_t H, float* out,
+                                void* stream);
+
+/* out[t] = sum over ranks w = 0..W-1 with row_index[t*W + w] >= 0 of partials[row_index[t*W + w]] (fp32, rank order)
+ * + sigmoid(shared_gate_logit[t]) * shared[t], rounded once to bf16 [S, H]: the owner's side of the
+ * expert-parallel combine (janus_b200_moe_combine with the k expert rows replaced by per-rank partial sums). */
+int janus_b200_moe_combine_ep(const float* partials, const int32_t* row_index, int64_t W, const void* shared,
+                              const float* shared_gate_logit, int64_t S, int64_t H, void* out, void* stream);
+
 /* The PointerHead readout of janus_b200_head_pointer for callers that cannot allocate device memory: it takes no
  * workspace and allocates nothing; the projected rows go to a static 1 MiB device array inside this library
  * (kept by every GPU that loads the library until the process exits). Limit: (n + Q) * R <= 262144 floats (2048

@@ -44,6 +44,11 @@ SIGNATURES = {
                                      c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64,
                                      c_void_p],
     "janus_b200_moe_combine": [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p],
+    "janus_b200_moe_plan": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
+                            c_size_t, c_void_p],
+    "janus_b200_moe_reduce_slots": [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p],
+    "janus_b200_moe_combine_ep": [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
+                                  c_void_p],
     "janus_b200_head_pointer_noalloc": [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_void_p,
                                         c_float, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_int64, c_void_p,
                                         c_void_p],

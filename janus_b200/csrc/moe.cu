@@ -147,8 +147,17 @@ __global__ void route_scatter_kernel(const int32_t* __restrict__ topk_idx, int64
   int32_t* cursors = ws + 2 * E;
   for (int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; a < n; a += (int64_t)gridDim.x * blockDim.x) {
     const int e = topk_idx[a];
+    if (e < 0 || e >= E) continue;  // a slot without an expert here (expert-parallel plans)
     const int pos = offsets[e] + atomicAdd(&cursors[e], 1);
     sorted_ids[pos] = (int32_t)a;
+  }
+}
+
+// per-expert counts of explicit slot -> expert ids (negative or >= E: no expert)
+__global__ void plan_count_kernel(const int32_t* __restrict__ ids, int64_t n, int E, int32_t* __restrict__ counts) {
+  for (int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; a < n; a += (int64_t)gridDim.x * blockDim.x) {
+    const int e = ids[a];
+    if (e >= 0 && e < E) atomicAdd(&counts[e], 1);
   }
 }
 
@@ -300,6 +309,53 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int k, c
   }
 }
 
+// out[r] = sum over the slots j of row r that have an expert of y[r*k + j], in fp32 (slot order)
+__global__ void reduce_slots_kernel(const __nv_bfloat16* __restrict__ y, int k, const int32_t* __restrict__ slot_expert,
+                                    int64_t R, int H, float* __restrict__ out) {
+  const int64_t n = R * (H / 8);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / (H / 8);
+    const int c = (int)(i - r * (H / 8)) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, v[8];
+    for (int j = 0; j < k; ++j) {
+      if (slot_expert && slot_expert[r * k + j] < 0) continue;
+      load8(y + (r * k + j) * H + c, v);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc[u] += v[u];
+    }
+    float4* o = reinterpret_cast<float4*>(out + r * H + c);
+    o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  }
+}
+
+// out[t] = sum over the ranks w (in rank order) of partials[row_index[t, w]] (fp32) + sigmoid(gate) * shared[t]
+__global__ void combine_ep_kernel(const float* __restrict__ partials, const int32_t* __restrict__ row_index, int W,
+                                  const __nv_bfloat16* __restrict__ shared, const float* __restrict__ gate_logit,
+                                  int64_t S, int H, __nv_bfloat16* __restrict__ out) {
+  const int64_t n = S * (H / 8);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / (H / 8);
+    const int c = (int)(i - t * (H / 8)) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, v[8];
+    for (int w = 0; w < W; ++w) {
+      const int32_t r = row_index[t * W + w];
+      if (r < 0) continue;
+      const float4* p = reinterpret_cast<const float4*>(partials + (int64_t)r * H + c);
+      const float4 a = p[0], b = p[1];
+      acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+      acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+    }
+    if (shared) {
+      const float gsig = sigmoidf_(gate_logit[t]);
+      load8(shared + t * H + c, v);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc[u] += gsig * v[u];
+    }
+    store8(out + t * H + c, acc);
+  }
+}
+
 }  // namespace
 }  // namespace jb
 
@@ -391,4 +447,69 @@ extern "C" int janus_b200_moe_combine(const void* y, int64_t k, const void* shar
       (const __nv_bfloat16*)y, (int)k, (const __nv_bfloat16*)shared, shared_gate_logit, S, (int)H,
       (__nv_bfloat16*)out);
   return launch_status("moe_combine");
+}
+
+extern "C" int janus_b200_moe_plan(const int32_t* expert_ids, int64_t n, int64_t E, int64_t tile_rows,
+                                   int32_t* sorted_ids, int32_t* tile_expert, int64_t max_tiles, int32_t* n_tiles,
+                                   int32_t* workspace, size_t workspace_bytes, void* stream) {
+  JB_REQUIRE((expert_ids || n == 0) && sorted_ids && tile_expert && n_tiles, JANUS_ERR_INVALID,
+             "moe_plan: null pointer");
+  JB_REQUIRE(n >= 0 && n <= 0x7fffffff && E > 0 && E <= 1024 && tile_rows == BM, JANUS_ERR_INVALID,
+             "moe_plan: n %lld, E %lld (<= 1024), tile rows %lld (must be %d)", (long long)n, (long long)E,
+             (long long)tile_rows, BM);
+  const int64_t need_tiles = (n + E * (tile_rows - 1) + tile_rows - 1) / tile_rows;
+  JB_REQUIRE(max_tiles >= need_tiles, JANUS_ERR_INVALID, "moe_plan: max_tiles %lld < worst case %lld",
+             (long long)max_tiles, (long long)need_tiles);
+  JB_REQUIRE(workspace && workspace_bytes >= (size_t)(3 * E) * sizeof(int32_t), JANUS_ERR_WORKSPACE,
+             "moe_plan: workspace needs %lld bytes", (long long)(3 * E * 4));
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t rows = max_tiles * tile_rows;
+  route_init_kernel<<<(unsigned)std::min<int64_t>(148 * 8, (rows + 255) / 256 + 1), 256, 0, s>>>(workspace, (int)E,
+                                                                                                 sorted_ids, rows);
+  int st = launch_status("moe_plan/init");
+  if (st) return st;
+  if (n > 0) {
+    plan_count_kernel<<<(unsigned)std::min<int64_t>(148 * 8, (n + 255) / 256), 256, 0, s>>>(expert_ids, n, (int)E,
+                                                                                             workspace);
+    st = launch_status("moe_plan/count");
+    if (st) return st;
+  }
+  route_plan_kernel<<<1, 256, E * sizeof(int32_t), s>>>(workspace, (int)E, (int)tile_rows, tile_expert, max_tiles,
+                                                        n_tiles);
+  st = launch_status("moe_plan/plan");
+  if (st) return st;
+  if (n > 0) {
+    route_scatter_kernel<<<(unsigned)std::min<int64_t>(148 * 8, (n + 255) / 256), 256, 0, s>>>(expert_ids, n,
+                                                                                               workspace, (int)E,
+                                                                                               sorted_ids);
+    st = launch_status("moe_plan/scatter");
+  }
+  return st;
+}
+
+extern "C" int janus_b200_moe_reduce_slots(const void* y, int64_t k, const int32_t* slot_expert, int64_t R, int64_t H,
+                                           float* out, void* stream) {
+  JB_REQUIRE(out && (y || R == 0) && k > 0 && R >= 0 && H > 0 && H % 8 == 0, JANUS_ERR_INVALID,
+             "moe_reduce_slots: arguments");
+  JB_REQUIRE(JB_ALIGNED(y, 16) && JB_ALIGNED(out, 16), JANUS_ERR_ALIGNMENT, "moe_reduce_slots: alignment");
+  if (R == 0) return JANUS_OK;
+  const int64_t n = R * (H / 8);
+  reduce_slots_kernel<<<(unsigned)std::min<int64_t>(148 * 32, (n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      (const __nv_bfloat16*)y, (int)k, slot_expert, R, (int)H, out);
+  return launch_status("moe_reduce_slots");
+}
+
+extern "C" int janus_b200_moe_combine_ep(const float* partials, const int32_t* row_index, int64_t W, const void* shared,
+                                         const float* shared_gate_logit, int64_t S, int64_t H, void* out,
+                                         void* stream) {
+  JB_REQUIRE(out && row_index && W > 0 && S >= 0 && H > 0 && H % 8 == 0, JANUS_ERR_INVALID,
+             "moe_combine_ep: arguments");
+  JB_REQUIRE(!shared || shared_gate_logit, JANUS_ERR_INVALID, "moe_combine_ep: shared expert needs its gate logits");
+  JB_REQUIRE(JB_ALIGNED(partials, 16) && JB_ALIGNED(out, 16) && (!shared || JB_ALIGNED(shared, 16)),
+             JANUS_ERR_ALIGNMENT, "moe_combine_ep: alignment");
+  if (S == 0) return JANUS_OK;
+  const int64_t n = S * (H / 8);
+  combine_ep_kernel<<<(unsigned)std::min<int64_t>(148 * 32, (n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      partials, row_index, (int)W, (const __nv_bfloat16*)shared, shared_gate_logit, S, (int)H, (__nv_bfloat16*)out);
+  return launch_status("moe_combine_ep");
 }

@@ -27,12 +27,15 @@ class _Layer:
 
 class DecisionReadout:
     """One model on one CUDA device. `weights`: name -> tensor (janus_b200.synthetic.make_weights layout, HF names),
-    on any device; `mode`: "tree" (ScalarHead per leaf) or "listwise" (PointerHead)."""
+    on any device; `mode`: "tree" (ScalarHead per leaf) or "listwise" (PointerHead). `ep`: a
+    janus_b200.ep.ExpertParallel for MoE shapes served expert-parallel (this rank keeps only its experts; every rank
+    of the group must run the same levels)."""
 
-    def __init__(self, shape: ModelShape, weights, mode="tree", device="cuda"):
+    def __init__(self, shape: ModelShape, weights, mode="tree", device="cuda", ep=None):
         if mode not in ("tree", "listwise"):
             raise ValueError("mode must be tree or listwise")
         self.shape, self.mode = shape, mode
+        self.ep = ep if shape.moe else None
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("janus_b200 runs on CUDA devices only")
@@ -61,9 +64,11 @@ class DecisionReadout:
             m = p + "mlp."
             if shape.moe:
                 L.router = w(m + "gate.weight")
-                u8 = lambda n: weights[n].to(dev).contiguous()
-                L.gu_codes, L.gu_scales = u8(m + "experts.gate_up_proj"), w(m + "experts.gate_up_proj.scales")
-                L.dn_codes, L.dn_scales = u8(m + "experts.down_proj"), w(m + "experts.down_proj.scales")
+                part = self.ep.shard if self.ep is not None else (lambda t: t)
+                u8 = lambda n: part(weights[n]).to(dev).contiguous()
+                bf = lambda n: part(weights[n]).to(dev, torch.bfloat16).contiguous()
+                L.gu_codes, L.gu_scales = u8(m + "experts.gate_up_proj"), bf(m + "experts.gate_up_proj.scales")
+                L.dn_codes, L.dn_scales = u8(m + "experts.down_proj"), bf(m + "experts.down_proj.scales")
                 L.shared_gate_up = torch.cat([w(m + "shared_expert.gate_proj.weight"), w(m + "shared_expert.up_proj.weight")])
                 L.shared_down = w(m + "shared_expert.down_proj.weight")
                 L.shared_gate = w(m + "shared_expert_gate.weight")
@@ -137,11 +142,31 @@ class DecisionReadout:
         k = self.shape.top_k
         logits = torch.mm(y, L.router.t(), out_dtype=torch.float32)
         plan = ops.moe_route(logits, k)
+        if self.ep is not None:
+            return self._moe_ep(y, L, plan[0], plan[1])
         h = ops.moe_grouped_w4a16(y, L.gu_codes, L.gu_scales, plan, True, k)
         y2 = ops.moe_grouped_w4a16(h, L.dn_codes, L.dn_scales, plan, False, k, topk_w=plan[1])
         shared = F.linear(ops.silu_mul(F.linear(y, L.shared_gate_up)), L.shared_down)
         sg = torch.mm(y, L.shared_gate.t(), out_dtype=torch.float32)
         return ops.moe_combine(y2, k, shared, sg.reshape(-1))
+
+    def _moe_ep(self, y, L, topk_idx, topk_w):
+        """The expert-parallel MoE block (janus_b200/ep.py): dispatch rows to the ranks owning their experts, grouped
+        GEMMs over this rank's experts, fp32 partial per received row, combine on the owner with the shared expert."""
+        k, ep = self.shape.top_k, self.ep
+        (rows, slot_e, slot_w), handle = ep.dispatch(y, topk_idx, topk_w)
+        H = y.shape[1]
+        if rows.shape[0]:
+            plan = ops.moe_plan(slot_e, ep.local)
+            h = ops.moe_grouped_w4a16(rows, L.gu_codes, L.gu_scales, plan, True, k)
+            y2 = ops.moe_grouped_w4a16(h, L.dn_codes, L.dn_scales, plan, False, k, topk_w=slot_w.reshape(-1))
+            part = ops.moe_reduce_slots(y2, k, slot_e)
+        else:
+            part = torch.empty(0, H, dtype=torch.float32, device=y.device)
+        shared = F.linear(ops.silu_mul(F.linear(y, L.shared_gate_up)), L.shared_down)
+        sg = torch.mm(y, L.shared_gate.t(), out_dtype=torch.float32)
+        back, row_index = ep.combine(part, handle)
+        return ops.moe_combine_ep(back, row_index, shared, sg.reshape(-1))
 
     CHUNK_MIN_TOKENS = 32  # mean row length from which a level runs the chunked rule (rows are read once per chunk)
 

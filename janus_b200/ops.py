@@ -328,3 +328,51 @@ def moe_combine(y, k, shared, shared_gate_logit, out=None):
     _lib.check(_lib.load().janus_b200_moe_combine(_ptr(y), k, _ptr(shared), _ptr(shared_gate_logit), S, H, _ptr(out),
                                                   _stream(y)), "moe_combine")
     return out
+
+
+# ------------------------------------------------------------------------------------------ expert parallel
+
+@_instrument("moe_plan", 4)
+def moe_plan(slot_expert, E):
+    """Tile plan from explicit slot -> local expert ids (int32 [R, k], negative = no expert on this rank):
+    (slot_expert, None, sorted_ids, tile_expert, n_tiles), the structure moe_grouped_w4a16 takes."""
+    _need(slot_expert, I32, "slot_expert")
+    R, k = slot_expert.shape
+    dev = slot_expert.device
+    mt = moe_max_tiles(R, E, k)
+    sorted_ids = torch.empty(mt * MOE_TILE, dtype=I32, device=dev)
+    tile_expert = torch.empty(mt, dtype=I32, device=dev)
+    n_tiles = torch.empty(1, dtype=I32, device=dev)
+    ws = torch.empty(3 * E, dtype=I32, device=dev)
+    _lib.check(_lib.load().janus_b200_moe_plan(_ptr(slot_expert), R * k, E, MOE_TILE, _ptr(sorted_ids),
+                                               _ptr(tile_expert), mt, _ptr(n_tiles), _ptr(ws), ws.numel() * 4,
+                                               _stream(slot_expert)), "moe_plan")
+    return slot_expert, None, sorted_ids, tile_expert, n_tiles
+
+
+@_instrument("moe_reduce_slots", 1)
+def moe_reduce_slots(y, k, slot_expert, out=None):
+    """fp32 [R, H]: per row the sum of its slots' expert outputs (bf16 [R*k, H]) that have an expert here."""
+    _need(y, BF16, "y")
+    R, H = y.shape[0] // k, y.shape[1]
+    out = torch.empty(R, H, dtype=F32, device=y.device) if out is None else out
+    if slot_expert is not None:
+        _need(slot_expert, I32, "slot_expert")
+    _lib.check(_lib.load().janus_b200_moe_reduce_slots(_ptr(y), k, _ptr(slot_expert), R, H, _ptr(out), _stream(y)),
+               "moe_reduce_slots")
+    return out
+
+
+@_instrument("moe_combine_ep", 1)
+def moe_combine_ep(partials, row_index, shared, shared_gate_logit, out=None):
+    """bf16 [S, H] = sum over ranks of the partial rows row_index [S, W] (-1: none) + sigmoid(gate) * shared."""
+    _need(partials, F32, "partials"); _need(row_index, I32, "row_index")
+    S, W = row_index.shape
+    H = partials.shape[1]
+    out = torch.empty(S, H, dtype=BF16, device=row_index.device) if out is None else out
+    if shared is not None:
+        _need(shared, BF16, "shared"); _need(shared_gate_logit, F32, "shared_gate_logit")
+    _lib.check(_lib.load().janus_b200_moe_combine_ep(_ptr(partials), _ptr(row_index), W, _ptr(shared),
+                                                     _ptr(shared_gate_logit), S, H, _ptr(out), _stream(row_index)),
+               "moe_combine_ep")
+    return out

@@ -76,3 +76,46 @@ def test_grouped_w4a16_gemms_and_combine(S, E, k, H, I):
     ref += torch.sigmoid(sg)[:, None] * shared.float()
     scale = ref.abs().max().item()
     np.testing.assert_allclose(out.float().cpu().numpy(), ref.numpy(), atol=2e-2 * scale, rtol=2e-2)
+
+
+@pytest.mark.parametrize("S,E,k,W", [(5, 8, 2, 2), (300, 32, 8, 4), (256, 256, 8, 8)])
+def test_expert_parallel_kernels_emulated_on_one_gpu(S, E, k, W):
+    """moe_plan / moe_reduce_slots / moe_combine_ep as W ranks would run them (every token sent to every rank,
+    each rank holding E/W experts), on one GPU: equal to the single-device route + GEMMs + combine."""
+    ops = _ops()
+    H, I = 256, 128
+    g = torch.Generator().manual_seed(S + W)
+    x = torch.randn(S, H, generator=g).to(torch.bfloat16).cuda()
+    logits = torch.randn(S, E, generator=g).cuda()
+    gu_codes, gu_scales = (t.cuda() for t in _experts(E, 2 * I, H, 21))
+    dn_codes, dn_scales = (t.cuda() for t in _experts(E, H, I, 22))
+    shared = torch.randn(S, H, generator=g).to(torch.bfloat16).cuda()
+    sg = torch.randn(S, generator=g).cuda()
+    plan = ops.moe_route(logits, k)
+    y2 = ops.moe_grouped_w4a16(ops.moe_grouped_w4a16(x, gu_codes, gu_scales, plan, True, k), dn_codes, dn_scales,
+                               plan, False, k, topk_w=plan[1])
+    ref = ops.moe_combine(y2, k, shared, sg)
+    idx, wts = plan[0], plan[1]
+    L = E // W
+    parts = []
+    for r in range(W):
+        local = idx - r * L
+        slot_e = torch.where((local >= 0) & (local < L), local, torch.full_like(local, -1)).to(torch.int32)
+        rp = ops.moe_plan(slot_e.contiguous(), L)
+        sl = slice(r * L, (r + 1) * L)
+        hh = ops.moe_grouped_w4a16(x, gu_codes[sl].contiguous(), gu_scales[sl].contiguous(), rp, True, k)
+        yy = ops.moe_grouped_w4a16(hh, dn_codes[sl].contiguous(), dn_scales[sl].contiguous(), rp, False, k,
+                                   topk_w=wts.reshape(-1))
+        parts.append(ops.moe_reduce_slots(yy, k, slot_e))
+    partials = torch.cat(parts)
+    row_index = (torch.arange(S, device="cuda")[:, None] + S * torch.arange(W, device="cuda")[None, :]).to(torch.int32)
+    got = ops.moe_combine_ep(partials, row_index.contiguous(), shared, sg)
+    torch.cuda.synchronize()
+    # the same bf16 expert rows summed in another fp32 order: equal up to the final bf16 rounding
+    np.testing.assert_allclose(got.float().cpu().numpy(), ref.float().cpu().numpy(), atol=2e-2, rtol=1e-2)
+    # plan of explicit ids: every slot with an expert exactly once, -1 slots never
+    n = int(rp[4].item())
+    ids = rp[2].cpu().numpy()[: n * 64]
+    live = np.sort(ids[ids >= 0])
+    expect = np.nonzero(slot_e.cpu().numpy().reshape(-1) >= 0)[0]
+    np.testing.assert_array_equal(live, expect)
