@@ -134,6 +134,12 @@ int janus_b200_tree_attention(const void* q, int64_t T, int64_t Hq, int64_t Hkv,
                               int64_t gate_stride, int64_t gate_head_stride, float scale, void* out, int32_t* status,
                               void* stream);
 
+/* Self-test of the device-side failure detection (no counterpart in the reference): launches one thread that waits
+ * on a barrier phase nothing completes, with the same bounded wait as janus_b200_tree_attention; after about 1 s the
+ * wait gives up and sets *status (device int32, zero on entry) to 1. Nothing faults or traps, so the context stays
+ * usable; tests use it to check that a wait that runs out is reported instead of hanging. */
+int janus_b200_selftest_wait_timeout(int32_t* status, void* stream);
+
 /* The largest number of query tokens per tile janus_b200_tree_attention accepts for this head dim and GQA layout
  * (128 rows of the tensor-core tile, or 64, divided by Hq/Hkv); 0 for an unsupported layout.
  * The tiling of the query axis that `_piece` bounds by PIECE_BYTES (janus/hybrid.py:407-420). */

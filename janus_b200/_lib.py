@@ -33,6 +33,7 @@ SIGNATURES = {
                                   c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_float,
                                   c_void_p, c_void_p, c_void_p],
     "janus_b200_tree_attention_tile_tokens": [c_int64, c_int64, c_int64],
+    "janus_b200_selftest_wait_timeout": [c_void_p, c_void_p],
     "janus_b200_head_scalar": [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_float, c_void_p, c_void_p, c_float,
                                c_void_p, c_void_p, c_void_p, c_void_p],
     "janus_b200_head_pointer": [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_float,

@@ -394,9 +394,16 @@ int tree_attention_tc(const void* q, int64_t Hq, int64_t Hkv, int64_t D, int32_t
                       const void* gate, int64_t gate_stride, int64_t gate_head_stride, float scale, void* out,
                       int32_t* err, cudaStream_t stream);
 
+int wait_timeout_selftest(int32_t* status, cudaStream_t stream);
+
 }  // namespace jb
 
 using namespace jb;
+
+extern "C" int janus_b200_selftest_wait_timeout(int32_t* status, void* stream) {
+  JB_REQUIRE(status, JANUS_ERR_INVALID, "selftest_wait_timeout: null status");
+  return wait_timeout_selftest(status, (cudaStream_t)stream);
+}
 
 extern "C" int janus_b200_tree_attention_tile_tokens(int64_t D, int64_t Hq, int64_t Hkv) {
   if (Hq <= 0 || Hkv <= 0 || Hq % Hkv) return 0;

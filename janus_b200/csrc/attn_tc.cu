@@ -539,6 +539,18 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(kTmemCols));
 }
 
+// Self-test of the bounded wait used above: one thread waits on an mbarrier phase that nothing completes; the
+// wait gives up after kWaitNs, sets the status word and the kernel returns (no trap, no fault; the context stays
+// usable).
+__global__ void wait_timeout_selftest_kernel(int32_t* status) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    bar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    wait_bar(&bar, 0, status);  // phase 0 never completes: nobody arrives
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ host side
 
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -595,6 +607,11 @@ int launch(const Params& p, int64_t n_tiles, cudaStream_t s) {
 }
 
 }  // namespace tc
+
+int wait_timeout_selftest(int32_t* status, cudaStream_t stream) {
+  tc::wait_timeout_selftest_kernel<<<1, 32, 0, stream>>>(status);
+  return launch_status("wait_timeout_selftest");
+}
 
 int tree_attention_tc(const void* q, int64_t Hq, int64_t Hkv, int64_t D, int32_t n_levels, const void* const* k_levels,
                       const void* const* v_levels, const int64_t* level_tokens, const int32_t* const* anc_lo,

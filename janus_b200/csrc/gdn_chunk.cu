@@ -319,7 +319,7 @@ struct StateSmem {
   __nv_bfloat16 qk[CT * CT];   // masked decayed scale Q K^T
   __nv_bfloat16 s[DH * DB];    // S slice (bf16) [dk][dv]
   __nv_bfloat16 vn[CT * DB];   // V' slice [tok][dv]
-  __nv_bfloat16 vnd[CT * DB];  // V' e^(G_last - G)
+  __nv_bfloat16 vnd[CT * DB];  // the chunk's U slice [tok][dv], replaced in place by V' e^(G_last - G)
   float G[CT];
 };
 
@@ -378,6 +378,16 @@ __global__ void __launch_bounds__(128, 3) gdn_chunk_state_kernel(
       const int r = x / (CT / 8), ch = (x % (CT / 8)) * 8;
       cpa16(&sm.qk[sw<CT>(r, ch)], qkc + r * CT + ch, true);
     }
+    for (int x = tid; x < CT * (DB / 8); x += 128) {  // this slice of U (zeros past the row's end)
+      const int r = x / (DB / 8), ch = (x % (DB / 8)) * 8;
+      const bool ok = r < nt;
+      cpa16(&sm.vnd[sw<DB>(r, ch)], Ug + ((ok ? t0 + r : t0) * Hv + h) * DH + c0 + ch, ok);
+    }
+    if (tid < CT) {  // G of the chunk, zeros past the row's end (g = 0 there: the cumulative sum stays flat)
+      const bool ok = tid < nt;
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s32(&sm.G[tid])),
+                   "l"(Gg + ((ok ? t0 + tid : t0) * Hv + h)), "r"(ok ? 4 : 0));
+    }
   };
   if (cbeg < cend) {
     load_w(cbeg);
@@ -387,7 +397,6 @@ __global__ void __launch_bounds__(128, 3) gdn_chunk_state_kernel(
   for (int c = cbeg; c < cend; ++c) {
     const int64_t t0 = chunk_t0(c);
     const int nt = chunk_nt(c);
-    if (tid < CT) sm.G[tid] = tid < nt ? Gg[(t0 + tid) * Hv + h] : 0.f;
     // bf16 copy of the state slice (rows of this warp)
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt)
@@ -425,9 +434,8 @@ __global__ void __launch_bounds__(128, 3) gdn_chunk_state_kernel(
 #pragma unroll
         for (int e = 0; e < 4; e += 2) {
           const int i = e ? rb : ra, j = n * 8 + (lane & 3) * 2;
-          float2 u = make_float2(0.f, 0.f);
-          if (i < nt)
-            u = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(Ug + ((t0 + i) * Hv + h) * DH + c0 + j));
+          // this thread reads U at (i, j) and then overwrites the same two elements with V' e^(Gl - G)
+          const float2 u = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sm.vnd[sw<DB>(i, j)]));
           const float v0 = u.x - P[n][e], v1 = u.y - P[n][e + 1];
           const float fk = e ? fkb : fka;
           *reinterpret_cast<__nv_bfloat162*>(&sm.vn[sw<DB>(i, j)]) = __floats2bfloat162_rn(v0, v1);

@@ -198,6 +198,14 @@ def attn_qk_prep(qkv, positions, inv_freq, q_norm_w, k_norm_w, eps, Hq, Hkv, D, 
     return q, k, v
 
 
+def selftest_wait_timeout(device="cuda"):
+    """Run the device-side wait self-test (a wait on a barrier phase nothing completes, bounded at ~1 s) and return
+    the status word it set (1: the wait ran out and was reported)."""
+    status = torch.zeros(1, dtype=I32, device=device)
+    _lib.check(_lib.load().janus_b200_selftest_wait_timeout(_ptr(status), _stream(status)), "selftest_wait_timeout")
+    return int(status.item())
+
+
 def tree_attention_tile_tokens(D, Hq, Hkv):
     """Query tokens per attention tile the library accepts for this layout."""
     n = _lib.load().janus_b200_tree_attention_tile_tokens(D, Hq, Hkv)
