@@ -88,20 +88,22 @@ int janus_b200_gdn_fork_recurrent(const void* q, const void* k, const void* v, c
 
 /* Gated delta rule in 64-token chunks for long rows (the state level), two launches: a fully parallel pass per
  * (chunk, value head) computes the intra-chunk WY form (K K^T, the triangular inverse, U = T V beta,
- * W = T K beta e^G, the decayed Q K^T) on the tensor cores into `workspace`; a second pass per (row, value head,
- * 32 value columns) carries the fp32 state across the row's chunks and writes o bf16 [T, Hv, Dv]. chunk_start
- * [B+1]: the first chunk of each row (prefix sum of ceil(rows' lengths / 64)), n_chunks = chunk_start[B]. Row b
- * starts from state_in[state_row[b]] ([*, Hv, Dk, Dv] fp32, read in place; state_row NULL: row b; state_in NULL:
- * zeros); state_out [B, Hv, Dk, Dv] (NULL: not kept). Dk = Dv = 128. workspace: 256-byte aligned, at least
- * janus_b200_gdn_chunk_scan_workspace(T, n_chunks, Hv) bytes. Same results as janus_b200_gdn_fork_recurrent up to
- * fp32/bf16 accumulation order.
+ * W = T K beta e^G, the decayed Q K^T) on the tensor cores into `workspace` (chunk-major); a second pass per
+ * (row, value head) carries the fp32 state across the row's chunks in TMEM (tcgen05) and writes o bf16
+ * [T, Hv, Dv]. chunk_start [B+1]: the first chunk of each row (prefix sum of ceil(rows' lengths / 64)),
+ * n_chunks = chunk_start[B]. Row b starts from state_in[state_row[b]] ([*, Hv, Dk, Dv] fp32, read in place;
+ * state_row NULL: row b; state_in NULL: zeros); state_out [B, Hv, Dk, Dv] (NULL: not kept). Dk = Dv = 128; q, k,
+ * v, o 16-byte aligned. workspace: 256-byte aligned, at least janus_b200_gdn_chunk_scan_workspace(T, n_chunks, Hv)
+ * bytes. status: optional device int32, zero on entry, set to 1 if a bounded device-side wait ran out (after 1 s;
+ * the output is then invalid); NULL: not reported. Same results as janus_b200_gdn_fork_recurrent up to fp32/bf16
+ * accumulation order.
  * Replaces fla chunk_gated_delta_rule (janus/hybrid.py:100-125, 1064-1069; transformers
  * torch_chunk_gated_delta_rule). */
 int janus_b200_gdn_chunk_scan(const void* q, const void* k, const void* v, const float* g, const float* beta,
                               int64_t T, int64_t B, const int32_t* row_start, const int32_t* chunk_start,
                               int64_t n_chunks, const float* state_in, const int32_t* state_row, float* state_out,
                               int64_t Hk, int64_t Hv, int64_t Dk, int64_t Dv, float scale, void* workspace,
-                              size_t workspace_bytes, void* o, void* stream);
+                              size_t workspace_bytes, void* o, int32_t* status, void* stream);
 
 /* Workspace bytes janus_b200_gdn_chunk_scan needs for T tokens, n_chunks chunks and Hv value heads. */
 size_t janus_b200_gdn_chunk_scan_workspace(int64_t T, int64_t n_chunks, int64_t Hv);

@@ -16,7 +16,7 @@ namespace jb {
 constexpr int kProThreads = 256;
 constexpr int kMaxTaps = 8;
 constexpr int kProTokens = 96;  // tokens per CTA: each thread slides its conv window over them
-constexpr int kProBatch = 6;    // token loads a thread has in flight at once
+constexpr int kProBatch = 4;    // token loads a thread has in flight at once
 
 // grid (token tiles of kProTokens, channel blocks of 8 * kProThreads). Thread = 8 consecutive channels; it keeps the
 // last K-1 conv inputs of its channels in registers while it walks the tile's tokens, so every projection element is
@@ -60,10 +60,17 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
       rows[b] = row_of_token[t];
       if (live) xr[b] = *reinterpret_cast<const bf16x8*>(proj + t * proj_stride + c0);
     }
+    // conv + silu of every token of the batch (the window refills at a row start), then the l2 sums of all of them
+    // reduced together (independent shuffle chains), then the stores
+    float acc[kProBatch][8];
 #pragma unroll
     for (int b = 0; b < kProBatch; ++b) {
       const int64_t t = tb + b;
-      if (t >= t1) break;
+      if (t >= t1) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc[b][u] = 0.f;
+        continue;
+      }
       const int row = rows[b];
       if (row != cur_row) {  // (re)fill the window from the row's earlier tokens or the parent's conv tail
         cur_row = row;
@@ -87,17 +94,12 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
           }
         }
       }
-      float x[8], acc[8];
-      if (live) {
+      float x[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float2 f = __bfloat1622float2(xr[b].h[u]);
-          x[2 * u] = f.x;
-          x[2 * u + 1] = f.y;
-        }
-      } else {
-#pragma unroll
-        for (int u = 0; u < 8; ++u) x[u] = 0.f;
+      for (int u = 0; u < 4; ++u) {
+        const float2 f = live ? __bfloat1622float2(xr[b].h[u]) : make_float2(0.f, 0.f);
+        x[2 * u] = f.x;
+        x[2 * u + 1] = f.y;
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
@@ -109,8 +111,8 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
           a0 += hist[j][2 * u] * wj.x;
           a1 += hist[j][2 * u + 1] * wj.y;
         }
-        acc[2 * u] = bf2f(f2bf(silu_fast(a0)));  // rounded once, as the reference does
-        acc[2 * u + 1] = bf2f(f2bf(silu_fast(a1)));
+        acc[b][2 * u] = bf2f(f2bf(silu_fast(a0)));  // rounded once, as the reference does
+        acc[b][2 * u + 1] = bf2f(f2bf(silu_fast(a1)));
       }
       // slide the window
 #pragma unroll
@@ -119,27 +121,38 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
         for (int u = 0; u < 8; ++u) hist[j][u] = hist[j + 1][u];
 #pragma unroll
       for (int u = 0; u < 8; ++u) hist[K - 2][u] = x[u];
-      // l2 norm over each q / k head: lanes_per_head consecutive lanes hold one head
-      float ss = 0.f;
+      if (live && tail_out && t == r0 + L - 1) {  // the row's last K-1 conv inputs are the window now
 #pragma unroll
-      for (int u = 0; u < 8; ++u) ss += acc[u] * acc[u];
-      for (int o = lanes_per_head >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      if (live) {
+        for (int j = 0; j < K - 1; ++j) store8(tail_out + ((int64_t)row * (K - 1) + j) * C + c0, hist[j]);
+      }
+    }
+    // l2 norm over each q / k head: lanes_per_head consecutive lanes hold one head
+    float ss[kProBatch];
+#pragma unroll
+    for (int b = 0; b < kProBatch; ++b) {
+      ss[b] = 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) ss[b] += acc[b][u] * acc[b][u];
+    }
+    for (int o = lanes_per_head >> 1; o > 0; o >>= 1)
+#pragma unroll
+      for (int b = 0; b < kProBatch; ++b) ss[b] += __shfl_xor_sync(0xffffffffu, ss[b], o);
+    if (live) {
+#pragma unroll
+      for (int b = 0; b < kProBatch; ++b) {
+        const int64_t t = tb + b;
+        if (t >= t1) break;
         if (c0 < 2 * key_dim) {
-          const float r = rsqrtf(ss + 1e-6f);
+          const float r = rsqrtf(ss[b] + 1e-6f);
           float o8[8];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) o8[u] = acc[u] * r;
+          for (int u = 0; u < 8; ++u) o8[u] = acc[b][u] * r;
           if (c0 < key_dim)
             store8(q + t * key_dim + c0, o8);
           else
             store8(k + t * key_dim + (c0 - key_dim), o8);
         } else {
-          store8(v + t * (int64_t)(Hv * Dv) + (c0 - 2 * key_dim), acc);
-        }
-        if (tail_out && t == r0 + L - 1) {  // the row's last K-1 conv inputs are the window now
-#pragma unroll
-          for (int j = 0; j < K - 1; ++j) store8(tail_out + ((int64_t)row * (K - 1) + j) * C + c0, hist[j]);
+          store8(v + t * (int64_t)(Hv * Dv) + (c0 - 2 * key_dim), acc[b]);
         }
       }
     }
@@ -159,63 +172,69 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
 
 // ------------------------------------------------------------------------------------------- fork recurrent rule
 
-template <int DK, int DV>
-__global__ void __launch_bounds__(256) gdn_fork_recurrent_kernel(
+template <int DK, int DV, int NT>
+__global__ void __launch_bounds__(NT) gdn_fork_recurrent_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
     const float* __restrict__ g, const float* __restrict__ beta, const int32_t* __restrict__ row_start,
     const int32_t* __restrict__ child_start, const float* __restrict__ state_in, float* __restrict__ state_out,
     int Hk, int Hv, float scale, __nv_bfloat16* __restrict__ o) {
-  constexpr int NT = 256;
   constexpr int NRG = NT / DV;     // row groups
   constexpr int ROWS = DK / NRG;   // key rows per thread
   static_assert(NT % DV == 0 && DK % NRG == 0, "state tiling");
-  __shared__ float s_k[DK], s_q[DK], s_v[DV], s_red[NRG][DV], s_gb[2];
+  // per token: k, q (scaled), v and (decay, beta) in a double buffer, so the loads of the next token overlap this
+  // one; separate reduction arrays for S^T k and S^T q, so each token needs two barriers
+  __shared__ float s_k[2][DK], s_q[2][DK], s_v[2][DV], s_gb[2][2], s_kv[NRG][DV], s_ov[NRG][DV];
   const int p = blockIdx.x, h = blockIdx.y;
   const int hk = h / (Hv / Hk);
   const int j = threadIdx.x % DV, rg = threadIdx.x / DV;
   const int64_t sbase_in = ((int64_t)p * Hv + h) * DK * DV;
+  const int64_t tbeg = row_start[child_start[p]], tend = row_start[child_start[p + 1]];
+  auto stage = [&](int64_t t, int buf) {  // the token's vectors into buffer buf (children are consecutive rows)
+    for (int x = threadIdx.x; x < DK; x += NT) {
+      s_k[buf][x] = bf2f(k[(t * Hk + hk) * DK + x]);
+      s_q[buf][x] = bf2f(q[(t * Hk + hk) * DK + x]) * scale;
+    }
+    for (int x = threadIdx.x; x < DV; x += NT) s_v[buf][x] = bf2f(v[(t * Hv + h) * DV + x]);
+    if (threadIdx.x == 0) {
+      s_gb[buf][0] = expf(g[t * Hv + h]);
+      s_gb[buf][1] = beta[t * Hv + h];
+    }
+  };
+  if (tbeg < tend) stage(tbeg, 0);
+  int64_t step = 0;  // tokens processed by this CTA: the buffer of token t is step & 1
   for (int c = child_start[p]; c < child_start[p + 1]; ++c) {
     float S[ROWS];
 #pragma unroll
     for (int r = 0; r < ROWS; ++r) S[r] = state_in ? state_in[sbase_in + (int64_t)(rg * ROWS + r) * DV + j] : 0.f;
-    for (int64_t t = row_start[c]; t < row_start[c + 1]; ++t) {
-      __syncthreads();  // the previous token's readers of s_k/s_q/s_v are done
-      for (int x = threadIdx.x; x < DK; x += NT) {
-        s_k[x] = bf2f(k[(t * Hk + hk) * DK + x]);
-        s_q[x] = bf2f(q[(t * Hk + hk) * DK + x]) * scale;
-      }
-      for (int x = threadIdx.x; x < DV; x += NT) s_v[x] = bf2f(v[(t * Hv + h) * DV + x]);
-      if (threadIdx.x == 0) {
-        s_gb[0] = expf(g[t * Hv + h]);
-        s_gb[1] = beta[t * Hv + h];
-      }
-      __syncthreads();
-      const float decay = s_gb[0];
+    for (int64_t t = row_start[c]; t < row_start[c + 1]; ++t, ++step) {
+      const int buf = (int)(step & 1);
+      __syncthreads();  // token t staged; every reader of the other buffer and of s_ov is done
+      if (t + 1 < tend) stage(t + 1, buf ^ 1);
+      const float decay = s_gb[buf][0];
       float kv = 0.f;
 #pragma unroll
       for (int r = 0; r < ROWS; ++r) {
         S[r] *= decay;
-        kv += S[r] * s_k[rg * ROWS + r];
+        kv += S[r] * s_k[buf][rg * ROWS + r];
       }
-      s_red[rg][j] = kv;
+      s_kv[rg][j] = kv;
       __syncthreads();
       kv = 0.f;
 #pragma unroll
-      for (int x = 0; x < NRG; ++x) kv += s_red[x][j];
-      const float delta = (s_v[j] - kv) * s_gb[1];
+      for (int x = 0; x < NRG; ++x) kv += s_kv[x][j];
+      const float delta = (s_v[buf][j] - kv) * s_gb[buf][1];
       float ov = 0.f;
 #pragma unroll
       for (int r = 0; r < ROWS; ++r) {
-        S[r] += s_k[rg * ROWS + r] * delta;
-        ov += S[r] * s_q[rg * ROWS + r];
+        S[r] += s_k[buf][rg * ROWS + r] * delta;
+        ov += S[r] * s_q[buf][rg * ROWS + r];
       }
-      __syncthreads();  // everyone has read s_red (kv) before it is reused for o
-      s_red[rg][j] = ov;
+      s_ov[rg][j] = ov;
       __syncthreads();
       if (rg == 0) {
         float acc = 0.f;
 #pragma unroll
-        for (int x = 0; x < NRG; ++x) acc += s_red[x][j];
+        for (int x = 0; x < NRG; ++x) acc += s_ov[x][j];
         o[(t * Hv + h) * DV + j] = f2bf(acc);
       }
     }
@@ -285,16 +304,16 @@ extern "C" int janus_b200_gdn_fork_recurrent(const void* q, const void* k, const
   JB_REQUIRE(P <= 0x7fffffff && Hv <= 65535, JANUS_ERR_INVALID, "gdn_fork_recurrent: grid too large");
   dim3 grid((unsigned)P, (unsigned)Hv);
   cudaStream_t s = (cudaStream_t)stream;
-#define JB_FORK(DK_, DV_)                                                                                        \
-  gdn_fork_recurrent_kernel<DK_, DV_><<<grid, 256, 0, s>>>(                                                      \
+#define JB_FORK(DK_, DV_, NT_)                                                                                 \
+  gdn_fork_recurrent_kernel<DK_, DV_, NT_><<<grid, NT_, 0, s>>>(                                               \
       (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, g, beta, row_start, child_start, \
       state_in, state_out, (int)Hk, (int)Hv, scale, (__nv_bfloat16*)o)
   if (Dk == 128 && Dv == 128) {
-    JB_FORK(128, 128);
+    JB_FORK(128, 128, 512);  // 32 state rows per thread
   } else if (Dk == 64 && Dv == 64) {
-    JB_FORK(64, 64);
+    JB_FORK(64, 64, 256);
   } else if (Dk == 32 && Dv == 32) {
-    JB_FORK(32, 32);
+    JB_FORK(32, 32, 256);
   } else {
     set_error("gdn_fork_recurrent: (Dk, Dv) = (%lld, %lld) not compiled", (long long)Dk, (long long)Dv);
     return JANUS_ERR_UNSUPPORTED;

@@ -7,15 +7,15 @@
 //                                                                    then doubling stages 16 -> 32 -> 64
 //      U  = T (V * beta),  W = T (K * beta * e^G)                    bf16 operands, fp32 accumulate, stored bf16
 //      QK = tril(scale Q K^T * e^(G_i - G_j))                        stored bf16, plus G itself
-// 2. gdn_chunk_state: one CTA per (row, value head, 32 of the 128 value columns) — the columns of the state evolve
-//    independently — walking the row's chunks in order with its fp32 slice of S in registers:
+// 2. the sequential pass (gdn_state_tc.cu, tcgen05): one CTA per (row, value head) walking the row's chunks in
+//    order with the fp32 state in TMEM:
 //      V' = U - W S;   O = scale e^G (Q S) + QK V';   S = e^(G_last) S + K^T (V' * e^(G_last - G))
 //    (S rounded to bf16 for the products, as fla's chunk kernels do; the e^G factors scale rows of fp32 results
-//    instead of the bf16 operands, so q and k are used as loaded). The next chunk's W is loaded while the output
-//    and the state update of this one run. The WY form of transformers'
+//    instead of the bf16 operands, so q and k are used as loaded). The WY form of transformers'
 //    torch_chunk_gated_delta_rule (the reference's CPU rule) and of fla's chunk kernels (its GPU rule). A row's last
 //    chunk is ragged: the missing tokens are zeros with g = beta = 0, which leaves the state untouched.
-// Both kernels use mma.sync m16n8k16 (bf16, fp32 accumulate) on XOR-swizzled shared tiles.
+// The prep writes W, U, QK and G chunk-major ([chunk][value head][64 tokens], zeros past a row's end) for the
+// sequential pass's TMA loads; it uses mma.sync m16n8k16 (bf16, fp32 accumulate) on XOR-swizzled shared tiles.
 #include "common.cuh"
 
 namespace jb {
@@ -23,7 +23,6 @@ namespace {
 
 constexpr int CT = 64;   // chunk tokens
 constexpr int DH = 128;  // Dk = Dv
-constexpr int DB = 32;   // value columns per state CTA
 constexpr int PADF = 65; // fp32 [64][65] tiles
 
 __device__ __forceinline__ uint32_t s32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -144,7 +143,7 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
   __syncthreads();
   if (tid < CT) {
     sm.eG[tid] = expf(sm.G[tid]);
-    if (tid < nt) Gg[(t0 + tid) * Hv + h] = sm.G[tid];
+    Gg[((int64_t)c * Hv + h) * CT + tid] = sm.G[tid];  // chunk-major; past the row's end G stays at G[nt - 1]
   }
   // K K^T -> N (fp32, smem), Q K^T -> QK (bf16, global); warp: m-tile w>>1, n-tiles (w&1)*4 .. +3
   {
@@ -302,237 +301,13 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
 #pragma unroll
     for (int e = 0; e < 4; e += 2) {
       const int i = mt * 16 + (lane >> 2) + (e >> 1) * 8, j = cb + n * 8 + (lane & 3) * 2;
-      if (i < nt) {
-        const int64_t off = ((t0 + i) * Hv + h) * DH + j;
-        *reinterpret_cast<__nv_bfloat162*>(Ug + off) = __floats2bfloat162_rn(U[n][e], U[n][e + 1]);
-        *reinterpret_cast<__nv_bfloat162*>(Wg + off) = __floats2bfloat162_rn(Wacc[n][e], Wacc[n][e + 1]);
-      }
+      // chunk-major [chunk][head][64 tokens][128], zeros past the row's end (the tokens there have no V, K)
+      const int64_t off = (((int64_t)c * Hv + h) * CT + i) * DH + j;
+      const bool in = i < nt;
+      *reinterpret_cast<__nv_bfloat162*>(Ug + off) = __floats2bfloat162_rn(in ? U[n][e] : 0.f, in ? U[n][e + 1] : 0.f);
+      *reinterpret_cast<__nv_bfloat162*>(Wg + off) =
+          __floats2bfloat162_rn(in ? Wacc[n][e] : 0.f, in ? Wacc[n][e + 1] : 0.f);
     }
-}
-
-// ------------------------------------------------------------------------------------------------ state pass
-
-struct StateSmem {
-  __nv_bfloat16 w[CT * DH];    // W
-  __nv_bfloat16 q[CT * DH];    // Q
-  __nv_bfloat16 k[CT * DH];    // K
-  __nv_bfloat16 qk[CT * CT];   // masked decayed scale Q K^T
-  __nv_bfloat16 s[DH * DB];    // S slice (bf16) [dk][dv]
-  __nv_bfloat16 vn[CT * DB];   // V' slice [tok][dv]
-  __nv_bfloat16 vnd[CT * DB];  // the chunk's U slice [tok][dv], replaced in place by V' e^(G_last - G)
-  float G[CT];
-};
-
-__global__ void __launch_bounds__(128, 3) gdn_chunk_state_kernel(
-    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const int32_t* __restrict__ row_start,
-    const int32_t* __restrict__ chunk_start, const float* __restrict__ state_in, const int32_t* __restrict__ state_row,
-    float* __restrict__ state_out, int Hk, int Hv, float scale, const __nv_bfloat16* __restrict__ Wg,
-    const __nv_bfloat16* __restrict__ Ug, const __nv_bfloat16* __restrict__ QKg, const float* __restrict__ Gg,
-    __nv_bfloat16* __restrict__ o) {
-  extern __shared__ __align__(16) unsigned char raw[];
-  StateSmem& sm = *reinterpret_cast<StateSmem*>(raw);
-  // slices fastest: the DH / DB CTAs of one (row, head) read the same W, q, k, QK tiles and run together (L2 hits)
-  const int c0 = blockIdx.x * DB, h = blockIdx.y, row = blockIdx.z;
-  const int hk = h / (Hv / Hk);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  // S slice: warp w owns key rows 32w..32w+31 (2 m-tiles) x DB columns (4 n-tiles)
-  float S[2][4][4];
-  {
-    const float* s0 =
-        state_in ? state_in + ((int64_t)(state_row ? state_row[row] : row) * Hv + h) * DH * DH : nullptr;
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-      for (int n = 0; n < 4; ++n)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int rr = warp * 32 + mt * 16 + (lane >> 2) + (e >> 1) * 8, cc = c0 + n * 8 + (lane & 3) * 2 + (e & 1);
-          S[mt][n][e] = s0 ? s0[rr * DH + cc] : 0.f;
-        }
-  }
-  const int64_t r0 = row_start[row], r1 = row_start[row + 1];
-  const int cbeg = chunk_start[row], cend = chunk_start[row + 1];
-  auto chunk_t0 = [&](int c) { return r0 + (int64_t)(c - cbeg) * CT; };
-  auto chunk_nt = [&](int c) { const int64_t t0 = chunk_t0(c); return (r1 - t0) < CT ? (int)(r1 - t0) : CT; };
-  auto load_w = [&](int c) {
-    const int64_t t0 = chunk_t0(c);
-    const int nt = chunk_nt(c);
-    for (int x = tid; x < CT * (DH / 8); x += 128) {
-      const int r = x / (DH / 8), ch = (x % (DH / 8)) * 8;
-      const bool ok = r < nt;
-      cpa16(&sm.w[sw<DH>(r, ch)], Wg + ((ok ? t0 + r : t0) * Hv + h) * DH + ch, ok);
-    }
-  };
-  auto load_qk = [&](int c) {
-    const int64_t t0 = chunk_t0(c);
-    const int nt = chunk_nt(c);
-    for (int x = tid; x < CT * (DH / 8); x += 128) {
-      const int r = x / (DH / 8), ch = (x % (DH / 8)) * 8;
-      const bool ok = r < nt;
-      const int64_t t = ok ? t0 + r : t0;
-      cpa16(&sm.q[sw<DH>(r, ch)], q + (t * Hk + hk) * DH + ch, ok);
-      cpa16(&sm.k[sw<DH>(r, ch)], k + (t * Hk + hk) * DH + ch, ok);
-    }
-    const __nv_bfloat16* qkc = QKg + ((int64_t)c * Hv + h) * CT * CT;
-    for (int x = tid; x < CT * (CT / 8); x += 128) {
-      const int r = x / (CT / 8), ch = (x % (CT / 8)) * 8;
-      cpa16(&sm.qk[sw<CT>(r, ch)], qkc + r * CT + ch, true);
-    }
-    for (int x = tid; x < CT * (DB / 8); x += 128) {  // this slice of U (zeros past the row's end)
-      const int r = x / (DB / 8), ch = (x % (DB / 8)) * 8;
-      const bool ok = r < nt;
-      cpa16(&sm.vnd[sw<DB>(r, ch)], Ug + ((ok ? t0 + r : t0) * Hv + h) * DH + c0 + ch, ok);
-    }
-    if (tid < CT) {  // G of the chunk, zeros past the row's end (g = 0 there: the cumulative sum stays flat)
-      const bool ok = tid < nt;
-      asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s32(&sm.G[tid])),
-                   "l"(Gg + ((ok ? t0 + tid : t0) * Hv + h)), "r"(ok ? 4 : 0));
-    }
-  };
-  if (cbeg < cend) {
-    load_w(cbeg);
-    load_qk(cbeg);
-    asm volatile("cp.async.commit_group;\n" ::);
-  }
-  for (int c = cbeg; c < cend; ++c) {
-    const int64_t t0 = chunk_t0(c);
-    const int nt = chunk_nt(c);
-    // bf16 copy of the state slice (rows of this warp)
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-      for (int n = 0; n < 4; ++n)
-#pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          const int rr = warp * 32 + mt * 16 + (lane >> 2) + (e >> 1) * 8, cc = n * 8 + (lane & 3) * 2;
-          *reinterpret_cast<__nv_bfloat162*>(&sm.s[sw<DB>(rr, cc)]) =
-              __floats2bfloat162_rn(S[mt][n][e], S[mt][n][e + 1]);
-        }
-    asm volatile("cp.async.wait_group 0;\n" ::);
-    __syncthreads();
-    const float Gl = sm.G[nt - 1];  // padded tokens carry g = 0: the cumulative sum stays at its last value
-    // this thread's two fragment rows: e^G scale for O, e^(Gl - G) for the state update
-    const int ra = warp * 16 + (lane >> 2), rb = ra + 8;
-    const float Ga = ra < nt ? sm.G[ra] : Gl, Gb = rb < nt ? sm.G[rb] : Gl;
-    const float fqa = expf(Ga) * scale, fqb = expf(Gb) * scale, fka = expf(Gl - Ga), fkb = expf(Gl - Gb);
-    // V' = U - W S (warp w: m-tile w, 4 n-tiles); V' and V' e^(Gl - G) to shared memory
-    {
-      float P[4][4] = {};
-#pragma unroll
-      for (int ks = 0; ks < DH; ks += 16) {
-        uint32_t a[4], b[4];
-        lda<DH>(a, sm.w, warp * 16, ks, lane);
-#pragma unroll
-        for (int np = 0; np < 2; ++np) {
-          ldb_kn<DB>(b, sm.s, np * 16, ks, lane);
-          mma(P[2 * np], a, b[0], b[1]);
-          mma(P[2 * np + 1], a, b[2], b[3]);
-        }
-      }
-#pragma unroll
-      for (int n = 0; n < 4; ++n)
-#pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          const int i = e ? rb : ra, j = n * 8 + (lane & 3) * 2;
-          // this thread reads U at (i, j) and then overwrites the same two elements with V' e^(Gl - G)
-          const float2 u = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sm.vnd[sw<DB>(i, j)]));
-          const float v0 = u.x - P[n][e], v1 = u.y - P[n][e + 1];
-          const float fk = e ? fkb : fka;
-          *reinterpret_cast<__nv_bfloat162*>(&sm.vn[sw<DB>(i, j)]) = __floats2bfloat162_rn(v0, v1);
-          *reinterpret_cast<__nv_bfloat162*>(&sm.vnd[sw<DB>(i, j)]) = __floats2bfloat162_rn(v0 * fk, v1 * fk);
-        }
-    }
-    __syncthreads();  // V' visible; sm.w is free
-    if (c + 1 < cend) {
-      load_w(c + 1);
-      asm volatile("cp.async.commit_group;\n" ::);
-    }
-    // O = ((Q S) * e^G scale) + QK V'
-    {
-      float O[4][4] = {};
-#pragma unroll
-      for (int ks = 0; ks < DH; ks += 16) {
-        uint32_t a[4], b[4];
-        lda<DH>(a, sm.q, warp * 16, ks, lane);
-#pragma unroll
-        for (int np = 0; np < 2; ++np) {
-          ldb_kn<DB>(b, sm.s, np * 16, ks, lane);
-          mma(O[2 * np], a, b[0], b[1]);
-          mma(O[2 * np + 1], a, b[2], b[3]);
-        }
-      }
-#pragma unroll
-      for (int n = 0; n < 4; ++n) {
-        O[n][0] *= fqa;
-        O[n][1] *= fqa;
-        O[n][2] *= fqb;
-        O[n][3] *= fqb;
-      }
-#pragma unroll
-      for (int ks = 0; ks < CT; ks += 16) {
-        uint32_t a[4], b[4];
-        lda<CT>(a, sm.qk, warp * 16, ks, lane);
-#pragma unroll
-        for (int np = 0; np < 2; ++np) {
-          ldb_kn<DB>(b, sm.vn, np * 16, ks, lane);
-          mma(O[2 * np], a, b[0], b[1]);
-          mma(O[2 * np + 1], a, b[2], b[3]);
-        }
-      }
-#pragma unroll
-      for (int n = 0; n < 4; ++n)
-#pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          const int i = e ? rb : ra, j = n * 8 + (lane & 3) * 2;
-          if (i < nt)
-            *reinterpret_cast<__nv_bfloat162*>(o + ((t0 + i) * Hv + h) * DH + c0 + j) =
-                __floats2bfloat162_rn(O[n][e], O[n][e + 1]);
-        }
-    }
-    // S = e^(G_last) S + K^T (V' e^(Gl - G))
-    {
-      const float dl = expf(Gl);
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-        for (int n = 0; n < 4; ++n)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) S[mt][n][e] *= dl;
-#pragma unroll
-      for (int ks = 0; ks < CT; ks += 16) {
-        uint32_t b[2][4];
-#pragma unroll
-        for (int np = 0; np < 2; ++np) ldb_kn<DB>(b[np], sm.vnd, np * 16, ks, lane);
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          uint32_t a[4];
-          lda_t<DH>(a, sm.k, warp * 32 + mt * 16, ks, lane);
-#pragma unroll
-          for (int np = 0; np < 2; ++np) {
-            mma(S[mt][2 * np], a, b[np][0], b[np][1]);
-            mma(S[mt][2 * np + 1], a, b[np][2], b[np][3]);
-          }
-        }
-      }
-    }
-    __syncthreads();  // q, k, QK, S and V' tiles are free for the next chunk
-    if (c + 1 < cend) {
-      load_qk(c + 1);
-      asm volatile("cp.async.commit_group;\n" ::);
-    }
-  }
-  if (state_out) {
-    float* so = state_out + ((int64_t)row * Hv + h) * DH * DH;
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-      for (int n = 0; n < 4; ++n)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int rr = warp * 32 + mt * 16 + (lane >> 2) + (e >> 1) * 8, cc = c0 + n * 8 + (lane & 3) * 2 + (e & 1);
-          so[rr * DH + cc] = S[mt][n][e];
-        }
-  }
 }
 
 size_t align_up(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -543,9 +318,16 @@ size_t align_up(size_t x) { return (x + 255) & ~(size_t)255; }
 using namespace jb;
 
 extern "C" size_t janus_b200_gdn_chunk_scan_workspace(int64_t T, int64_t n_chunks, int64_t Hv) {
-  const size_t tok = (size_t)T * Hv;
-  return 2 * align_up(tok * DH * sizeof(__nv_bfloat16)) + align_up((size_t)n_chunks * Hv * CT * CT * 2) +
-         align_up(tok * sizeof(float));
+  (void)T;
+  const size_t rows = (size_t)n_chunks * Hv * CT;  // chunk-major: [chunk][head][64 tokens]
+  return 2 * align_up(rows * DH * sizeof(__nv_bfloat16)) + align_up(rows * CT * 2) + align_up(rows * sizeof(float));
+}
+
+namespace jb {
+int gdn_state_tc(const void* q, const void* k, int64_t T, int64_t B, const int32_t* row_start,
+                 const int32_t* chunk_start, int64_t n_chunks, const float* state_in, const int32_t* state_row,
+                 float* state_out, int64_t Hk, int64_t Hv, float scale, const void* W, const void* U, const void* QK,
+                 const float* G, int32_t* err, void* o, cudaStream_t stream);
 }
 
 extern "C" int janus_b200_gdn_chunk_scan(const void* q, const void* k, const void* v, const float* g,
@@ -553,33 +335,29 @@ extern "C" int janus_b200_gdn_chunk_scan(const void* q, const void* k, const voi
                                          const int32_t* chunk_start, int64_t n_chunks, const float* state_in,
                                          const int32_t* state_row, float* state_out, int64_t Hk, int64_t Hv,
                                          int64_t Dk, int64_t Dv, float scale, void* workspace, size_t workspace_bytes,
-                                         void* o, void* stream) {
+                                         void* o, int32_t* status, void* stream) {
   JB_REQUIRE(q && k && v && g && beta && row_start && chunk_start && o, JANUS_ERR_INVALID,
              "gdn_chunk_scan: null pointer");
   JB_REQUIRE(Dk == DH && Dv == DH, JANUS_ERR_UNSUPPORTED, "gdn_chunk_scan: Dk = Dv = 128 only (got %lld, %lld)",
              (long long)Dk, (long long)Dv);
-  JB_REQUIRE(T >= 0 && B >= 0 && B <= 65535 && n_chunks >= 0 && n_chunks <= 65535 && Hk > 0 && Hv > 0 &&
-                 Hv % Hk == 0 && Hv <= 65535,
+  JB_REQUIRE(T >= 0 && T <= 0x7fffffff && B >= 0 && B <= 65535 && n_chunks >= 0 && n_chunks <= 65535 && Hk > 0 &&
+                 Hv > 0 && Hv % Hk == 0 && Hv <= 65535 && n_chunks * Hv * CT <= 0x7fffffff,
              JANUS_ERR_INVALID, "gdn_chunk_scan: sizes");
-  JB_REQUIRE(JB_ALIGNED(q, 16) && JB_ALIGNED(k, 16) && JB_ALIGNED(v, 16) && JB_ALIGNED(o, 4), JANUS_ERR_ALIGNMENT,
-             "gdn_chunk_scan: alignment");
+  JB_REQUIRE(JB_ALIGNED(q, 16) && JB_ALIGNED(k, 16) && JB_ALIGNED(v, 16) && JB_ALIGNED(o, 16), JANUS_ERR_ALIGNMENT,
+             "gdn_chunk_scan: q, k, v, o must be 16-byte aligned");
   const size_t need = janus_b200_gdn_chunk_scan_workspace(T, n_chunks, Hv);
   JB_REQUIRE(workspace && workspace_bytes >= need && JB_ALIGNED(workspace, 256), JANUS_ERR_WORKSPACE,
              "gdn_chunk_scan: workspace %zu bytes (256-aligned) < %zu", workspace_bytes, need);
   if (B == 0 || T == 0) return JANUS_OK;
-  const size_t tok = (size_t)T * Hv;
+  const size_t rows = (size_t)n_chunks * Hv * CT;
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   __nv_bfloat16* Wg = reinterpret_cast<__nv_bfloat16*>(ws);
-  __nv_bfloat16* Ug = reinterpret_cast<__nv_bfloat16*>(ws + align_up(tok * DH * 2));
-  __nv_bfloat16* QKg = reinterpret_cast<__nv_bfloat16*>(ws + 2 * align_up(tok * DH * 2));
-  float* Gg =
-      reinterpret_cast<float*>(ws + 2 * align_up(tok * DH * 2) + align_up((size_t)n_chunks * Hv * CT * CT * 2));
+  __nv_bfloat16* Ug = reinterpret_cast<__nv_bfloat16*>(ws + align_up(rows * DH * 2));
+  __nv_bfloat16* QKg = reinterpret_cast<__nv_bfloat16*>(ws + 2 * align_up(rows * DH * 2));
+  float* Gg = reinterpret_cast<float*>(ws + 2 * align_up(rows * DH * 2) + align_up(rows * CT * 2));
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e = cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)sizeof(PrepSmem));
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(gdn_chunk_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)sizeof(StateSmem));
   if (e != cudaSuccess) {
     set_error("gdn_chunk_scan: smem attribute: %s", cudaGetErrorString(e));
     return JANUS_ERR_CUDA;
@@ -591,8 +369,6 @@ extern "C" int janus_b200_gdn_chunk_scan(const void* q, const void* k, const voi
     int st = launch_status("gdn_chunk_scan/prep");
     if (st) return st;
   }
-  gdn_chunk_state_kernel<<<dim3(DH / DB, (unsigned)Hv, (unsigned)B), 128, sizeof(StateSmem), s>>>(
-      (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, row_start, chunk_start, state_in, state_row, state_out,
-      (int)Hk, (int)Hv, scale, Wg, Ug, QKg, Gg, (__nv_bfloat16*)o);
-  return launch_status("gdn_chunk_scan/state");
+  return gdn_state_tc(q, k, T, B, row_start, chunk_start, n_chunks, state_in, state_row, state_out, Hk, Hv, scale,
+                      Wg, Ug, QKg, Gg, status, o, s);
 }

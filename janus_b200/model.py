@@ -109,7 +109,7 @@ class DecisionReadout:
                 if self._chunked(lv):
                     o, S = ops.gdn_chunk_scan(q, k, v, g, beta, rs, plan[(d, "chunk_start")], int(lv.chunk_start[-1]),
                                               parent_state[1], plan[(d, "parent")] if d > 0 else None, lv.keep,
-                                              1.0 / math.sqrt(s.lin_k_dim))
+                                              1.0 / math.sqrt(s.lin_k_dim), status=self.status)
                 else:
                     o, S = ops.gdn_fork_recurrent(q, k, v, g, beta, rs, plan[(d, "child_start")], parent_state[1],
                                                   lv.keep, 1.0 / math.sqrt(s.lin_k_dim))
@@ -228,7 +228,8 @@ class DecisionReadout:
     def check_status(self):
         """Raise if a bounded device-side wait of the last run ran out (its results are then invalid)."""
         if int(self.status.item()) != 0:
-            raise _lib.JanusError("tree_attention: a device-side wait ran out; the results of this run are invalid")
+            raise _lib.JanusError("a device-side wait (tree attention or chunk scan) ran out; the results of this run "
+                                  "are invalid")
 
     def forward_many(self, packs):
         """Per pack, per question, the logits as fp32 CPU tensors (janus/model.py:368-373 + :319-366)."""

@@ -246,8 +246,10 @@ def test_gdn_chunk_scan_matches_recurrent_oracle():
     scale = D ** -0.5
     cs = torch.from_numpy(np.concatenate([[0], np.cumsum([(n + 63) // 64 for n in lengths])]).astype(np.int32))
     nc = int(cs[-1])
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
     o, S = ops.gdn_chunk_scan(q.cuda(), k.cuda(), v.cuda(), gg.cuda(), beta.cuda(), rs.cuda(), cs.cuda(), nc,
-                              S0.cuda(), state_row.cuda(), True, scale)
+                              S0.cuda(), state_row.cuda(), True, scale, status=status)
+    assert int(status.item()) == 0
     for r in range(len(lengths)):
         a, b = int(rs[r]), int(rs[r + 1])
         ro, rS = oracle.delta_recurrent(q[a:b].float(), k[a:b].float(), v[a:b].float(), gg[a:b], beta[a:b],
