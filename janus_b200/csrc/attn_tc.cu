@@ -391,19 +391,17 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
     {  // this warp's half of the Q row into TMEM (bf16 pairs, even dim in the low half)
       const bool live = tq < ntok;
       const __nv_bfloat16* qr = p.q + ((int64_t)(live ? q0 + tq : q0) * p.Hq + hkv * G + r % G) * D + half * HD;
-#pragma unroll 1
-      for (int c = 0; c < HD / 2; c += 16) {
-        uint32_t v[16];
+      uint32_t v[HD / 2];  // every load before the first TMEM store (which orders after all earlier memory ops)
 #pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-          const uint4 x = live ? *reinterpret_cast<const uint4*>(qr + 2 * (c + i)) : make_uint4(0, 0, 0, 0);
-          v[i] = x.x;
-          v[i + 1] = x.y;
-          v[i + 2] = x.z;
-          v[i + 3] = x.w;
-        }
-        tst16u(lane_addr + kColQ + half * (HD / 2) + c, v);
+      for (int i = 0; i < HD / 2; i += 4) {
+        const uint4 x = live ? *reinterpret_cast<const uint4*>(qr + 2 * i) : make_uint4(0, 0, 0, 0);
+        v[i] = x.x;
+        v[i + 1] = x.y;
+        v[i + 2] = x.z;
+        v[i + 3] = x.w;
       }
+#pragma unroll
+      for (int c = 0; c < HD / 2; c += 16) tst16u(lane_addr + kColQ + half * (HD / 2) + c, v + c);
       tst_wait();
       fence_before();
       bar_arrive(&bars.q_full);
@@ -513,16 +511,24 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
       const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
       const __nv_bfloat16* gr = p.gate + t * p.gate_stride + (int64_t)h * p.gate_head_stride + half * HD;
       __nv_bfloat16* orow = p.out + (t * p.Hq + h) * D + half * HD;
-#pragma unroll 1
+      // the whole gate row first: the output stores could alias it as far as the compiler knows, so loads issued
+      // between them would each wait for the one before
+      bf16x8 gate[HD / 8];
+#pragma unroll
+      for (int c = 0; c < HD / 8; ++c)
+        gate[c] = live ? *reinterpret_cast<const bf16x8*>(gr + 8 * c) : bf16x8{};
+#pragma unroll
       for (int c = 0; c < HD; c += 16) {
         float o[16];
         tld16(lane_addr + kColO + half * HD + c, o);
         if (live) {
-          float gv[16], res[16];
+          float res[16];
 #pragma unroll
-          for (int i = 0; i < 16; i += 8) load8(gr + c + i, gv + i);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) res[i] = o[i] * inv * sigmoidf_(gv[i]);
+          for (int i = 0; i < 16; ++i) {
+            const __nv_bfloat162 gp = gate[(c + i) / 8].h[((c + i) % 8) / 2];
+            const float gv = (i & 1) ? __high2float(gp) : __low2float(gp);
+            res[i] = o[i] * inv * sigmoidf_(gv);
+          }
           store8(orow + c, res);
           store8(orow + c + 8, res + 8);
         }

@@ -5,7 +5,7 @@
 //      N  = -tril_strict(diag(beta) K K^T * e^(G_i - G_j))          tensor cores, fp32 accumulate
 //      T  = (I - N)^-1                                               fp32: 16x16 diagonal blocks by substitution,
 //                                                                    then doubling stages 16 -> 32 -> 64
-//      U  = T (V * beta),  W = T (K * beta * e^G)                    bf16 operands, fp32 accumulate, stored bf16
+//      U  = (T diag(beta)) V,  W = (T diag(beta e^G)) K              bf16 operands, fp32 accumulate, stored bf16
 //      QK = tril(scale Q K^T * e^(G_i - G_j))                        stored bf16, plus G itself
 // 2. the sequential pass (gdn_state_tc.cu, tcgen05): one CTA per (row, value head) walking the row's chunks in
 //    order with the fp32 state in TMEM:
@@ -89,10 +89,11 @@ __device__ __forceinline__ int chunk_row(const int32_t* chunk_start, int B, int 
 // ------------------------------------------------------------------------------------------------ chunk prep
 
 struct PrepSmem {
-  __nv_bfloat16 q[CT * DH];  // Q, then K * beta * e^G
+  __nv_bfloat16 q[CT * DH];
   __nv_bfloat16 k[CT * DH];
-  __nv_bfloat16 v[CT * DH];  // V, then V * beta
-  __nv_bfloat16 t[CT * CT];  // T (bf16)
+  __nv_bfloat16 v[CT * DH];
+  __nv_bfloat16 t[CT * CT];   // T diag(beta) (bf16): U = T diag(beta) V
+  __nv_bfloat16 t2[CT * CT];  // T diag(beta e^G) (bf16): W = T diag(beta e^G) K
   float n[CT * PADF];
   float tf[CT * PADF];
   float m[32 * 33];
@@ -172,31 +173,14 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
         float qv[2];
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-          const float dec = (j + u <= i) ? expf(sm.G[i] - sm.G[j + u]) : 0.f;
+          const float dec = (j + u <= i) ? __expf(sm.G[i] - sm.G[j + u]) : 0.f;  // G_i - G_j <= 0
           sm.n[i * PADF + j + u] = (j + u < i) ? -sm.beta[i] * kk[n][e + u] * dec : 0.f;
           qv[u] = (j + u <= i) ? qk[n][e + u] * dec * scale : 0.f;
         }
         *reinterpret_cast<__nv_bfloat162*>(qkc + i * CT + j) = __floats2bfloat162_rn(qv[0], qv[1]);
       }
   }
-  __syncthreads();  // every warp is done reading sm.q as Q
-  if (tid < CT) sm.eG[tid] = sm.beta[tid] * sm.eG[tid];  // row factor of K: beta e^G (beta alone for V below)
-  __syncthreads();
-  for (int x = tid; x < CT * DH / 8; x += 256) {  // q <- K beta e^G, v <- V beta, 8 elements per step
-    const int r = x / (DH / 8), cc = (x % (DH / 8)) * 8;
-    const int off = sw<DH>(r, cc);
-    float kf[8], vf[8];
-    load8(&sm.k[off], kf);
-    load8(&sm.v[off], vf);
-    const float fk = sm.eG[r], fv = sm.beta[r];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      kf[u] *= fk;
-      vf[u] *= fv;
-    }
-    store8(&sm.q[off], kf);
-    store8(&sm.v[off], vf);
-  }
+  __syncthreads();  // N complete
   // T = (I - N)^-1: diagonal 16x16 blocks (warps 0-3, lane c < 16 owns column c)
   if (warp < 4) {
     const int base = warp * 16;
@@ -274,26 +258,30 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
     for (int u = 0; u < 4; ++u) sm.tf[(32 + i0 + 8 * u) * PADF + j] = a[u];
   }
   __syncthreads();
+  // the beta and beta e^G factors of the tokens go on T's columns (rather than on V's and K's rows)
   for (int x = tid; x < CT * CT; x += 256) {
     const int i = x >> 6, j = x & 63;
-    sm.t[sw<CT>(i, j)] = __float2bfloat16_rn(j <= i ? sm.tf[i * PADF + j] : 0.f);
+    const float tv = j <= i ? sm.tf[i * PADF + j] * sm.beta[j] : 0.f;
+    sm.t[sw<CT>(i, j)] = __float2bfloat16_rn(tv);
+    sm.t2[sw<CT>(i, j)] = __float2bfloat16_rn(tv * sm.eG[j]);
   }
   __syncthreads();
-  // U = T vb, W = T kb (64 x 128; warp: m-tile w>>1, columns (w&1)*64 .. +63), stored bf16 per token
+  // U = T diag(beta) V, W = T diag(beta e^G) K (64 x 128; warp: m-tile w>>1, columns (w&1)*64 .. +63)
   const int mt = warp >> 1, cb = (warp & 1) * 64;
   float U[8][4] = {}, Wacc[8][4] = {};
 #pragma unroll
   for (int ks = 0; ks < CT; ks += 16) {
-    uint32_t a[4], b[4];
+    uint32_t a[4], a2[4], b[4];
     lda<CT>(a, sm.t, mt * 16, ks, lane);
+    lda<CT>(a2, sm.t2, mt * 16, ks, lane);
 #pragma unroll
     for (int np = 0; np < 4; ++np) {
       ldb_kn<DH>(b, sm.v, cb + np * 16, ks, lane);
       mma(U[2 * np], a, b[0], b[1]);
       mma(U[2 * np + 1], a, b[2], b[3]);
-      ldb_kn<DH>(b, sm.q, cb + np * 16, ks, lane);
-      mma(Wacc[2 * np], a, b[0], b[1]);
-      mma(Wacc[2 * np + 1], a, b[2], b[3]);
+      ldb_kn<DH>(b, sm.k, cb + np * 16, ks, lane);
+      mma(Wacc[2 * np], a2, b[0], b[1]);
+      mma(Wacc[2 * np + 1], a2, b[2], b[3]);
     }
   }
 #pragma unroll

@@ -231,14 +231,28 @@ __global__ void __launch_bounds__(NT, 1) gdn_state_tc_kernel(const __grid_consta
         float ot[CT], o2[CT];
         tld64f(la + cOT(st), ot);
         tld64f(la + cVT(st), o2);
+        // every factor is read before the first store: the stores go through a generic pointer the compiler
+        // cannot tell apart from s_fq, and interleaving them would serialise each load behind a store
+        __nv_bfloat16 res[CT];
 #pragma unroll
-        for (int e = 0; e < CT; ++e) ost[e * DH + v] = __float2bfloat16_rn(ot[e] * s_fq[st][e] + o2[e]);
+        for (int e = 0; e < CT; ++e) res[e] = __float2bfloat16_rn(ot[e] * s_fq[st][e] + o2[e]);
+#pragma unroll
+        for (int e = 0; e < CT; ++e) ost[e * DH + v] = res[e];
       }
       osync();  // the output tile is complete
-      for (int x = v; x < nt * (DH / 8); x += 128) {
-        const int tok = x / (DH / 8), ch = (x % (DH / 8)) * 8;
-        *reinterpret_cast<uint4*>(p.o + ((t0 + tok) * p.Hv + h) * DH + ch) =
-            *reinterpret_cast<const uint4*>(ost + tok * DH + ch);
+      {  // 8 rows x 16 B per thread: all loads first, then the stores
+        uint4 val[CT * (DH / 8) / 128];
+#pragma unroll
+        for (int n = 0; n < CT * (DH / 8) / 128; ++n) {
+          const int x = v + 128 * n;
+          val[n] = *reinterpret_cast<const uint4*>(ost + (x / (DH / 8)) * DH + (x % (DH / 8)) * 8);
+        }
+#pragma unroll
+        for (int n = 0; n < CT * (DH / 8) / 128; ++n) {
+          const int x = v + 128 * n, tok = x / (DH / 8);
+          if (tok < nt)
+            *reinterpret_cast<uint4*>(p.o + ((t0 + tok) * p.Hv + h) * DH + (x % (DH / 8)) * 8) = val[n];
+        }
       }
       fence_before();
       bar_arrive(&bars.empty[st]);  // OT / O2T of this parity and the stage are free
@@ -251,16 +265,19 @@ __global__ void __launch_bounds__(NT, 1) gdn_state_tc_kernel(const __grid_consta
                                  : nullptr;
     // the initial state: ST (fp32) and its bf16 copy SB, column v of S = lane v of S^T
 #pragma unroll 1
-    for (int k0 = 0; k0 < DH; k0 += 32) {
-      float f[32];
-      uint32_t b[16];
+    for (int k0 = 0; k0 < DH; k0 += 64) {  // 64 loads in flight before the TMEM stores (which order after them)
+      float f[64];
+      uint32_t b[32];
 #pragma unroll
-      for (int e = 0; e < 32; ++e) f[e] = s0 ? s0[(int64_t)(k0 + e) * DH + v] : 0.f;
+      for (int e = 0; e < 64; ++e) f[e] = s0 ? s0[(int64_t)(k0 + e) * DH + v] : 0.f;
 #pragma unroll
-      for (int e = 0; e < 16; ++e) b[e] = pack_bf16(f[2 * e], f[2 * e + 1]);
-      tst16f(la + cST + k0, f);
-      tst16f(la + cST + k0 + 16, f + 16);
-      tst16(la + cSB + k0 / 2, b);
+      for (int e = 0; e < 32; ++e) b[e] = pack_bf16(f[2 * e], f[2 * e + 1]);
+      uint32_t w[64];
+#pragma unroll
+      for (int e = 0; e < 64; ++e) w[e] = __float_as_uint(f[e]);
+      tst32(la + cST + k0, w);
+      tst32(la + cST + k0 + 32, w + 32);
+      tst32(la + cSB + k0 / 2, b);
     }
     tst_wait();
     fence_before();
