@@ -4,7 +4,7 @@
 //    cumulative g (every exponential is of a difference of G, so nothing overflows):
 //      N  = -tril_strict(diag(beta) K K^T * e^(G_i - G_j))          tensor cores, fp32 accumulate
 //      T  = (I - N)^-1                                               fp32: 16x16 diagonal blocks by substitution,
-//                                                                    then doubling stages 16 -> 32 -> 64
+//                                                                    then doubling stages 16 -> 32 -> 64 (tf32 MMAs)
 //      U  = (T diag(beta)) V,  W = (T diag(beta e^G)) K              bf16 operands, fp32 accumulate, stored bf16
 //      QK = tril(scale Q K^T * e^(G_i - G_j))                        stored bf16, plus G itself
 // 2. the sequential pass (gdn_state_tc.cu, tcgen05): one CTA per (row, value head) walking the row's chunks in
@@ -46,6 +46,37 @@ __device__ __forceinline__ void mma(float* c, const uint32_t* a, uint32_t b0, ui
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// tf32 tensor-core products on fp32 shared tiles, for the blocks of the triangular inverse (tf32 keeps 10 mantissa
+// bits, more than the bf16 that T is rounded to afterwards; fla's Triton solve multiplies its fp32 blocks in tf32 too)
+__device__ __forceinline__ uint32_t tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+// C[16 x 8] += A[16 x K] B[K x 8] (row-major fp32, leading dimensions lda, ldb), K a multiple of 8
+__device__ __forceinline__ void tile_mma_tf32(float* c, const float* A, int lda, const float* B, int ldb, int K,
+                                              int lane) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int k0 = 0; k0 < K; k0 += 8) {
+    const uint32_t a0 = tf32(A[g * lda + k0 + t]), a1 = tf32(A[(g + 8) * lda + k0 + t]);
+    const uint32_t a2 = tf32(A[g * lda + k0 + t + 4]), a3 = tf32(A[(g + 8) * lda + k0 + t + 4]);
+    const uint32_t b0 = tf32(B[(k0 + t) * ldb + g]), b1 = tf32(B[(k0 + t + 4) * ldb + g]);
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+// the 16 x 8 accumulator tile to a row-major fp32 matrix
+__device__ __forceinline__ void store_tile(const float* c, float* D, int ldd, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  D[g * ldd + 2 * t] = c[0];
+  D[g * ldd + 2 * t + 1] = c[1];
+  D[(g + 8) * ldd + 2 * t] = c[2];
+  D[(g + 8) * ldd + 2 * t + 1] = c[3];
 }
 
 // swizzled bf16 tiles [rows][COLS]: COLS >= 64 XOR the 16-byte chunk with row & 7; COLS == 32 (64-byte rows) with
@@ -207,55 +238,36 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
     }
   }
   __syncthreads();
-  // stage 1: T[2h+1, 2h] = T[2h+1, 2h+1] N[2h+1, 2h] T[2h, 2h] (16x16 blocks), h = 0, 1. Thread: column j, two rows.
-  // The triangular zeros of N and T make the full-length sums exact, so every loop has a fixed trip count.
-  {
-    const int hb = tid >> 7, j = tid & 15, i0 = (tid >> 4) & 7;  // rows i0 and i0 + 8
+  // stage 1: T[2h+1, 2h] = T[2h+1, 2h+1] N[2h+1, 2h] T[2h, 2h] (16x16 blocks), h = 0, 1, on the tensor cores in
+  // tf32 (warps 0-3: block h = w >> 1, 8 columns (w & 1) * 8). The triangular zeros of N and T make full-length
+  // products exact.
+  if (warp < 4) {
+    const int hb = warp >> 1, nt = warp & 1;
     const int bi = (2 * hb + 1) * 16, bj = 2 * hb * 16;
-    float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      const float t = sm.tf[(bj + m) * PADF + bj + j];
-      a0 += sm.n[(bi + i0) * PADF + bj + m] * t;
-      a1 += sm.n[(bi + i0 + 8) * PADF + bj + m] * t;
-    }
-    sm.m[(hb * 16 + i0) * 33 + j] = a0;
-    sm.m[(hb * 16 + i0 + 8) * 33 + j] = a1;
-    __syncthreads();
-    a0 = a1 = 0.f;
-#pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      const float mm = sm.m[(hb * 16 + m) * 33 + j];
-      a0 += sm.tf[(bi + i0) * PADF + bi + m] * mm;
-      a1 += sm.tf[(bi + i0 + 8) * PADF + bi + m] * mm;
-    }
-    sm.tf[(bi + i0) * PADF + bj + j] = a0;
-    sm.tf[(bi + i0 + 8) * PADF + bj + j] = a1;
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    tile_mma_tf32(c, &sm.n[bi * PADF + bj], PADF, &sm.tf[bj * PADF + bj + 8 * nt], PADF, 16, lane);
+    store_tile(c, &sm.m[(hb * 16) * 33 + 8 * nt], 33, lane);
   }
   __syncthreads();
-  // stage 2: T[32:, :32] = T[32:, 32:] N[32:, :32] T[:32, :32]. Thread: column j, rows i0, i0+8, i0+16, i0+24.
+  if (warp < 4) {
+    const int hb = warp >> 1, nt = warp & 1;
+    const int bi = (2 * hb + 1) * 16, bj = 2 * hb * 16;
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    tile_mma_tf32(c, &sm.tf[bi * PADF + bi], PADF, &sm.m[(hb * 16) * 33 + 8 * nt], 33, 16, lane);
+    store_tile(c, &sm.tf[bi * PADF + bj + 8 * nt], PADF, lane);
+  }
+  __syncthreads();
+  // stage 2: T[32:, :32] = T[32:, 32:] N[32:, :32] T[:32, :32] (32x32 blocks, tf32; warp: rows 16 (w >> 2), 8 columns
+  // (w & 3) * 8)
   {
-    const int j = tid & 31, i0 = tid >> 5;
-    float a[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int m = 0; m < 32; ++m) {
-      const float t = sm.tf[m * PADF + j];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) a[u] += sm.n[(32 + i0 + 8 * u) * PADF + m] * t;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) sm.m[(i0 + 8 * u) * 33 + j] = a[u];
+    const int mt = warp >> 2, nt = warp & 3;
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    tile_mma_tf32(c, &sm.n[(32 + 16 * mt) * PADF], PADF, &sm.tf[8 * nt], PADF, 32, lane);
+    store_tile(c, &sm.m[(16 * mt) * 33 + 8 * nt], 33, lane);
     __syncthreads();
-#pragma unroll
-    for (int u = 0; u < 4; ++u) a[u] = 0.f;
-#pragma unroll
-    for (int m = 0; m < 32; ++m) {
-      const float mm = sm.m[m * 33 + j];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) a[u] += sm.tf[(32 + i0 + 8 * u) * PADF + 32 + m] * mm;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) sm.tf[(32 + i0 + 8 * u) * PADF + j] = a[u];
+    c[0] = c[1] = c[2] = c[3] = 0.f;
+    tile_mma_tf32(c, &sm.tf[(32 + 16 * mt) * PADF + 32], PADF, &sm.m[8 * nt], 33, 32, lane);
+    store_tile(c, &sm.tf[(32 + 16 * mt) * PADF + 8 * nt], PADF, lane);
   }
   __syncthreads();
   // the beta and beta e^G factors of the tokens go on T's columns (rather than on V's and K's rows)
