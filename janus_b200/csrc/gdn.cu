@@ -172,78 +172,121 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
 
 // ------------------------------------------------------------------------------------------- fork recurrent rule
 
-template <int DK, int DV, int NT>
-__global__ void __launch_bounds__(NT) gdn_fork_recurrent_kernel(
+// One CTA per (parent row, value head), kForkSplit threads per value column j (consecutive lanes of a warp, each
+// with a slice of the key rows): they keep column j of the state in registers, so the recurrence needs a few
+// shuffles per reduction and no barrier: per token kv_j = sum_k S[k][j] k[k] (after the decay), delta_j =
+// (v_j - kv_j) beta, S[:, j] += k delta_j, o_j = scale sum_k S[k][j] q[k]. The parent's state is read from global
+// memory once into shared memory and every child starts from that copy. The tokens' k, q, v (bf16), g and beta
+// stream through a ring of kForkRing shared buffers with cp.async, kForkRing - 1 tokens ahead, so no thread waits
+// for a load of the token it computes; one barrier per token.
+constexpr int kForkSplit = 4;  // threads per value column
+constexpr int kForkRing = 8;   // token buffers
+
+__device__ __forceinline__ void cp_async(void* dst, const void* src, int bytes) {
+  if (bytes == 16)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src));
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src));
+}
+
+template <int DK, int DV>
+__global__ void __launch_bounds__(kForkSplit * DV) gdn_fork_recurrent_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
     const float* __restrict__ g, const float* __restrict__ beta, const int32_t* __restrict__ row_start,
     const int32_t* __restrict__ child_start, const float* __restrict__ state_in, float* __restrict__ state_out,
     int Hk, int Hv, float scale, __nv_bfloat16* __restrict__ o) {
-  constexpr int NRG = NT / DV;     // row groups
-  constexpr int ROWS = DK / NRG;   // key rows per thread
-  static_assert(NT % DV == 0 && DK % NRG == 0, "state tiling");
-  // per token: k, q (scaled), v and (decay, beta) in a double buffer, so the loads of the next token overlap this
-  // one; separate reduction arrays for S^T k and S^T q, so each token needs two barriers
-  __shared__ float s_k[2][DK], s_q[2][DK], s_v[2][DV], s_gb[2][2], s_kv[NRG][DV], s_ov[NRG][DV];
-  const int p = blockIdx.x, h = blockIdx.y;
+  constexpr int NT = kForkSplit * DV, ROWS = DK / kForkSplit;
+  constexpr int CK = DK / 8, CV = DV / 8;  // 16-byte chunks of a k (q) row and of a v row
+  static_assert(2 * CK + CV + 2 <= NT && ROWS % 4 == 0, "staging threads and row split");
+  extern __shared__ float s0[];  // [DK][DV]: the parent's state
+  __shared__ __align__(16) __nv_bfloat16 s_k[kForkRing][DK], s_q[kForkRing][DK], s_v[kForkRing][DV];
+  __shared__ float s_g[kForkRing], s_b[kForkRing];
+  const int p = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int j = tid / kForkSplit, r0 = (tid % kForkSplit) * ROWS;  // value column, first key row of this thread
   const int hk = h / (Hv / Hk);
-  const int j = threadIdx.x % DV, rg = threadIdx.x / DV;
-  const int64_t sbase_in = ((int64_t)p * Hv + h) * DK * DV;
-  const int64_t tbeg = row_start[child_start[p]], tend = row_start[child_start[p + 1]];
-  auto stage = [&](int64_t t, int buf) {  // the token's vectors into buffer buf (children are consecutive rows)
-    for (int x = threadIdx.x; x < DK; x += NT) {
-      s_k[buf][x] = bf2f(k[(t * Hk + hk) * DK + x]);
-      s_q[buf][x] = bf2f(q[(t * Hk + hk) * DK + x]) * scale;
+  const int c0 = child_start[p], c1 = child_start[p + 1];
+  if (c0 >= c1) return;
+  if (state_in) {
+    const float* src = state_in + ((int64_t)p * Hv + h) * DK * DV;
+#pragma unroll 8
+    for (int r = r0; r < r0 + ROWS; ++r) s0[r * DV + j] = src[(int64_t)r * DV + j];  // this thread's own entries
+  }
+  const int64_t tbeg = row_start[c0], tend = row_start[c1];
+  auto stage = [&](int64_t t, int buf) {  // one commit group per call on every thread (empty ones included)
+    if (t < tend) {
+      if (tid < CK) {
+        cp_async(&s_k[buf][tid * 8], k + (t * Hk + hk) * DK + tid * 8, 16);
+      } else if (tid < 2 * CK) {
+        cp_async(&s_q[buf][(tid - CK) * 8], q + (t * Hk + hk) * DK + (tid - CK) * 8, 16);
+      } else if (tid < 2 * CK + CV) {
+        cp_async(&s_v[buf][(tid - 2 * CK) * 8], v + (t * Hv + h) * DV + (tid - 2 * CK) * 8, 16);
+      } else if (tid == 2 * CK + CV) {
+        cp_async(&s_g[buf], g + t * Hv + h, 4);
+      } else if (tid == 2 * CK + CV + 1) {
+        cp_async(&s_b[buf], beta + t * Hv + h, 4);
+      }
     }
-    for (int x = threadIdx.x; x < DV; x += NT) s_v[buf][x] = bf2f(v[(t * Hv + h) * DV + x]);
-    if (threadIdx.x == 0) {
-      s_gb[buf][0] = expf(g[t * Hv + h]);
-      s_gb[buf][1] = beta[t * Hv + h];
-    }
+    asm volatile("cp.async.commit_group;\n" ::);
   };
-  if (tbeg < tend) stage(tbeg, 0);
-  int64_t step = 0;  // tokens processed by this CTA: the buffer of token t is step & 1
-  for (int c = child_start[p]; c < child_start[p + 1]; ++c) {
+  for (int d = 0; d < kForkRing - 1; ++d) stage(tbeg + d, d);
+  int64_t step = 0;  // tokens processed by this CTA: the buffer of token t is step % kForkRing
+  for (int c = c0; c < c1; ++c) {
     float S[ROWS];
 #pragma unroll
-    for (int r = 0; r < ROWS; ++r) S[r] = state_in ? state_in[sbase_in + (int64_t)(rg * ROWS + r) * DV + j] : 0.f;
+    for (int r = 0; r < ROWS; ++r) S[r] = state_in ? s0[(r0 + r) * DV + j] : 0.f;
     for (int64_t t = row_start[c]; t < row_start[c + 1]; ++t, ++step) {
-      const int buf = (int)(step & 1);
-      __syncthreads();  // token t staged; every reader of the other buffer and of s_ov is done
-      if (t + 1 < tend) stage(t + 1, buf ^ 1);
-      const float decay = s_gb[buf][0];
-      float kv = 0.f;
+      const int buf = (int)(step % kForkRing);
+      asm volatile("cp.async.wait_group %0;\n" ::"n"(kForkRing - 2) : "memory");  // this token's copies landed
+      __syncthreads();  // ... for every thread's copies; every reader of the buffer staged next is done
+      stage(t + kForkRing - 1, (int)((step + kForkRing - 1) % kForkRing));
+      const float decay = expf(s_g[buf]);
+      const __nv_bfloat162* kb = reinterpret_cast<const __nv_bfloat162*>(&s_k[buf][r0]);
+      const __nv_bfloat162* qb = reinterpret_cast<const __nv_bfloat162*>(&s_q[buf][r0]);
+      float k4[4] = {0.f, 0.f, 0.f, 0.f};  // four independent partial sums (short dependency chains)
 #pragma unroll
-      for (int r = 0; r < ROWS; ++r) {
+      for (int r = 0; r < ROWS; r += 4) {
+        const float2 ka = __bfloat1622float2(kb[r / 2]), kc = __bfloat1622float2(kb[r / 2 + 1]);
         S[r] *= decay;
-        kv += S[r] * s_k[buf][rg * ROWS + r];
+        S[r + 1] *= decay;
+        S[r + 2] *= decay;
+        S[r + 3] *= decay;
+        k4[0] += S[r] * ka.x;
+        k4[1] += S[r + 1] * ka.y;
+        k4[2] += S[r + 2] * kc.x;
+        k4[3] += S[r + 3] * kc.y;
       }
-      s_kv[rg][j] = kv;
-      __syncthreads();
-      kv = 0.f;
+      float kv = (k4[0] + k4[1]) + (k4[2] + k4[3]);
 #pragma unroll
-      for (int x = 0; x < NRG; ++x) kv += s_kv[x][j];
-      const float delta = (s_v[buf][j] - kv) * s_gb[buf][1];
-      float ov = 0.f;
+      for (int x = 1; x < kForkSplit; x <<= 1) kv += __shfl_xor_sync(0xffffffffu, kv, x);
+      const float delta = (__bfloat162float(s_v[buf][j]) - kv) * s_b[buf];
+      float o4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int r = 0; r < ROWS; ++r) {
-        S[r] += s_k[buf][rg * ROWS + r] * delta;
-        ov += S[r] * s_q[buf][rg * ROWS + r];
+      for (int r = 0; r < ROWS; r += 4) {
+        const float2 ka = __bfloat1622float2(kb[r / 2]), kc = __bfloat1622float2(kb[r / 2 + 1]);
+        const float2 qa = __bfloat1622float2(qb[r / 2]), qc = __bfloat1622float2(qb[r / 2 + 1]);
+        S[r] += ka.x * delta;
+        S[r + 1] += ka.y * delta;
+        S[r + 2] += kc.x * delta;
+        S[r + 3] += kc.y * delta;
+        o4[0] += S[r] * qa.x;
+        o4[1] += S[r + 1] * qa.y;
+        o4[2] += S[r + 2] * qc.x;
+        o4[3] += S[r + 3] * qc.y;
       }
-      s_ov[rg][j] = ov;
-      __syncthreads();
-      if (rg == 0) {
-        float acc = 0.f;
+      float ov = (o4[0] + o4[1]) + (o4[2] + o4[3]);
 #pragma unroll
-        for (int x = 0; x < NRG; ++x) acc += s_ov[x][j];
-        o[(t * Hv + h) * DV + j] = f2bf(acc);
-      }
+      for (int x = 1; x < kForkSplit; x <<= 1) ov += __shfl_xor_sync(0xffffffffu, ov, x);
+      if (tid % kForkSplit == 0) o[(t * Hv + h) * DV + j] = f2bf(ov * scale);
     }
     if (state_out) {
-      const int64_t sb = ((int64_t)c * Hv + h) * DK * DV;
+      float* dst = state_out + ((int64_t)c * Hv + h) * DK * DV;
 #pragma unroll
-      for (int r = 0; r < ROWS; ++r) state_out[sb + (int64_t)(rg * ROWS + r) * DV + j] = S[r];
+      for (int r = 0; r < ROWS; ++r) dst[(int64_t)(r0 + r) * DV + j] = S[r];
     }
   }
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");  // no copy outlives the CTA
 }
 
 }  // namespace jb
@@ -300,20 +343,31 @@ extern "C" int janus_b200_gdn_fork_recurrent(const void* q, const void* k, const
              "gdn_fork_recurrent: null pointer");
   JB_REQUIRE(T >= 0 && B >= 0 && P >= 0 && Hk > 0 && Hv > 0 && Hv % Hk == 0, JANUS_ERR_INVALID,
              "gdn_fork_recurrent: sizes");
+  JB_REQUIRE(JB_ALIGNED(q, 16) && JB_ALIGNED(k, 16) && JB_ALIGNED(v, 16) && JB_ALIGNED(g, 4) && JB_ALIGNED(beta, 4),
+             JANUS_ERR_ALIGNMENT, "gdn_fork_recurrent: q, k, v must be 16-byte aligned");
   if (P == 0 || T == 0) return JANUS_OK;
   JB_REQUIRE(P <= 0x7fffffff && Hv <= 65535, JANUS_ERR_INVALID, "gdn_fork_recurrent: grid too large");
   dim3 grid((unsigned)P, (unsigned)Hv);
   cudaStream_t s = (cudaStream_t)stream;
-#define JB_FORK(DK_, DV_, NT_)                                                                                 \
-  gdn_fork_recurrent_kernel<DK_, DV_, NT_><<<grid, NT_, 0, s>>>(                                               \
-      (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, g, beta, row_start, child_start, \
-      state_in, state_out, (int)Hk, (int)Hv, scale, (__nv_bfloat16*)o)
+#define JB_FORK(DK_, DV_)                                                                                     \
+  do {                                                                                                        \
+    const int smem = (DK_) * (DV_) * (int)sizeof(float);                                                      \
+    cudaError_t e = cudaFuncSetAttribute(gdn_fork_recurrent_kernel<DK_, DV_>,                                 \
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                  \
+    if (e != cudaSuccess) {                                                                                   \
+      set_error("gdn_fork_recurrent: smem attribute %s", cudaGetErrorString(e));                              \
+      return JANUS_ERR_CUDA;                                                                                  \
+    }                                                                                                         \
+    gdn_fork_recurrent_kernel<DK_, DV_><<<grid, kForkSplit * (DV_), smem, s>>>(                                              \
+        (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, g, beta, row_start,       \
+        child_start, state_in, state_out, (int)Hk, (int)Hv, scale, (__nv_bfloat16*)o);                        \
+  } while (0)
   if (Dk == 128 && Dv == 128) {
-    JB_FORK(128, 128, 512);  // 32 state rows per thread
+    JB_FORK(128, 128);
   } else if (Dk == 64 && Dv == 64) {
-    JB_FORK(64, 64, 256);
+    JB_FORK(64, 64);
   } else if (Dk == 32 && Dv == 32) {
-    JB_FORK(32, 32, 256);
+    JB_FORK(32, 32);
   } else {
     set_error("gdn_fork_recurrent: (Dk, Dv) = (%lld, %lld) not compiled", (long long)Dk, (long long)Dv);
     return JANUS_ERR_UNSUPPORTED;
