@@ -22,14 +22,11 @@
 // The running max m is refreshed only when a row's max grows by more than 2^8 (the row's O is then rescaled in
 // TMEM), so P stays <= 256 and the normaliser l uses the same m: the exact softmax. Every mbarrier wait is bounded;
 // a wait that runs out sets the status word and the CTA winds down (its TMA loads and MMAs drained first).
-#include <cuda.h>
-
-#include <mutex>
-
-#include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace jb {
 namespace tc {
+using namespace tcx;
 
 constexpr int BM = 128, BN = 128;
 constexpr int kSoftmaxThreads = 256;              // 8 softmax warps: two per TMEM lane quarter
@@ -41,9 +38,6 @@ constexpr uint32_t kSlotBytes = BN * 128 * 2;     // 128 keys x 128 head dims (t
 constexpr uint32_t kBoxBytes = BN * 128;          // one [128 keys][64 dims] box: 16 KB
 constexpr int kItemBars = 6;                      // > the K/V items in flight (at most kSlots)
 constexpr uint32_t kColO = 0, kColS = 256, kColQ = 384, kTmemCols = 512;
-constexpr long kSpinLimit = 1L << 30;         // a backstop; the wall-time limit ends waits first
-constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s: no legitimate hand-off here takes a millisecond
-constexpr unsigned kFull = 0xffffffffu;
 
 struct Params {
   CUtensorMap kmap[kMaxLevels], vmap[kMaxLevels];  // [T_l keys][Hkv][D] bf16, box 64 dims x 1 head x 128 keys
@@ -61,85 +55,6 @@ struct Params {
   float scale_log2;
 };
 
-__device__ __forceinline__ uint32_t s32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-// UMMA shared-memory descriptor, 128B swizzle, sm_100 version bits
-__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-// UMMA instruction descriptor: bf16 x bf16 -> f32, M x N, operand majors (0 = K-major, 1 = MN-major)
-__host__ __device__ constexpr uint32_t idesc(int M, int N, int amaj, int bmaj) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)amaj << 15) | ((uint32_t)bmaj << 16) |
-         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-__device__ __forceinline__ void mma(uint32_t tm, uint64_t da, uint64_t db, uint32_t id, uint32_t acc) {
-  asm volatile(
-      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}\n" ::"r"(tm),
-      "l"(da), "l"(db), "r"(id), "r"(acc), "r"(0));
-}
-__device__ __forceinline__ void commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(s32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void bar_init(uint64_t* bar, int count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(s32(bar)), "r"(count));
-}
-__device__ __forceinline__ void bar_arrive(uint64_t* bar) {
-  asm volatile("{\n.reg .b64 st;\nmbarrier.arrive.shared::cta.b64 st, [%0];\n}\n" ::"r"(s32(bar)) : "memory");
-}
-__device__ __forceinline__ void bar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("{\n.reg .b64 st;\nmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}\n" ::"r"(s32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-// bounded wait for the completion of the mbarrier phase of this parity. Gives up (returns false and sets the status
-// word) after kWaitNs of wall time, or as soon as any CTA of the grid has set the status word, so a grid that cannot
-// make progress ends within about one limit instead of one limit per wave.
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int32_t* err) {
-  uint32_t done = 0;
-  uint64_t t0 = 0;
-  for (long it = 0; !done; ++it) {
-    asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
-                 : "=r"(done)
-                 : "r"(s32(bar)), "r"(parity)
-                 : "memory");
-    if (!done && (it & 1023) == 1023) {
-      const uint64_t now = global_ns();
-      if (t0 == 0) t0 = now;
-      const bool other = err && *reinterpret_cast<volatile int32_t*>(err) != 0;
-      if (other || now - t0 > kWaitNs || it > kSpinLimit) break;
-    }
-  }
-  if (!done && err) atomicExch(err, 1);
-  return done != 0;
-}
-// TMA tile load (no multicast) of a 3D tensor map into this CTA's shared memory, completing on `bar`
-__device__ __forceinline__ void tma_load3(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
-                                          uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-      "[%5];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(s32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void tld16(uint32_t addr, float* f) {
-  uint32_t v[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
-      "tcgen05.wait::ld.sync.aligned;\n"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-      : "r"(addr)
-      : "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) f[i] = __uint_as_float(v[i]);
-}
 // 32 consecutive fp32 TMEM columns of this thread's lane, waited for inside the same statement
 __device__ __forceinline__ void tld32(uint32_t addr, float* f) {
   uint32_t v[32];
@@ -155,44 +70,11 @@ __device__ __forceinline__ void tld32(uint32_t addr, float* f) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
 }
-__device__ __forceinline__ void tst16(uint32_t addr, const float* f) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
-          addr),
-      "r"(__float_as_uint(f[0])), "r"(__float_as_uint(f[1])), "r"(__float_as_uint(f[2])), "r"(__float_as_uint(f[3])),
-      "r"(__float_as_uint(f[4])), "r"(__float_as_uint(f[5])), "r"(__float_as_uint(f[6])), "r"(__float_as_uint(f[7])),
-      "r"(__float_as_uint(f[8])), "r"(__float_as_uint(f[9])), "r"(__float_as_uint(f[10])),
-      "r"(__float_as_uint(f[11])), "r"(__float_as_uint(f[12])), "r"(__float_as_uint(f[13])),
-      "r"(__float_as_uint(f[14])), "r"(__float_as_uint(f[15])));
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
 __device__ __forceinline__ float ex2(float x) {  // 2^x on the MUFU unit, flush-to-zero (irrelevant for weights)
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-__device__ __forceinline__ void mma_ts(uint32_t tm, uint32_t ta, uint64_t db, uint32_t id, uint32_t acc) {
-  asm volatile(  // A from TMEM
-      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tm),
-      "r"(ta), "l"(db), "r"(id), "r"(acc));
-}
-__device__ __forceinline__ void tst16u(uint32_t addr, const uint32_t* v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
-          addr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]));
-}
-__device__ __forceinline__ void tst_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // named barrier of the two softmax warps that share a TMEM lane quarter
 __device__ __forceinline__ void pair_sync(int quarter) {
@@ -401,7 +283,7 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
         v[i + 3] = x.w;
       }
 #pragma unroll
-      for (int c = 0; c < HD / 2; c += 16) tst16u(lane_addr + kColQ + half * (HD / 2) + c, v + c);
+      for (int c = 0; c < HD / 2; c += 16) tst16(lane_addr + kColQ + half * (HD / 2) + c, v + c);
       tst_wait();
       fence_before();
       bar_arrive(&bars.q_full);
@@ -480,11 +362,12 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
 #pragma unroll 1
           for (int c = 0; c < HD; c += 16) {
             float o[16];
-            tld16(lane_addr + kColO + half * HD + c, o);
+            tld16f(lane_addr + kColO + half * HD + c, o);
 #pragma unroll
             for (int i = 0; i < 16; ++i) o[i] *= alpha;
-            tst16(lane_addr + kColO + half * HD + c, o);
+            tst16f(lane_addr + kColO + half * HD + c, o);
           }
+          tst_wait();  // the rescaled O is in TMEM before the next P V accumulates onto it
         }
         unsigned char* prow = base + Lay::P + half * (BM * 128) + r * 128;  // atom `half`: keys half*64 ..
 #pragma unroll
@@ -520,7 +403,7 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
 #pragma unroll
       for (int c = 0; c < HD; c += 16) {
         float o[16];
-        tld16(lane_addr + kColO + half * HD + c, o);
+        tld16f(lane_addr + kColO + half * HD + c, o);
         if (live) {
           float res[16];
 #pragma unroll
@@ -559,27 +442,10 @@ __global__ void wait_timeout_selftest_kernel(int32_t* status) {
 
 // ------------------------------------------------------------------------------------------------ host side
 
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiled encode_fn() {
-  static EncodeTiled fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiled>(ptr);
-  });
-  return fn;
-}
-
 // K or V of one level: [T keys][Hkv][D] bf16, boxes of 64 dims x 1 head x 128 keys, 128B swizzle; keys past T
 // read as zeros (and are masked)
 static int make_kv_map(CUtensorMap* map, const void* ptr, int64_t T, int64_t Hkv, int64_t D) {
-  EncodeTiled enc = encode_fn();
+  EncodeTiled enc = encode_tiled_fn();
   if (!enc) {
     set_error("tree_attention(tcgen05): cuTensorMapEncodeTiled unavailable");
     return JANUS_ERR_CUDA;
