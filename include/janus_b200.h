@@ -165,8 +165,8 @@ int janus_b200_head_pointer(const float* x, int64_t H, const int32_t* option_row
 
 /* MoE routing and tile plan, sync-free: softmax over fp32 router logits [S, E] (E <= 512), top-k (k <= 16),
  * renormalised weights (topk_idx int32 / topk_w fp32 [S, k]); assignments a = t*k + j sorted by expert into
- * sorted_ids [max_tiles * tile_rows] (-1 pads each expert to a multiple of tile_rows, which must be 64),
- * tile_expert [max_tiles], the tile count in n_tiles[0] on the device. max_tiles >= ceil((S*k + E*63) / 64).
+ * sorted_ids [max_tiles * tile_rows] (-1 pads each expert to a multiple of tile_rows, which must be 128),
+ * tile_expert [max_tiles], the tile count in n_tiles[0] on the device. max_tiles >= ceil((S*k + E*127) / 128).
  * workspace: int32, at least 3*E.
  * Replaces Qwen3_5MoeTopKRouter.forward (transformers qwen3_5_moe :754-770) and `align`
  * (janus/moe_w4a16.py:89-106). */
@@ -174,18 +174,21 @@ int janus_b200_moe_route(const float* logits, int64_t S, int64_t E, int64_t k, i
                          float* topk_w, int32_t* sorted_ids, int32_t* tile_expert, int64_t max_tiles,
                          int32_t* n_tiles, int32_t* workspace, size_t workspace_bytes, void* stream);
 
-/* W4A16 grouped GEMM over the expert-sorted tiles of janus_b200_moe_route. Weights: codes uint8 [E, rows, K/2]
- * (two int4 per byte, even element in the low nibble, two's complement) and bf16 scales [E, rows, K/128]; the
- * value fed to the tensor cores is code * scale computed in fp32 and rounded once to bf16.
+/* W4A16 grouped GEMM over the expert-sorted 128-row tiles of janus_b200_moe_route / janus_b200_moe_plan, on the
+ * tcgen05 tensor cores. Weights: codes uint8 [E, rows, K/2] (two int4 per byte, even element in the low nibble,
+ * two's complement) and bf16 scales [E, rows, K/128]; the value fed to the tensor cores is code * scale rounded
+ * once to bf16 (the fp32 product's rounding).
  * gated = 1 (gate_up, rows = 2N): x rows are tokens (assignment / topk), out[sorted row, n] =
- * silu(x W_gate^T) * (x W_up^T) in bf16, out rows = max_tiles*64 sorted rows.
+ * silu(x W_gate^T) * (x W_up^T) in bf16, out rows = max_tiles*128 sorted rows.
  * gated = 0 (down, rows = N): x rows are the sorted rows of the first GEMM's output, out[assignment, n] =
- * topk_w[assignment] * x W^T in bf16. N % 64 == 0, K % 128 == 0.
+ * topk_w[assignment] * x W^T in bf16. N % 128 == 0, K % 128 == 0; x, codes, out 16-byte aligned, ldx and ldo
+ * multiples of 8. status: NULL or an int32 that is 0 on entry; a device-side wait that ran out sets it to 1 (the
+ * affected tiles are not stored).
  * Replaces _w4a16_moe_kernel / fused_moe (janus/moe_w4a16.py:37-86, 122-140) for the int4-g128 format. */
 int janus_b200_moe_grouped_w4a16(const void* x, int64_t ldx, const uint8_t* codes, const void* scales, int64_t E,
                                  int64_t N, int64_t K, int32_t gated, const int32_t* sorted_ids,
                                  const int32_t* tile_expert, const int32_t* n_tiles, int64_t max_tiles, int64_t topk,
-                                 const float* topk_w, void* out, int64_t ldo, void* stream);
+                                 const float* topk_w, void* out, int64_t ldo, int32_t* status, void* stream);
 
 /* MoE output: out[t] = sum_j y[t*k + j] (fp32 sum of the weighted expert rows) + sigmoid(shared_gate_logit[t]) *
  * shared[t] (shared NULL: none), bf16 [S, H].

@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
       }
       // every issued load has landed before the CTA may leave (no-ops on the normal path: all consumed)
       for (int i = issued - kItemBars < 0 ? 0 : issued - kItemBars; i < issued; ++i)
-        wait_bar(&bars.full[i % kItemBars], (i / kItemBars) & 1, p.err);
+        wait_bar_quiet(&bars.full[i % kItemBars], (i / kItemBars) & 1, p.err);
     }
   } else if (warp == kMmaSWarp) {
     // ------------------------------------------------------------------------------------------ S issuer
@@ -422,7 +422,7 @@ __global__ void __launch_bounds__(NT, 1) tree_attention_tc_kernel(const __grid_c
   fence_before();
   __syncthreads();
   fence_after();
-  wait_bar(&bars.drain, 0, p.err);
+  wait_bar_quiet(&bars.drain, 0, p.err);
   fence_before();
   __syncthreads();
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(kTmemCols));

@@ -174,7 +174,8 @@ __global__ void __launch_bounds__(NT, 1) gdn_state_tc_kernel(const __grid_consta
         issued = i + 1;
       }
       // every issued load has landed before the CTA may leave (no-ops on the normal path: all consumed)
-      for (int i = issued - 2 < 0 ? 0 : issued - 2; i < issued; ++i) wait_bar(&bars.full[i & 1], (i >> 1) & 1, p.err);
+      for (int i = issued - 2 < 0 ? 0 : issued - 2; i < issued; ++i)
+        wait_bar_quiet(&bars.full[i & 1], (i >> 1) & 1, p.err);
     }
   } else if (warp == 5) {
     // -------------------------------------------------------------------------------------------- MMA issuer
@@ -365,7 +366,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_state_tc_kernel(const __grid_consta
   fence_before();
   __syncthreads();
   fence_after();
-  wait_bar(&bars.drain, 0, p.err);
+  wait_bar_quiet(&bars.drain, 0, p.err);
   fence_before();
   __syncthreads();
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(kTmemCols));

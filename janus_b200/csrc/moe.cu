@@ -7,13 +7,10 @@
 // launched for the worst case (every expert padded) and tiles past the count exit at once — the plan of
 // janus/moe_w4a16.py:89-106, computed by three small kernels instead of argsort/bincount/searchsorted.
 //
-// moe_gemm: one CTA per (tile of 64 expert-sorted rows, 64 output columns). Per 128-deep k-block the CTA stages the
-// activation rows (gathered by token for the first GEMM), the packed int4 weight rows and their scales with
-// cp.async (double-buffered), decodes the codes once into a bf16 tile in shared memory (code * scale in fp32, one
-// rounding to bf16: the value the reference's dequantise path feeds its GEMM) and runs mma.sync on it. The first
-// GEMM computes gate and up columns together and stores silu(gate) * up per sorted row; the second multiplies by the
-// routing weight and stores per assignment. moe_combine sums the k assignments of a token in fp32 and adds the gated
-// shared expert.
+// The grouped GEMMs between the plan and the combine are in moe_tc.cu (tcgen05, int4 decoded on the fly). The first
+// stores silu(gate) * up per sorted row; the second multiplies by the routing weight and stores per assignment.
+// moe_combine sums the k assignments of a token in fp32 and adds the gated shared expert; moe_plan, reduce_slots and
+// combine_ep are the receiving and owning sides of the expert-parallel layout.
 #include <algorithm>
 
 #include "common.cuh"
@@ -21,26 +18,7 @@
 namespace jb {
 namespace {
 
-constexpr int BM = 64, BN = 64, BK = 128, GROUP = 128;
-constexpr int NT = 128;
-constexpr int PACKED_ROW = BK / 2 + 16;  // bytes per packed weight row in shared memory (16-byte aligned, padded)
-
-__device__ __forceinline__ uint32_t s32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-__device__ __forceinline__ void cpa16(void* dst, const void* src, bool ok) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s32(dst)), "l"(src), "r"(ok ? 16 : 0));
-}
-__device__ __forceinline__ void ldx4(uint32_t* r, const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(s32(p)));
-}
-__device__ __forceinline__ void mma(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-// swizzled bf16 tile [rows][BK]
-__device__ __forceinline__ int sw(int r, int c) { return r * BK + (((c >> 3) ^ (r & 7)) << 3) + (c & 7); }
+constexpr int BM = 128;  // rows per tile of the plan: the M of the grouped GEMMs' MMAs (moe_tc.cu)
 
 // ------------------------------------------------------------------------------------------------------- routing
 
@@ -161,130 +139,6 @@ __global__ void plan_count_kernel(const int32_t* __restrict__ ids, int64_t n, in
   }
 }
 
-// ---------------------------------------------------------------------------------------------- grouped GEMM
-
-struct MoeSmem {
-  __nv_bfloat16 a[2][BM * BK];
-  uint8_t wq[2][2][BN * PACKED_ROW];  // [stage][gate/up][row][bytes]
-  __nv_bfloat16 ws[2][2][BN];         // scales of the k-block
-  __nv_bfloat16 b[2][BN * BK];        // decoded weights [gate/up][n][k]
-  int32_t rows[BM];
-};
-
-template <bool GATED>
-__global__ void __launch_bounds__(NT) moe_gemm_kernel(const __nv_bfloat16* __restrict__ A, int64_t lda,
-                                                      const uint8_t* __restrict__ W, const __nv_bfloat16* __restrict__ Ws,
-                                                      const int32_t* __restrict__ sorted_ids,
-                                                      const int32_t* __restrict__ tile_expert,
-                                                      const int32_t* __restrict__ n_tiles, int N, int K, int topk,
-                                                      const float* __restrict__ topk_w, __nv_bfloat16* __restrict__ out,
-                                                      int64_t ldo) {
-  extern __shared__ __align__(16) unsigned char raw[];
-  MoeSmem& sm = *reinterpret_cast<MoeSmem*>(raw);
-  const int tile = blockIdx.x;
-  if (tile >= n_tiles[0]) return;
-  const int e = tile_expert[tile];
-  const int n0 = blockIdx.y * BN;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int NW = GATED ? 2 * N : N;  // weight rows of the expert
-  const uint8_t* We = W + (int64_t)e * NW * (K / 2);
-  const __nv_bfloat16* Wse = Ws + (int64_t)e * NW * (K / GROUP);
-  if (tid < BM) {
-    const int id = sorted_ids[(int64_t)tile * BM + tid];
-    // GEMM 1 gathers the token of the assignment; GEMM 2 reads its own sorted row
-    sm.rows[tid] = GATED ? (id >= 0 ? id / topk : -1) : (id >= 0 ? tile * BM + tid : -1);
-  }
-  __syncthreads();
-  const int nkb = K / BK;
-  auto load = [&](int kb, int st) {
-    const int k0 = kb * BK;
-    for (int x = tid; x < BM * (BK / 8); x += NT) {
-      const int r = x / (BK / 8), c = (x % (BK / 8)) * 8;
-      const int row = sm.rows[r];
-      cpa16(&sm.a[st][sw(r, c)], A + (int64_t)(row >= 0 ? row : 0) * lda + k0 + c, row >= 0);
-    }
-    for (int x = tid; x < (GATED ? 2 : 1) * BN * (BK / 32); x += NT) {
-      const int half = x / (BN * (BK / 32));
-      const int y = x % (BN * (BK / 32));
-      const int r = y / (BK / 32), c = (y % (BK / 32)) * 16;
-      const int wrow = n0 + r + half * N;
-      cpa16(&sm.wq[st][half][r * PACKED_ROW + c], We + (int64_t)wrow * (K / 2) + k0 / 2 + c, true);
-    }
-    if (tid < (GATED ? 2 : 1) * BN) {
-      const int half = tid / BN, r = tid % BN;
-      sm.ws[st][half][r] = Wse[(int64_t)(n0 + r + half * N) * (K / GROUP) + k0 / GROUP];
-    }
-  };
-  float acc[2][BN / 8][4];
-#pragma unroll
-  for (int h = 0; h < 2; ++h)
-#pragma unroll
-    for (int n = 0; n < BN / 8; ++n) acc[h][n][0] = acc[h][n][1] = acc[h][n][2] = acc[h][n][3] = 0.f;
-  load(0, 0);
-  asm volatile("cp.async.commit_group;\n" ::);
-  for (int kb = 0; kb < nkb; ++kb) {
-    const int st = kb & 1;
-    if (kb + 1 < nkb) {
-      load(kb + 1, st ^ 1);
-      asm volatile("cp.async.commit_group;\n" ::);
-      asm volatile("cp.async.wait_group 1;\n" ::);
-    } else {
-      asm volatile("cp.async.wait_group 0;\n" ::);
-    }
-    __syncthreads();
-    // decode: byte j of a row holds k = 2j (low nibble) and 2j + 1 (high nibble); value = code * scale, rounded once
-    for (int x = tid; x < (GATED ? 2 : 1) * BN * (BK / 2); x += NT) {
-      const int half = x / (BN * (BK / 2));
-      const int y = x % (BN * (BK / 2));
-      const int r = y / (BK / 2), j = y % (BK / 2);
-      const uint32_t byte = sm.wq[st][half][r * PACKED_ROW + j];
-      const float sc = bf2f(sm.ws[st][half][r]);
-      const float lo = (float)((int)((byte & 15u) ^ 8u) - 8) * sc;
-      const float hi = (float)((int)((byte >> 4) ^ 8u) - 8) * sc;
-      *reinterpret_cast<__nv_bfloat162*>(&sm.b[half][sw(r, 2 * j)]) = __floats2bfloat162_rn(lo, hi);
-    }
-    __syncthreads();
-#pragma unroll
-    for (int ks = 0; ks < BK; ks += 16) {
-      uint32_t a[4];
-      ldx4(a, &sm.a[st][sw(warp * 16 + (lane & 15), ks + ((lane >> 4) << 3))]);
-#pragma unroll
-      for (int h = 0; h < (GATED ? 2 : 1); ++h) {
-#pragma unroll
-        for (int np = 0; np < BN / 16; ++np) {
-          uint32_t b[4];
-          ldx4(b, &sm.b[h][sw(np * 16 + (lane & 7) + ((lane >> 4) << 3), ks + (((lane >> 3) & 1) << 3))]);
-          mma(acc[h][2 * np], a, b[0], b[1]);
-          mma(acc[h][2 * np + 1], a, b[2], b[3]);
-        }
-      }
-    }
-    __syncthreads();  // sm.b and the stage are free for the next k-block
-  }
-  // epilogue
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int r = warp * 16 + (lane >> 2) + i * 8;
-    const int id = sorted_ids[(int64_t)tile * BM + r];
-    if (id < 0) continue;
-    const int64_t orow = GATED ? (int64_t)tile * BM + r : (int64_t)id;
-    const float wgt = GATED ? 1.f : topk_w[id];
-#pragma unroll
-    for (int n = 0; n < BN / 8; ++n) {
-      const int c = n0 + n * 8 + (lane & 3) * 2;
-      float v0, v1;
-      if (GATED) {
-        v0 = silu(acc[0][n][2 * i]) * acc[1][n][2 * i];
-        v1 = silu(acc[0][n][2 * i + 1]) * acc[1][n][2 * i + 1];
-      } else {
-        v0 = acc[0][n][2 * i] * wgt;
-        v1 = acc[0][n][2 * i + 1] * wgt;
-      }
-      *reinterpret_cast<__nv_bfloat162*>(out + orow * ldo + c) = __floats2bfloat162_rn(v0, v1);
-    }
-  }
-}
-
 // out[t] = sum_j y[t*k + j] (fp32) + sigmoid(gate_logit[t]) * shared[t]
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int k, const __nv_bfloat16* __restrict__ shared,
                                    const float* __restrict__ gate_logit, int64_t S, int H,
@@ -397,42 +251,6 @@ extern "C" int janus_b200_moe_route(const float* logits, int64_t S, int64_t E, i
     st = launch_status("moe_route/scatter");
   }
   return st;
-}
-
-extern "C" int janus_b200_moe_grouped_w4a16(const void* x, int64_t ldx, const uint8_t* codes, const void* scales,
-                                            int64_t E, int64_t N, int64_t K, int32_t gated, const int32_t* sorted_ids,
-                                            const int32_t* tile_expert, const int32_t* n_tiles, int64_t max_tiles,
-                                            int64_t topk, const float* topk_w, void* out, int64_t ldo, void* stream) {
-  JB_REQUIRE(x && codes && scales && sorted_ids && tile_expert && n_tiles && out, JANUS_ERR_INVALID,
-             "moe_grouped_w4a16: null pointer");
-  JB_REQUIRE(E > 0 && N > 0 && N % BN == 0 && K > 0 && K % BK == 0 && topk > 0, JANUS_ERR_UNSUPPORTED,
-             "moe_grouped_w4a16: N %lld must be a multiple of %d and K %lld of %d", (long long)N, BN, (long long)K, BK);
-  JB_REQUIRE(gated || topk_w, JANUS_ERR_INVALID, "moe_grouped_w4a16: the down projection needs routing weights");
-  JB_REQUIRE(ldx % 8 == 0 && ldo % 2 == 0 && JB_ALIGNED(x, 16) && JB_ALIGNED(codes, 16) && JB_ALIGNED(out, 4),
-             JANUS_ERR_ALIGNMENT, "moe_grouped_w4a16: alignment");
-  if (max_tiles == 0) return JANUS_OK;
-  const size_t smem = sizeof(MoeSmem);
-  cudaStream_t s = (cudaStream_t)stream;
-  dim3 grid((unsigned)max_tiles, (unsigned)(N / BN));
-  cudaError_t e;
-  if (gated) {
-    e = cudaFuncSetAttribute(moe_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess)
-      moe_gemm_kernel<true><<<grid, NT, smem, s>>>((const __nv_bfloat16*)x, ldx, codes, (const __nv_bfloat16*)scales,
-                                                   sorted_ids, tile_expert, n_tiles, (int)N, (int)K, (int)topk, topk_w,
-                                                   (__nv_bfloat16*)out, ldo);
-  } else {
-    e = cudaFuncSetAttribute(moe_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess)
-      moe_gemm_kernel<false><<<grid, NT, smem, s>>>((const __nv_bfloat16*)x, ldx, codes, (const __nv_bfloat16*)scales,
-                                                    sorted_ids, tile_expert, n_tiles, (int)N, (int)K, (int)topk, topk_w,
-                                                    (__nv_bfloat16*)out, ldo);
-  }
-  if (e != cudaSuccess) {
-    set_error("moe_grouped_w4a16: smem attribute: %s", cudaGetErrorString(e));
-    return JANUS_ERR_CUDA;
-  }
-  return launch_status("moe_grouped_w4a16");
 }
 
 extern "C" int janus_b200_moe_combine(const void* y, int64_t k, const void* shared, const float* shared_gate_logit,

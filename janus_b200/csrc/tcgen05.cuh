@@ -80,6 +80,25 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int32_t
   if (!done && err) atomicExch(err, 1);
   return done != 0;
 }
+// the same, bounded by wall time only: for the wind-down waits (the CTA's own TMA loads landing, its MMAs
+// draining) that must not be cut short because another CTA gave up
+__device__ __forceinline__ bool wait_bar_quiet(uint64_t* bar, uint32_t parity, int32_t* err) {
+  uint32_t done = 0;
+  uint64_t t0 = 0;
+  for (long it = 0; !done; ++it) {
+    asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(done)
+                 : "r"(s32(bar)), "r"(parity)
+                 : "memory");
+    if (!done && (it & 1023) == 1023) {
+      const uint64_t now = global_ns();
+      if (t0 == 0) t0 = now;
+      if (now - t0 > kWaitNs || it > kSpinLimit) break;
+    }
+  }
+  if (!done && err) atomicExch(err, 1);
+  return done != 0;
+}
 // TMA tile loads (no multicast) of a 2D / 3D tensor map into this CTA's shared memory, completing on `bar`
 __device__ __forceinline__ void tma_load2(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
   asm volatile(

@@ -144,8 +144,8 @@ class DecisionReadout:
         plan = ops.moe_route(logits, k)
         if self.ep is not None:
             return self._moe_ep(y, L, plan[0], plan[1])
-        h = ops.moe_grouped_w4a16(y, L.gu_codes, L.gu_scales, plan, True, k)
-        y2 = ops.moe_grouped_w4a16(h, L.dn_codes, L.dn_scales, plan, False, k, topk_w=plan[1])
+        h = ops.moe_grouped_w4a16(y, L.gu_codes, L.gu_scales, plan, True, k, status=self.status)
+        y2 = ops.moe_grouped_w4a16(h, L.dn_codes, L.dn_scales, plan, False, k, topk_w=plan[1], status=self.status)
         shared = F.linear(ops.silu_mul(F.linear(y, L.shared_gate_up)), L.shared_down)
         sg = torch.mm(y, L.shared_gate.t(), out_dtype=torch.float32)
         return ops.moe_combine(y2, k, shared, sg.reshape(-1))
@@ -158,8 +158,9 @@ class DecisionReadout:
         H = y.shape[1]
         if rows.shape[0]:
             plan = ops.moe_plan(slot_e, ep.local)
-            h = ops.moe_grouped_w4a16(rows, L.gu_codes, L.gu_scales, plan, True, k)
-            y2 = ops.moe_grouped_w4a16(h, L.dn_codes, L.dn_scales, plan, False, k, topk_w=slot_w.reshape(-1))
+            h = ops.moe_grouped_w4a16(rows, L.gu_codes, L.gu_scales, plan, True, k, status=self.status)
+            y2 = ops.moe_grouped_w4a16(h, L.dn_codes, L.dn_scales, plan, False, k, topk_w=slot_w.reshape(-1),
+                                      status=self.status)
             part = ops.moe_reduce_slots(y2, k, slot_e)
         else:
             part = torch.empty(0, H, dtype=torch.float32, device=y.device)

@@ -279,7 +279,7 @@ def head_pointer(x, option_rows, option_question, decision_rows, final_w, rms_ep
     return logits
 
 
-MOE_TILE = 64
+MOE_TILE = 128  # rows per tile of the routing plan = the M of the grouped GEMMs' tensor-core tiles
 
 
 def moe_max_tiles(S, E, k):
@@ -306,8 +306,9 @@ def moe_route(logits, k):
 
 
 @_instrument("moe_grouped_w4a16", 1)
-def moe_grouped_w4a16(x, codes, scales, plan, gated, k, topk_w=None, out=None):
-    """x bf16 [rows, K] (unit column stride); codes uint8 [E, NW, K/2], scales bf16 [E, NW, K/128] (NW = 2N gated)."""
+def moe_grouped_w4a16(x, codes, scales, plan, gated, k, topk_w=None, out=None, status=None):
+    """x bf16 [rows, K] (unit column stride); codes uint8 [E, NW, K/2], scales bf16 [E, NW, K/128] (NW = 2N gated).
+    status: optional device int32 [1], zero on entry, set to 1 by a device-side wait that ran out."""
     _need(x, BF16, "x", contiguous=False)
     if x.stride(1) != 1:
         raise ValueError("x must have unit column stride")
@@ -322,7 +323,7 @@ def moe_grouped_w4a16(x, codes, scales, plan, gated, k, topk_w=None, out=None):
         out = torch.empty((mt * MOE_TILE if gated else S * k), N, dtype=BF16, device=x.device)
     _lib.check(_lib.load().janus_b200_moe_grouped_w4a16(
         _ptr(x), x.stride(0), _ptr(codes), _ptr(scales), E, N, K, 1 if gated else 0, _ptr(sorted_ids),
-        _ptr(tile_expert), _ptr(n_tiles), mt, k, _ptr(topk_w), _ptr(out), out.stride(0), _stream(x)),
+        _ptr(tile_expert), _ptr(n_tiles), mt, k, _ptr(topk_w), _ptr(out), out.stride(0), _ptr(status), _stream(x)),
         "moe_grouped_w4a16")
     return out
 

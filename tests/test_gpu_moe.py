@@ -32,16 +32,17 @@ def test_route_topk_and_plan(S, E, k):
     np.testing.assert_array_equal(idx.cpu().numpy(), ref_idx.numpy())
     np.testing.assert_allclose(w.cpu().numpy(), (top / top.sum(-1, keepdim=True)).numpy(), atol=1e-6, rtol=1e-5)
     n = int(n_tiles.item())
-    ids = sorted_ids.cpu().numpy()[: n * 64]
+    T = ops.MOE_TILE
+    ids = sorted_ids.cpu().numpy()[: n * T]
     te = tile_expert.cpu().numpy()[:n]
     live = ids[ids >= 0]
     assert sorted(live.tolist()) == list(range(S * k))  # every assignment exactly once
     flat = idx.cpu().numpy().reshape(-1)
     for t in range(n):  # every row of a tile belongs to the tile's expert
-        rows = ids[t * 64:(t + 1) * 64]
+        rows = ids[t * T:(t + 1) * T]
         assert (flat[rows[rows >= 0]] == te[t]).all()
     counts = np.bincount(flat, minlength=E)
-    assert n == sum((c + 63) // 64 for c in counts)
+    assert n == sum((c + T - 1) // T for c in counts)
 
 
 @pytest.mark.parametrize("S,E,k,H,I", [(5, 8, 2, 128, 128), (700, 16, 4, 2048, 512), (300, 256, 8, 2048, 512)])
@@ -115,7 +116,7 @@ def test_expert_parallel_kernels_emulated_on_one_gpu(S, E, k, W):
     np.testing.assert_allclose(got.float().cpu().numpy(), ref.float().cpu().numpy(), atol=2e-2, rtol=1e-2)
     # plan of explicit ids: every slot with an expert exactly once, -1 slots never
     n = int(rp[4].item())
-    ids = rp[2].cpu().numpy()[: n * 64]
+    ids = rp[2].cpu().numpy()[: n * ops.MOE_TILE]
     live = np.sort(ids[ids >= 0])
     expect = np.nonzero(slot_e.cpu().numpy().reshape(-1) >= 0)[0]
     np.testing.assert_array_equal(live, expect)
