@@ -11,10 +11,12 @@
 // gathered with cp.async (GEMM 1 reads the token of each assignment; GEMM 2 the sorted rows), and one thread issues
 // M=128 MMAs into an fp32 accumulator in TMEM, so decode, gather and the tensor core overlap across a 4-stage ring.
 //
-// Warps: 0 TMA producer (codes), 1 TMEM owner and MMA issuer, 2-3 activation gather, 4-7 converters; all eight
-// read the accumulator in the epilogue (warp w reads TMEM lanes 32 (w % 4) .. +31, columns half w / 4).
-// Every hand-off is an mbarrier with a bounded wait: a wait that runs out sets the status word and the CTA
-// winds down (loads in flight are waited for, MMAs drained, TMEM released) without storing.
+// Persistent CTAs (one per SM) walk the work items; the fp32 accumulator is double-buffered in TMEM so an item's
+// epilogue overlaps the next item's main loop. Warps: 0 TMA producer (codes), 1 TMEM owner and MMA issuer, 2-3
+// activation gather, 4-11 converters (two groups of four: even and odd k-blocks, so the decode of two k-blocks is
+// in flight at once), 12-15 epilogue (warp w reads TMEM lanes 32 (w % 4) .. +31). Every hand-off is an mbarrier
+// with a bounded wait: a wait that runs out sets the status word and the CTA winds down (loads in flight are
+// waited for, MMAs drained, TMEM released).
 #include "tcgen05.cuh"
 
 namespace jb {
@@ -24,7 +26,7 @@ using namespace tcx;
 constexpr int BM = 128;    // rows per tile (the routing plan's tile height)
 constexpr int BK = 64;     // one 128-byte swizzle atom of bf16 along k
 constexpr int GROUP = 128;  // inputs per scale
-constexpr int NT = 256;
+constexpr int NT = 512;  // producer, MMA, 2 gather, 8 converter (two groups), 4 epilogue warps
 constexpr int S = 4;  // activation + decoded-weight stages
 constexpr int C = 4;  // packed-code slots
 constexpr uint32_t kA = BM * BK * 2;  // 16 KB
@@ -55,7 +57,7 @@ struct Params {
 };
 
 struct Bars {
-  uint64_t full[S], empty[S], cfull[C], cempty[C], drain;
+  uint64_t full[S], empty[S], cfull[C], cempty[C], acc_full[2], acc_empty[2], drain;
 };
 
 // 8 int4 codes (k = 0..7 of a 32-bit word, k even in the low nibble) -> 8 bf16 (code * scale, one rounding).
@@ -81,7 +83,9 @@ __device__ __forceinline__ void cpa16(uint32_t dst, const void* src, bool ok) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0) : "memory");
 }
 
-// BN = MMA width: 256 for the gated GEMM (128 output columns: 128 gate + 128 up rows of B), 128 or 256 otherwise
+// BN = MMA width: 256 for the gated GEMM (128 output columns: 128 gate + 128 up rows of B), 128 or 256 otherwise.
+// Persistent: CTA b takes the work items (tile, column block) b, b + grid, ...; the accumulator is double-buffered
+// in TMEM so the epilogue of one item overlaps the main loop of the next.
 template <bool GATED, int BN>
 __global__ void __launch_bounds__(NT, 1) moe_w4a16_tc_kernel(const __grid_constant__ Params p) {
   using L = Layout<BN>;
@@ -90,38 +94,39 @@ __global__ void __launch_bounds__(NT, 1) moe_w4a16_tc_kernel(const __grid_consta
   const uint32_t sbase = s32(base);
   __shared__ Bars bars;
   __shared__ uint32_t tmem_base;
-  __shared__ int32_t s_rows[BM];
-  __shared__ int s_ok;
 
-  const int tile = blockIdx.x / p.nblk, nb = blockIdx.x % p.nblk;
-  if (tile >= p.n_tiles[0]) return;  // worst-case grid: tiles past the plan's count have no rows
+  const int n_items = p.n_tiles[0] * p.nblk;
+  if ((int)blockIdx.x >= n_items) return;  // worst-case grid: nothing for this CTA
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int e = p.tile_expert[tile];
+  const int G = gridDim.x;
   const int NW = GATED ? 2 * p.N : p.N;
-  const int n0 = nb * (GATED ? BN / 2 : BN);  // first output column of the block
-  const int nkb = p.K / BK;
+  const int nkb = p.K / BK;  // even: K is a multiple of the scale group
+  // item -> (tile, first output column); B-tile row r -> weight row of expert e
+  auto tile_of = [&](int it) { return it / p.nblk; };
+  auto n0_of = [&](int it) { return (it % p.nblk) * (GATED ? BN / 2 : BN); };
+  auto wrow = [&](int e, int n0, int r) {
+    return e * NW + (GATED ? (r < 128 ? n0 + r : p.N + n0 + r - 128) : n0 + r);
+  };
 
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s32(&tmem_base)),
-                 "r"(BN));
+                 "r"(2 * BN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
-  }
-  if (tid < BM) {
-    const int id = p.sorted_ids[(int64_t)tile * BM + tid];
-    // GEMM 1 gathers the token (or received row) of the assignment; GEMM 2 reads its own sorted row
-    s_rows[tid] = id < 0 ? -1 : (GATED ? id / p.topk : tile * BM + tid);
   }
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
-      bar_init(&bars.full[s], 64 + 128);  // the gather threads and the converter threads
+      bar_init(&bars.full[s], 64 + 128);  // the gather threads and one converter group
       bar_init(&bars.empty[s], 1);        // the stage's MMAs (commit)
     }
     for (int c = 0; c < C; ++c) {
       bar_init(&bars.cfull[c], 1);   // the producer's expect_tx, then the TMA bytes
-      bar_init(&bars.cempty[c], 4);  // one arrival per converter warp
+      bar_init(&bars.cempty[c], 4);  // one arrival per warp of the converter group
+    }
+    for (int a = 0; a < 2; ++a) {
+      bar_init(&bars.acc_full[a], 1);   // the item's last MMAs (commit)
+      bar_init(&bars.acc_empty[a], 4);  // one arrival per epilogue warp
     }
     bar_init(&bars.drain, 1);
-    s_ok = 1;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   fence_before();
@@ -133,180 +138,230 @@ __global__ void __launch_bounds__(NT, 1) moe_w4a16_tc_kernel(const __grid_consta
     // ------------------------------------------------------------------------------------ TMA producer (codes)
     if (lane == 0) {
       bool ok = true;
-      int issued = 0;
-      const int wrow = e * NW + n0;  // first weight row of box 0
-      for (int kb = 0; kb < nkb && ok; ++kb) {
-        const int c = kb % C;
-        if (kb >= C) ok = wait_bar(&bars.cempty[c], ((kb / C) - 1) & 1, p.err);
-        if (!ok) break;
-        bar_expect_tx(&bars.cfull[c], L::kCode);
+      int q = 0, issued = 0;
+      int e_next = p.tile_expert[tile_of(blockIdx.x)];
+      for (int it = blockIdx.x; it < n_items && ok; it += G) {
+        const int e = e_next, n0 = n0_of(it);
+        if (it + G < n_items) e_next = p.tile_expert[tile_of(it + G)];
+        for (int kb = 0; kb < nkb; ++kb, ++q) {
+          const int c = q % C;
+          if (q >= C) ok = wait_bar(&bars.cempty[c], ((q / C) - 1) & 1, p.err);
+          if (!ok) break;
+          bar_expect_tx(&bars.cfull[c], L::kCode);
 #pragma unroll
-        for (int bx = 0; bx < BN / 128; ++bx) {
-          const int r = GATED ? (bx == 0 ? wrow : wrow + p.N) : wrow + bx * 128;
-          tma_load2(sbase + L::code(c) + bx * 128 * 32, &p.cmap, kb * (BK / 2), r, &bars.cfull[c]);
+          for (int bx = 0; bx < BN / 128; ++bx)
+            tma_load2(sbase + L::code(c) + bx * 128 * 32, &p.cmap, kb * (BK / 2), wrow(e, n0, bx * 128),
+                      &bars.cfull[c]);
+          issued = q + 1;
         }
-        issued = kb + 1;
       }
-      if (!ok) s_ok = 0;
       // every issued load has landed before the CTA may leave (on the normal path the converters consume them all)
-      for (int kb = issued - C < 0 ? 0 : issued - C; kb < issued; ++kb)
-        wait_bar_quiet(&bars.cfull[kb % C], (kb / C) & 1, p.err);
+      for (int j = issued - C < 0 ? 0 : issued - C; j < issued; ++j)
+        wait_bar_quiet(&bars.cfull[j % C], (j / C) & 1, p.err);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t ID = idesc(BM, BN, 0, 0);
       bool ok = true;
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % S;
-        ok = wait_bar(&bars.full[s], (kb / S) & 1, p.err);
+      int q = 0, i = 0;
+      for (int it = blockIdx.x; it < n_items && ok; it += G, ++i) {
+        const int ab = i & 1;
+        if (i >= 2) ok = wait_bar(&bars.acc_empty[ab], ((i >> 1) - 1) & 1, p.err);
         if (!ok) break;
         fence_after();
+        const uint32_t acc = tm + ab * BN;
+        for (int kb = 0; kb < nkb; ++kb, ++q) {
+          const int s = q % S;
+          ok = wait_bar(&bars.full[s], (q / S) & 1, p.err);
+          if (!ok) break;
+          fence_after();
 #pragma unroll
-        for (int ks = 0; ks < BK / 16; ++ks)
-          mma(tm, sdesc(sbase + L::a(s) + ks * 32, 16, 1024), sdesc(sbase + L::b(s) + ks * 32, 16, 1024), ID,
-              (kb | ks) != 0);
-        commit(&bars.empty[s]);
+          for (int ks = 0; ks < BK / 16; ++ks)
+            mma(acc, sdesc(sbase + L::a(s) + ks * 32, 16, 1024), sdesc(sbase + L::b(s) + ks * 32, 16, 1024), ID,
+                (kb | ks) != 0);
+          commit(&bars.empty[s]);
+        }
+        if (ok) commit(&bars.acc_full[ab]);
       }
-      if (!ok) s_ok = 0;
       commit(&bars.drain);  // completes once every MMA issued above has finished
     }
   } else if (warp < 4) {
     // ---------------------------------------------------------------------------------- activation gather
-    const int gt = tid - 64;
+    // thread: 16-byte chunk c8 of rows rb + 8 i (i = 0..15) of the tile; smem row rb + 8 i of the swizzled stage
+    const int gt = tid - 64, c8 = gt & 7, rb = gt >> 3;
+    const uint32_t doff = rb * 128 + ((c8 ^ rb) << 4);
     bool ok = true;
-    int pending = -1;  // k-block whose loads are in flight and not yet signalled
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % S;
-      if (kb >= S) ok = wait_bar(&bars.empty[s], ((kb / S) - 1) & 1, p.err);
-      if (!ok) break;
-      const uint32_t dst = sbase + L::a(s);
+    int q = 0, pending = -1;
+    int id_next[16];
 #pragma unroll
-      for (int i = 0; i < BM * (BK / 8) / 64; ++i) {
-        const int x = gt + 64 * i, r = x >> 3, c = x & 7;
-        const int row = s_rows[r];
-        cpa16(dst + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4),
-              p.A + (int64_t)(row < 0 ? 0 : row) * p.lda + kb * BK + c * 8, row >= 0);
+    for (int i = 0; i < 16; ++i) id_next[i] = p.sorted_ids[(int64_t)tile_of(blockIdx.x) * BM + rb + 8 * i];
+    for (int it = blockIdx.x; it < n_items && ok; it += G) {
+      const int tile = tile_of(it);
+      int64_t off[16];  // element offset of the row's chunk; -1: padding row (zero-filled)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int id = id_next[i];
+        // GEMM 1 gathers the token (or received row) of the assignment; GEMM 2 reads its own sorted row
+        const int64_t row = id < 0 ? -1 : (GATED ? id / p.topk : (int64_t)tile * BM + rb + 8 * i);
+        off[i] = row < 0 ? -1 : row * p.lda + c8 * 8;
       }
-      asm volatile("cp.async.commit_group;\n" ::: "memory");
-      if (pending >= 0) {
-        asm volatile("cp.async.wait_group 1;\n" ::: "memory");
-        fence_async_smem();  // the generic-proxy writes are visible to the tensor core's reads
-        bar_arrive(&bars.full[pending % S]);
+      if (it + G < n_items) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) id_next[i] = p.sorted_ids[(int64_t)tile_of(it + G) * BM + rb + 8 * i];
       }
-      pending = kb;
+      for (int kb = 0; kb < nkb; ++kb, ++q) {
+        const int s = q % S;
+        if (q >= S) ok = wait_bar(&bars.empty[s], ((q / S) - 1) & 1, p.err);
+        if (!ok) break;
+        const uint32_t dst = sbase + L::a(s) + doff;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          cpa16(dst + i * 1024, p.A + (off[i] < 0 ? 0 : off[i] + kb * BK), off[i] >= 0);
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+        if (pending >= 0) {
+          asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+          fence_async_smem();  // the generic-proxy writes are visible to the tensor core's reads
+          bar_arrive(&bars.full[pending % S]);
+        }
+        pending = q;
+      }
     }
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     if (ok && pending >= 0) {
       fence_async_smem();
       bar_arrive(&bars.full[pending % S]);
     }
-    if (!ok) s_ok = 0;
-  } else {
+  } else if (warp < 12) {
     // ----------------------------------------------------------------------------------------- converters
-    constexpr int U = BN / 64;  // units (one row, 32 codes) per thread and k-block
-    const int ct = tid - 128, hf = ct & 1;
-    const __nv_bfloat16* sc[U];
-    int rr[U];
-#pragma unroll
-    for (int j = 0; j < U; ++j) {
-      const int r = (ct >> 1) + 64 * j;  // row of the B tile
-      rr[j] = r;
-      const int wr = GATED ? (r < 128 ? n0 + r : p.N + n0 + r - 128) : n0 + r;
-      sc[j] = p.scales + ((int64_t)e * NW + wr) * (p.K / GROUP);
-    }
-    __nv_bfloat16 s_cur[U], s_nxt[U];
-#pragma unroll
-    for (int j = 0; j < U; ++j) {
-      s_cur[j] = sc[j][0];
-      s_nxt[j] = p.K / GROUP > 1 ? sc[j][1] : s_cur[j];
-    }
+    // two groups of four warps take the even and the odd k-blocks; thread: half hf of rows rr0 + 64 j of B
+    constexpr int U = BN / 64;
+    const int grp = (warp - 4) >> 2, ct = ((warp - 4) & 3) * 32 + lane, hf = ct & 1, rr0 = ct >> 1;
+    const int gk = p.K / GROUP;
     bool ok = true;
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % S, c = kb % C;
-      if (kb > 0 && (kb & 1) == 0) {  // a new scale group; prefetch the one after it
-        const int g = kb >> 1;
-#pragma unroll
-        for (int j = 0; j < U; ++j) {
-          s_cur[j] = s_nxt[j];
-          if (g + 1 < p.K / GROUP) s_nxt[j] = sc[j][g + 1];
-        }
-      }
-      ok = wait_bar(&bars.cfull[c], (kb / C) & 1, p.err);
-      if (!ok) break;
-      uint4 q[U];
-#pragma unroll
-      for (int j = 0; j < U; ++j)
-        q[j] = *reinterpret_cast<const uint4*>(base + L::code(c) + rr[j] * 32 + hf * 16);
-      __syncwarp();
-      if (lane == 0) bar_arrive(&bars.cempty[c]);
-      if (kb >= S) ok = wait_bar(&bars.empty[s], ((kb / S) - 1) & 1, p.err);
-      if (!ok) break;
-      unsigned char* bt = base + L::b(s);
+    int q = 0;
+    const __nv_bfloat16* sp[U];  // this thread's rows' scales for the current item
+    __nv_bfloat16 s_nxt[U];      // the scales of the next k-block this group decodes
+    {
+      const int it = blockIdx.x, e = p.tile_expert[tile_of(it)], n0 = n0_of(it);
 #pragma unroll
       for (int j = 0; j < U; ++j) {
-        const __nv_bfloat162 s2 = __halves2bfloat162(s_cur[j], s_cur[j]);
-        const uint32_t wv[4] = {q[j].x, q[j].y, q[j].z, q[j].w};
-        const int r = rr[j];
-#pragma unroll
-        for (int w = 0; w < 4; ++w)
-          *reinterpret_cast<uint4*>(bt + (r >> 3) * 1024 + (r & 7) * 128 + (((hf * 4 + w) ^ (r & 7)) << 4)) =
-              decode8(wv[w], s2);
+        sp[j] = p.scales + (int64_t)wrow(e, n0, rr0 + 64 * j) * gk;
+        s_nxt[j] = sp[j][0];  // the first k-block of either group is in scale group 0
       }
-      fence_async_smem();
-      bar_arrive(&bars.full[s]);
     }
-    if (!ok) s_ok = 0;
+    for (int it = blockIdx.x; it < n_items && ok; it += G) {
+      const int nit = it + G;
+      const int e_nxt = nit < n_items ? p.tile_expert[tile_of(nit)] : 0;
+      for (int kb = grp; kb < nkb; kb += 2) {
+        const int qq = q + kb;
+        __nv_bfloat16 s_cur[U];
+#pragma unroll
+        for (int j = 0; j < U; ++j) s_cur[j] = s_nxt[j];
+        if (kb + 2 < nkb) {  // prefetch the scales of this group's next k-block, in this item or the next
+#pragma unroll
+          for (int j = 0; j < U; ++j) s_nxt[j] = sp[j][(kb + 2) / (GROUP / BK)];
+        } else if (nit < n_items) {
+          const int n0 = n0_of(nit);
+#pragma unroll
+          for (int j = 0; j < U; ++j) {
+            sp[j] = p.scales + (int64_t)wrow(e_nxt, n0, rr0 + 64 * j) * gk;
+            s_nxt[j] = sp[j][0];
+          }
+        }
+        const int c = qq % C, s = qq % S;
+        ok = wait_bar(&bars.cfull[c], (qq / C) & 1, p.err);
+        if (!ok) break;
+        // the codes are decoded into registers while the stage may still be in use; the slot is released only after
+        // the stores that consume them: a release right after the loads let the TMA refilling the slot overwrite
+        // codes whose loads had not returned yet
+        uint4 dv[U][4];
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+          const uint4 cw = *reinterpret_cast<const uint4*>(base + L::code(c) + (rr0 + 64 * j) * 32 + hf * 16);
+          const __nv_bfloat162 s2 = __halves2bfloat162(s_cur[j], s_cur[j]);
+          dv[j][0] = decode8(cw.x, s2);
+          dv[j][1] = decode8(cw.y, s2);
+          dv[j][2] = decode8(cw.z, s2);
+          dv[j][3] = decode8(cw.w, s2);
+        }
+        if (qq >= S) ok = wait_bar(&bars.empty[s], ((qq / S) - 1) & 1, p.err);
+        if (!ok) break;
+        unsigned char* bt = base + L::b(s);
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+          const int r = rr0 + 64 * j;
+#pragma unroll
+          for (int w = 0; w < 4; ++w)
+            *reinterpret_cast<uint4*>(bt + (r >> 3) * 1024 + (r & 7) * 128 + (((hf * 4 + w) ^ (r & 7)) << 4)) =
+                dv[j][w];
+        }
+        fence_async_smem();
+        bar_arrive(&bars.full[s]);
+        __syncwarp();
+        if (lane == 0) bar_arrive(&bars.cempty[c]);
+      }
+      q += nkb;
+    }
+  } else {
+    // ------------------------------------------------------------------------------------------- epilogue
+    // thread = accumulator row (TMEM lane 32 (warp % 4) + lane)
+    const int r = 32 * (warp & 3) + lane;
+    bool ok = true;
+    int i = 0;
+    for (int it = blockIdx.x; it < n_items && ok; it += G, ++i) {
+      const int ab = i & 1, tile = tile_of(it), n0 = n0_of(it);
+      const int id = p.sorted_ids[(int64_t)tile * BM + r];
+      const float wgt = (!GATED && id >= 0) ? p.topk_w[id] : 0.f;
+      ok = __all_sync(kFull, wait_bar(&bars.acc_full[ab], (i >> 1) & 1, p.err));
+      if (!ok) break;
+      fence_after();
+      const uint32_t la = tm + ((uint32_t)(32 * (warp & 3)) << 16) + ab * BN;
+      if (GATED) {  // silu(gate) * up: gate in accumulator columns 0..127, up in 128..255
+        __nv_bfloat16* dst = p.out + ((int64_t)tile * BM + r) * p.ldo + n0;
+#pragma unroll 2
+        for (int cc = 0; cc < 128; cc += 16) {
+          float g[16], u[16];
+          tld16f(la + cc, g);
+          tld16f(la + 128 + cc, u);
+          uint32_t o[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            o[k] = pack_bf16(silu(g[2 * k]) * u[2 * k], silu(g[2 * k + 1]) * u[2 * k + 1]);
+          if (id >= 0) {
+            reinterpret_cast<uint4*>(dst + cc)[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            reinterpret_cast<uint4*>(dst + cc)[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+        }
+      } else {
+        __nv_bfloat16* dst = p.out + (int64_t)(id < 0 ? 0 : id) * p.ldo + n0;
+#pragma unroll 2
+        for (int cc = 0; cc < BN; cc += 16) {
+          float a[16];
+          tld16f(la + cc, a);
+          uint32_t o[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) o[k] = pack_bf16(a[2 * k] * wgt, a[2 * k + 1] * wgt);
+          if (id >= 0) {
+            reinterpret_cast<uint4*>(dst + cc)[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            reinterpret_cast<uint4*>(dst + cc)[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) bar_arrive(&bars.acc_empty[ab]);  // this warp's lanes of the buffer are read
+    }
   }
 
-  // ------------------------------------------------------------------------------------------------ epilogue
+  // wind down: every MMA issued has completed before TMEM is released
   fence_before();
   __syncthreads();
   fence_after();
   wait_bar_quiet(&bars.drain, 0, p.err);
-  fence_after();
-  if (s_ok) {
-    const int q = warp & 3, hc = warp >> 2;
-    const int r = 32 * q + lane;
-    const int id = p.sorted_ids[(int64_t)tile * BM + r];
-    const uint32_t la = tm + ((uint32_t)(32 * q) << 16);
-    if (GATED) {
-      // 64 output columns per warp: gate columns hc*64 .. +63 of the accumulator, up columns 128 + the same
-      __nv_bfloat16* dst = p.out + ((int64_t)tile * BM + r) * p.ldo + n0 + hc * 64;
-#pragma unroll
-      for (int cc = 0; cc < 64; cc += 16) {
-        float g[16], u[16];
-        tld16f(la + hc * 64 + cc, g);
-        tld16f(la + 128 + hc * 64 + cc, u);
-        uint32_t o[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = pack_bf16(silu(g[2 * i]) * u[2 * i], silu(g[2 * i + 1]) * u[2 * i + 1]);
-        if (id >= 0) {
-          reinterpret_cast<uint4*>(dst + cc)[0] = make_uint4(o[0], o[1], o[2], o[3]);
-          reinterpret_cast<uint4*>(dst + cc)[1] = make_uint4(o[4], o[5], o[6], o[7]);
-        }
-      }
-    } else {
-      constexpr int CW = BN / 2;  // columns per warp
-      const float wgt = id >= 0 ? p.topk_w[id] : 0.f;
-      __nv_bfloat16* dst = p.out + (int64_t)(id < 0 ? 0 : id) * p.ldo + n0 + hc * CW;
-#pragma unroll
-      for (int cc = 0; cc < CW; cc += 16) {
-        float a[16];
-        tld16f(la + hc * CW + cc, a);
-        uint32_t o[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = pack_bf16(a[2 * i] * wgt, a[2 * i + 1] * wgt);
-        if (id >= 0) {
-          reinterpret_cast<uint4*>(dst + cc)[0] = make_uint4(o[0], o[1], o[2], o[3]);
-          reinterpret_cast<uint4*>(dst + cc)[1] = make_uint4(o[4], o[5], o[6], o[7]);
-        }
-      }
-    }
-  }
   fence_before();
   __syncthreads();
-  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(BN));
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(2 * BN));
 }
 
 }  // namespace mtc
@@ -348,7 +403,14 @@ int launch(const mtc::Params& p, int64_t max_tiles, cudaStream_t s) {
     set_error("moe_grouped_w4a16: smem attribute: %s", cudaGetErrorString(e));
     return JANUS_ERR_CUDA;
   }
-  kern<<<(unsigned)(max_tiles * p.nblk), mtc::NT, smem, s>>>(p);
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                                 cudaSuccess || sms <= 0) {
+    set_error("moe_grouped_w4a16: device query failed");
+    return JANUS_ERR_CUDA;
+  }
+  const int64_t items = max_tiles * p.nblk;  // worst case; the CTAs read the plan's count on the device
+  kern<<<(unsigned)(items < sms ? items : sms), mtc::NT, smem, s>>>(p);
   return launch_status("moe_grouped_w4a16");
 }
 
