@@ -9,7 +9,7 @@
 // warps turn them into bf16 in registers (code * scale, rounded once to bf16: the value the reference's
 // dequantise path feeds its GEMM) and write the 128B-swizzled K-major tile the MMA reads. The activation rows are
 // gathered with cp.async (GEMM 1 reads the token of each assignment; GEMM 2 the sorted rows), and one thread issues
-// M=128 MMAs into an fp32 accumulator in TMEM, so decode, gather and the tensor core overlap across a 4-stage ring.
+// M=128 MMAs into an fp32 accumulator in TMEM, so decode, gather and the tensor core overlap across a 3-stage ring.
 //
 // Persistent CTAs (one per SM) walk the work items; the fp32 accumulator is double-buffered in TMEM so an item's
 // epilogue overlaps the next item's main loop. Warps: 0 TMA producer (codes), 1 TMEM owner and MMA issuer, 2-3
@@ -27,7 +27,7 @@ constexpr int BM = 128;    // rows per tile (the routing plan's tile height)
 constexpr int BK = 64;     // one 128-byte swizzle atom of bf16 along k
 constexpr int GROUP = 128;  // inputs per scale
 constexpr int NT = 512;  // producer, MMA, 2 gather, 8 converter (two groups), 4 epilogue warps
-constexpr int S = 4;  // activation + decoded-weight stages
+constexpr int S = 3;  // activation + decoded-weight stages
 constexpr int C = 4;  // packed-code slots
 constexpr uint32_t kA = BM * BK * 2;  // 16 KB
 
@@ -38,7 +38,8 @@ struct Layout {
   __host__ __device__ static constexpr uint32_t a(int s) { return s * kA; }
   __host__ __device__ static constexpr uint32_t b(int s) { return S * kA + s * kB; }
   __host__ __device__ static constexpr uint32_t code(int c) { return S * (kA + kB) + c * kCode; }
-  static constexpr uint32_t bytes = S * (kA + kB) + C * kCode;
+  static constexpr uint32_t out_stage = S * (kA + kB) + C * kCode;  // 4 epilogue warps x 32 rows x 64 bytes
+  static constexpr uint32_t bytes = out_stage + 4 * 32 * 64;
 };
 
 struct Params {
@@ -305,48 +306,68 @@ __global__ void __launch_bounds__(NT, 1) moe_w4a16_tc_kernel(const __grid_consta
     }
   } else {
     // ------------------------------------------------------------------------------------------- epilogue
-    // thread = accumulator row (TMEM lane 32 (warp % 4) + lane)
-    const int r = 32 * (warp & 3) + lane;
+    // thread = accumulator row (TMEM lane 32 (warp % 4) + lane). Each 32-column slice of the warp's rows goes through
+    // a small shared-memory buffer so the global stores cover 8 rows x 64 bytes per instruction instead of 32 rows x
+    // 16 bytes; the assignment ids and routing weights are loaded an item ahead of their use.
+    const int eq = warp & 3, r = 32 * eq + lane;
+    unsigned char* stg = base + L::out_stage + eq * (32 * 64);  // [32 rows][64 bytes], 16-byte units swizzled by row
     bool ok = true;
     int i = 0;
+    int id_a = p.sorted_ids[(int64_t)tile_of(blockIdx.x) * BM + r];
+    float w_a = (!GATED && id_a >= 0) ? p.topk_w[id_a] : 0.f;
+    int id_b = (int)blockIdx.x + G < n_items ? p.sorted_ids[(int64_t)tile_of(blockIdx.x + G) * BM + r] : -1;
     for (int it = blockIdx.x; it < n_items && ok; it += G, ++i) {
       const int ab = i & 1, tile = tile_of(it), n0 = n0_of(it);
-      const int id = p.sorted_ids[(int64_t)tile * BM + r];
-      const float wgt = (!GATED && id >= 0) ? p.topk_w[id] : 0.f;
+      const int id = id_a;
+      const float wgt = w_a;
+      w_a = (!GATED && id_b >= 0) ? p.topk_w[id_b] : 0.f;  // the next item's ids arrived an item ago
+      id_a = id_b;
+      id_b = it + 2 * G < n_items ? p.sorted_ids[(int64_t)tile_of(it + 2 * G) * BM + r] : -1;
+      int64_t orow[4];  // output row of the rows k * 8 + lane / 4 this lane stores; -1: padding, not stored
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int src = k * 8 + (lane >> 2);
+        const int sid = __shfl_sync(kFull, id, src);
+        orow[k] = sid < 0 ? -1 : (GATED ? (int64_t)tile * BM + 32 * eq + src : (int64_t)sid);
+      }
       ok = __all_sync(kFull, wait_bar(&bars.acc_full[ab], (i >> 1) & 1, p.err));
       if (!ok) break;
       fence_after();
-      const uint32_t la = tm + ((uint32_t)(32 * (warp & 3)) << 16) + ab * BN;
-      if (GATED) {  // silu(gate) * up: gate in accumulator columns 0..127, up in 128..255
-        __nv_bfloat16* dst = p.out + ((int64_t)tile * BM + r) * p.ldo + n0;
-#pragma unroll 2
-        for (int cc = 0; cc < 128; cc += 16) {
-          float g[16], u[16];
-          tld16f(la + cc, g);
-          tld16f(la + 128 + cc, u);
-          uint32_t o[8];
+      const uint32_t la = tm + ((uint32_t)(32 * eq) << 16) + ab * BN;
+      constexpr int OUTC = GATED ? BN / 2 : BN;  // output columns of an item
+#pragma unroll 1
+      for (int cc = 0; cc < OUTC; cc += 32) {
+        uint32_t o[16];
 #pragma unroll
-          for (int k = 0; k < 8; ++k)
-            o[k] = pack_bf16(silu(g[2 * k]) * u[2 * k], silu(g[2 * k + 1]) * u[2 * k + 1]);
-          if (id >= 0) {
-            reinterpret_cast<uint4*>(dst + cc)[0] = make_uint4(o[0], o[1], o[2], o[3]);
-            reinterpret_cast<uint4*>(dst + cc)[1] = make_uint4(o[4], o[5], o[6], o[7]);
-          }
-        }
-      } else {
-        __nv_bfloat16* dst = p.out + (int64_t)(id < 0 ? 0 : id) * p.ldo + n0;
-#pragma unroll 2
-        for (int cc = 0; cc < BN; cc += 16) {
+        for (int h2 = 0; h2 < 2; ++h2) {
           float a[16];
-          tld16f(la + cc, a);
-          uint32_t o[8];
+          tld16f(la + cc + 16 * h2, a);
+          if (GATED) {  // silu(gate) * up: gate in accumulator columns 0..127, up in 128..255
+            float u[16];
+            tld16f(la + 128 + cc + 16 * h2, u);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) o[k] = pack_bf16(a[2 * k] * wgt, a[2 * k + 1] * wgt);
-          if (id >= 0) {
-            reinterpret_cast<uint4*>(dst + cc)[0] = make_uint4(o[0], o[1], o[2], o[3]);
-            reinterpret_cast<uint4*>(dst + cc)[1] = make_uint4(o[4], o[5], o[6], o[7]);
+            for (int k = 0; k < 8; ++k)
+              o[8 * h2 + k] = pack_bf16(silu(a[2 * k]) * u[2 * k], silu(a[2 * k + 1]) * u[2 * k + 1]);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) o[8 * h2 + k] = pack_bf16(a[2 * k] * wgt, a[2 * k + 1] * wgt);
           }
         }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          *reinterpret_cast<uint4*>(stg + lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4)) =
+              make_uint4(o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
+        __syncwarp();
+        uint4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int rr = k * 8 + (lane >> 2);
+          v[k] = *reinterpret_cast<const uint4*>(stg + rr * 64 + (((lane & 3) ^ ((rr >> 1) & 3)) << 4));
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (orow[k] >= 0) *reinterpret_cast<uint4*>(p.out + orow[k] * p.ldo + n0 + cc + (lane & 3) * 8) = v[k];
+        __syncwarp();  // the buffer is read before the next slice overwrites it
       }
       fence_before();
       __syncwarp();

@@ -120,3 +120,27 @@ def test_expert_parallel_kernels_emulated_on_one_gpu(S, E, k, W):
     live = np.sort(ids[ids >= 0])
     expect = np.nonzero(slot_e.cpu().numpy().reshape(-1) >= 0)[0]
     np.testing.assert_array_equal(live, expect)
+
+
+@pytest.mark.parametrize("S,E,k", [(300, 256, 8), (4096, 64, 8)])
+def test_grouped_w4a16_run_to_run_identical(S, E, k):
+    """The grouped GEMMs accumulate in a fixed order, so repeated launches must agree bit for bit; a difference is a
+    race between the pipeline stages (a tolerance check alone can miss one that corrupts a few tiles)."""
+    ops = _ops()
+    H, I = 2048, 512
+    g = torch.Generator().manual_seed(S + E)
+    x = torch.randn(S, H, generator=g).to(torch.bfloat16).cuda()
+    logits = torch.randn(S, E, generator=g).cuda()
+    gu_codes, gu_scales = (t.cuda() for t in _experts(E, 2 * I, H, 31))
+    dn_codes, dn_scales = (t.cuda() for t in _experts(E, H, I, 32))
+    plan = ops.moe_route(logits, k)
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    valid = plan[2] >= 0
+    h0 = ops.moe_grouped_w4a16(x, gu_codes, gu_scales, plan, True, k, status=st)
+    y0 = ops.moe_grouped_w4a16(h0, dn_codes, dn_scales, plan, False, k, topk_w=plan[1], status=st)
+    for _ in range(6):
+        h = ops.moe_grouped_w4a16(x, gu_codes, gu_scales, plan, True, k, status=st)
+        y = ops.moe_grouped_w4a16(h0, dn_codes, dn_scales, plan, False, k, topk_w=plan[1], status=st)
+        assert torch.equal(h[valid], h0[valid])
+        assert torch.equal(y, y0)
+    assert int(st.item()) == 0

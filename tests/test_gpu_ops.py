@@ -275,3 +275,50 @@ def test_device_wait_that_runs_out_is_reported_and_the_context_survives():
     y = ops.silu_mul(torch.randn(4, 256, device="cuda").to(torch.bfloat16))
     torch.cuda.synchronize()
     assert torch.isfinite(y.float()).all() and torch.isfinite(x).all()
+
+
+def test_tcgen05_kernels_run_to_run_identical():
+    """Tree attention and the chunk scan on many CTAs at once: repeated launches agree bit for bit (their
+    accumulation orders are fixed, so any difference is a race between pipeline stages)."""
+    ops = _ops()
+    from janus_b200.plan import build_levels
+    from janus_b200 import synthetic
+    g = torch.Generator().manual_seed(11)
+    packs = [synthetic.q4b_request(vocab=4096, seed=s, state_tokens=1500 + 300 * s, questions=4, block_tokens=16)
+             for s in range(4)]
+    levels, _ = build_levels(packs)
+    Hq, Hkv, D = 16, 4, 256
+    K = [torch.randn(lv.T, Hkv, D, generator=g).to(BF).cuda() for lv in levels]
+    V = [torch.randn(lv.T, Hkv, D, generator=g).to(BF).cuda() for lv in levels]
+    cuda = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    for d, lv in enumerate(levels):
+        q = torch.randn(lv.T, Hq, D, generator=g).to(BF).cuda()
+        gate_buf = torch.randn(lv.T, Hq, 2 * D, generator=g).to(BF).cuda()
+        tiles = cuda(lv.attention_tiles(ops.tree_attention_tile_tokens(D, Hq, Hkv)))
+        args = (q, K[:d + 1], V[:d + 1], [cuda(x) for x in lv.anc_lo], [cuda(x) for x in lv.anc_hi],
+                cuda(lv.row_start), cuda(lv.row_of_token), tiles, gate_buf[:, :, D:], D ** -0.5)
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        first = ops.tree_attention(*args, status=status).clone()
+        for _ in range(4):
+            assert torch.equal(ops.tree_attention(*args, status=status), first)
+        assert int(status.item()) == 0
+    Hk, Hv, Dk = 16, 32, 128
+    lengths = [700 + 37 * i for i in range(24)]
+    rs, _ = _level(lengths)
+    T = int(rs[-1])
+    qq = oracle.l2norm(torch.randn(T, Hk, Dk, generator=g)).to(BF).cuda()
+    kk = oracle.l2norm(torch.randn(T, Hk, Dk, generator=g)).to(BF).cuda()
+    vv = torch.randn(T, Hv, Dk, generator=g).to(BF).cuda()
+    gg = (-torch.rand(T, Hv, generator=g) * 0.2).cuda()
+    beta = torch.sigmoid(torch.randn(T, Hv, generator=g)).cuda()
+    cs = torch.from_numpy(np.concatenate([[0], np.cumsum([(n + 63) // 64 for n in lengths])]).astype(np.int32))
+    nc = int(cs[-1])
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    o0, S0 = ops.gdn_chunk_scan(qq, kk, vv, gg, beta, rs.cuda(), cs.cuda(), nc, None, None, True, Dk ** -0.5,
+                                status=status)
+    o0, S0 = o0.clone(), S0.clone()
+    for _ in range(4):
+        o, S = ops.gdn_chunk_scan(qq, kk, vv, gg, beta, rs.cuda(), cs.cuda(), nc, None, None, True, Dk ** -0.5,
+                                  status=status)
+        assert torch.equal(o, o0) and torch.equal(S, S0)
+    assert int(status.item()) == 0
