@@ -80,6 +80,14 @@ __device__ __forceinline__ uint4 decode8(uint32_t x, __nv_bfloat162 s2) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
 __device__ __forceinline__ void cpa16(uint32_t dst, const void* src, bool ok) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0) : "memory");
 }
@@ -199,13 +207,15 @@ __global__ void __launch_bounds__(NT, 1) moe_w4a16_tc_kernel(const __grid_consta
     for (int i = 0; i < 16; ++i) id_next[i] = p.sorted_ids[(int64_t)tile_of(blockIdx.x) * BM + rb + 8 * i];
     for (int it = blockIdx.x; it < n_items && ok; it += G) {
       const int tile = tile_of(it);
-      int64_t off[16];  // element offset of the row's chunk; -1: padding row (zero-filled)
+      const __nv_bfloat16* src[16];  // the row's 16-byte chunk at k = 0 (row 0 for a padding row, zero-filled)
+      uint32_t live = 0;             // bit i: row rb + 8 i is an assignment
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int id = id_next[i];
         // GEMM 1 gathers the token (or received row) of the assignment; GEMM 2 reads its own sorted row
-        const int64_t row = id < 0 ? -1 : (GATED ? id / p.topk : (int64_t)tile * BM + rb + 8 * i);
-        off[i] = row < 0 ? -1 : row * p.lda + c8 * 8;
+        const int64_t row = id < 0 ? 0 : (GATED ? id / p.topk : (int64_t)tile * BM + rb + 8 * i);
+        src[i] = p.A + row * p.lda + c8 * 8;
+        live |= (id >= 0 ? 1u : 0u) << i;
       }
       if (it + G < n_items) {
 #pragma unroll
@@ -217,8 +227,7 @@ __global__ void __launch_bounds__(NT, 1) moe_w4a16_tc_kernel(const __grid_consta
         if (!ok) break;
         const uint32_t dst = sbase + L::a(s) + doff;
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          cpa16(dst + i * 1024, p.A + (off[i] < 0 ? 0 : off[i] + kb * BK), off[i] >= 0);
+        for (int i = 0; i < 16; ++i) cpa16(dst + i * 1024, src[i] + kb * BK, (live >> i) & 1u);
         asm volatile("cp.async.commit_group;\n" ::: "memory");
         if (pending >= 0) {
           asm volatile("cp.async.wait_group 1;\n" ::: "memory");
@@ -239,6 +248,13 @@ __global__ void __launch_bounds__(NT, 1) moe_w4a16_tc_kernel(const __grid_consta
     constexpr int U = BN / 64;
     const int grp = (warp - 4) >> 2, ct = ((warp - 4) & 3) * 32 + lane, hf = ct & 1, rr0 = ct >> 1;
     const int gk = p.K / GROUP;
+    // 32-bit shared addresses: the codes of row rr0 (+ 64 j rows), and row rr0 of the B stage: row r of a 128B-swizzled
+    // K-major tile starts at r * 128, its 16-byte unit u sits at (u ^ (r & 7)) * 16; r & 7 is the same for every j
+    const uint32_t code0 = sbase + L::code(0) + rr0 * 32 + hf * 16;
+    const uint32_t b0 = sbase + L::b(0) + rr0 * 128;
+    uint32_t xo[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) xo[w] = (uint32_t)(((hf * 4 + w) ^ (rr0 & 7)) << 4);
     bool ok = true;
     int q = 0;
     const __nv_bfloat16* sp[U];  // this thread's rows' scales for the current item
@@ -279,7 +295,7 @@ __global__ void __launch_bounds__(NT, 1) moe_w4a16_tc_kernel(const __grid_consta
         uint4 dv[U][4];
 #pragma unroll
         for (int j = 0; j < U; ++j) {
-          const uint4 cw = *reinterpret_cast<const uint4*>(base + L::code(c) + (rr0 + 64 * j) * 32 + hf * 16);
+          const uint4 cw = lds128(code0 + c * L::kCode + j * (64 * 32));
           const __nv_bfloat162 s2 = __halves2bfloat162(s_cur[j], s_cur[j]);
           dv[j][0] = decode8(cw.x, s2);
           dv[j][1] = decode8(cw.y, s2);
@@ -288,15 +304,11 @@ __global__ void __launch_bounds__(NT, 1) moe_w4a16_tc_kernel(const __grid_consta
         }
         if (qq >= S) ok = wait_bar(&bars.empty[s], ((qq / S) - 1) & 1, p.err);
         if (!ok) break;
-        unsigned char* bt = base + L::b(s);
+        const uint32_t bt = b0 + s * L::kB;
 #pragma unroll
-        for (int j = 0; j < U; ++j) {
-          const int r = rr0 + 64 * j;
+        for (int j = 0; j < U; ++j)
 #pragma unroll
-          for (int w = 0; w < 4; ++w)
-            *reinterpret_cast<uint4*>(bt + (r >> 3) * 1024 + (r & 7) * 128 + (((hf * 4 + w) ^ (r & 7)) << 4)) =
-                dv[j][w];
-        }
+          for (int w = 0; w < 4; ++w) sts128(bt + j * (64 * 128) + xo[w], dv[j][w]);
         fence_async_smem();
         bar_arrive(&bars.full[s]);
         __syncwarp();
