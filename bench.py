@@ -11,6 +11,10 @@ device; requests are seeded synthetic token ids (no dataset). Multi-GPU: one pro
 replica serving its own 16 requests (requests are independent: weak scaling, no collective on the data path); the
 step time is the max over ranks.
 
+`--op moe` times the W4A16 MoE block of the 35B-A3B shape instead (hidden 2048, 256 experts of FFN 512, top-8;
+`--moe-tokens` rows, default 131072 = a level-0 pass of 8 requests of 16384 tokens): routing, the two grouped GEMMs
+and the combine per step, each timed with CUDA events, TFLOP/s of the grouped GEMMs against the measured bf16 peak.
+
 `--impl reference` times the reference algorithm on the host cores instead: the CPU oracle (oracle/hybrid.py, a
 restatement of the reference's readout pinned to its golden outputs) on one request of the same workload through a
 2-layer slice of the model (one DeltaNet and one attention layer over every level), its per-layer times weighted by
@@ -168,6 +172,57 @@ def cpu_reference_rate(steps=1, warmup=0):
     return 1.0 / per_request, sample
 
 
+def run_moe(args):
+    """The MoE block of the A3B shape on one GPU: route -> gate/up GEMM -> down GEMM -> combine."""
+    from janus_b200 import ops
+    from janus_b200.synthetic import int4_quantized
+    device = torch.device("cuda", 0)
+    S, E, k, H, I = args.moe_tokens, 256, 8, 2048, 512
+    g = torch.Generator(device=device).manual_seed(0)
+    x = (torch.randn(S, H, generator=g, device=device) * 0.5).to(torch.bfloat16)
+    logits = torch.randn(S, E, generator=g, device=device)
+    shared = torch.randn(S, H, generator=g, device=device).to(torch.bfloat16)
+    sgate = torch.randn(S, generator=g, device=device)
+    gu_codes, gu_scales = int4_quantized((E, 2 * I, H), 11, "experts", device)
+    dn_codes, dn_scales = int4_quantized((E, H, I), 12, "experts", device)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)  # > L2 between steps
+    names = ["moe_route", "gemm_gate_up", "gemm_down", "moe_combine"]
+    times = {n: [] for n in names}
+    for step in range(args.warmup + args.steps):
+        flush.zero_()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        ev[0].record()
+        plan = ops.moe_route(logits, k)
+        ev[1].record()
+        h = ops.moe_grouped_w4a16(x, gu_codes, gu_scales, plan, True, k, status=status)
+        ev[2].record()
+        y2 = ops.moe_grouped_w4a16(h, dn_codes, dn_scales, plan, False, k, topk_w=plan[1], status=status)
+        ev[3].record()
+        ops.moe_combine(y2, k, shared, sgate)
+        ev[4].record()
+        torch.cuda.synchronize()
+        if step >= args.warmup:
+            for i, n in enumerate(names):
+                times[n].append(ev[i].elapsed_time(ev[i + 1]))
+    if int(status.item()) != 0:
+        raise RuntimeError("moe bench: a device-side wait ran out")
+    ms = {n: statistics.median(v) for n, v in times.items()}
+    A = S * k
+    flops = {"gemm_gate_up": 2.0 * A * 2 * I * H, "gemm_down": 2.0 * A * H * I}
+    pk, kind = peaks()
+    gemm_ms = ms["gemm_gate_up"] + ms["gemm_down"]
+    achieved = (flops["gemm_gate_up"] + flops["gemm_down"]) / (gemm_ms * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": "MoE W4A16 grouped GEMMs, A3B shape (hidden 2048, 256 experts x FFN 512, top-8)",
+        "value": achieved, "unit": "TFLOP/s", "steps": args.steps, "warmup": args.warmup,
+        "config": {"tokens": S, "assignments": A, "experts": E, "top_k": k, "l2": "256 MiB written between steps"},
+        "ms": ms, "tflops": {n: flops[n] / (ms[n] * 1e-3) / 1e12 for n in flops},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / pk["bf16_tflops"], "peak_kind": kind + " (burst bf16)"},
+    }))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -177,9 +232,14 @@ def main():
     ap.add_argument("--requests", type=int, default=REQUESTS_PER_GPU)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="debug: fewer layers (not a valid bench number)")
+    ap.add_argument("--op", default="readout", choices=["readout", "moe"])
+    ap.add_argument("--moe-tokens", type=int, default=131072)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.op == "moe":
+        run_moe(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return

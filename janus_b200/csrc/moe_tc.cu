@@ -342,7 +342,7 @@ __global__ void __launch_bounds__(NT, 1) moe_w4a16_tc_kernel(const __grid_consta
         const int sid = __shfl_sync(kFull, id, src);
         orow[k] = sid < 0 ? -1 : (GATED ? (int64_t)tile * BM + 32 * eq + src : (int64_t)sid);
       }
-      ok = __all_sync(kFull, wait_bar(&bars.acc_full[ab], (i >> 1) & 1, p.err));
+      ok = __all_sync(kFull, wait_bar_sleep(&bars.acc_full[ab], (i >> 1) & 1, p.err));
       if (!ok) break;
       fence_after();
       const uint32_t la = tm + ((uint32_t)(32 * eq) << 16) + ab * BN;

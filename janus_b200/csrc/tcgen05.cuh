@@ -80,6 +80,29 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int32_t
   if (!done && err) atomicExch(err, 1);
   return done != 0;
 }
+// the same for long waits of warps off the critical path (an epilogue waiting for a whole accumulation): try_wait
+// with a suspend-time hint, so the warp sleeps until the phase completes instead of polling and taking issue slots
+// from the warps on its scheduler that do the work
+__device__ __forceinline__ bool wait_bar_sleep(uint64_t* bar, uint32_t parity, int32_t* err) {
+  constexpr uint32_t kHintNs = 20000;
+  uint32_t done = 0;
+  uint64_t t0 = 0;
+  for (long it = 0; !done; ++it) {
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(s32(bar)), "r"(parity), "r"(kHintNs)
+        : "memory");
+    if (!done && (it & 15) == 15) {
+      const uint64_t now = global_ns();
+      if (t0 == 0) t0 = now;
+      const bool other = err && *reinterpret_cast<volatile int32_t*>(err) != 0;
+      if (other || now - t0 > kWaitNs || it > kSpinLimit) break;
+    }
+  }
+  if (!done && err) atomicExch(err, 1);
+  return done != 0;
+}
 // the same, bounded by wall time only: for the wind-down waits (the CTA's own TMA loads landing, its MMAs
 // draining) that must not be cut short because another CTA gave up
 __device__ __forceinline__ bool wait_bar_quiet(uint64_t* bar, uint32_t parity, int32_t* err) {
