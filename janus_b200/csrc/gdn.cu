@@ -16,7 +16,7 @@ namespace jb {
 constexpr int kProThreads = 256;
 constexpr int kMaxTaps = 8;
 constexpr int kProTokens = 96;  // tokens per CTA: each thread slides its conv window over them
-constexpr int kProBatch = 4;    // token loads a thread has in flight at once
+constexpr int kProBatch = 2;    // tokens per step; the next step's loads are in flight while a step computes
 
 // grid (token tiles of kProTokens, channel blocks of 8 * kProThreads). Thread = 8 consecutive channels; it keeps the
 // last K-1 conv inputs of its channels in registers while it walks the tile's tokens, so every projection element is
@@ -37,38 +37,46 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
   const bool live = vec * 8 < C;
   const int c0 = live ? vec * 8 : 0;
   const int lanes_per_head = Dk >> 3;
-  __nv_bfloat162 wp[4][K];  // conv taps of channel pairs (2u, 2u+1), kept packed to save registers
+  // q and k channels get an l2 norm over their head (a shuffle reduction); v channels skip it. Uniform over a warp
+  // whenever 2 * Hk * Dk is a multiple of 256 channels; otherwise the warp reduces for all its lanes.
+  const bool warp_qk = __any_sync(0xffffffffu, live && c0 < 2 * key_dim);
+  float wf[8][K];  // conv taps, fp32
 #pragma unroll
-  for (int u = 0; u < 4; ++u)
+  for (int u = 0; u < 8; ++u)
 #pragma unroll
-    for (int j = 0; j < K; ++j) {
-      const __nv_bfloat16 zero = __float2bfloat16(0.f);
-      wp[u][j] = live ? __halves2bfloat162(conv_w[(int64_t)(c0 + 2 * u) * K + j], conv_w[(int64_t)(c0 + 2 * u + 1) * K + j])
-                      : __halves2bfloat162(zero, zero);
-    }
+    for (int j = 0; j < K; ++j) wf[u][j] = live ? bf2f(conv_w[(int64_t)(c0 + u) * K + j]) : 0.f;
   float hist[K - 1][8];  // hist[j]: conv input at relative position j - (K-1) before the current token
   int cur_row = -1;
   int64_t r0 = 0, L = 0;
   const __nv_bfloat16* tail = nullptr;
+  // the next batch's loads are issued before the current batch is processed (software pipelining)
+  bf16x8 xn[kProBatch];
+  int rows_n[kProBatch];
+  auto load_batch = [&](int64_t tb) {
+#pragma unroll
+    for (int b = 0; b < kProBatch; ++b) {
+      const int64_t t = tb + b < t1 ? tb + b : t1 - 1;
+      rows_n[b] = row_of_token[t];
+      if (live) xn[b] = *reinterpret_cast<const bf16x8*>(proj + t * proj_stride + c0);
+    }
+  };
+  load_batch(t0);
   for (int64_t tb = t0; tb < t1; tb += kProBatch) {
-    // the batch's loads go out together (memory-level parallelism), then the tokens are processed in order
     bf16x8 xr[kProBatch];
     int rows[kProBatch];
 #pragma unroll
     for (int b = 0; b < kProBatch; ++b) {
-      const int64_t t = tb + b < t1 ? tb + b : t1 - 1;
-      rows[b] = row_of_token[t];
-      if (live) xr[b] = *reinterpret_cast<const bf16x8*>(proj + t * proj_stride + c0);
+      xr[b] = xn[b];
+      rows[b] = rows_n[b];
     }
-    // conv + silu of every token of the batch (the window refills at a row start), then the l2 sums of all of them
-    // reduced together (independent shuffle chains), then the stores
-    float acc[kProBatch][8];
+    if (tb + kProBatch < t1) load_batch(tb + kProBatch);
+    bf16x8 acc[kProBatch];  // conv + silu, rounded once to bf16 as the reference does
 #pragma unroll
     for (int b = 0; b < kProBatch; ++b) {
       const int64_t t = tb + b;
       if (t >= t1) {
 #pragma unroll
-        for (int u = 0; u < 8; ++u) acc[b][u] = 0.f;
+        for (int u = 0; u < 4; ++u) acc[b].h[u] = __floats2bfloat162_rn(0.f, 0.f);
         continue;
       }
       const int row = rows[b];
@@ -81,12 +89,9 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
 #pragma unroll
         for (int j = 0; j < K - 1; ++j) {
           const int64_t e = i + j;  // ext index of relative position j - (K-1)
-          if (!live) {
-#pragma unroll
-            for (int u = 0; u < 8; ++u) hist[j][u] = 0.f;
-          } else if (e >= K - 1) {
+          if (live && e >= K - 1) {
             load8(proj + (r0 + e - (K - 1)) * proj_stride + c0, hist[j]);
-          } else if (tail) {
+          } else if (live && tail) {
             load8(tail + e * C + c0, hist[j]);
           } else {
 #pragma unroll
@@ -101,19 +106,15 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
         x[2 * u] = f.x;
         x[2 * u + 1] = f.y;
       }
+      float a[8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float2 wl = __bfloat1622float2(wp[u][K - 1]);
-        float a0 = x[2 * u] * wl.x, a1 = x[2 * u + 1] * wl.y;
+      for (int u = 0; u < 8; ++u) {
+        a[u] = x[u] * wf[u][K - 1];
 #pragma unroll
-        for (int j = 0; j < K - 1; ++j) {
-          const float2 wj = __bfloat1622float2(wp[u][j]);
-          a0 += hist[j][2 * u] * wj.x;
-          a1 += hist[j][2 * u + 1] * wj.y;
-        }
-        acc[b][2 * u] = bf2f(f2bf(silu_fast(a0)));  // rounded once, as the reference does
-        acc[b][2 * u + 1] = bf2f(f2bf(silu_fast(a1)));
+        for (int j = 0; j < K - 1; ++j) a[u] += hist[j][u] * wf[u][j];
       }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[b].h[u] = __floats2bfloat162_rn(silu_fast(a[2 * u]), silu_fast(a[2 * u + 1]));
       // slide the window
 #pragma unroll
       for (int j = 0; j < K - 2; ++j)
@@ -126,33 +127,42 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
         for (int j = 0; j < K - 1; ++j) store8(tail_out + ((int64_t)row * (K - 1) + j) * C + c0, hist[j]);
       }
     }
-    // l2 norm over each q / k head: lanes_per_head consecutive lanes hold one head
-    float ss[kProBatch];
+    float rn[kProBatch];  // 1 / l2 norm of the token's head (q, k channels)
+    if (warp_qk) {
 #pragma unroll
-    for (int b = 0; b < kProBatch; ++b) {
-      ss[b] = 0.f;
+      for (int b = 0; b < kProBatch; ++b) {
+        rn[b] = 0.f;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) ss[b] += acc[b][u] * acc[b][u];
+        for (int u = 0; u < 4; ++u) {
+          const float2 f = __bfloat1622float2(acc[b].h[u]);
+          rn[b] += f.x * f.x + f.y * f.y;
+        }
+      }
+      for (int o = lanes_per_head >> 1; o > 0; o >>= 1)
+#pragma unroll
+        for (int b = 0; b < kProBatch; ++b) rn[b] += __shfl_xor_sync(0xffffffffu, rn[b], o);
+#pragma unroll
+      for (int b = 0; b < kProBatch; ++b) rn[b] = rsqrtf(rn[b] + 1e-6f);
     }
-    for (int o = lanes_per_head >> 1; o > 0; o >>= 1)
-#pragma unroll
-      for (int b = 0; b < kProBatch; ++b) ss[b] += __shfl_xor_sync(0xffffffffu, ss[b], o);
     if (live) {
 #pragma unroll
       for (int b = 0; b < kProBatch; ++b) {
         const int64_t t = tb + b;
         if (t >= t1) break;
         if (c0 < 2 * key_dim) {
-          const float r = rsqrtf(ss[b] + 1e-6f);
           float o8[8];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) o8[u] = acc[b][u] * r;
+          for (int u = 0; u < 4; ++u) {
+            const float2 f = __bfloat1622float2(acc[b].h[u]);
+            o8[2 * u] = f.x * rn[b];
+            o8[2 * u + 1] = f.y * rn[b];
+          }
           if (c0 < key_dim)
             store8(q + t * key_dim + c0, o8);
           else
             store8(k + t * key_dim + (c0 - key_dim), o8);
         } else {
-          store8(v + t * (int64_t)(Hv * Dv) + (c0 - 2 * key_dim), acc[b]);
+          *reinterpret_cast<bf16x8*>(v + t * (int64_t)(Hv * Dv) + (c0 - 2 * key_dim)) = acc[b];
         }
       }
     }
