@@ -97,13 +97,18 @@ int janus_b200_gdn_fork_recurrent(const void* q, const void* k, const void* v, c
  * bytes. status: optional device int32, zero on entry, set to 1 if a bounded device-side wait ran out (after 1 s;
  * the output is then invalid); NULL: not reported. Same results as janus_b200_gdn_fork_recurrent up to fp32/bf16
  * accumulation order.
+ * segment: NULL, or int32 [T] ids of consecutive token segments (the state fork packed into chunks): tokens of
+ * different segments do not interact and every segment of row b starts from state_in[state_row[b]] (the parent
+ * state of sibling rows whose tokens were packed into one row of at most 64 tokens). Every row must then be a
+ * single chunk and state_out NULL.
  * Replaces fla chunk_gated_delta_rule (janus/hybrid.py:100-125, 1064-1069; transformers
  * torch_chunk_gated_delta_rule). */
 int janus_b200_gdn_chunk_scan(const void* q, const void* k, const void* v, const float* g, const float* beta,
                               int64_t T, int64_t B, const int32_t* row_start, const int32_t* chunk_start,
-                              int64_t n_chunks, const float* state_in, const int32_t* state_row, float* state_out,
-                              int64_t Hk, int64_t Hv, int64_t Dk, int64_t Dv, float scale, void* workspace,
-                              size_t workspace_bytes, void* o, int32_t* status, void* stream);
+                              int64_t n_chunks, const float* state_in, const int32_t* state_row,
+                              const int32_t* segment, float* state_out, int64_t Hk, int64_t Hv, int64_t Dk,
+                              int64_t Dv, float scale, void* workspace, size_t workspace_bytes, void* o,
+                              int32_t* status, void* stream);
 
 /* Workspace bytes janus_b200_gdn_chunk_scan needs for T tokens, n_chunks chunks and Hv value heads. */
 size_t janus_b200_gdn_chunk_scan_workspace(int64_t T, int64_t n_chunks, int64_t Hv);

@@ -129,12 +129,14 @@ struct PrepSmem {
   float tf[CT * PADF];
   float m[32 * 33];
   float G[CT], eG[CT], beta[CT], graw[CT];
+  int32_t seg[CT];  // segment of each token (tokens of different segments do not interact); 0 when unsegmented
 };
 
 __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
     const float* __restrict__ g, const float* __restrict__ beta, const int32_t* __restrict__ row_start,
-    const int32_t* __restrict__ chunk_start, int B, int Hk, int Hv, float scale, __nv_bfloat16* __restrict__ Wg,
+    const int32_t* __restrict__ chunk_start, const int32_t* __restrict__ segment, int B, int Hk, int Hv, float scale,
+    __nv_bfloat16* __restrict__ Wg,
     __nv_bfloat16* __restrict__ Ug, __nv_bfloat16* __restrict__ QKg, float* __restrict__ Gg) {
   extern __shared__ __align__(16) unsigned char raw[];
   PrepSmem& sm = *reinterpret_cast<PrepSmem*>(raw);
@@ -157,10 +159,28 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
     const bool ok = tid < nt;
     sm.graw[tid] = ok ? g[(t0 + tid) * Hv + h] : 0.f;
     sm.beta[tid] = ok ? beta[(t0 + tid) * Hv + h] : 0.f;
+    sm.seg[tid] = segment ? (ok ? segment[t0 + tid] : -1) : 0;
   }
   cp_commit_wait();
   __syncthreads();
-  if (warp == 0) {  // in-chunk cumulative sum of g (two values per lane)
+  if (warp == 0 && segment) {  // cumulative sum of g within each segment (a segmented scan, two tokens per lane)
+    const float ga = sm.graw[2 * lane], gb = sm.graw[2 * lane + 1];
+    const int sa = sm.seg[2 * lane], sb = sm.seg[2 * lane + 1], sp = lane > 0 ? sm.seg[2 * lane - 1] : -2;
+    const bool ha = sa != sp, hb = sb != sa;  // the token starts a segment
+    float v = hb ? gb : ga + gb;               // the pair's sum within the segment its last token belongs to
+    int f = (ha || hb) ? 1 : 0;                // a segment starts inside the range v covers
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, v, off);
+      const int yf = __shfl_up_sync(0xffffffffu, f, off);
+      if (lane >= off && !f) v += y;
+      if (lane >= off) f |= yf;
+    }
+    const float prev = __shfl_up_sync(0xffffffffu, v, 1);  // up to the previous lane's last token
+    const float Ga = ha ? ga : prev + ga;
+    sm.G[2 * lane] = Ga;
+    sm.G[2 * lane + 1] = hb ? gb : Ga + gb;
+  } else if (warp == 0) {  // in-chunk cumulative sum of g (two values per lane)
     const float a = sm.graw[2 * lane], b = a + sm.graw[2 * lane + 1];
     float inc = b;
 #pragma unroll
@@ -204,7 +224,7 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
         float qv[2];
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-          const float dec = (j + u <= i) ? __expf(sm.G[i] - sm.G[j + u]) : 0.f;  // G_i - G_j <= 0
+          const float dec = (j + u <= i && sm.seg[i] == sm.seg[j + u]) ? __expf(sm.G[i] - sm.G[j + u]) : 0.f;
           sm.n[i * PADF + j + u] = (j + u < i) ? -sm.beta[i] * kk[n][e + u] * dec : 0.f;
           qv[u] = (j + u <= i) ? qk[n][e + u] * dec * scale : 0.f;
         }
@@ -333,7 +353,8 @@ int gdn_state_tc(const void* q, const void* k, int64_t T, int64_t B, const int32
 extern "C" int janus_b200_gdn_chunk_scan(const void* q, const void* k, const void* v, const float* g,
                                          const float* beta, int64_t T, int64_t B, const int32_t* row_start,
                                          const int32_t* chunk_start, int64_t n_chunks, const float* state_in,
-                                         const int32_t* state_row, float* state_out, int64_t Hk, int64_t Hv,
+                                         const int32_t* state_row, const int32_t* segment, float* state_out,
+                                         int64_t Hk, int64_t Hv,
                                          int64_t Dk, int64_t Dv, float scale, void* workspace, size_t workspace_bytes,
                                          void* o, int32_t* status, void* stream) {
   JB_REQUIRE(q && k && v && g && beta && row_start && chunk_start && o, JANUS_ERR_INVALID,
@@ -345,6 +366,8 @@ extern "C" int janus_b200_gdn_chunk_scan(const void* q, const void* k, const voi
              JANUS_ERR_INVALID, "gdn_chunk_scan: sizes");
   JB_REQUIRE(JB_ALIGNED(q, 16) && JB_ALIGNED(k, 16) && JB_ALIGNED(v, 16) && JB_ALIGNED(o, 16), JANUS_ERR_ALIGNMENT,
              "gdn_chunk_scan: q, k, v, o must be 16-byte aligned");
+  JB_REQUIRE(!segment || !state_out, JANUS_ERR_INVALID,
+             "gdn_chunk_scan: a segmented scan has no final state (its segments each end their own)");
   const size_t need = janus_b200_gdn_chunk_scan_workspace(T, n_chunks, Hv);
   JB_REQUIRE(workspace && workspace_bytes >= need && JB_ALIGNED(workspace, 256), JANUS_ERR_WORKSPACE,
              "gdn_chunk_scan: workspace %zu bytes (256-aligned) < %zu", workspace_bytes, need);
@@ -365,7 +388,7 @@ extern "C" int janus_b200_gdn_chunk_scan(const void* q, const void* k, const voi
   if (n_chunks > 0) {
     gdn_chunk_prep_kernel<<<dim3((unsigned)Hv, (unsigned)n_chunks), 256, sizeof(PrepSmem), s>>>(
         (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, g, beta, row_start, chunk_start,
-        (int)B, (int)Hk, (int)Hv, scale, Wg, Ug, QKg, Gg);
+        segment, (int)B, (int)Hk, (int)Hv, scale, Wg, Ug, QKg, Gg);
     int st = launch_status("gdn_chunk_scan/prep");
     if (st) return st;
   }

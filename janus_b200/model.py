@@ -110,6 +110,11 @@ class DecisionReadout:
                     o, S = ops.gdn_chunk_scan(q, k, v, g, beta, rs, plan[(d, "chunk_start")], int(lv.chunk_start[-1]),
                                               parent_state[1], plan[(d, "parent")] if d > 0 else None, lv.keep,
                                               1.0 / math.sqrt(s.lin_k_dim), status=self.status)
+                elif self._packed_fork(lv):
+                    fc_parent = plan[(d, "fc_parent")]
+                    o, S = ops.gdn_chunk_scan(q, k, v, g, beta, plan[(d, "fc_start")], plan[(d, "fc_chunks")],
+                                              int(fc_parent.numel()), parent_state[1], fc_parent, False,
+                                              1.0 / math.sqrt(s.lin_k_dim), status=self.status, segment=rot)
                 else:
                     o, S = ops.gdn_fork_recurrent(q, k, v, g, beta, rs, plan[(d, "child_start")], parent_state[1],
                                                   lv.keep, 1.0 / math.sqrt(s.lin_k_dim))
@@ -176,6 +181,13 @@ class DecisionReadout:
         (the reference's split at janus/hybrid.py:115-118, RECURRENT_TOKENS = 16)."""
         s = self.shape
         return s.lin_k_dim == 128 and s.lin_v_dim == 128 and lv.T >= self.CHUNK_MIN_TOKENS * lv.B
+
+    def _packed_fork(self, lv):
+        """Short sibling rows that keep no state run as the segmented chunk scan: their tokens packed into 64-token
+        runs per parent, each row starting from the parent's state (tensor cores instead of a token-by-token walk)."""
+        s = self.shape
+        return (s.lin_k_dim == 128 and s.lin_v_dim == 128 and lv.depth > 0 and not lv.keep
+                and lv.fork_chunks() is not None)
 
     def _heads(self, d, x, plan, logits):
         ro = self._readout

@@ -157,10 +157,15 @@ def gdn_fork_recurrent(q, k, v, g, beta, row_start, child_start, state_in, keep_
 
 @_instrument("gdn_chunk_scan", 2)
 def gdn_chunk_scan(q, k, v, g, beta, row_start, chunk_start, n_chunks, state_in, state_row, keep_state, scale,
-                   status=None):
+                   status=None, segment=None):
     """Long rows in 64-token chunks; row b starts from state_in[state_row[b]] (None: zeros / identity map).
     chunk_start int32 [B+1] (first chunk of each row), n_chunks = chunk_start[B]. status: optional device int32
-    word set to 1 if a bounded device-side wait ran out."""
+    word set to 1 if a bounded device-side wait ran out. segment: optional int32 [T] ids of token segments that do
+    not interact, each starting from the row's initial state (rows of at most 64 tokens, no kept state)."""
+    if segment is not None:
+        _need(segment, I32, "segment")
+        if keep_state:
+            raise ValueError("gdn_chunk_scan: a segmented scan keeps no state")
     T, Hk, Dk = q.shape
     Hv, Dv = v.shape[1], v.shape[2]
     B = row_start.shape[0] - 1
@@ -178,8 +183,8 @@ def gdn_chunk_scan(q, k, v, g, beta, row_start, chunk_start, n_chunks, state_in,
     _lib.check(lib.janus_b200_gdn_chunk_scan(
         _ptr(q), _ptr(k), _ptr(v), _ptr(_need(g, F32, "g")), _ptr(_need(beta, F32, "beta")), T, B,
         _ptr(_need(row_start, I32, "row_start")), _ptr(_need(chunk_start, I32, "chunk_start")), n_chunks,
-        _ptr(state_in), _ptr(state_row), _ptr(state_out), Hk, Hv, Dk, Dv, scale, _ptr(ws), ws.numel(), _ptr(o),
-        _ptr(status), _stream(q)), "gdn_chunk_scan")
+        _ptr(state_in), _ptr(state_row), _ptr(segment), _ptr(state_out), Hk, Hv, Dk, Dv, scale, _ptr(ws), ws.numel(),
+        _ptr(o), _ptr(status), _stream(q)), "gdn_chunk_scan")
     return o, state_out
 
 

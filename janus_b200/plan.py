@@ -47,6 +47,36 @@ class Level:
     def B(self):
         return int(self.row_start.shape[0] - 1)
 
+    def fork_chunks(self, max_tokens=64):
+        """The rows packed into chunks for the segmented chunk scan: whole sibling rows (consecutive, same parent)
+        are gathered into runs of at most `max_tokens` tokens. Returns (token start of each run [n+1], parent row of
+        each run [n]) as int32, or None when a row is longer than max_tokens (or at depth 0)."""
+        key = ("fork", max_tokens)
+        if key in self.tiles:
+            return self.tiles[key]
+        out = None
+        lengths = np.diff(self.row_start)
+        if self.depth > 0 and (lengths.size == 0 or int(lengths.max()) <= max_tokens):
+            starts, parents = [], []
+            for p in range(self.child_start.shape[0] - 1):
+                a, b = int(self.child_start[p]), int(self.child_start[p + 1])
+                run_start, run_len = None, 0
+                for r in range(a, b):
+                    n = int(lengths[r])
+                    if run_start is None or run_len + n > max_tokens:
+                        if run_start is not None:
+                            starts.append(run_start)
+                            parents.append(p)
+                        run_start, run_len = int(self.row_start[r]), 0
+                    run_len += n
+                if run_start is not None and run_len > 0:
+                    starts.append(run_start)
+                    parents.append(p)
+            starts.append(self.T)
+            out = (np.asarray(starts, dtype=np.int32), np.asarray(parents, dtype=np.int32))
+        self.tiles[key] = out
+        return out
+
     def attention_tiles(self, tokens):
         """Query tiles of at most `tokens` tokens (janus_b200_tree_attention_tile_tokens)."""
         if tokens in self.tiles:
@@ -215,6 +245,11 @@ class DevicePlan:
                 add((d, "hi", l), hi)
             for n in tile_tokens:
                 add((d, "tiles", n), lv.attention_tiles(n))
+            fc = lv.fork_chunks()
+            if fc is not None:
+                add((d, "fc_start"), fc[0])
+                add((d, "fc_parent"), fc[1])
+                add((d, "fc_chunks"), np.arange(fc[1].shape[0] + 1, dtype=np.int32))
         for d, (rows, _) in readout.scalar.items():
             add((d, "scalar_rows"), rows)
         for d, (orows, oq, drows, _) in readout.pointer.items():

@@ -322,3 +322,40 @@ def test_tcgen05_kernels_run_to_run_identical():
                                   status=status)
         assert torch.equal(o, o0) and torch.equal(S, S0)
     assert int(status.item()) == 0
+
+
+def test_segmented_chunk_scan_is_the_state_fork():
+    """Sibling rows packed into 64-token runs (the segmented chunk scan) equal the fork: every child row runs the
+    token-by-token rule from its parent's state (oracle), rows of 1..20 tokens, several runs per parent."""
+    ops = _ops()
+    from janus_b200.plan import Level
+    Hk, Hv, D = 16, 32, 128
+    g = torch.Generator().manual_seed(21)
+    rng = np.random.default_rng(21)
+    children = [list(rng.integers(1, 21, size=n)) for n in (1, 7, 12, 3)]  # per parent: child row lengths
+    lengths = [int(x) for c in children for x in c]
+    child_start = np.concatenate([[0], np.cumsum([len(c) for c in children])]).astype(np.int32)
+    parent = np.repeat(np.arange(len(children)), [len(c) for c in children]).astype(np.int32)
+    rs, rot = _level(lengths)
+    T = int(rs[-1])
+    lv = Level(1, np.zeros(T, np.int32), np.zeros(T, np.int32), rs.numpy(), rot.numpy(), parent, [], [], child_start,
+               np.zeros(len(lengths) + 1, np.int32), [])
+    starts, parents = lv.fork_chunks()
+    q = oracle.l2norm(torch.randn(T, Hk, D, generator=g)).to(BF)
+    k = oracle.l2norm(torch.randn(T, Hk, D, generator=g)).to(BF)
+    v = torch.randn(T, Hv, D, generator=g).to(BF)
+    gg = -torch.rand(T, Hv, generator=g) * 0.5
+    beta = torch.sigmoid(torch.randn(T, Hv, generator=g))
+    S0 = torch.randn(len(children), Hv, D, D, generator=g) * 0.1
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    n = int(parents.shape[0])
+    cuda = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    o, S = ops.gdn_chunk_scan(q.cuda(), k.cuda(), v.cuda(), gg.cuda(), beta.cuda(), cuda(starts),
+                              cuda(np.arange(n + 1, dtype=np.int32)), n, S0.cuda(), cuda(parents), False, D ** -0.5,
+                              status=status, segment=rot.cuda())
+    assert S is None and int(status.item()) == 0
+    for r in range(len(lengths)):
+        a, b = int(rs[r]), int(rs[r + 1])
+        ro, _ = oracle.delta_recurrent(q[a:b].float(), k[a:b].float(), v[a:b].float(), gg[a:b], beta[a:b],
+                                       S0[int(parent[r])])
+        close(o[a:b], ro, atol=3e-2, rtol=3e-2)

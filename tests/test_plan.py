@@ -47,6 +47,25 @@ def test_tiles_cover_every_token_once_and_stay_in_one_request():
             assert (cover == 1).all()
 
 
+def test_fork_chunks_pack_whole_sibling_rows():
+    packs = [synthetic.q4b_request(vocab=4096, seed=s, state_tokens=300, questions=5) for s in range(3)]
+    levels, _ = build_levels(packs)
+    assert levels[0].fork_chunks() is None  # the state level has no parent
+    leaves = levels[-1]
+    starts, parents = leaves.fork_chunks()
+    assert starts[0] == 0 and starts[-1] == leaves.T and (np.diff(starts) > 0).all()
+    assert (np.diff(starts) <= 64).all()
+    row_bounds = set(leaves.row_start.tolist())
+    for i, p in enumerate(parents.tolist()):
+        a, b = int(starts[i]), int(starts[i + 1])
+        assert a in row_bounds and b in row_bounds  # whole rows only
+        rows = set(leaves.row_of_token[a:b].tolist())
+        assert all(int(leaves.parent[r]) == p for r in rows)  # siblings of one parent
+    assert (np.diff(parents) >= 0).all()
+    # a row longer than a run cannot be packed
+    assert leaves.fork_chunks(max_tokens=1) is None or int(np.diff(leaves.row_start).max()) <= 1
+
+
 def test_readout_layout_tree_and_listwise():
     packs = [synthetic.tiny_request(seed=0, mode="tree")]
     levels, index = build_levels(packs)
