@@ -23,7 +23,8 @@ namespace {
 
 constexpr int CT = 64;   // chunk tokens
 constexpr int DH = 128;  // Dk = Dv
-constexpr int PADF = 65; // fp32 [64][65] tiles
+constexpr int PADF = 68;  // fp32 [64][68] tiles: row stride = 4 banks, tf32 A fragments hit 32 distinct banks
+constexpr int PADM = 40;  // fp32 [32][40]: stride = 8 banks, the B fragments read from it hit 32 distinct banks
 
 __device__ __forceinline__ uint32_t s32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 __device__ __forceinline__ void cpa16(void* dst, const void* src, bool ok) {
@@ -127,7 +128,7 @@ struct PrepSmem {
   __nv_bfloat16 t2[CT * CT];  // T diag(beta e^G) (bf16): W = T diag(beta e^G) K
   float n[CT * PADF];
   float tf[CT * PADF];
-  float m[32 * 33];
+  float m[32 * PADM];
   float G[CT], eG[CT], beta[CT], graw[CT];
   int32_t seg[CT];  // segment of each token (tokens of different segments do not interact); 0 when unsegmented
 };
@@ -266,14 +267,14 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
     const int bi = (2 * hb + 1) * 16, bj = 2 * hb * 16;
     float c[4] = {0.f, 0.f, 0.f, 0.f};
     tile_mma_tf32(c, &sm.n[bi * PADF + bj], PADF, &sm.tf[bj * PADF + bj + 8 * nt], PADF, 16, lane);
-    store_tile(c, &sm.m[(hb * 16) * 33 + 8 * nt], 33, lane);
+    store_tile(c, &sm.m[(hb * 16) * PADM + 8 * nt], PADM, lane);
   }
   __syncthreads();
   if (warp < 4) {
     const int hb = warp >> 1, nt = warp & 1;
     const int bi = (2 * hb + 1) * 16, bj = 2 * hb * 16;
     float c[4] = {0.f, 0.f, 0.f, 0.f};
-    tile_mma_tf32(c, &sm.tf[bi * PADF + bi], PADF, &sm.m[(hb * 16) * 33 + 8 * nt], 33, 16, lane);
+    tile_mma_tf32(c, &sm.tf[bi * PADF + bi], PADF, &sm.m[(hb * 16) * PADM + 8 * nt], PADM, 16, lane);
     store_tile(c, &sm.tf[bi * PADF + bj + 8 * nt], PADF, lane);
   }
   __syncthreads();
@@ -283,10 +284,10 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
     const int mt = warp >> 2, nt = warp & 3;
     float c[4] = {0.f, 0.f, 0.f, 0.f};
     tile_mma_tf32(c, &sm.n[(32 + 16 * mt) * PADF], PADF, &sm.tf[8 * nt], PADF, 32, lane);
-    store_tile(c, &sm.m[(16 * mt) * 33 + 8 * nt], 33, lane);
+    store_tile(c, &sm.m[(16 * mt) * PADM + 8 * nt], PADM, lane);
     __syncthreads();
     c[0] = c[1] = c[2] = c[3] = 0.f;
-    tile_mma_tf32(c, &sm.tf[(32 + 16 * mt) * PADF + 32], PADF, &sm.m[8 * nt], 33, 32, lane);
+    tile_mma_tf32(c, &sm.tf[(32 + 16 * mt) * PADF + 32], PADF, &sm.m[8 * nt], PADM, 32, lane);
     store_tile(c, &sm.tf[(32 + 16 * mt) * PADF + 8 * nt], PADF, lane);
   }
   __syncthreads();
