@@ -2,21 +2,27 @@
 //
 // 1. gdn_chunk_prep: one CTA per (chunk, value head), all chunks of all rows in parallel. With G the in-chunk
 //    cumulative g (every exponential is of a difference of G, so nothing overflows):
-//      N  = -tril_strict(diag(beta) K K^T * e^(G_i - G_j))          tensor cores, fp32 accumulate
+//      N  = -tril_strict(diag(beta) K K^T * e^(G_i - G_j))          tcgen05 (M = 128: [K; Q] K^T), fp32 in TMEM
+//      QK = tril(scale Q K^T * e^(G_i - G_j))                        the same product's lower half, stored bf16
 //      T  = (I - N)^-1                                               fp32: 16x16 diagonal blocks by substitution,
 //                                                                    then doubling stages 16 -> 32 -> 64 (tf32 MMAs)
-//      U  = (T diag(beta)) V,  W = (T diag(beta e^G)) K              bf16 operands, fp32 accumulate, stored bf16
-//      QK = tril(scale Q K^T * e^(G_i - G_j))                        stored bf16, plus G itself
+//      U  = (T diag(beta)) V,  W = (T diag(beta e^G)) K              tcgen05 as U^T = V^T (T diag(beta))^T and
+//                                                                    W^T = K^T (T diag(beta e^G))^T (M = 128
+//                                                                    value / key columns), stored bf16
+//    K, Q, V arrive by TMA; U, W, QK leave by TMA stores from swizzled staging tiles.
 // 2. the sequential pass (gdn_state_tc.cu, tcgen05): one CTA per (row, value head) walking the row's chunks in
 //    order with the fp32 state in TMEM:
 //      V' = U - W S;   O = scale e^G (Q S) + QK V';   S = e^(G_last) S + K^T (V' * e^(G_last - G))
 //    (S rounded to bf16 for the products, as fla's chunk kernels do; the e^G factors scale rows of fp32 results
 //    instead of the bf16 operands, so q and k are used as loaded). The WY form of transformers'
 //    torch_chunk_gated_delta_rule (the reference's CPU rule) and of fla's chunk kernels (its GPU rule). A row's last
-//    chunk is ragged: the missing tokens are zeros with g = beta = 0, which leaves the state untouched.
+//    chunk is ragged: the tokens past its end get g = beta = 0 and are masked, which leaves the state untouched.
+// With a segment id per token (the state fork packed into chunks: sibling rows of one parent share a chunk), G is a
+// cumulative sum within each segment and every mask also requires the same segment, so each segment runs from the
+// chunk's initial state on its own.
 // The prep writes W, U, QK and G chunk-major ([chunk][value head][64 tokens], zeros past a row's end) for the
-// sequential pass's TMA loads; it uses mma.sync m16n8k16 (bf16, fp32 accumulate) on XOR-swizzled shared tiles.
-#include "common.cuh"
+// sequential pass's TMA loads.
+#include "tcgen05.cuh"
 
 namespace jb {
 namespace {
@@ -25,29 +31,6 @@ constexpr int CT = 64;   // chunk tokens
 constexpr int DH = 128;  // Dk = Dv
 constexpr int PADF = 68;  // fp32 [64][68] tiles: row stride = 4 banks, tf32 A fragments hit 32 distinct banks
 constexpr int PADM = 40;  // fp32 [32][40]: stride = 8 banks, the B fragments read from it hit 32 distinct banks
-
-__device__ __forceinline__ uint32_t s32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-__device__ __forceinline__ void cpa16(void* dst, const void* src, bool ok) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s32(dst)), "l"(src), "r"(ok ? 16 : 0));
-}
-__device__ __forceinline__ void cp_commit_wait() {
-  asm volatile("cp.async.commit_group;\n" ::);
-  asm volatile("cp.async.wait_group 0;\n" ::);
-}
-__device__ __forceinline__ void ldx4(uint32_t* r, const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(s32(p)));
-}
-__device__ __forceinline__ void ldx4t(uint32_t* r, const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(s32(p)));
-}
-__device__ __forceinline__ void mma(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
 
 // tf32 tensor-core products on fp32 shared tiles, for the blocks of the triangular inverse (tf32 keeps 10 mantissa
 // bits, more than the bf16 that T is rounded to afterwards; fla's Triton solve multiplies its fp32 blocks in tf32 too)
@@ -80,34 +63,6 @@ __device__ __forceinline__ void store_tile(const float* c, float* D, int ldd, in
   D[(g + 8) * ldd + 2 * t + 1] = c[3];
 }
 
-// swizzled bf16 tiles [rows][COLS]: COLS >= 64 XOR the 16-byte chunk with row & 7; COLS == 32 (64-byte rows) with
-// (row >> 1) & 3, so the 8 rows of an ldmatrix hit 8 distinct bank groups either way
-template <int COLS>
-__device__ __forceinline__ int sw(int r, int c) {
-  if constexpr (COLS == 32) return r * 32 + (((c >> 3) ^ ((r >> 1) & 3)) << 3) + (c & 7);
-  else return r * COLS + (((c >> 3) ^ (r & 7)) << 3) + (c & 7);
-}
-// A fragment (16x16) at (m0, k0) of a row-major tile [m][k]
-template <int COLS>
-__device__ __forceinline__ void lda(uint32_t* a, const __nv_bfloat16* t, int m0, int k0, int lane) {
-  ldx4(a, t + sw<COLS>(m0 + (lane & 15), k0 + ((lane >> 4) << 3)));
-}
-// A fragment (16x16) at (m0, k0) of A = X^T, X row-major [k][m]
-template <int COLS>
-__device__ __forceinline__ void lda_t(uint32_t* a, const __nv_bfloat16* t, int m0, int k0, int lane) {
-  ldx4t(a, t + sw<COLS>(k0 + (lane & 7) + ((lane >> 4) << 3), m0 + (((lane >> 3) & 1) << 3)));
-}
-// B fragments of n-tiles n0, n0+8 at k0 with B[k][n] = X[n][k], X row-major [n][k]
-template <int COLS>
-__device__ __forceinline__ void ldb_nk(uint32_t* b, const __nv_bfloat16* t, int n0, int k0, int lane) {
-  ldx4(b, t + sw<COLS>(n0 + (lane & 7) + ((lane >> 4) << 3), k0 + (((lane >> 3) & 1) << 3)));
-}
-// B fragments of n-tiles n0, n0+8 at k0 with B[k][n] = X[k][n], X row-major [k][n]
-template <int COLS>
-__device__ __forceinline__ void ldb_kn(uint32_t* b, const __nv_bfloat16* t, int n0, int k0, int lane) {
-  ldx4t(b, t + sw<COLS>(k0 + (lane & 7) + (((lane >> 3) & 1) << 3), n0 + ((lane >> 4) << 3)));
-}
-
 // the row of global chunk c (chunk_start: prefix sum of the rows' chunk counts, rows with no chunk skipped over)
 __device__ __forceinline__ int chunk_row(const int32_t* chunk_start, int B, int c) {
   int lo = 0, hi = B;  // invariant: chunk_start[lo] <= c < chunk_start[hi]
@@ -120,53 +75,117 @@ __device__ __forceinline__ int chunk_row(const int32_t* chunk_start, int B, int 
 
 // ------------------------------------------------------------------------------------------------ chunk prep
 
-struct PrepSmem {
-  __nv_bfloat16 q[CT * DH];
-  __nv_bfloat16 k[CT * DH];
-  __nv_bfloat16 v[CT * DH];
-  __nv_bfloat16 t[CT * CT];   // T diag(beta) (bf16): U = T diag(beta) V
-  __nv_bfloat16 t2[CT * CT];  // T diag(beta e^G) (bf16): W = T diag(beta e^G) K
-  float n[CT * PADF];
-  float tf[CT * PADF];
-  float m[32 * PADM];
-  float G[CT], eG[CT], beta[CT], graw[CT];
-  int32_t seg[CT];  // segment of each token (tokens of different segments do not interact); 0 when unsegmented
+// Shared memory of the prep (byte offsets from a 1024-aligned base). Operand tiles are in the UMMA 128B-swizzled
+// K-major layout: [64-column atom][rows][128 bytes], the 16-byte unit u of row r at (u ^ (r & 7)) * 16.
+//   KQ  [2 atoms][128 rows]: rows 0-63 the chunk's K, rows 64-127 its Q, so [K; Q] is one M=128 operand and K
+//       alone (rows 0-63) the N=64 one; QK^T is staged in the Q half of atom 0 once the products are done
+//   V   [2 atoms][64 rows];  T1 = T diag(beta), T2 = T diag(beta e^G) [64 rows][64] (one atom each)
+//   N, TF fp32 [64][PADF] (the triangular inverse), then the staging of U and W for their TMA stores
+constexpr uint32_t kOffKQ = 0, kOffV = 32768, kOffT1 = 49152, kOffT2 = 57344;
+constexpr uint32_t kOffN = 65536, kOffTF = 83968, kOffM = 102400;  // N, TF on 1024-byte boundaries (staging)
+constexpr uint32_t kOffVec = kOffM + 32 * PADM * 4;                 // G, eG, beta, graw (fp32 [64]), seg (int [64])
+constexpr uint32_t kOffBar = kOffVec + 5 * CT * 4;
+constexpr uint32_t kPrepSmem = kOffBar + 32 + 1024;  // + alignment slack
+constexpr uint32_t kPrepTmemCols = 256;  // P1 (KK^T | QK^T) cols 0-63, U^T cols 64-127, W^T cols 128-191
+
+struct PrepParams {
+  CUtensorMap qmap, kmap, vmap;       // [T][H][128] bf16 loads, boxes 64 dims x 1 head x 64 tokens
+  CUtensorMap wmap, umap, qkmap;      // chunk-major workspace stores, boxes 64 x 64
+  const float* g;
+  const float* beta;
+  const int32_t* row_start;
+  const int32_t* chunk_start;
+  const int32_t* segment;
+  float* Gg;
+  int32_t* err;
+  int B, Hk, Hv;
+  float scale;
 };
 
-__global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
-    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
-    const float* __restrict__ g, const float* __restrict__ beta, const int32_t* __restrict__ row_start,
-    const int32_t* __restrict__ chunk_start, const int32_t* __restrict__ segment, int B, int Hk, int Hv, float scale,
-    __nv_bfloat16* __restrict__ Wg,
-    __nv_bfloat16* __restrict__ Ug, __nv_bfloat16* __restrict__ QKg, float* __restrict__ Gg) {
-  extern __shared__ __align__(16) unsigned char raw[];
-  PrepSmem& sm = *reinterpret_cast<PrepSmem*>(raw);
+// 2D TMA tile store from this CTA's shared memory (no multicast); x is a multiple of 64 elements (16-byte rule)
+__device__ __forceinline__ void tma_store2(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+// byte offset of element (r, c) of a 64-column swizzled atom [rows][128 B]
+__device__ __forceinline__ uint32_t swz(int r, int c) { return r * 128 + ((((c >> 3) ^ r) & 7) << 4) + (c & 7) * 2; }
+
+__global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(const __grid_constant__ PrepParams p) {
+  extern __shared__ unsigned char raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~(uintptr_t)1023);
+  const uint32_t sbase = tcx::s32(base);
+  float* sN = reinterpret_cast<float*>(base + kOffN);
+  float* sTF = reinterpret_cast<float*>(base + kOffTF);
+  float* sM = reinterpret_cast<float*>(base + kOffM);
+  float* sG = reinterpret_cast<float*>(base + kOffVec);
+  float* seG = sG + CT;
+  float* sBeta = sG + 2 * CT;
+  float* sGraw = sG + 3 * CT;
+  int32_t* sSeg = reinterpret_cast<int32_t*>(sG + 4 * CT);
+  uint64_t* bar_load = reinterpret_cast<uint64_t*>(base + kOffBar);
+  uint64_t* bar_mma = bar_load + 1;
+  __shared__ uint32_t tmem_base;
+  __shared__ int s_ok;
+
   const int h = blockIdx.x, c = blockIdx.y;  // heads fastest: the Hv/Hk heads sharing q and k run together
-  const int hk = h / (Hv / Hk);
+  const int hk = h / (p.Hv / p.Hk);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int row = chunk_row(chunk_start, B, c);
-  const int64_t t0 = row_start[row] + (int64_t)(c - chunk_start[row]) * CT;
-  const int64_t rend = row_start[row + 1];
+  const int row = chunk_row(p.chunk_start, p.B, c);
+  const int64_t t0 = p.row_start[row] + (int64_t)(c - p.chunk_start[row]) * CT;
+  const int64_t rend = p.row_start[row + 1];
   const int nt = (rend - t0) < CT ? (int)(rend - t0) : CT;
-  for (int x = tid; x < CT * (DH / 8); x += 256) {
-    const int r = x / (DH / 8), ch = (x % (DH / 8)) * 8;
-    const bool ok = r < nt;
-    const int64_t t = ok ? t0 + r : t0;
-    cpa16(&sm.q[sw<DH>(r, ch)], q + (t * Hk + hk) * DH + ch, ok);
-    cpa16(&sm.k[sw<DH>(r, ch)], k + (t * Hk + hk) * DH + ch, ok);
-    cpa16(&sm.v[sw<DH>(r, ch)], v + (t * Hv + h) * DH + ch, ok);
+  const int rb = (c * p.Hv + h) * CT;  // first row of the chunk in the chunk-major workspace
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tcx::s32(&tmem_base)),
+                 "r"(kPrepTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+  }
+  if (tid == 0) {
+    tcx::bar_init(bar_load, 1);
+    tcx::bar_init(bar_mma, 1);
+    s_ok = 1;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (tid < CT) {
-    const bool ok = tid < nt;
-    sm.graw[tid] = ok ? g[(t0 + tid) * Hv + h] : 0.f;
-    sm.beta[tid] = ok ? beta[(t0 + tid) * Hv + h] : 0.f;
-    sm.seg[tid] = segment ? (ok ? segment[t0 + tid] : -1) : 0;
+    const bool in = tid < nt;  // tokens past the row's end: g = beta = 0 (they touch nothing)
+    sGraw[tid] = in ? p.g[(t0 + tid) * p.Hv + h] : 0.f;
+    sBeta[tid] = in ? p.beta[(t0 + tid) * p.Hv + h] : 0.f;
+    sSeg[tid] = p.segment ? (in ? p.segment[t0 + tid] : -1) : 0;
   }
-  cp_commit_wait();
+  tcx::fence_before();
   __syncthreads();
-  if (warp == 0 && segment) {  // cumulative sum of g within each segment (a segmented scan, two tokens per lane)
-    const float ga = sm.graw[2 * lane], gb = sm.graw[2 * lane + 1];
-    const int sa = sm.seg[2 * lane], sb = sm.seg[2 * lane + 1], sp = lane > 0 ? sm.seg[2 * lane - 1] : -2;
+  tcx::fence_after();
+  const uint32_t tm = tmem_base;
+  if (tid == 0) {  // K, Q, V tiles of the chunk (rows past the row's end meet beta = 0 and the masks)
+    tcx::bar_expect_tx(bar_load, 2 * 3 * CT * 64 * 2);
+#pragma unroll
+    for (int a = 0; a < 2; ++a) {
+      tcx::tma_load3(sbase + kOffKQ + a * 16384, &p.kmap, 64 * a, hk, (int)t0, bar_load);
+      tcx::tma_load3(sbase + kOffKQ + a * 16384 + 8192, &p.qmap, 64 * a, hk, (int)t0, bar_load);
+      tcx::tma_load3(sbase + kOffV + a * 8192, &p.vmap, 64 * a, h, (int)t0, bar_load);
+    }
+    // P1: [K; Q] K^T (M = 128, N = 64, K = 128): lanes 0-63 K K^T, lanes 64-127 Q K^T, columns 0-63
+    bool ok = tcx::wait_bar(bar_load, 0, p.err);
+    if (ok) {
+      tcx::fence_after();
+#pragma unroll
+      for (int s = 0; s < DH / 16; ++s) {
+        const uint32_t off = kOffKQ + (s >> 2) * 16384 + (s & 3) * 32;
+        tcx::mma(tm, tcx::sdesc(sbase + off, 16, 1024), tcx::sdesc(sbase + off, 16, 1024), tcx::idesc(128, 64, 0, 0),
+                 s > 0);
+      }
+      tcx::commit(bar_mma);
+    } else {
+      s_ok = 0;
+      tcx::wait_bar_quiet(bar_load, 0, p.err);  // the loads land before the CTA may leave
+    }
+  }
+  if (warp == 1 && p.segment) {  // cumulative sum of g within each segment (a segmented scan, two tokens per lane)
+    const float ga = sGraw[2 * lane], gb = sGraw[2 * lane + 1];
+    const int sa = sSeg[2 * lane], sb = sSeg[2 * lane + 1], sp = lane > 0 ? sSeg[2 * lane - 1] : -2;
     const bool ha = sa != sp, hb = sb != sa;  // the token starts a segment
     float v = hb ? gb : ga + gb;               // the pair's sum within the segment its last token belongs to
     int f = (ha || hb) ? 1 : 0;                // a segment starts inside the range v covers
@@ -179,10 +198,10 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
     }
     const float prev = __shfl_up_sync(0xffffffffu, v, 1);  // up to the previous lane's last token
     const float Ga = ha ? ga : prev + ga;
-    sm.G[2 * lane] = Ga;
-    sm.G[2 * lane + 1] = hb ? gb : Ga + gb;
-  } else if (warp == 0) {  // in-chunk cumulative sum of g (two values per lane)
-    const float a = sm.graw[2 * lane], b = a + sm.graw[2 * lane + 1];
+    sG[2 * lane] = Ga;
+    sG[2 * lane + 1] = hb ? gb : Ga + gb;
+  } else if (warp == 1) {  // in-chunk cumulative sum of g (two values per lane)
+    const float a = sGraw[2 * lane], b = a + sGraw[2 * lane + 1];
     float inc = b;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
@@ -190,52 +209,66 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
       if (lane >= off) inc += y;
     }
     const float excl = inc - b;
-    sm.G[2 * lane] = excl + a;
-    sm.G[2 * lane + 1] = excl + b;
+    sG[2 * lane] = excl + a;
+    sG[2 * lane + 1] = excl + b;
   }
   __syncthreads();
   if (tid < CT) {
-    sm.eG[tid] = expf(sm.G[tid]);
-    Gg[((int64_t)c * Hv + h) * CT + tid] = sm.G[tid];  // chunk-major; past the row's end G stays at G[nt - 1]
+    seG[tid] = expf(sG[tid]);
+    p.Gg[(int64_t)rb + tid] = sG[tid];  // chunk-major; past the row's end G stays at G[nt - 1]
   }
-  // K K^T -> N (fp32, smem), Q K^T -> QK (bf16, global); warp: m-tile w>>1, n-tiles (w&1)*4 .. +3
-  {
-    const int mt = warp >> 1, nb = (warp & 1) * 32;
-    float kk[4][4] = {}, qk[4][4] = {};
+  __syncthreads();
+  const bool live = s_ok != 0;
+  // P1 epilogue: warp w reads TMEM lanes 32 (w & 3) .. +31, columns 32 (w >> 2) .. +31. Lanes 0-63: N = -beta_i
+  // (K K^T)_ij e^(G_i - G_j) for j < i in the same segment (fp32, shared); lanes 64-127: QK = scale (Q K^T)_ij
+  // e^(G_i - G_j) for j <= i in the same segment, rows past the row's end zero (bf16, staged for the TMA store)
+  if (live) {
+    const bool done = __all_sync(0xffffffffu, tcx::wait_bar(bar_mma, 0, p.err));
+    tcx::fence_after();
+    const int qw = warp & 3, j0 = (warp >> 2) * 32;
+    const int i = 32 * (qw & 1) + lane;
+    const uint32_t la = tm + ((uint32_t)(32 * qw) << 16) + j0;
+    float d[32];
+    tcx::tld16f(la, d);
+    tcx::tld16f(la + 16, d + 16);
+    if (done) {
+      const float Gi = sG[i];
+      const int si = sSeg[i];
+      if (qw < 2) {
+        const float nb = -sBeta[i];
+        float nv[32];
 #pragma unroll
-    for (int ks = 0; ks < DH; ks += 16) {
-      uint32_t ak[4], aq[4], b[4];
-      lda<DH>(ak, sm.k, mt * 16, ks, lane);
-      lda<DH>(aq, sm.q, mt * 16, ks, lane);
+        for (int x = 0; x < 32; ++x) {
+          const int j = j0 + x;
+          nv[x] = (j < i && sSeg[j] == si) ? nb * d[x] * __expf(Gi - sG[j]) : 0.f;
+        }
 #pragma unroll
-      for (int np = 0; np < 2; ++np) {
-        ldb_nk<DH>(b, sm.k, nb + np * 16, ks, lane);
-        mma(kk[2 * np], ak, b[0], b[1]);
-        mma(kk[2 * np + 1], ak, b[2], b[3]);
-        mma(qk[2 * np], aq, b[0], b[1]);
-        mma(qk[2 * np + 1], aq, b[2], b[3]);
+        for (int x = 0; x < 32; x += 4)
+          *reinterpret_cast<float4*>(&sN[i * PADF + j0 + x]) = make_float4(nv[x], nv[x + 1], nv[x + 2], nv[x + 3]);
+      } else {
+        uint32_t qv[16];
+#pragma unroll
+        for (int x = 0; x < 32; x += 2) {
+          float e[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int j = j0 + x + u;
+            e[u] = (j <= i && i < nt && sSeg[j] == si) ? p.scale * d[x + u] * __expf(Gi - sG[j]) : 0.f;
+          }
+          qv[x / 2] = tcx::pack_bf16(e[0], e[1]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          *reinterpret_cast<uint4*>(base + kOffKQ + 8192 + swz(i, j0 + 8 * u)) =
+              make_uint4(qv[4 * u], qv[4 * u + 1], qv[4 * u + 2], qv[4 * u + 3]);
+        tcx::fence_async_smem();  // the staged QK is read by the TMA store
       }
     }
-    __nv_bfloat16* qkc = QKg + ((int64_t)c * Hv + h) * CT * CT;
-#pragma unroll
-    for (int n = 0; n < 4; ++n)
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        const int i = mt * 16 + (lane >> 2) + (e >> 1) * 8, j = nb + n * 8 + (lane & 3) * 2;
-        float qv[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const float dec = (j + u <= i && sm.seg[i] == sm.seg[j + u]) ? __expf(sm.G[i] - sm.G[j + u]) : 0.f;
-          sm.n[i * PADF + j + u] = (j + u < i) ? -sm.beta[i] * kk[n][e + u] * dec : 0.f;
-          qv[u] = (j + u <= i) ? qk[n][e + u] * dec * scale : 0.f;
-        }
-        *reinterpret_cast<__nv_bfloat162*>(qkc + i * CT + j) = __floats2bfloat162_rn(qv[0], qv[1]);
-      }
   }
   __syncthreads();  // N complete
   // T = (I - N)^-1: diagonal 16x16 blocks (warps 0-3, lane c < 16 owns column c)
   if (warp < 4) {
-    const int base = warp * 16;
+    const int bs = warp * 16;
     const int cc = lane & 15;
     float col[16];
 #pragma unroll
@@ -245,17 +278,17 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
       float acc = 0.f;
 #pragma unroll
       for (int m = 0; m < 16; ++m)
-        if (m < r && m >= cc) acc += sm.n[(base + r) * PADF + base + m] * col[m];
+        if (m < r && m >= cc) acc += sN[(bs + r) * PADF + bs + m] * col[m];
       if (cc < r) col[r] = acc;
     }
     if (lane < 16) {
 #pragma unroll
-      for (int r = 0; r < 16; ++r) sm.tf[(base + r) * PADF + base + cc] = col[r];
+      for (int r = 0; r < 16; ++r) sTF[(bs + r) * PADF + bs + cc] = col[r];
     }
   } else {  // zeros above the block diagonal that the full-length sums below read: T[0:16, 16:32], T[32:48, 48:64]
     for (int x = tid - 128; x < 512; x += 128) {
       const int blk = x >> 8, r = (x >> 4) & 15, cc = x & 15;
-      sm.tf[(blk * 32 + r) * PADF + blk * 32 + 16 + cc] = 0.f;
+      sTF[(blk * 32 + r) * PADF + blk * 32 + 16 + cc] = 0.f;
     }
   }
   __syncthreads();
@@ -263,72 +296,95 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(
   // tf32 (warps 0-3: block h = w >> 1, 8 columns (w & 1) * 8). The triangular zeros of N and T make full-length
   // products exact.
   if (warp < 4) {
-    const int hb = warp >> 1, nt = warp & 1;
+    const int hb = warp >> 1, ntile = warp & 1;
     const int bi = (2 * hb + 1) * 16, bj = 2 * hb * 16;
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-    tile_mma_tf32(c, &sm.n[bi * PADF + bj], PADF, &sm.tf[bj * PADF + bj + 8 * nt], PADF, 16, lane);
-    store_tile(c, &sm.m[(hb * 16) * PADM + 8 * nt], PADM, lane);
+    float cacc[4] = {0.f, 0.f, 0.f, 0.f};
+    tile_mma_tf32(cacc, &sN[bi * PADF + bj], PADF, &sTF[bj * PADF + bj + 8 * ntile], PADF, 16, lane);
+    store_tile(cacc, &sM[(hb * 16) * PADM + 8 * ntile], PADM, lane);
   }
   __syncthreads();
   if (warp < 4) {
-    const int hb = warp >> 1, nt = warp & 1;
+    const int hb = warp >> 1, ntile = warp & 1;
     const int bi = (2 * hb + 1) * 16, bj = 2 * hb * 16;
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-    tile_mma_tf32(c, &sm.tf[bi * PADF + bi], PADF, &sm.m[(hb * 16) * PADM + 8 * nt], PADM, 16, lane);
-    store_tile(c, &sm.tf[bi * PADF + bj + 8 * nt], PADF, lane);
+    float cacc[4] = {0.f, 0.f, 0.f, 0.f};
+    tile_mma_tf32(cacc, &sTF[bi * PADF + bi], PADF, &sM[(hb * 16) * PADM + 8 * ntile], PADM, 16, lane);
+    store_tile(cacc, &sTF[bi * PADF + bj + 8 * ntile], PADF, lane);
   }
   __syncthreads();
   // stage 2: T[32:, :32] = T[32:, 32:] N[32:, :32] T[:32, :32] (32x32 blocks, tf32; warp: rows 16 (w >> 2), 8 columns
   // (w & 3) * 8)
   {
-    const int mt = warp >> 2, nt = warp & 3;
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-    tile_mma_tf32(c, &sm.n[(32 + 16 * mt) * PADF], PADF, &sm.tf[8 * nt], PADF, 32, lane);
-    store_tile(c, &sm.m[(16 * mt) * PADM + 8 * nt], PADM, lane);
+    const int mt = warp >> 2, ntile = warp & 3;
+    float cacc[4] = {0.f, 0.f, 0.f, 0.f};
+    tile_mma_tf32(cacc, &sN[(32 + 16 * mt) * PADF], PADF, &sTF[8 * ntile], PADF, 32, lane);
+    store_tile(cacc, &sM[(16 * mt) * PADM + 8 * ntile], PADM, lane);
     __syncthreads();
-    c[0] = c[1] = c[2] = c[3] = 0.f;
-    tile_mma_tf32(c, &sm.tf[(32 + 16 * mt) * PADF + 32], PADF, &sm.m[8 * nt], PADM, 32, lane);
-    store_tile(c, &sm.tf[(32 + 16 * mt) * PADF + 8 * nt], PADF, lane);
+    cacc[0] = cacc[1] = cacc[2] = cacc[3] = 0.f;
+    tile_mma_tf32(cacc, &sTF[(32 + 16 * mt) * PADF + 32], PADF, &sM[8 * ntile], PADM, 32, lane);
+    store_tile(cacc, &sTF[(32 + 16 * mt) * PADF + 8 * ntile], PADF, lane);
   }
   __syncthreads();
-  // the beta and beta e^G factors of the tokens go on T's columns (rather than on V's and K's rows)
-  for (int x = tid; x < CT * CT; x += 256) {
-    const int i = x >> 6, j = x & 63;
-    const float tv = j <= i ? sm.tf[i * PADF + j] * sm.beta[j] : 0.f;
-    sm.t[sw<CT>(i, j)] = __float2bfloat16_rn(tv);
-    sm.t2[sw<CT>(i, j)] = __float2bfloat16_rn(tv * sm.eG[j]);
+  // the beta and beta e^G factors of the tokens go on T's columns (rather than on V's and K's rows): T1, T2 bf16 in
+  // the swizzled K-major layout (B operands of the U, W products)
+  for (int x = tid; x < CT * CT / 2; x += 256) {
+    const int i = x >> 5, j = (x & 31) * 2;
+    float tv[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) tv[u] = j + u <= i ? sTF[i * PADF + j + u] * sBeta[j + u] : 0.f;
+    *reinterpret_cast<uint32_t*>(base + kOffT1 + swz(i, j)) = tcx::pack_bf16(tv[0], tv[1]);
+    *reinterpret_cast<uint32_t*>(base + kOffT2 + swz(i, j)) = tcx::pack_bf16(tv[0] * seG[j], tv[1] * seG[j + 1]);
+  }
+  tcx::fence_async_smem();
+  tcx::fence_before();
+  __syncthreads();
+  tcx::fence_after();
+  // P2: U^T = V^T (T diag(beta))^T and W^T = K^T (T diag(beta e^G))^T (M = 128 value / key columns, N = 64 tokens i,
+  // K = 64 tokens j): A = the V / K tile read MN-major (its two 64-column atoms LBO apart), B = T1 / T2 K-major
+  if (tid == 0 && live) {
+#pragma unroll
+    for (int s = 0; s < CT / 16; ++s) {
+      tcx::mma(tm + 64, tcx::sdesc(sbase + kOffV + s * 16 * 128, 8192, 1024), tcx::sdesc(sbase + kOffT1 + s * 32, 16, 1024),
+               tcx::idesc(128, 64, 1, 0), s > 0);
+      tcx::mma(tm + 128, tcx::sdesc(sbase + kOffKQ + s * 16 * 128, 16384, 1024),
+               tcx::sdesc(sbase + kOffT2 + s * 32, 16, 1024), tcx::idesc(128, 64, 1, 0), s > 0);
+    }
+    tcx::commit(bar_mma);
+  }
+  // P2 epilogue: warps 0-3 U^T (lane = value column), warps 4-7 W^T (lane = key column), 64 tokens each, bf16 into
+  // the swizzled [token][128] staging (the fp32 tiles are dead now) for the TMA stores
+  if (live) {
+    const bool done = __all_sync(0xffffffffu, tcx::wait_bar(bar_mma, 1, p.err));
+    tcx::fence_after();
+    const int qw = warp & 3, isw = warp >> 2;
+    const int dcol = 32 * qw + lane;
+    float d[CT];
+    tcx::tld64f(tm + ((uint32_t)(32 * qw) << 16) + 64 + 64 * isw, d);
+    if (done) {
+      unsigned char* stg = base + (isw ? kOffTF : kOffN) + (dcol >> 6) * 8192;
+      __nv_bfloat16 hv[CT];
+#pragma unroll
+      for (int t = 0; t < CT; ++t) hv[t] = __float2bfloat16_rn(d[t]);
+#pragma unroll
+      for (int t = 0; t < CT; ++t) *reinterpret_cast<__nv_bfloat16*>(stg + swz(t, dcol & 63)) = hv[t];
+      tcx::fence_async_smem();
+    }
+  }
+  tcx::fence_before();
+  __syncthreads();
+  if (tid == 0) {
+    if (live) {  // U and W [64 tokens][128] as two 64-column boxes each, QK [64][64]
+      tma_store2(&p.umap, sbase + kOffN, 0, rb);
+      tma_store2(&p.umap, sbase + kOffN + 8192, 64, rb);
+      tma_store2(&p.wmap, sbase + kOffTF, 0, rb);
+      tma_store2(&p.wmap, sbase + kOffTF + 8192, 64, rb);
+      tma_store2(&p.qkmap, sbase + kOffKQ + 8192, 0, rb);
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // the staging is read before the CTA leaves
+      tcx::wait_bar_quiet(bar_mma, 1, p.err);  // (completed: the epilogue waited for it)
+    }
   }
   __syncthreads();
-  // U = T diag(beta) V, W = T diag(beta e^G) K (64 x 128; warp: m-tile w>>1, columns (w&1)*64 .. +63)
-  const int mt = warp >> 1, cb = (warp & 1) * 64;
-  float U[8][4] = {}, Wacc[8][4] = {};
-#pragma unroll
-  for (int ks = 0; ks < CT; ks += 16) {
-    uint32_t a[4], a2[4], b[4];
-    lda<CT>(a, sm.t, mt * 16, ks, lane);
-    lda<CT>(a2, sm.t2, mt * 16, ks, lane);
-#pragma unroll
-    for (int np = 0; np < 4; ++np) {
-      ldb_kn<DH>(b, sm.v, cb + np * 16, ks, lane);
-      mma(U[2 * np], a, b[0], b[1]);
-      mma(U[2 * np + 1], a, b[2], b[3]);
-      ldb_kn<DH>(b, sm.k, cb + np * 16, ks, lane);
-      mma(Wacc[2 * np], a2, b[0], b[1]);
-      mma(Wacc[2 * np + 1], a2, b[2], b[3]);
-    }
-  }
-#pragma unroll
-  for (int n = 0; n < 8; ++n)
-#pragma unroll
-    for (int e = 0; e < 4; e += 2) {
-      const int i = mt * 16 + (lane >> 2) + (e >> 1) * 8, j = cb + n * 8 + (lane & 3) * 2;
-      // chunk-major [chunk][head][64 tokens][128], zeros past the row's end (the tokens there have no V, K)
-      const int64_t off = (((int64_t)c * Hv + h) * CT + i) * DH + j;
-      const bool in = i < nt;
-      *reinterpret_cast<__nv_bfloat162*>(Ug + off) = __floats2bfloat162_rn(in ? U[n][e] : 0.f, in ? U[n][e + 1] : 0.f);
-      *reinterpret_cast<__nv_bfloat162*>(Wg + off) =
-          __floats2bfloat162_rn(in ? Wacc[n][e] : 0.f, in ? Wacc[n][e + 1] : 0.f);
-    }
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(kPrepTmemCols));
 }
 
 size_t align_up(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -345,6 +401,8 @@ extern "C" size_t janus_b200_gdn_chunk_scan_workspace(int64_t T, int64_t n_chunk
 }
 
 namespace jb {
+int map2d(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows);
+int map3d(CUtensorMap* m, const void* ptr, uint64_t T, uint64_t H);
 int gdn_state_tc(const void* q, const void* k, int64_t T, int64_t B, const int32_t* row_start,
                  const int32_t* chunk_start, int64_t n_chunks, const float* state_in, const int32_t* state_row,
                  float* state_out, int64_t Hk, int64_t Hv, float scale, const void* W, const void* U, const void* QK,
@@ -380,17 +438,35 @@ extern "C" int janus_b200_gdn_chunk_scan(const void* q, const void* k, const voi
   __nv_bfloat16* QKg = reinterpret_cast<__nv_bfloat16*>(ws + 2 * align_up(rows * DH * 2));
   float* Gg = reinterpret_cast<float*>(ws + 2 * align_up(rows * DH * 2) + align_up(rows * CT * 2));
   cudaStream_t s = (cudaStream_t)stream;
-  cudaError_t e = cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)sizeof(PrepSmem));
-  if (e != cudaSuccess) {
-    set_error("gdn_chunk_scan: smem attribute: %s", cudaGetErrorString(e));
-    return JANUS_ERR_CUDA;
-  }
   if (n_chunks > 0) {
-    gdn_chunk_prep_kernel<<<dim3((unsigned)Hv, (unsigned)n_chunks), 256, sizeof(PrepSmem), s>>>(
-        (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, g, beta, row_start, chunk_start,
-        segment, (int)B, (int)Hk, (int)Hv, scale, Wg, Ug, QKg, Gg);
-    int st = launch_status("gdn_chunk_scan/prep");
+    PrepParams pp{};
+    const uint64_t wrows = (uint64_t)n_chunks * Hv * CT;
+    int st = map3d(&pp.qmap, q, (uint64_t)T, (uint64_t)Hk);
+    if (!st) st = map3d(&pp.kmap, k, (uint64_t)T, (uint64_t)Hk);
+    if (!st) st = map3d(&pp.vmap, v, (uint64_t)T, (uint64_t)Hv);
+    if (!st) st = map2d(&pp.wmap, Wg, DH, wrows);
+    if (!st) st = map2d(&pp.umap, Ug, DH, wrows);
+    if (!st) st = map2d(&pp.qkmap, QKg, CT, wrows);
+    if (st) return st;
+    pp.g = g;
+    pp.beta = beta;
+    pp.row_start = row_start;
+    pp.chunk_start = chunk_start;
+    pp.segment = segment;
+    pp.Gg = Gg;
+    pp.err = status;
+    pp.B = (int)B;
+    pp.Hk = (int)Hk;
+    pp.Hv = (int)Hv;
+    pp.scale = scale;
+    cudaError_t e = cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kPrepSmem);
+    if (e != cudaSuccess) {
+      set_error("gdn_chunk_scan: smem attribute: %s", cudaGetErrorString(e));
+      return JANUS_ERR_CUDA;
+    }
+    gdn_chunk_prep_kernel<<<dim3((unsigned)Hv, (unsigned)n_chunks), 256, kPrepSmem, s>>>(pp);
+    st = launch_status("gdn_chunk_scan/prep");
     if (st) return st;
   }
   return gdn_state_tc(q, k, T, B, row_start, chunk_start, n_chunks, state_in, state_row, state_out, Hk, Hv, scale,

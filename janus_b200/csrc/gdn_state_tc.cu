@@ -376,8 +376,8 @@ __global__ void __launch_bounds__(NT, 1) gdn_state_tc_kernel(const __grid_consta
 
 // ------------------------------------------------------------------------------------------------ host side
 
-// row-major [rows][cols] bf16, boxes of 64 x 64 (128B swizzle)
-static int map2d(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows) {
+// row-major [rows][cols] bf16, boxes of 64 x 64 (128B swizzle); also the chunk prep's store maps
+int map2d(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows) {
   tcx::EncodeTiled enc = tcx::encode_tiled_fn();
   if (!enc) {
     set_error("gdn_chunk_scan(tcgen05): cuTensorMapEncodeTiled unavailable");
@@ -397,8 +397,8 @@ static int map2d(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows) 
   return JANUS_OK;
 }
 
-// [T][H][128] bf16, boxes of 64 dims x 1 head x 64 tokens (128B swizzle), zeros past T
-static int map3d(CUtensorMap* m, const void* ptr, uint64_t T, uint64_t H) {
+// [T][H][128] bf16, boxes of 64 dims x 1 head x 64 tokens (128B swizzle), zeros past T; also the chunk prep's loads
+int map3d(CUtensorMap* m, const void* ptr, uint64_t T, uint64_t H) {
   tcx::EncodeTiled enc = tcx::encode_tiled_fn();
   if (!enc) {
     set_error("gdn_chunk_scan(tcgen05): cuTensorMapEncodeTiled unavailable");
