@@ -143,11 +143,19 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(const __grid_con
                  "r"(kPrepTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
-  if (tid == 0) {
+  if (tid == 0) {  // the barriers, then at once the K, Q, V tiles of the chunk (rows past the row's end meet
+                   // beta = 0 and the masks)
     tcx::bar_init(bar_load, 1);
     tcx::bar_init(bar_mma, 1);
     s_ok = 1;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tcx::bar_expect_tx(bar_load, 2 * 3 * CT * 64 * 2);
+#pragma unroll
+    for (int a = 0; a < 2; ++a) {
+      tcx::tma_load3(sbase + kOffKQ + a * 16384, &p.kmap, 64 * a, hk, (int)t0, bar_load);
+      tcx::tma_load3(sbase + kOffKQ + a * 16384 + 8192, &p.qmap, 64 * a, hk, (int)t0, bar_load);
+      tcx::tma_load3(sbase + kOffV + a * 8192, &p.vmap, 64 * a, h, (int)t0, bar_load);
+    }
   }
   if (tid < CT) {
     const bool in = tid < nt;  // tokens past the row's end: g = beta = 0 (they touch nothing)
@@ -159,14 +167,7 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(const __grid_con
   __syncthreads();
   tcx::fence_after();
   const uint32_t tm = tmem_base;
-  if (tid == 0) {  // K, Q, V tiles of the chunk (rows past the row's end meet beta = 0 and the masks)
-    tcx::bar_expect_tx(bar_load, 2 * 3 * CT * 64 * 2);
-#pragma unroll
-    for (int a = 0; a < 2; ++a) {
-      tcx::tma_load3(sbase + kOffKQ + a * 16384, &p.kmap, 64 * a, hk, (int)t0, bar_load);
-      tcx::tma_load3(sbase + kOffKQ + a * 16384 + 8192, &p.qmap, 64 * a, hk, (int)t0, bar_load);
-      tcx::tma_load3(sbase + kOffV + a * 8192, &p.vmap, 64 * a, h, (int)t0, bar_load);
-    }
+  if (tid == 0) {
     // P1: [K; Q] K^T (M = 128, N = 64, K = 128): lanes 0-63 K K^T, lanes 64-127 Q K^T, columns 0-63
     bool ok = tcx::wait_bar(bar_load, 0, p.err);
     if (ok) {
@@ -238,9 +239,11 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(const __grid_con
         const float nb = -sBeta[i];
         float nv[32];
 #pragma unroll
-        for (int x = 0; x < 32; ++x) {
+        for (int x = 0; x < 32; ++x) {  // branch-free: the mask selects (a divergent branch per element is slow)
           const int j = j0 + x;
-          nv[x] = (j < i && sSeg[j] == si) ? nb * d[x] * __expf(Gi - sG[j]) : 0.f;
+          const bool m = (j < i) & (sSeg[j] == si);
+          const float val = nb * d[x] * __expf(fminf(Gi - sG[j], 0.f));
+          nv[x] = m ? val : 0.f;
         }
 #pragma unroll
         for (int x = 0; x < 32; x += 4)
@@ -253,7 +256,9 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(const __grid_con
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int j = j0 + x + u;
-            e[u] = (j <= i && i < nt && sSeg[j] == si) ? p.scale * d[x + u] * __expf(Gi - sG[j]) : 0.f;
+            const bool m = (j <= i) & (i < nt) & (sSeg[j] == si);
+            const float val = p.scale * d[x + u] * __expf(fminf(Gi - sG[j], 0.f));
+            e[u] = m ? val : 0.f;
           }
           qv[x / 2] = tcx::pack_bf16(e[0], e[1]);
         }
@@ -266,6 +271,10 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(const __grid_con
     }
   }
   __syncthreads();  // N complete
+  if (tid == 0 && live) {  // the staged QK leaves while the inverse runs (its wait is at the end)
+    tma_store2(&p.qkmap, sbase + kOffKQ + 8192, 0, rb);
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  }
   // T = (I - N)^-1: diagonal 16x16 blocks (warps 0-3, lane c < 16 owns column c)
   if (warp < 4) {
     const int bs = warp * 16;
@@ -277,9 +286,11 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(const __grid_con
     for (int r = 1; r < 16; ++r) {
       float acc = 0.f;
 #pragma unroll
-      for (int m = 0; m < 16; ++m)
-        if (m < r && m >= cc) acc += sN[(bs + r) * PADF + bs + m] * col[m];
-      if (cc < r) col[r] = acc;
+      for (int m = 0; m < r; ++m) {  // m < r is known at compile time; the lane condition is a select
+        const float nm = sN[(bs + r) * PADF + bs + m];
+        acc += (m >= cc) ? nm * col[m] : 0.f;
+      }
+      col[r] = (cc < r) ? acc : col[r];
     }
     if (lane < 16) {
 #pragma unroll
@@ -330,7 +341,10 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(const __grid_con
     const int i = x >> 5, j = (x & 31) * 2;
     float tv[2];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) tv[u] = j + u <= i ? sTF[i * PADF + j + u] * sBeta[j + u] : 0.f;
+    for (int u = 0; u < 2; ++u) {
+      const float t = sTF[i * PADF + j + u] * sBeta[j + u];
+      tv[u] = (j + u <= i) ? t : 0.f;
+    }
     *reinterpret_cast<uint32_t*>(base + kOffT1 + swz(i, j)) = tcx::pack_bf16(tv[0], tv[1]);
     *reinterpret_cast<uint32_t*>(base + kOffT2 + swz(i, j)) = tcx::pack_bf16(tv[0] * seG[j], tv[1] * seG[j + 1]);
   }
@@ -377,7 +391,6 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(const __grid_con
       tma_store2(&p.umap, sbase + kOffN + 8192, 64, rb);
       tma_store2(&p.wmap, sbase + kOffTF, 0, rb);
       tma_store2(&p.wmap, sbase + kOffTF + 8192, 64, rb);
-      tma_store2(&p.qkmap, sbase + kOffKQ + 8192, 0, rb);
       asm volatile("cp.async.bulk.commit_group;" ::: "memory");
       asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // the staging is read before the CTA leaves
       tcx::wait_bar_quiet(bar_mma, 1, p.err);  // (completed: the epilogue waited for it)
