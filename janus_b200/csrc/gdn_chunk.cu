@@ -75,22 +75,27 @@ __device__ __forceinline__ int chunk_row(const int32_t* chunk_start, int B, int 
 
 // ------------------------------------------------------------------------------------------------ chunk prep
 
-// Shared memory of the prep (byte offsets from a 1024-aligned base). Operand tiles are in the UMMA 128B-swizzled
-// K-major layout: [64-column atom][rows][128 bytes], the 16-byte unit u of row r at (u ^ (r & 7)) * 16.
-//   KQ  [2 atoms][128 rows]: rows 0-63 the chunk's K, rows 64-127 its Q, so [K; Q] is one M=128 operand and K
-//       alone (rows 0-63) the N=64 one; QK^T is staged in the Q half of atom 0 once the products are done
-//   V   [2 atoms][64 rows];  T1 = T diag(beta), T2 = T diag(beta e^G) [64 rows][64] (one atom each)
-//   N, TF fp32 [64][PADF] (the triangular inverse), then the staging of U and W for their TMA stores
-constexpr uint32_t kOffKQ = 0, kOffV = 32768, kOffT1 = 49152, kOffT2 = 57344;
-constexpr uint32_t kOffN = 65536, kOffTF = 83968, kOffM = 102400;  // N, TF on 1024-byte boundaries (staging)
-constexpr uint32_t kOffVec = kOffM + 32 * PADM * 4;                 // G, eG, beta, graw (fp32 [64]), seg (int [64])
+// Shared memory of the prep (byte offsets from a 1024-aligned base), small enough for three CTAs per SM: regions are
+// reused as their contents die. Operand tiles are in the UMMA 128B-swizzled K-major layout: [64-column atom][rows]
+// [128 bytes], the 16-byte unit u of row r at (u ^ (r & 7)) * 16.
+//   KQ [2 atoms][128 rows]: rows 0-63 the chunk's K, rows 64-127 its Q, so [K; Q] is one M=128 operand and K alone
+//      (rows 0-63) the N=64 one. Once Q is consumed, the Q half of atom 0 stages QK for its TMA store and then holds
+//      T1 = T diag(beta); the Q half of atom 1 holds the fp32 scratch M of the inverse, then T2 = T diag(beta e^G)
+//   NV fp32 N [64][PADF] for the inverse; once N is consumed, the chunk's V [2 atoms][64 rows] (a second TMA load)
+//   TF fp32 T [64][PADF]
+constexpr uint32_t kOffKQ = 0, kOffT1 = 8192, kOffM = 16384 + 8192, kOffT2 = 16384 + 8192;
+constexpr uint32_t kOffNV = 32768, kOffTF = 51200;  // 1024-byte boundaries
+constexpr uint32_t kOffVec = kOffTF + CT * PADF * 4;  // G, eG, beta, graw (fp32 [64]), seg (int [64])
 constexpr uint32_t kOffBar = kOffVec + 5 * CT * 4;
 constexpr uint32_t kPrepSmem = kOffBar + 32 + 1024;  // + alignment slack
-constexpr uint32_t kPrepTmemCols = 256;  // P1 (KK^T | QK^T) cols 0-63, U^T cols 64-127, W^T cols 128-191
+constexpr uint32_t kPrepTmemCols = 128;  // P1 (KK^T | QK^T) cols 0-63, then U^T cols 0-63 and W^T cols 64-127
+static_assert(CT * PADF * 4 <= kOffTF - kOffNV && 32 * PADM * 4 <= 8192, "prep shared-memory regions");
 
 struct PrepParams {
   CUtensorMap qmap, kmap, vmap;       // [T][H][128] bf16 loads, boxes 64 dims x 1 head x 64 tokens
-  CUtensorMap wmap, umap, qkmap;      // chunk-major workspace stores, boxes 64 x 64
+  CUtensorMap qkmap;                  // chunk-major QK store, boxes 64 x 64
+  __nv_bfloat16* Wg;                  // chunk-major [chunk][head][64 tokens][128]
+  __nv_bfloat16* Ug;
   const float* g;
   const float* beta;
   const int32_t* row_start;
@@ -112,11 +117,11 @@ __device__ __forceinline__ void tma_store2(const CUtensorMap* map, uint32_t src,
 // byte offset of element (r, c) of a 64-column swizzled atom [rows][128 B]
 __device__ __forceinline__ uint32_t swz(int r, int c) { return r * 128 + ((((c >> 3) ^ r) & 7) << 4) + (c & 7) * 2; }
 
-__global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(const __grid_constant__ PrepParams p) {
+__global__ void __launch_bounds__(256, 3) gdn_chunk_prep_kernel(const __grid_constant__ PrepParams p) {
   extern __shared__ unsigned char raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~(uintptr_t)1023);
   const uint32_t sbase = tcx::s32(base);
-  float* sN = reinterpret_cast<float*>(base + kOffN);
+  float* sN = reinterpret_cast<float*>(base + kOffNV);
   float* sTF = reinterpret_cast<float*>(base + kOffTF);
   float* sM = reinterpret_cast<float*>(base + kOffM);
   float* sG = reinterpret_cast<float*>(base + kOffVec);
@@ -149,12 +154,11 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(const __grid_con
     tcx::bar_init(bar_mma, 1);
     s_ok = 1;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    tcx::bar_expect_tx(bar_load, 2 * 3 * CT * 64 * 2);
+    tcx::bar_expect_tx(bar_load, 2 * 2 * CT * 64 * 2);
 #pragma unroll
     for (int a = 0; a < 2; ++a) {
       tcx::tma_load3(sbase + kOffKQ + a * 16384, &p.kmap, 64 * a, hk, (int)t0, bar_load);
       tcx::tma_load3(sbase + kOffKQ + a * 16384 + 8192, &p.qmap, 64 * a, hk, (int)t0, bar_load);
-      tcx::tma_load3(sbase + kOffV + a * 8192, &p.vmap, 64 * a, h, (int)t0, bar_load);
     }
   }
   if (tid < CT) {
@@ -271,7 +275,7 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(const __grid_con
     }
   }
   __syncthreads();  // N complete
-  if (tid == 0 && live) {  // the staged QK leaves while the inverse runs (its wait is at the end)
+  if (tid == 0 && live) {  // the staged QK leaves while the inverse runs (its read is waited for before T1)
     tma_store2(&p.qkmap, sbase + kOffKQ + 8192, 0, rb);
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
   }
@@ -330,10 +334,17 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(const __grid_con
     tile_mma_tf32(cacc, &sN[(32 + 16 * mt) * PADF], PADF, &sTF[8 * ntile], PADF, 32, lane);
     store_tile(cacc, &sM[(16 * mt) * PADM + 8 * ntile], PADM, lane);
     __syncthreads();
+    if (tid == 0 && live) {  // N is consumed: the chunk's V goes into its place (the U product needs it)
+      tcx::fence_async_smem();
+      tcx::bar_expect_tx(bar_load, 2 * CT * 64 * 2);
+      tcx::tma_load3(sbase + kOffNV, &p.vmap, 0, h, (int)t0, bar_load);
+      tcx::tma_load3(sbase + kOffNV + 8192, &p.vmap, 64, h, (int)t0, bar_load);
+    }
     cacc[0] = cacc[1] = cacc[2] = cacc[3] = 0.f;
     tile_mma_tf32(cacc, &sTF[(32 + 16 * mt) * PADF + 32], PADF, &sM[8 * ntile], PADM, 32, lane);
     store_tile(cacc, &sTF[(32 + 16 * mt) * PADF + 8 * ntile], PADF, lane);
   }
+  if (tid == 0 && live) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // QK staging read: T1's place
   __syncthreads();
   // the beta and beta e^G factors of the tokens go on T's columns (rather than on V's and K's rows): T1, T2 bf16 in
   // the swizzled K-major layout (B operands of the U, W products)
@@ -353,49 +364,54 @@ __global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(const __grid_con
   __syncthreads();
   tcx::fence_after();
   // P2: U^T = V^T (T diag(beta))^T and W^T = K^T (T diag(beta e^G))^T (M = 128 value / key columns, N = 64 tokens i,
-  // K = 64 tokens j): A = the V / K tile read MN-major (its two 64-column atoms LBO apart), B = T1 / T2 K-major
+  // K = 64 tokens j): A = the V / K tile read MN-major (its two 64-column atoms LBO apart), B = T1 / T2 K-major; the
+  // accumulators reuse P1's TMEM columns (read out long ago)
+  bool p2 = false;  // (thread 0) the U, W products were issued
   if (tid == 0 && live) {
+    if (tcx::wait_bar(bar_load, 1, p.err)) {
+      p2 = true;
+      tcx::fence_after();
 #pragma unroll
-    for (int s = 0; s < CT / 16; ++s) {
-      tcx::mma(tm + 64, tcx::sdesc(sbase + kOffV + s * 16 * 128, 8192, 1024), tcx::sdesc(sbase + kOffT1 + s * 32, 16, 1024),
-               tcx::idesc(128, 64, 1, 0), s > 0);
-      tcx::mma(tm + 128, tcx::sdesc(sbase + kOffKQ + s * 16 * 128, 16384, 1024),
-               tcx::sdesc(sbase + kOffT2 + s * 32, 16, 1024), tcx::idesc(128, 64, 1, 0), s > 0);
+      for (int s = 0; s < CT / 16; ++s) {
+        tcx::mma(tm, tcx::sdesc(sbase + kOffNV + s * 16 * 128, 8192, 1024), tcx::sdesc(sbase + kOffT1 + s * 32, 16, 1024),
+                 tcx::idesc(128, 64, 1, 0), s > 0);
+        tcx::mma(tm + 64, tcx::sdesc(sbase + kOffKQ + s * 16 * 128, 16384, 1024),
+                 tcx::sdesc(sbase + kOffT2 + s * 32, 16, 1024), tcx::idesc(128, 64, 1, 0), s > 0);
+      }
+      tcx::commit(bar_mma);
+    } else {
+      s_ok = 0;
+      tcx::wait_bar_quiet(bar_load, 1, p.err);  // the V load lands before the CTA may leave
     }
-    tcx::commit(bar_mma);
   }
-  // P2 epilogue: warps 0-3 U^T (lane = value column), warps 4-7 W^T (lane = key column), 64 tokens each, bf16 into
-  // the swizzled [token][128] staging (the fp32 tiles are dead now) for the TMA stores
+  // P2 epilogue: warps 0-3 U^T (lane = value column d), warps 4-7 W^T (lane = key column d), bf16 straight to the
+  // chunk-major workspace: lanes d and d^1 swap one token of each pair, so every lane stores two columns of one token
   if (live) {
     const bool done = __all_sync(0xffffffffu, tcx::wait_bar(bar_mma, 1, p.err));
     tcx::fence_after();
     const int qw = warp & 3, isw = warp >> 2;
-    const int dcol = 32 * qw + lane;
-    float d[CT];
-    tcx::tld64f(tm + ((uint32_t)(32 * qw) << 16) + 64 + 64 * isw, d);
-    if (done) {
-      unsigned char* stg = base + (isw ? kOffTF : kOffN) + (dcol >> 6) * 8192;
-      __nv_bfloat16 hv[CT];
+    const int dcol = 32 * qw + lane, odd = lane & 1;
+    __nv_bfloat16* dst = (isw ? p.Wg : p.Ug) + (int64_t)rb * DH + (dcol & ~1);
+#pragma unroll 1
+    for (int tb = 0; tb < CT; tb += 32) {
+      float d[32];
+      const uint32_t la = tm + ((uint32_t)(32 * qw) << 16) + 64 * isw + tb;
+      tcx::tld16f(la, d);
+      tcx::tld16f(la + 16, d + 16);
+      if (done) {
 #pragma unroll
-      for (int t = 0; t < CT; ++t) hv[t] = __float2bfloat16_rn(d[t]);
-#pragma unroll
-      for (int t = 0; t < CT; ++t) *reinterpret_cast<__nv_bfloat16*>(stg + swz(t, dcol & 63)) = hv[t];
-      tcx::fence_async_smem();
+        for (int t = 0; t < 32; t += 2) {
+          const float mine = odd ? d[t + 1] : d[t];  // this lane's column at the token it stores
+          const float give = odd ? d[t] : d[t + 1];  // the partner's token
+          const float got = __shfl_xor_sync(0xffffffffu, give, 1);
+          const uint32_t w2 = odd ? tcx::pack_bf16(got, mine) : tcx::pack_bf16(mine, got);
+          *reinterpret_cast<uint32_t*>(dst + (int64_t)(tb + t + odd) * DH) = w2;
+        }
+      }
     }
   }
+  if (p2) tcx::wait_bar_quiet(bar_mma, 1, p.err);  // no MMA in flight at the dealloc (the epilogue waited already)
   tcx::fence_before();
-  __syncthreads();
-  if (tid == 0) {
-    if (live) {  // U and W [64 tokens][128] as two 64-column boxes each, QK [64][64]
-      tma_store2(&p.umap, sbase + kOffN, 0, rb);
-      tma_store2(&p.umap, sbase + kOffN + 8192, 64, rb);
-      tma_store2(&p.wmap, sbase + kOffTF, 0, rb);
-      tma_store2(&p.wmap, sbase + kOffTF + 8192, 64, rb);
-      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // the staging is read before the CTA leaves
-      tcx::wait_bar_quiet(bar_mma, 1, p.err);  // (completed: the epilogue waited for it)
-    }
-  }
   __syncthreads();
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(kPrepTmemCols));
 }
@@ -457,8 +473,6 @@ extern "C" int janus_b200_gdn_chunk_scan(const void* q, const void* k, const voi
     int st = map3d(&pp.qmap, q, (uint64_t)T, (uint64_t)Hk);
     if (!st) st = map3d(&pp.kmap, k, (uint64_t)T, (uint64_t)Hk);
     if (!st) st = map3d(&pp.vmap, v, (uint64_t)T, (uint64_t)Hv);
-    if (!st) st = map2d(&pp.wmap, Wg, DH, wrows);
-    if (!st) st = map2d(&pp.umap, Ug, DH, wrows);
     if (!st) st = map2d(&pp.qkmap, QKg, CT, wrows);
     if (st) return st;
     pp.g = g;
@@ -467,6 +481,8 @@ extern "C" int janus_b200_gdn_chunk_scan(const void* q, const void* k, const voi
     pp.chunk_start = chunk_start;
     pp.segment = segment;
     pp.Gg = Gg;
+    pp.Wg = Wg;
+    pp.Ug = Ug;
     pp.err = status;
     pp.B = (int)B;
     pp.Hk = (int)Hk;
