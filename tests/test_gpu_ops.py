@@ -48,6 +48,13 @@ def test_silu_mul_and_gated_rmsnorm():
     gu = torch.randn(17, 2 * 96, generator=g).to(BF)
     out = ops.silu_mul(gu.cuda())
     close(out, torch.nn.functional.silu(gu.float()[:, :96]) * gu.float()[:, 96:])
+    # many units per CTA (stage and output-buffer reuse), a ragged last column block (9216 = 4.5 x 2048)
+    for T, I in ((3001, 9216), (700, 2048)):
+        gu = torch.randn(T, 2 * I, generator=g).to(BF).cuda()
+        out = ops.silu_mul(gu)
+        ref = torch.nn.functional.silu(gu.float()[:, :I]) * gu.float()[:, I:]
+        close(out, ref)
+        assert torch.equal(ops.silu_mul(gu), out)
     for Dv in (32, 128):
         T, Hv = 9, 4
         core = torch.randn(T, Hv, Dv, generator=g).to(BF)
