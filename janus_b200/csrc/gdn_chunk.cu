@@ -20,7 +20,8 @@
 // With a segment id per token (the state fork packed into chunks: sibling rows of one parent share a chunk), G is a
 // cumulative sum within each segment and every mask also requires the same segment, so each segment runs from the
 // chunk's initial state on its own.
-// The prep writes W, U, QK and G chunk-major ([chunk][value head][64 tokens], zeros past a row's end) for the
+// The prep writes W, QK and G chunk-major ([chunk][value head][64 tokens], zeros past a row's end) and U transposed
+// ([chunk][value head][128 value columns][64 tokens], the rows the sequential pass's value threads read) for the
 // sequential pass's TMA loads.
 #include "tcgen05.cuh"
 
@@ -385,20 +386,28 @@ __global__ void __launch_bounds__(256, 3) gdn_chunk_prep_kernel(const __grid_con
     }
   }
   // P2 epilogue: warps 0-3 U^T (lane = value column d), warps 4-7 W^T (lane = key column d), bf16 straight to the
-  // chunk-major workspace: lanes d and d^1 swap one token of each pair, so every lane stores two columns of one token
+  // chunk-major workspace. U is kept transposed ([value column][64 tokens], the row the state pass's value thread
+  // reads): a lane writes its column's tokens contiguously. W is [token][128]: lanes d and d^1 swap one token of each
+  // pair, so every lane stores two columns of one token.
   if (live) {
     const bool done = __all_sync(0xffffffffu, tcx::wait_bar(bar_mma, 1, p.err));
     tcx::fence_after();
     const int qw = warp & 3, isw = warp >> 2;
     const int dcol = 32 * qw + lane, odd = lane & 1;
-    __nv_bfloat16* dst = (isw ? p.Wg : p.Ug) + (int64_t)rb * DH + (dcol & ~1);
+    __nv_bfloat16* dst = isw ? p.Wg + (int64_t)rb * DH + (dcol & ~1) : p.Ug + ((int64_t)rb * 2 + dcol) * CT;
 #pragma unroll 1
     for (int tb = 0; tb < CT; tb += 32) {
       float d[32];
       const uint32_t la = tm + ((uint32_t)(32 * qw) << 16) + 64 * isw + tb;
       tcx::tld16f(la, d);
       tcx::tld16f(la + 16, d + 16);
-      if (done) {
+      if (done && !isw) {
+#pragma unroll
+        for (int t = 0; t < 32; t += 8)
+          *reinterpret_cast<uint4*>(dst + tb + t) =
+              make_uint4(tcx::pack_bf16(d[t], d[t + 1]), tcx::pack_bf16(d[t + 2], d[t + 3]),
+                         tcx::pack_bf16(d[t + 4], d[t + 5]), tcx::pack_bf16(d[t + 6], d[t + 7]));
+      } else if (done) {
 #pragma unroll
         for (int t = 0; t < 32; t += 2) {
           const float mine = odd ? d[t + 1] : d[t];  // this lane's column at the token it stores
@@ -430,7 +439,7 @@ extern "C" size_t janus_b200_gdn_chunk_scan_workspace(int64_t T, int64_t n_chunk
 }
 
 namespace jb {
-int map2d(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows);
+int map2d(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows, uint32_t box_rows);
 int map3d(CUtensorMap* m, const void* ptr, uint64_t T, uint64_t H);
 int gdn_state_tc(const void* q, const void* k, int64_t T, int64_t B, const int32_t* row_start,
                  const int32_t* chunk_start, int64_t n_chunks, const float* state_in, const int32_t* state_row,
@@ -450,7 +459,7 @@ extern "C" int janus_b200_gdn_chunk_scan(const void* q, const void* k, const voi
   JB_REQUIRE(Dk == DH && Dv == DH, JANUS_ERR_UNSUPPORTED, "gdn_chunk_scan: Dk = Dv = 128 only (got %lld, %lld)",
              (long long)Dk, (long long)Dv);
   JB_REQUIRE(T >= 0 && T <= 0x7fffffff && B >= 0 && B <= 65535 && n_chunks >= 0 && n_chunks <= 65535 && Hk > 0 &&
-                 Hv > 0 && Hv % Hk == 0 && Hv <= 65535 && n_chunks * Hv * CT <= 0x7fffffff,
+                 Hv > 0 && Hv % Hk == 0 && Hv <= 65535 && n_chunks * Hv * 2 * CT <= 0x7fffffff,
              JANUS_ERR_INVALID, "gdn_chunk_scan: sizes");
   JB_REQUIRE(JB_ALIGNED(q, 16) && JB_ALIGNED(k, 16) && JB_ALIGNED(v, 16) && JB_ALIGNED(o, 16), JANUS_ERR_ALIGNMENT,
              "gdn_chunk_scan: q, k, v, o must be 16-byte aligned");
@@ -473,7 +482,7 @@ extern "C" int janus_b200_gdn_chunk_scan(const void* q, const void* k, const voi
     int st = map3d(&pp.qmap, q, (uint64_t)T, (uint64_t)Hk);
     if (!st) st = map3d(&pp.kmap, k, (uint64_t)T, (uint64_t)Hk);
     if (!st) st = map3d(&pp.vmap, v, (uint64_t)T, (uint64_t)Hv);
-    if (!st) st = map2d(&pp.qkmap, QKg, CT, wrows);
+    if (!st) st = map2d(&pp.qkmap, QKg, CT, wrows, 64);
     if (st) return st;
     pp.g = g;
     pp.beta = beta;

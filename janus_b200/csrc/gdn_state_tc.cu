@@ -9,9 +9,10 @@
 //
 // with V' = U - S W (fp32), f_k = e^(G_last - G), the state decayed by e^(G_last) before the update, and
 // O = e^G scale OT + O2T: the same rounding points as the mma.sync formulation (bf16 state and V' as MMA operands,
-// fp32 accumulation, the fp32 state carried in TMEM). W, U, QK and G come from the prep pass in chunk-major layout
-// (zeros past a row's end); q and k straight from the projections (tokens past a row's end belong to the next row,
-// but they meet zero rows of W, U, QK and contribute nothing, and their outputs are not stored).
+// fp32 accumulation, the fp32 state carried in TMEM). W, U (transposed: a value column's tokens per row), QK and G
+// come from the prep pass in chunk-major layout (zeros past a row's end); q and k straight from the projections
+// (tokens past a row's end belong to the next row, but they meet zero rows of W, U, QK and contribute nothing, and
+// their outputs are not stored).
 //
 // Warps: 0-3 one thread per value column v (TMEM lane v): state in/out, V', the decay, the bf16 state copy;
 // warp 4 lane 0 the TMA producer (double-buffered chunk stages); warp 5 lane 0 the MMA issuer; warps 6-9 (again
@@ -59,7 +60,8 @@ constexpr uint32_t kStageBytes = 4 * kTile + CT * 128 + CT * 4;  // bytes the TM
 constexpr uint32_t kSmemBytes = 2 * kStage;
 
 struct Params {
-  CUtensorMap wmap, umap, qkmap;  // chunk-major workspace [n_chunks*Hv*64 rows][128 | 64], box 64 x 64
+  CUtensorMap wmap, qkmap;  // chunk-major workspace [n_chunks*Hv*64 rows][128 | 64], boxes 64 x 64
+  CUtensorMap umap;         // U^T [n_chunks*Hv*128 value columns][64 tokens], box 64 x 128
   CUtensorMap qmap, kmap;         // projections [T][Hk][128], box 64 x 1 x 64
   const float* G;                 // chunk-major [n_chunks][Hv][64]
   const int32_t* row_start;
@@ -163,8 +165,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_state_tc_kernel(const __grid_consta
         const uint32_t dst = sbase + st * kStage;
         tma_load2(dst + sW, &p.wmap, 0, rb, fb);
         tma_load2(dst + sW + kTile / 2, &p.wmap, 64, rb, fb);
-        tma_load2(dst + sU, &p.umap, 0, rb, fb);
-        tma_load2(dst + sU + kTile / 2, &p.umap, 64, rb, fb);
+        tma_load2(dst + sU, &p.umap, 0, 2 * rb, fb);  // U^T [128 value columns][64 tokens]: one box
         tma_load2(dst + sQK, &p.qkmap, 0, rb, fb);
         tma_load3(dst + sQ, &p.qmap, 0, hk, t0, fb);
         tma_load3(dst + sQ + kTile / 2, &p.qmap, 64, hk, t0, fb);
@@ -298,16 +299,22 @@ __global__ void __launch_bounds__(NT, 1) gdn_state_tc_kernel(const __grid_consta
       fence_after();
       // V' = U - S W (fp32) -> V'^T and (V' f_k)^T as bf16 A operands
       {
-        const unsigned char* ut = stage + sU + (v >> 6) * (kTile / 2);
+        // U^T row v: the value column's 64 tokens, eight 16-byte units (swizzled by v & 7)
+        const unsigned char* ut = stage + sU + v * 128;
+        uint4 uu[CT / 8];
+#pragma unroll
+        for (int c = 0; c < CT / 8; ++c) uu[c] = *reinterpret_cast<const uint4*>(ut + ((c ^ (v & 7)) << 4));
         float vt[CT];
         tld64f(la + cVT(st), vt);
         uint32_t vb[CT / 2], vd[CT / 2];
 #pragma unroll
-        for (int e = 0; e < CT; ++e) {
-          const float u = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(
-              ut + e * 128 + ((((v & 63) >> 3) ^ (e & 7)) << 4) + (v & 7) * 2));
-          vt[e] = u - vt[e];
-        }
+        for (int c = 0; c < CT / 8; ++c)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 u2 = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(&uu[c])[i]);
+            vt[8 * c + 2 * i] = u2.x - vt[8 * c + 2 * i];
+            vt[8 * c + 2 * i + 1] = u2.y - vt[8 * c + 2 * i + 1];
+          }
 #pragma unroll
         for (int e = 0; e < CT / 2; ++e) {
           vb[e] = pack_bf16(vt[2 * e], vt[2 * e + 1]);
@@ -376,8 +383,8 @@ __global__ void __launch_bounds__(NT, 1) gdn_state_tc_kernel(const __grid_consta
 
 // ------------------------------------------------------------------------------------------------ host side
 
-// row-major [rows][cols] bf16, boxes of 64 x 64 (128B swizzle); also the chunk prep's store maps
-int map2d(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows) {
+// row-major [rows][cols] bf16, boxes of 64 columns x box_rows rows (128B swizzle); also the chunk prep's store map
+int map2d(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows, uint32_t box_rows) {
   tcx::EncodeTiled enc = tcx::encode_tiled_fn();
   if (!enc) {
     set_error("gdn_chunk_scan(tcgen05): cuTensorMapEncodeTiled unavailable");
@@ -385,7 +392,7 @@ int map2d(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows) {
   }
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {cols * 2};
-  const cuuint32_t box[2] = {64, 64};
+  const cuuint32_t box[2] = {64, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -426,9 +433,9 @@ int gdn_state_tc(const void* q, const void* k, int64_t T, int64_t B, const int32
                  const float* G, int32_t* err, void* o, cudaStream_t stream) {
   gst::Params p{};
   const uint64_t rows = (uint64_t)n_chunks * Hv * 64;
-  int st = map2d(&p.wmap, W, 128, rows);
-  if (!st) st = map2d(&p.umap, U, 128, rows);
-  if (!st) st = map2d(&p.qkmap, QK, 64, rows);
+  int st = map2d(&p.wmap, W, 128, rows, 64);
+  if (!st) st = map2d(&p.umap, U, 64, 2 * rows, 128);  // U^T: [chunk][head][128 value columns][64 tokens]
+  if (!st) st = map2d(&p.qkmap, QK, 64, rows, 64);
   if (!st) st = map3d(&p.qmap, q, (uint64_t)T, (uint64_t)Hk);
   if (!st) st = map3d(&p.kmap, k, (uint64_t)T, (uint64_t)Hk);
   if (st) return st;
