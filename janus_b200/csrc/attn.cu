@@ -17,42 +17,90 @@ namespace jb {
 
 // ------------------------------------------------------------------------------------------------- q/k preparation
 
+// CTA per token: each warp computes the rotary cos / sin of the token's position once (for all its heads), then a
+// warp per head: 16-byte loads of 8 consecutive dims per lane, RMSNorm(1 + w) over the head with a warp reduction, the
+// rotation of the first `rot` dims from the normalised row kept in shared memory, 16-byte stores.
 __global__ void attn_qk_prep_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t stride,
                                     const int32_t* __restrict__ positions, const float* __restrict__ inv_freq, int rot,
                                     const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw,
                                     float eps, int Hq, int Hkv, int D, __nv_bfloat16* __restrict__ q,
                                     __nv_bfloat16* __restrict__ k, __nv_bfloat16* __restrict__ v) {
-  extern __shared__ float sh[];  // [warps][D]
+  extern __shared__ float sh[];  // per warp: [D] row, [rot / 2] cos, [rot / 2] sin
   const int64_t t = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  float* buf = sh + warp * D;
+  const int half = rot >> 1;
+  float* buf = sh + warp * ((D + rot + 3) & ~3);  // 16-byte aligned rows
+  float* cs = buf + D;
+  float* sn = cs + half;
   const float pos = (float)positions[t];
+  for (int f = lane; f < half; f += 32) {  // each warp its own table: no block-wide barrier
+    const float ang = pos * inv_freq[f];
+    cs[f] = cosf(ang);
+    sn[f] = sinf(ang);
+  }
+  __syncwarp();
   const __nv_bfloat16* row = qkv + t * stride;
+  const int nvec = D >> 3;
   for (int head = warp; head < Hq + Hkv; head += nw) {
     const bool isq = head < Hq;
     const __nv_bfloat16* src = isq ? row + (int64_t)head * 2 * D : row + (int64_t)Hq * 2 * D + (int64_t)(head - Hq) * D;
     const __nv_bfloat16* w = isq ? qw : kw;
-    float ss = 0.f;
-    for (int d = lane; d < D; d += 32) {
-      const float x = bf2f(src[d]);
-      buf[d] = x;
-      ss += x * x;
+    float x[8], ss = 0.f;
+    if (lane < nvec) {
+      load8(src + lane * 8, x);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+    }
+    for (int c = lane + 32; c < nvec; c += 32) {  // heads wider than 256 dims
+      float y[8];
+      load8(src + c * 8, y);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += y[i] * y[i];
     }
     ss = warp_sum(ss);
     const float r = rsqrtf(ss / (float)D + eps);
-    for (int d = lane; d < D; d += 32) buf[d] = buf[d] * r * (1.f + bf2f(w[d]));
+    float nx[8];  // this lane's normalised dims (first 256)
+    for (int c = lane; c < nvec; c += 32) {
+      float y[8], wv[8];
+      if (c == lane) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = x[i];
+      } else {
+        load8(src + c * 8, y);
+      }
+      load8(w + c * 8, wv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = y[i] * r * (1.f + wv[i]);
+      if (c == lane) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) nx[i] = y[i];
+      }
+      // 32 contiguous bytes per lane: whole 128-byte wavefronts, no bank conflicts
+      reinterpret_cast<float4*>(buf + c * 8)[0] = make_float4(y[0], y[1], y[2], y[3]);
+      reinterpret_cast<float4*>(buf + c * 8)[1] = make_float4(y[4], y[5], y[6], y[7]);
+    }
     __syncwarp();
     __nv_bfloat16* dst = isq ? q + (t * Hq + head) * D : k + (t * Hkv + (head - Hq)) * D;
-    const int half = rot >> 1;
-    for (int d = lane; d < D; d += 32) {
-      float y = buf[d];
-      if (d < rot) {
-        const int fi = d < half ? d : d - half;
-        const float ang = pos * inv_freq[fi];
-        const float c = cosf(ang), s = sinf(ang);
-        y = d < half ? buf[d] * c - buf[d + half] * s : buf[d] * c + buf[d - half] * s;
+    for (int c = lane; c < nvec; c += 32) {
+      float o[8];
+      if (c != lane) {
+        const float4 a = reinterpret_cast<const float4*>(buf + c * 8)[0], b = reinterpret_cast<const float4*>(buf + c * 8)[1];
+        o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = nx[i];
       }
-      dst[d] = f2bf(y);
+      if (c * 8 < rot) {  // the rotated dims: the partner of d is d -/+ half, from the shared row
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int d = c * 8 + i;
+          if (d < rot) {
+            const int fi = d < half ? d : d - half;
+            o[i] = d < half ? o[i] * cs[fi] - buf[d + half] * sn[fi] : o[i] * cs[fi] + buf[d - half] * sn[fi];
+          }
+        }
+      }
+      store8(dst + c * 8, o);
     }
     __syncwarp();
   }
@@ -422,10 +470,14 @@ extern "C" int janus_b200_attn_qk_prep(const void* qkv, int64_t qkv_stride, int6
              JANUS_ERR_INVALID, "attn_qk_prep: sizes");
   JB_REQUIRE(qkv_stride >= Hq * 2 * D + 2 * Hkv * D && qkv_stride % 8 == 0, JANUS_ERR_INVALID,
              "attn_qk_prep: qkv stride");
-  JB_REQUIRE(JB_ALIGNED(qkv, 16) && JB_ALIGNED(v, 16), JANUS_ERR_ALIGNMENT, "attn_qk_prep: alignment");
+  JB_REQUIRE(JB_ALIGNED(qkv, 16) && JB_ALIGNED(v, 16) && JB_ALIGNED(q, 16) && JB_ALIGNED(k, 16) &&
+                 JB_ALIGNED(q_norm_w, 16) && JB_ALIGNED(k_norm_w, 16),
+             JANUS_ERR_ALIGNMENT, "attn_qk_prep: 16-byte alignment of qkv, q, k, v and the norm weights");
+  JB_REQUIRE((128 / 32) * ((D + rot + 3) & ~3) * 4 <= 48 * 1024, JANUS_ERR_UNSUPPORTED, "attn_qk_prep: head dim %lld",
+             (long long)D);
   if (T == 0) return JANUS_OK;
   const int th = 128;
-  attn_qk_prep_kernel<<<(unsigned)T, th, (th / 32) * D * sizeof(float), (cudaStream_t)stream>>>(
+  attn_qk_prep_kernel<<<(unsigned)T, th, (th / 32) * ((D + rot + 3) & ~3) * sizeof(float), (cudaStream_t)stream>>>(
       (const __nv_bfloat16*)qkv, qkv_stride, positions, inv_freq, (int)rot, (const __nv_bfloat16*)q_norm_w,
       (const __nv_bfloat16*)k_norm_w, eps, (int)Hq, (int)Hkv, (int)D, (__nv_bfloat16*)q, (__nv_bfloat16*)k,
       (__nv_bfloat16*)v);
