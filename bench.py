@@ -40,6 +40,12 @@ REQUESTS_PER_GPU = 16
 METRIC = "decision requests/s (4B shape, 8K state, 8 questions)"
 UNIT = "requests/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one level-0 launch, from ncu captures of this build
+# (profiles/): the chunk scan (prep + state pass) of one DeltaNet layer at 16 requests x 8192 tokens, and the tree
+# attention of one layer captured at 2 requests and scaled by 8 to 16 (each request reads only its own K/V, so the
+# traffic grows in proportion to the requests). Scaled to other request counts the same way.
+NCU_LEVEL0_TRAFFIC = {"gdn_chunk_scan": (2.18e9 + 2.66e9) + (3.78e9 + 1.09e9), "tree_attention": 447.7e6 * 8}
+NCU_LEVEL0_REQUESTS = 16
 
 
 def peaks():
@@ -360,6 +366,16 @@ def main():
                     "unit": "GB/s", "frac": by / sec / b_peak, "traffic": None}
         roof["ms_per_step"] = kernel_ms[dominant]
         roof["peak_kind"] = pk_kind
+    if roof is not None and roof["kernel"] in NCU_LEVEL0_TRAFFIC and not args.layers:
+        # DRAM traffic of one level-0 launch (ncu) beside the algorithmic bytes of that launch
+        lv0 = levels[0]
+        if roof["kernel"] == "tree_attention":
+            alg0 = lv0.T * (3 * shape.heads * shape.head_dim * 2 + 2 * shape.kv_heads * shape.head_dim * 2)
+        else:
+            alg0 = chunk_algorithmic(levels[:1], shape, [True])[0][1]
+        roof["traffic"] = NCU_LEVEL0_TRAFFIC[roof["kernel"]] * args.requests / NCU_LEVEL0_REQUESTS
+        roof["traffic_per"] = "level-0 launch (ncu capture, profiles/)"
+        roof["algorithmic_bytes_per_level0_launch"] = float(alg0)
 
     # end to end through the public API: host packing -> H2D -> device pass -> D2H -> softmax
     e2e_ms = []

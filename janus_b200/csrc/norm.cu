@@ -98,6 +98,61 @@ __global__ void __launch_bounds__(kSiluThreads) silu_mul_kernel(const __nv_bfloa
   }
 }
 
+// The same op with 32-byte accesses (ld/st .v8.b32, sm_100): half the load instructions per byte of the 16-byte
+// version above, whose rate is set by its load queue. Thread per 16 columns, 192 threads x 3 vectors cover a
+// 9216-wide row in one round. Needs I % 16 == 0 and 32-byte aligned rows; the results are bit-identical.
+__device__ __forceinline__ void ldg_nc32(const void* p, uint32_t (&r)[8]) {
+  asm volatile("ld.global.nc.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "l"(p));
+}
+__device__ __forceinline__ void stg32(void* p, const uint32_t (&r)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(r[0]), "r"(r[1]), "r"(r[2]),
+               "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+constexpr int kSilu32Threads = 192, kSilu32Unroll = 3;
+__global__ void __launch_bounds__(kSilu32Threads, 4) silu_mul32_kernel(const __nv_bfloat16* __restrict__ gu, int64_t T,
+                                                                    int I, __nv_bfloat16* __restrict__ out) {
+  const int nv = I >> 4;
+  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+    const __nv_bfloat16* gr = gu + t * 2 * I;
+    __nv_bfloat16* orow = out + t * I;
+    for (int c0 = threadIdx.x; c0 < nv; c0 += kSilu32Threads * kSilu32Unroll) {
+      uint32_t g[kSilu32Unroll][8], u[kSilu32Unroll][8];
+#pragma unroll
+      for (int j = 0; j < kSilu32Unroll; ++j) {
+        const int c = c0 + j * kSilu32Threads;
+        if (c < nv) {
+          ldg_nc32(gr + c * 16, g[j]);
+          ldg_nc32(gr + I + c * 16, u[j]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kSilu32Unroll; ++j) {
+        const int c = c0 + j * kSilu32Threads;
+        if (c < nv) {
+          uint32_t o[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float2 a = unpack_bf16x2(g[j][i]), b = unpack_bf16x2(u[j][i]);
+            o[i] = pack_bf16x2(silu_fast(a.x) * b.x, silu_fast(a.y) * b.y);
+          }
+          stg32(orow + c * 16, o);
+        }
+      }
+    }
+  }
+}
+
 // Thread per 8 consecutive elements of one (token, value head); the DV / 8 threads of a head are consecutive lanes
 // of one warp and reduce the sum of squares with shuffles.
 template <int DV>
@@ -182,6 +237,12 @@ extern "C" int janus_b200_silu_mul(const void* gu, int64_t T, int64_t inter, voi
              "silu_mul: bad arguments (inter %lld must be a multiple of 8)", (long long)inter);
   JB_REQUIRE(JB_ALIGNED(gu, 16) && JB_ALIGNED(out, 16), JANUS_ERR_ALIGNMENT, "silu_mul: alignment");
   if (T == 0) return JANUS_OK;
+  if (inter % 16 == 0 && JB_ALIGNED(gu, 32) && JB_ALIGNED(out, 32)) {
+    const int64_t blocks = T < 148 * 4 ? T : 148 * 4;  // 4 CTAs of 192 threads per SM (76 registers)
+    silu_mul32_kernel<<<(unsigned)blocks, kSilu32Threads, 0, (cudaStream_t)stream>>>(
+        (const __nv_bfloat16*)gu, T, (int)inter, (__nv_bfloat16*)out);
+    return launch_status("silu_mul");
+  }
   const int64_t blocks = T < 148 * 16 ? T : 148 * 16;
   silu_mul_kernel<<<(unsigned)blocks, kSiluThreads, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)gu, T,
                                                                                 (int)inter, (__nv_bfloat16*)out);

@@ -48,8 +48,9 @@ def test_silu_mul_and_gated_rmsnorm():
     gu = torch.randn(17, 2 * 96, generator=g).to(BF)
     out = ops.silu_mul(gu.cuda())
     close(out, torch.nn.functional.silu(gu.float()[:, :96]) * gu.float()[:, 96:])
-    # many units per CTA (stage and output-buffer reuse), a ragged last column block (9216 = 4.5 x 2048)
-    for T, I in ((3001, 9216), (700, 2048)):
+    # many units per CTA, a ragged last column block (9216 = 4.5 x 2048); I = 104 is not a multiple of 16 and
+    # takes the 16-byte kernel, the others the 32-byte one
+    for T, I in ((3001, 9216), (700, 2048), (513, 104)):
         gu = torch.randn(T, 2 * I, generator=g).to(BF).cuda()
         out = ops.silu_mul(gu)
         ref = torch.nn.functional.silu(gu.float()[:, :I]) * gu.float()[:, I:]
