@@ -1,9 +1,34 @@
 // Row-wise glue between the GEMMs: embedding + RMSNorm, residual add + RMSNorm, SwiGLU gate, gated RMSNorm.
-// All HBM-bound: one CTA (or warp) per token row, 16-byte vector loads, one pass over the inputs, fp32 math and
-// a single rounding to bf16 at each output.
+// All HBM-bound: one CTA (or warp) per token row, 16- or 32-byte vector accesses, one pass over the inputs, fp32
+// math and a single rounding to bf16 at each output.
 #include "common.cuh"
 
 namespace jb {
+
+// 32-byte global accesses (ld/st .v8.b32, sm_100): half the instructions per byte of 16-byte vectors, which
+// matters where a kernel's rate is set by its load queue. The .nc form only for data no thread writes.
+__device__ __forceinline__ void ldg32(const void* p, uint32_t (&r)[8]) {
+  asm volatile("ld.global.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "l"(p));
+}
+__device__ __forceinline__ void ldg_nc32(const void* p, uint32_t (&r)[8]) {
+  asm volatile("ld.global.nc.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "l"(p));
+}
+__device__ __forceinline__ void stg32(void* p, const uint32_t (&r)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(r[0]), "r"(r[1]), "r"(r[2]),
+               "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
 
 constexpr int kNormThreads = 128;
 constexpr int kNormVec = 4;  // vectors of 8 per thread kept in registers: hidden <= 8 * 4 * threads
@@ -22,6 +47,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_kernel(const __nv_b
   float vals[kNormVec][8];
   float ss = 0.f;
   float* xr = x + t * (int64_t)H;
+  const bool wide = JB_ALIGNED(x, 32);  // rows of H % 8 == 0 floats keep 32-byte alignment
 #pragma unroll
   for (int j = 0; j < kNormVec; ++j) {
     const int v = threadIdx.x + j * blockDim.x;
@@ -29,10 +55,17 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_kernel(const __nv_b
       if (kEmbed) {
         load8(table + (int64_t)ids[t] * H + v * 8, vals[j]);
       } else {
-        float4 a = reinterpret_cast<const float4*>(xr)[2 * v];
-        float4 b = reinterpret_cast<const float4*>(xr)[2 * v + 1];
-        vals[j][0] = a.x; vals[j][1] = a.y; vals[j][2] = a.z; vals[j][3] = a.w;
-        vals[j][4] = b.x; vals[j][5] = b.y; vals[j][6] = b.z; vals[j][7] = b.w;
+        if (wide) {  // one 32-byte load
+          uint32_t raw[8];
+          ldg32(xr + 8 * v, raw);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) vals[j][i] = __uint_as_float(raw[i]);
+        } else {
+          float4 a = reinterpret_cast<const float4*>(xr)[2 * v];
+          float4 b = reinterpret_cast<const float4*>(xr)[2 * v + 1];
+          vals[j][0] = a.x; vals[j][1] = a.y; vals[j][2] = a.z; vals[j][3] = a.w;
+          vals[j][4] = b.x; vals[j][5] = b.y; vals[j][6] = b.z; vals[j][7] = b.w;
+        }
         if (delta) {
           float d[8];
           load8(delta + t * delta_stride + v * 8, d);
@@ -41,8 +74,15 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_kernel(const __nv_b
         }
       }
       if (kEmbed || delta) {
-        reinterpret_cast<float4*>(xr)[2 * v] = make_float4(vals[j][0], vals[j][1], vals[j][2], vals[j][3]);
-        reinterpret_cast<float4*>(xr)[2 * v + 1] = make_float4(vals[j][4], vals[j][5], vals[j][6], vals[j][7]);
+        if (wide) {
+          uint32_t raw[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) raw[i] = __float_as_uint(vals[j][i]);
+          stg32(xr + 8 * v, raw);
+        } else {
+          reinterpret_cast<float4*>(xr)[2 * v] = make_float4(vals[j][0], vals[j][1], vals[j][2], vals[j][3]);
+          reinterpret_cast<float4*>(xr)[2 * v + 1] = make_float4(vals[j][4], vals[j][5], vals[j][6], vals[j][7]);
+        }
       }
 #pragma unroll
       for (int i = 0; i < 8; ++i) ss += vals[j][i] * vals[j][i];
@@ -98,27 +138,9 @@ __global__ void __launch_bounds__(kSiluThreads) silu_mul_kernel(const __nv_bfloa
   }
 }
 
-// The same op with 32-byte accesses (ld/st .v8.b32, sm_100): half the load instructions per byte of the 16-byte
-// version above, whose rate is set by its load queue. Thread per 16 columns, 192 threads x 3 vectors cover a
-// 9216-wide row in one round. Needs I % 16 == 0 and 32-byte aligned rows; the results are bit-identical.
-__device__ __forceinline__ void ldg_nc32(const void* p, uint32_t (&r)[8]) {
-  asm volatile("ld.global.nc.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "l"(p));
-}
-__device__ __forceinline__ void stg32(void* p, const uint32_t (&r)[8]) {
-  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(r[0]), "r"(r[1]), "r"(r[2]),
-               "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
-               : "memory");
-}
-__device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
-  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
-}
-__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-
+// silu_mul with 32-byte accesses: half the load instructions per byte of the 16-byte version above, whose rate is
+// set by its load queue. Thread per 16 columns, 192 threads x 3 vectors cover a 9216-wide row in one round. Needs
+// I % 16 == 0 and 32-byte aligned rows; the results are bit-identical.
 constexpr int kSilu32Threads = 192, kSilu32Unroll = 3;
 __global__ void __launch_bounds__(kSilu32Threads, 4) silu_mul32_kernel(const __nv_bfloat16* __restrict__ gu, int64_t T,
                                                                     int I, __nv_bfloat16* __restrict__ out) {
@@ -186,6 +208,62 @@ __global__ void gated_rmsnorm_kernel(const __nv_bfloat16* __restrict__ core, con
   }
 }
 
+// The same op with 32-byte accesses: thread per 16 elements (DV / 16 lanes per head), the lane's 16 weights loaded
+// once, warps striding over the (token, head) units. The sum of squares is taken in a different order from the
+// kernel above (16 per thread, then DV / 16 lanes), so results may differ from it in the last bit.
+template <int DV>
+__global__ void __launch_bounds__(256, 4) gated_rmsnorm32_kernel(const __nv_bfloat16* __restrict__ core,
+                                                                 const __nv_bfloat16* __restrict__ z, int64_t z_stride,
+                                                                 uint32_t n_heads, uint32_t Hv,
+                                                                 const __nv_bfloat16* __restrict__ w, float eps,
+                                                                 __nv_bfloat16* __restrict__ out) {
+  constexpr int LPH = DV / 16;
+  static_assert(LPH >= 1 && LPH <= 32 && (32 % LPH) == 0, "head must span a power-of-two lane group");
+  const uint32_t lane = threadIdx.x & 31, sub = lane % LPH;
+  const uint32_t total = n_heads * LPH, stride = gridDim.x * blockDim.x;
+  float wv[16];
+  {
+    uint32_t raw[8];
+    ldg_nc32(w + sub * 16, raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float2 f = unpack_bf16x2(raw[i]);
+      wv[2 * i] = f.x;
+      wv[2 * i + 1] = f.y;
+    }
+  }
+  // the loop bound is uniform over a warp (base is the warp's first unit), so every lane reaches the shuffles
+  for (uint32_t base = blockIdx.x * blockDim.x + (threadIdx.x & ~31u); base < total; base += stride) {
+    const uint32_t gi = base + lane;
+    const bool live = gi < total;
+    const uint32_t head = live ? gi / LPH : 0;
+    uint32_t c[8], zz[8];
+    float ss = 0.f;
+    if (live) {
+      const uint32_t t = head / Hv, h = head - t * Hv;
+      ldg_nc32(core + (int64_t)head * DV + sub * 16, c);
+      ldg_nc32(z + (int64_t)t * z_stride + h * DV + sub * 16, zz);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float2 f = unpack_bf16x2(c[i]);
+        ss += f.x * f.x + f.y * f.y;
+      }
+    }
+#pragma unroll
+    for (int o = LPH >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (live) {
+      const float r = rsqrtf(ss / (float)DV + eps);
+      uint32_t res[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float2 f = unpack_bf16x2(c[i]), zf = unpack_bf16x2(zz[i]);
+        res[i] = pack_bf16x2(wv[2 * i] * (f.x * r) * silu_fast(zf.x), wv[2 * i + 1] * (f.y * r) * silu_fast(zf.y));
+      }
+      stg32(out + (int64_t)head * DV + sub * 16, res);
+    }
+  }
+}
+
 static int check_norm_args(int64_t T, int64_t H, const void* y, const void* w) {
   JB_REQUIRE(T >= 0 && H > 0 && H % 8 == 0 && H <= 8 * kNormVec * kNormThreads, JANUS_ERR_INVALID,
              "rmsnorm: hidden %lld must be a positive multiple of 8 up to %d", (long long)H, 8 * kNormVec * kNormThreads);
@@ -238,7 +316,7 @@ extern "C" int janus_b200_silu_mul(const void* gu, int64_t T, int64_t inter, voi
   JB_REQUIRE(JB_ALIGNED(gu, 16) && JB_ALIGNED(out, 16), JANUS_ERR_ALIGNMENT, "silu_mul: alignment");
   if (T == 0) return JANUS_OK;
   if (inter % 16 == 0 && JB_ALIGNED(gu, 32) && JB_ALIGNED(out, 32)) {
-    const int64_t blocks = T < 148 * 4 ? T : 148 * 4;  // 4 CTAs of 192 threads per SM (76 registers)
+    const int64_t blocks = T < 148 * 4 ? T : 148 * 4;  // 4 CTAs of 192 threads per SM (80 registers)
     silu_mul32_kernel<<<(unsigned)blocks, kSilu32Threads, 0, (cudaStream_t)stream>>>(
         (const __nv_bfloat16*)gu, T, (int)inter, (__nv_bfloat16*)out);
     return launch_status("silu_mul");
@@ -257,8 +335,23 @@ extern "C" int janus_b200_gated_rmsnorm(const void* core, const void* z, int64_t
              JANUS_ERR_ALIGNMENT, "gated_rmsnorm: 16-byte alignment of core/z/w/out and z_stride % 8");
   if (T == 0) return JANUS_OK;
   const int th = 256;
-  const unsigned blocks = (unsigned)((T * Hv * (Dv / 8) + th - 1) / th);
   cudaStream_t s = (cudaStream_t)stream;
+  if ((Dv == 64 || Dv == 128) && T * Hv * (Dv / 16) < (int64_t(1) << 31) && z_stride % 16 == 0 &&
+      JB_ALIGNED(core, 32) && JB_ALIGNED(z, 32) && JB_ALIGNED(w, 32) && JB_ALIGNED(out, 32)) {
+    const int64_t units = T * Hv * (Dv / 16);
+    const int64_t want = (units + th - 1) / th;
+    const unsigned blocks32 = (unsigned)(want < 148 * 4 ? want : 148 * 4);  // 4 CTAs of 256 threads per SM
+    if (Dv == 128)
+      gated_rmsnorm32_kernel<128><<<blocks32, th, 0, s>>>((const __nv_bfloat16*)core, (const __nv_bfloat16*)z,
+                                                          z_stride, (uint32_t)(T * Hv), (uint32_t)Hv,
+                                                          (const __nv_bfloat16*)w, eps, (__nv_bfloat16*)out);
+    else
+      gated_rmsnorm32_kernel<64><<<blocks32, th, 0, s>>>((const __nv_bfloat16*)core, (const __nv_bfloat16*)z, z_stride,
+                                                         (uint32_t)(T * Hv), (uint32_t)Hv, (const __nv_bfloat16*)w,
+                                                         eps, (__nv_bfloat16*)out);
+    return launch_status("gated_rmsnorm");
+  }
+  const unsigned blocks = (unsigned)((T * Hv * (Dv / 8) + th - 1) / th);
   switch (Dv) {
     case 32:
       gated_rmsnorm_kernel<32><<<blocks, th, 0, s>>>((const __nv_bfloat16*)core, (const __nv_bfloat16*)z, z_stride, T,

@@ -40,6 +40,14 @@ def test_embed_and_add_rmsnorm():
     y2 = ops.add_rmsnorm(x, delta.cuda(), w2.cuda(), 1e-6)
     close(x, ref_x + delta.float(), atol=1e-6, rtol=1e-6)
     close(y2, oracle.rmsnorm(ref_x + delta.float(), w2, 1e-6))
+    # a residual 16- but not 32-byte aligned takes the 16-byte accesses; same results bit for bit
+    buf = torch.zeros(T * H + 4, device="cuda")
+    x16 = buf[4:].view(T, H)
+    x16.copy_(ref_x.cuda())
+    xw = ref_x.cuda().clone()
+    y16 = ops.add_rmsnorm(x16, delta.cuda(), w2.cuda(), 1e-6)
+    yw = ops.add_rmsnorm(xw, delta.cuda(), w2.cuda(), 1e-6)
+    assert torch.equal(x16, xw) and torch.equal(y16, yw)
 
 
 def test_silu_mul_and_gated_rmsnorm():
@@ -63,6 +71,14 @@ def test_silu_mul_and_gated_rmsnorm():
         w = (1 + 0.1 * torch.randn(Dv, generator=g)).to(BF)
         out = ops.gated_rmsnorm(core.cuda(), zbuf.cuda()[:, 8:8 + Hv * Dv], w.cuda(), 1e-6)
         ref = oracle.gated_rmsnorm(core.float(), zbuf.float()[:, 8:8 + Hv * Dv].reshape(T, Hv, Dv), w, 1e-6)
+        close(out, ref.reshape(T, -1))
+    # 32-byte aligned z (the 32-byte kernel), many units per thread
+    for T, Hv, Dv in ((5000, 32, 128), (37, 3, 64)):
+        core = torch.randn(T, Hv, Dv, generator=g).to(BF)
+        zbuf = torch.randn(T, Hv * Dv + 48, generator=g).to(BF)
+        w = (1 + 0.1 * torch.randn(Dv, generator=g)).to(BF)
+        out = ops.gated_rmsnorm(core.cuda(), zbuf.cuda()[:, 16:16 + Hv * Dv], w.cuda(), 1e-6)
+        ref = oracle.gated_rmsnorm(core.float(), zbuf.float()[:, 16:16 + Hv * Dv].reshape(T, Hv, Dv), w, 1e-6)
         close(out, ref.reshape(T, -1))
 
 
