@@ -16,7 +16,17 @@ namespace jb {
 constexpr int kProThreads = 256;
 constexpr int kMaxTaps = 8;
 constexpr int kProTokens = 96;  // tokens per CTA: each thread slides its conv window over them
-constexpr int kProBatch = 2;    // tokens per step; the next step's loads are in flight while a step computes
+constexpr int kProBatch = 2;    // tokens per step (the l2 norms of a step share their shuffle rounds)
+constexpr int kProRing = 8;     // tokens staged ahead per thread in the shared-memory ring (power of two)
+
+__device__ __forceinline__ void cp_async(void* dst, const void* src, int bytes) {
+  if (bytes == 16)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src));
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src));
+}
 
 // grid (token tiles of kProTokens, channel blocks of 8 * kProThreads). Thread = 8 consecutive channels; it keeps the
 // last K-1 conv inputs of its channels in registers while it walks the tile's tokens, so every projection element is
@@ -29,6 +39,7 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
     const __nv_bfloat16* __restrict__ conv_w, const __nv_bfloat16* __restrict__ A_log,
     const __nv_bfloat16* __restrict__ dt_bias, int Hk, int Dk, int Hv, int Dv, __nv_bfloat16* __restrict__ q,
     __nv_bfloat16* __restrict__ k, __nv_bfloat16* __restrict__ v, float* __restrict__ g, float* __restrict__ beta) {
+  __shared__ uint4 ring[kProRing][kProThreads];
   const int64_t t0 = (int64_t)blockIdx.x * kProTokens;
   const int64_t t1 = t0 + kProTokens < T ? t0 + kProTokens : T;
   const int key_dim = Hk * Dk;
@@ -49,27 +60,35 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
   int cur_row = -1;
   int64_t r0 = 0, L = 0;
   const __nv_bfloat16* tail = nullptr;
-  // the next batch's loads are issued before the current batch is processed (software pipelining)
-  bf16x8 xn[kProBatch];
-  int rows_n[kProBatch];
-  auto load_batch = [&](int64_t tb) {
-#pragma unroll
-    for (int b = 0; b < kProBatch; ++b) {
-      const int64_t t = tb + b < t1 ? tb + b : t1 - 1;
-      rows_n[b] = row_of_token[t];
-      if (live) xn[b] = *reinterpret_cast<const bf16x8*>(proj + t * proj_stride + c0);
-    }
+  // the thread's 8 channels of the next kProRing tokens stream through its own column of a shared-memory ring
+  // (cp.async: the loads in flight hold no registers); a slot is refilled only after the stores that depend on
+  // the value read from it, so the refill cannot overtake that read
+  uint4* my = &ring[0][threadIdx.x];
+  const __nv_bfloat16* src = proj + c0;
+  auto issue = [&](int64_t t) {  // one commit group per token; an empty group past the tile keeps the count
+    if (live && t < t1) cp_async(my + ((int)(t - t0) & (kProRing - 1)) * kProThreads, src + t * proj_stride, 16);
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
   };
-  load_batch(t0);
+#pragma unroll
+  for (int i = 0; i < kProRing; ++i) issue(t0 + i);
+  int rows_n[kProBatch];
+#pragma unroll
+  for (int b = 0; b < kProBatch; ++b) rows_n[b] = row_of_token[t0 + b < t1 ? t0 + b : t1 - 1];
   for (int64_t tb = t0; tb < t1; tb += kProBatch) {
-    bf16x8 xr[kProBatch];
     int rows[kProBatch];
 #pragma unroll
-    for (int b = 0; b < kProBatch; ++b) {
-      xr[b] = xn[b];
-      rows[b] = rows_n[b];
+    for (int b = 0; b < kProBatch; ++b) rows[b] = rows_n[b];
+    if (tb + kProBatch < t1) {
+#pragma unroll
+      for (int b = 0; b < kProBatch; ++b)
+        rows_n[b] = row_of_token[tb + kProBatch + b < t1 ? tb + kProBatch + b : t1 - 1];
     }
-    if (tb + kProBatch < t1) load_batch(tb + kProBatch);
+    // kProRing groups are outstanding (tokens tb .. tb + kProRing - 1): the oldest kProBatch are complete after
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(kProRing - kProBatch) : "memory");
+    bf16x8 xr[kProBatch];
+#pragma unroll
+    for (int b = 0; b < kProBatch; ++b)
+      if (live) xr[b] = *reinterpret_cast<const bf16x8*>(my + ((int)(tb + b - t0) & (kProRing - 1)) * kProThreads);
     bf16x8 acc[kProBatch];  // conv + silu, rounded once to bf16 as the reference does
 #pragma unroll
     for (int b = 0; b < kProBatch; ++b) {
@@ -166,7 +185,11 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
         }
       }
     }
+    asm volatile("" ::: "memory");  // the slots' reads and the stores above stay before their refill
+#pragma unroll
+    for (int b = 0; b < kProBatch; ++b) issue(tb + kProRing + b);  // into the slots just read
   }
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");  // no copy outlives the CTA
   // gates, by the first channel block: b at column C + Hv*Dv + h, a at C + Hv*Dv + Hv + h
   if (blockIdx.y == 0) {
     for (int x = threadIdx.x; x < (int)(t1 - t0) * Hv; x += blockDim.x) {
@@ -192,14 +215,6 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
 constexpr int kForkSplit = 4;  // threads per value column
 constexpr int kForkRing = 8;   // token buffers
 
-__device__ __forceinline__ void cp_async(void* dst, const void* src, int bytes) {
-  if (bytes == 16)
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
-                 "l"(src));
-  else
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
-                 "l"(src));
-}
 
 template <int DK, int DV>
 __global__ void __launch_bounds__(kForkSplit * DV) gdn_fork_recurrent_kernel(

@@ -95,8 +95,8 @@ def test_gdn_prologue_with_parent_tails(dims):
     K = 4
     C = 2 * Hk * Dk + Hv * Dv
     g = torch.Generator().manual_seed(2)
-    lengths = [5, 1, 2, 70]
-    parent = torch.tensor([1, 0, 1, 2], dtype=torch.int32)
+    lengths = [5, 1, 2, 70, 300, 3]  # rows across the 96-token tiles, a last tile of an odd token count
+    parent = torch.tensor([1, 0, 1, 2, 0, 2], dtype=torch.int32)
     rs, rot = _level(lengths)
     T = int(rs[-1])
     stride = C + Hv * Dv + 2 * Hv + 8
