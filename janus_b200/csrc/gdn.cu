@@ -63,12 +63,18 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
   // the thread's 8 channels of the next kProRing tokens stream through its own column of a shared-memory ring
   // (cp.async: the loads in flight hold no registers); a slot is refilled only after the stores that depend on
   // the value read from it, so the refill cannot overtake that read
+  // (threads past the last channel read channel 0 and store nothing: no per-token checks for them)
   uint4* my = &ring[0][threadIdx.x];
-  const __nv_bfloat16* src = proj + c0;
+  const __nv_bfloat16* src = proj + t0 * proj_stride + c0;  // the next token to stage
   auto issue = [&](int64_t t) {  // one commit group per token; an empty group past the tile keeps the count
-    if (live && t < t1) cp_async(my + ((int)(t - t0) & (kProRing - 1)) * kProThreads, src + t * proj_stride, 16);
+    if (t < t1) cp_async(my + ((int)(t - t0) & (kProRing - 1)) * kProThreads, src, 16);
+    src += proj_stride;
     asm volatile("cp.async.commit_group;\n" ::: "memory");
   };
+  // this thread's output: q, k (l2-normalised) or v channels, advanced by one row per token
+  const bool is_qk = c0 < 2 * key_dim;
+  const int64_t dst_stride = is_qk ? key_dim : (int64_t)Hv * Dv;
+  __nv_bfloat16* dst = (c0 < key_dim ? q + c0 : is_qk ? k + (c0 - key_dim) : v + (c0 - 2 * key_dim)) + t0 * dst_stride;
 #pragma unroll
   for (int i = 0; i < kProRing; ++i) issue(t0 + i);
   int rows_n[kProBatch];
@@ -88,7 +94,7 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
     bf16x8 xr[kProBatch];
 #pragma unroll
     for (int b = 0; b < kProBatch; ++b)
-      if (live) xr[b] = *reinterpret_cast<const bf16x8*>(my + ((int)(tb + b - t0) & (kProRing - 1)) * kProThreads);
+      xr[b] = *reinterpret_cast<const bf16x8*>(my + ((int)(tb + b - t0) & (kProRing - 1)) * kProThreads);
     bf16x8 acc[kProBatch];  // conv + silu, rounded once to bf16 as the reference does
 #pragma unroll
     for (int b = 0; b < kProBatch; ++b) {
@@ -108,9 +114,9 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
 #pragma unroll
         for (int j = 0; j < K - 1; ++j) {
           const int64_t e = i + j;  // ext index of relative position j - (K-1)
-          if (live && e >= K - 1) {
+          if (e >= K - 1) {
             load8(proj + (r0 + e - (K - 1)) * proj_stride + c0, hist[j]);
-          } else if (live && tail) {
+          } else if (tail) {
             load8(tail + e * C + c0, hist[j]);
           } else {
 #pragma unroll
@@ -121,7 +127,7 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
       float x[8];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const float2 f = live ? __bfloat1622float2(xr[b].h[u]) : make_float2(0.f, 0.f);
+        const float2 f = __bfloat1622float2(xr[b].h[u]);
         x[2 * u] = f.x;
         x[2 * u + 1] = f.y;
       }
@@ -166,9 +172,8 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
     if (live) {
 #pragma unroll
       for (int b = 0; b < kProBatch; ++b) {
-        const int64_t t = tb + b;
-        if (t >= t1) break;
-        if (c0 < 2 * key_dim) {
+        if (tb + b >= t1) break;
+        if (is_qk) {
           float o8[8];
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
@@ -176,15 +181,13 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
             o8[2 * u] = f.x * rn[b];
             o8[2 * u + 1] = f.y * rn[b];
           }
-          if (c0 < key_dim)
-            store8(q + t * key_dim + c0, o8);
-          else
-            store8(k + t * key_dim + (c0 - key_dim), o8);
+          store8(dst + b * dst_stride, o8);
         } else {
-          *reinterpret_cast<bf16x8*>(v + t * (int64_t)(Hv * Dv) + (c0 - 2 * key_dim)) = acc[b];
+          *reinterpret_cast<bf16x8*>(dst + b * dst_stride) = acc[b];
         }
       }
     }
+    dst += kProBatch * dst_stride;
     asm volatile("" ::: "memory");  // the slots' reads and the stores above stay before their refill
 #pragma unroll
     for (int b = 0; b < kProBatch; ++b) issue(tb + kProRing + b);  // into the slots just read
