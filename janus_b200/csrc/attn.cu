@@ -32,6 +32,19 @@ __global__ void attn_qk_prep_kernel(const __nv_bfloat16* __restrict__ qkv, int64
   float* buf = sh + warp * ((D + rot + 3) & ~3);  // 16-byte aligned rows
   float* cs = buf + D;
   float* sn = cs + half;
+  const __nv_bfloat16* row = qkv + t * stride;
+  const int nvec = D >> 3;
+  auto head_src = [&](int h) {
+    return h < Hq ? row + (int64_t)h * 2 * D : row + (int64_t)Hq * 2 * D + (int64_t)(h - Hq) * D;
+  };
+  // the first 8 dims per lane of the warp's next head are loaded one head ahead (issued before the cos / sin)
+  bf16x8 xnext;
+  if (warp < Hq + Hkv && lane < nvec) xnext = *reinterpret_cast<const bf16x8*>(head_src(warp) + lane * 8);
+  {  // v: a plain copy of the Hkv*D columns after k, issued first so it overlaps the heads
+    const __nv_bfloat16* vs = row + (int64_t)Hq * 2 * D + (int64_t)Hkv * D;
+    for (int c = threadIdx.x * 8; c < Hkv * D; c += blockDim.x * 8)
+      *reinterpret_cast<bf16x8*>(v + t * Hkv * D + c) = *reinterpret_cast<const bf16x8*>(vs + c);
+  }
   const float pos = (float)positions[t];
   for (int f = lane; f < half; f += 32) {  // each warp its own table: no block-wide barrier
     const float ang = pos * inv_freq[f];
@@ -39,15 +52,21 @@ __global__ void attn_qk_prep_kernel(const __nv_bfloat16* __restrict__ qkv, int64
     sn[f] = sinf(ang);
   }
   __syncwarp();
-  const __nv_bfloat16* row = qkv + t * stride;
-  const int nvec = D >> 3;
   for (int head = warp; head < Hq + Hkv; head += nw) {
     const bool isq = head < Hq;
-    const __nv_bfloat16* src = isq ? row + (int64_t)head * 2 * D : row + (int64_t)Hq * 2 * D + (int64_t)(head - Hq) * D;
+    const __nv_bfloat16* src = head_src(head);
     const __nv_bfloat16* w = isq ? qw : kw;
+    const bf16x8 xcur = xnext;
+    if (head + nw < Hq + Hkv && lane < nvec)
+      xnext = *reinterpret_cast<const bf16x8*>(head_src(head + nw) + lane * 8);
     float x[8], ss = 0.f;
     if (lane < nvec) {
-      load8(src + lane * 8, x);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float2 f = __bfloat1622float2(xcur.h[u]);
+        x[2 * u] = f.x;
+        x[2 * u + 1] = f.y;
+      }
 #pragma unroll
       for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
     }
@@ -104,10 +123,6 @@ __global__ void attn_qk_prep_kernel(const __nv_bfloat16* __restrict__ qkv, int64
     }
     __syncwarp();
   }
-  // v: a plain copy of the Hkv*D columns after k
-  const __nv_bfloat16* vs = row + (int64_t)Hq * 2 * D + (int64_t)Hkv * D;
-  for (int c = threadIdx.x * 8; c < Hkv * D; c += blockDim.x * 8)
-    *reinterpret_cast<bf16x8*>(v + t * Hkv * D + c) = *reinterpret_cast<const bf16x8*>(vs + c);
 }
 
 // ------------------------------------------------------------------------------------------------ tree attention
