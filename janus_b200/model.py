@@ -10,6 +10,7 @@ tree attention with the output gate, the SwiGLU gate and the heads fused with th
 DeltaNet states (conv tail, fp32 recurrent matrix) and attention keys/values only when a deeper level reads them.
 """
 
+import dataclasses
 import math
 
 import numpy as np
@@ -19,6 +20,7 @@ import torch.nn.functional as F
 from . import _lib, ops
 from .config import LINEAR, ModelShape
 from .plan import DevicePlan, build_levels, build_readout
+from .prefix import PrefixSnapshot, stack_level0
 
 
 class _Layer:
@@ -215,10 +217,69 @@ class DecisionReadout:
         readout = build_readout(packs, levels, index, self.mode)
         return levels, readout
 
-    def prepare(self, packs):
-        """Host planning plus the one host-to-device copy of the level tables: (levels, readout, device plan)."""
+    def prepare(self, packs, prefixes=None):
+        """Host planning plus the one host-to-device copy of the level tables: (levels, readout, device plan).
+
+        `prefixes` (parallel to `packs`, as `HybridBackbone.encode_many(prefixes=...)`, janus/hybrid.py:1648-1659):
+        per pack a PrefixSnapshot of its state (`encode_prefixes`) or None. The state level then runs only for the
+        packs without one (as one batch), every snapshot is checked against its pack's state tokens, and the pass
+        starts at level 1 from the snapshots stacked in pack order."""
         levels, readout = self.plan(packs)
-        return levels, readout, DevicePlan(levels, readout, self.device, tile_tokens=(self.tile_tokens,))
+        plan = DevicePlan(levels, readout, self.device, tile_tokens=(self.tile_tokens,))
+        plan.prefix_history = None if prefixes is None else self._prefix_history(packs, levels, readout, prefixes)
+        return levels, readout, plan
+
+    def encode_prefixes(self, packs):
+        """HybridBackbone.encode_prefixes (janus/hybrid.py:1641-1646): the state level of several packs as one
+        batch, one PrefixSnapshot per pack (conv tails and recurrent states of the DeltaNet layers, keys and values
+        of the attention layers after the state's last token), copied out of the level batch so it outlives the
+        call. Raises if a device-side wait of the pass ran out."""
+        levels, readout = self.plan(packs)
+        lv = levels[0] if levels else None
+        self._check_state_rows(lv, len(packs))
+        plan = DevicePlan(levels[:1], readout, self.device, tile_tokens=(self.tile_tokens,))
+        self._readout = readout
+        logits = torch.zeros(readout.n_slots, dtype=torch.float32, device=self.device)
+        self.status.zero_()
+        kept = self._level(dataclasses.replace(lv, keep=True), plan, [], logits)
+        self.check_status()
+        attention = [L.kind != LINEAR for L in self.layers]
+        snaps = []
+        for r in range(len(packs)):
+            a, b = int(lv.row_start[r]), int(lv.row_start[r + 1])
+            states = [(first[a:b].clone(), second[a:b].clone()) if att else (first[r].clone(), second[r].clone())
+                      for att, (first, second) in zip(attention, kept)]
+            snaps.append(PrefixSnapshot(states, attention, lv.ids[a:b]))
+        return snaps
+
+    @staticmethod
+    def _check_state_rows(lv, n_packs):
+        if lv is None or lv.B != n_packs or any(int(row[0]) != r for r, row in enumerate(lv.rows)):
+            raise ValueError("prefix snapshots need one state segment per pack at level 0")
+
+    def _prefix_history(self, packs, levels, readout, prefixes):
+        if len(prefixes) != len(packs):
+            raise ValueError(f"{len(prefixes)} prefixes for {len(packs)} packs")
+        if 0 in readout.scalar or 0 in readout.pointer:
+            raise ValueError("a pack reads out at its state level, which a snapshot skips")
+        lv = levels[0] if levels else None
+        self._check_state_rows(lv, len(packs))
+        snaps = list(prefixes)
+        missing = [i for i, s in enumerate(snaps) if s is None]
+        if missing:
+            for i, s in zip(missing, self.encode_prefixes([packs[i] for i in missing])):
+                snaps[i] = s
+        attention = [L.kind != LINEAR for L in self.layers]
+        for r, s in enumerate(snaps):
+            a, b = int(lv.row_start[r]), int(lv.row_start[r + 1])
+            if not isinstance(s, PrefixSnapshot) or s.attention != attention:
+                raise ValueError(f"pack {r}: not a snapshot of this model's layers")
+            if s.tokens != b - a or not np.array_equal(s.ids, lv.ids[a:b]):
+                raise ValueError(f"pack {r}: the snapshot is of another state")
+            dev = s.device
+            if dev is None or dev.type != "cuda" or (self.device.index is not None and dev.index != self.device.index):
+                raise ValueError(f"pack {r}: the snapshot lives on {dev}, the model on {self.device}")
+        return stack_level0(snaps, attention)
 
     def run(self, prepared):
         """The device pass over prepared levels: all option logits as one fp32 device tensor [slots]."""
@@ -228,14 +289,18 @@ class DecisionReadout:
         logits = torch.zeros(readout.n_slots, dtype=torch.float32, device=self.device)
         self.status.zero_()
         history = []
-        for lv in levels:
+        prefix = getattr(plan, "prefix_history", None)
+        if prefix is not None:  # every pack's state level comes from a snapshot: start at level 1
+            history.append(prefix)
+        for lv in levels[len(history):]:
             history.append(self._level(lv, plan, history, logits))
         return logits
 
-    def logits_flat(self, packs):
+    def logits_flat(self, packs, prefixes=None):
         """All option logits of a batch as one fp32 device tensor [slots] (order: pack, question, option; the
-        constant false option of a tree-mode noul has no slot) plus the host readout layout."""
-        prepared = self.prepare(packs)
+        constant false option of a tree-mode noul has no slot) plus the host readout layout. `prefixes`: per pack
+        a PrefixSnapshot of its state or None (see `prepare`)."""
+        prepared = self.prepare(packs, prefixes)
         return self.run(prepared), prepared[1]
 
     def check_status(self):
@@ -244,17 +309,17 @@ class DecisionReadout:
             raise _lib.JanusError("a device-side wait (tree attention or chunk scan) ran out; the results of this run "
                                   "are invalid")
 
-    def forward_many(self, packs):
+    def forward_many(self, packs, prefixes=None):
         """Per pack, per question, the logits as fp32 CPU tensors (janus/model.py:368-373 + :319-366)."""
-        flat, readout = self.logits_flat(packs)
+        flat, readout = self.logits_flat(packs, prefixes)
         host = flat.cpu()
         self.check_status()
         return assemble(host, readout)
 
-    def probabilities(self, packs, temperatures=None):
+    def probabilities(self, packs, temperatures=None, prefixes=None):
         """Worker.probabilities (janus/server.py:277-282): softmax(logits / T) per question, T = 1 by default."""
         out = []
-        for i, per in enumerate(self.forward_many(packs)):
+        for i, per in enumerate(self.forward_many(packs, prefixes)):
             ts = (temperatures[i] if temperatures else None) or [1.0] * len(per)
             out.append([torch.softmax(z / t, dim=-1) for z, t in zip(per, ts)])
         return out
