@@ -15,6 +15,9 @@ step time is the max over ranks.
 `--moe-tokens` rows, default 131072 = a level-0 pass of 8 requests of 16384 tokens): routing, the two grouped GEMMs
 and the combine per step, each timed with CUDA events, TFLOP/s of the grouped GEMMs against the measured bf16 peak.
 
+`--op prefix` times the same batch with every state a prefix-cache hit: the states are encoded once into
+snapshots (DecisionReadout.encode_prefixes) and each step runs the branch levels only.
+
 `--impl reference` times the reference algorithm on the host cores instead: the CPU oracle (oracle/hybrid.py, a
 restatement of the reference's readout pinned to its golden outputs) on one request of the same workload through a
 2-layer slice of the model (one DeltaNet and one attention layer over every level), its per-layer times weighted by
@@ -229,6 +232,48 @@ def run_moe(args):
     }))
 
 
+def run_prefix(args):
+    """Repeated states (a prefix-cache hit for every request): the state level of the 16 requests is encoded once
+    into snapshots; each timed step then runs the branch levels only, from the snapshots. A side line for the
+    serving cache, not the headline (whose states are all new)."""
+    from janus_b200 import synthetic
+    from janus_b200.config import SHAPES
+    from janus_b200.model import DecisionReadout
+    device = torch.device("cuda", 0)
+    shape = SHAPES["4b"]
+    weights = synthetic.make_weights(shape, seed=0, head="scalar", device=device)
+    model = DecisionReadout(shape, weights, "tree", device=device)
+    del weights
+    packs = [synthetic.q4b_request(seed=j) for j in range(args.requests)]
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    snaps = model.encode_prefixes(packs)
+    e.record()
+    torch.cuda.synchronize()
+    encode_ms = s.elapsed_time(e)
+    prepared = model.prepare(packs, prefixes=snaps)
+    for _ in range(args.warmup):
+        model.run(prepared)
+    torch.cuda.synchronize()
+    ev = []
+    for _ in range(args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        model.run(prepared)
+        b.record()
+        ev.append((a, b))
+    torch.cuda.synchronize()
+    model.check_status()
+    ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+    print(json.dumps({
+        "metric": "decision requests/s with every state a prefix-cache hit (4B shape, 8K state, 8 questions)",
+        "value": args.requests / (ms / 1000.0), "unit": "requests/s", "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "state_encode_ms": encode_ms,
+        "snapshot_bytes_per_request": snaps[0].bytes if snaps else 0,
+        "config": {"workload": "4b-tree-8k-state-8q, states from snapshots", "requests_per_gpu": args.requests},
+    }))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -238,13 +283,16 @@ def main():
     ap.add_argument("--requests", type=int, default=REQUESTS_PER_GPU)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="debug: fewer layers (not a valid bench number)")
-    ap.add_argument("--op", default="readout", choices=["readout", "moe"])
+    ap.add_argument("--op", default="readout", choices=["readout", "moe", "prefix"])
     ap.add_argument("--moe-tokens", type=int, default=131072)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.op == "moe":
         run_moe(args)
+        return
+    if args.op == "prefix":
+        run_prefix(args)
         return
     if args.impl == "reference":
         run_reference(args)
