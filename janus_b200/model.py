@@ -326,11 +326,11 @@ class DecisionReadout:
 
 
 def assemble(host_logits, readout):
-    """Per pack, per question logits from the flat host tensor and the readout layout."""
+    """Per pack, per question logits (fp32 CPU tensors) from the flat host tensor and the readout layout; a slot of
+    None (the false option of a tree-mode noul) is the constant 0."""
+    flat = np.append(host_logits.numpy().astype(np.float32, copy=False), np.float32(0.0))  # index -1: the constant 0
     res = []
     for layout in readout.layout:
-        per = []
-        for slots in layout:
-            per.append(torch.stack([host_logits[s] if s is not None else torch.zeros(()) for s in slots]))
-        res.append(per)
+        res.append([torch.from_numpy(flat[np.array([-1 if s is None else s for s in slots], dtype=np.int64)])
+                    for slots in layout])
     return res

@@ -128,6 +128,12 @@ def build_levels(packs):
     """Levels of a batch of packs (module docstring)."""
     per_pack = [tree_levels(p.segment_ids, p.parents) for p in packs]
     depth = max(len(t) for t in per_pack)
+    # every pack's tokens and positions once, back to back: a level's tokens are one gather from them
+    all_ids = np.concatenate([np.asarray(p.input_ids[0], dtype=np.int32) for p in packs])
+    all_pos = np.concatenate([np.asarray(p.position_ids[0], dtype=np.int32) for p in packs])
+    pack_off = np.zeros(len(packs) + 1, dtype=np.int64)
+    np.cumsum([int(p.input_ids.shape[1]) for p in packs], out=pack_off[1:])
+    parents = [p.parents.tolist() for p in packs]
     levels = []
     row_index = {}  # (pack, segment) -> (depth, row, first packed position)
     for d in range(depth):
@@ -135,7 +141,7 @@ def build_levels(packs):
         for i, (p, tree) in enumerate(zip(packs, per_pack)):
             if d >= len(tree):
                 continue
-            par = p.parents.tolist()
+            par = parents[i]
             for seg, a, b in tree[d]:
                 prow = -1 if d == 0 else row_index[(i, par[seg])][1]
                 entries.append((prow, i, seg, a, b))
@@ -146,15 +152,13 @@ def build_levels(packs):
         row_start = np.zeros(B + 1, dtype=np.int64)
         np.cumsum(lengths, out=row_start[1:])
         T = int(row_start[-1])
-        ids = np.empty(T, dtype=np.int32)
-        pos = np.empty(T, dtype=np.int32)
         rot = np.repeat(np.arange(B, dtype=np.int32), lengths)
-        parent = np.full(B, -1, dtype=np.int32)
+        src = np.array([pack_off[i] + a for _, i, _, a, _ in entries], dtype=np.int64)
+        gather = np.arange(T, dtype=np.int64) + np.repeat(src - row_start[:-1], lengths)
+        ids, pos = all_ids[gather], all_pos[gather]
+        parent = np.array([prow for prow, _, _, _, _ in entries], dtype=np.int32).reshape(B)
         rows = []
         for r, (prow, i, seg, a, b) in enumerate(entries):
-            ids[row_start[r]:row_start[r + 1]] = packs[i].input_ids[0, a:b].numpy()
-            pos[row_start[r]:row_start[r + 1]] = packs[i].position_ids[0, a:b].numpy()
-            parent[r] = prow
             row_index[(i, seg)] = (d, r, a)
             rows.append((i, seg, a))
         if d == 0:
