@@ -78,35 +78,24 @@ class Level:
         return out
 
     def attention_tiles(self, tokens):
-        """Query tiles of at most `tokens` tokens (janus_b200_tree_attention_tile_tokens)."""
+        """Query tiles of at most `tokens` tokens (janus_b200_tree_attention_tile_tokens): the level's tokens are cut
+        where a row's long ancestors change (a tile reads one state) and after every long row (a tile never leaves
+        one); between cuts, consecutive tiles of `tokens` tokens, the last one shorter."""
         if tokens in self.tiles:
             return self.tiles[tokens]
         tq = max(1, int(tokens))
-        out = []
-        start = None
-        count = 0
-        long_anc = [(hi - lo) > LONG_ANCESTOR for lo, hi in zip(self.anc_lo, self.anc_hi)]
-        prev_key = None
-        for r in range(self.B):
-            a, b = int(self.row_start[r]), int(self.row_start[r + 1])
-            key = tuple(int(self.anc_lo[l][r]) for l in range(len(self.anc_lo)) if long_anc[l][r])
-            if start is not None and key != prev_key:
-                out.append((start, start + count)); start = None; count = 0
-            prev_key = key
-            t = a
-            while t < b:
-                if start is None:
-                    start, count = t, 0
-                take = min(tq - count, b - t)
-                count += take
-                t += take
-                if count == tq:
-                    out.append((start, start + count)); start = None; count = 0
-            if start is not None and (b - a) > LONG_OWN:
-                out.append((start, start + count)); start = None; count = 0
-        if start is not None:
-            out.append((start, start + count))
-        arr = np.asarray(out, dtype=np.int32).reshape(-1, 2)
+        rs = self.row_start.astype(np.int64)
+        cuts = [np.array([0, self.T], dtype=np.int64), rs[np.flatnonzero(np.diff(rs) > LONG_OWN) + 1]]
+        if self.B > 1 and self.anc_lo:
+            key = np.stack([np.where((hi - lo) > LONG_ANCESTOR, lo, -1) for lo, hi in zip(self.anc_lo, self.anc_hi)], 1)
+            cuts.append(rs[np.flatnonzero((key[1:] != key[:-1]).any(axis=1)) + 1])
+        b = np.unique(np.concatenate(cuts))
+        s, e = b[:-1], b[1:]
+        n = (e - s + tq - 1) // tq
+        first = np.repeat(np.cumsum(n) - n, n)
+        starts = np.repeat(s, n) + (np.arange(int(n.sum()), dtype=np.int64) - first) * tq
+        ends = np.minimum(starts + tq, np.repeat(e, n))
+        arr = np.stack([starts, ends], axis=1).astype(np.int32).reshape(-1, 2)
         self.tiles[tokens] = arr
         return arr
 
