@@ -80,3 +80,45 @@ def test_readout_layout_tree_and_listwise():
     assert ro.n_slots == 4 + 3 + 2
     orows, oq, drows, slots = ro.pointer[1]
     assert len(drows) == 3 and oq.tolist() == [0] * 4 + [1] * 3 + [2] * 2
+
+
+def _greedy_tiles(lv, n):
+    """The tile rule written as a plain walk over the rows: tiles of n tokens fill across rows, closed where the
+    row's long ancestors (> LONG_ANCESTOR keys) change and after every long row (> LONG_OWN tokens)."""
+    from janus_b200.plan import LONG_ANCESTOR, LONG_OWN
+    out, start, count, prev = [], None, 0, None
+    for r in range(lv.B):
+        a, b = int(lv.row_start[r]), int(lv.row_start[r + 1])
+        key = tuple(int(lo[r]) if int(hi[r]) - int(lo[r]) > LONG_ANCESTOR else -1
+                    for lo, hi in zip(lv.anc_lo, lv.anc_hi))
+        if start is not None and key != prev:
+            out.append((start, start + count)); start, count = None, 0
+        prev = key
+        t = a
+        while t < b:
+            if start is None:
+                start, count = t, 0
+            take = min(n - count, b - t)
+            count += take
+            t += take
+            if count == n:
+                out.append((start, start + count)); start, count = None, 0
+        if start is not None and b - a > LONG_OWN:
+            out.append((start, start + count)); start, count = None, 0
+    if start is not None:
+        out.append((start, start + count))
+    return np.asarray(out, dtype=np.int32).reshape(-1, 2)
+
+
+def test_vectorised_tables_equal_a_row_by_row_restatement():
+    packs = [synthetic.q4b_request(vocab=4096, seed=s, state_tokens=st, questions=q)
+             for s, st, q in ((0, 300, 3), (1, 70, 5), (2, 1000, 2))]
+    packs += [synthetic.tiny_request(seed=3, mode="tree")]
+    levels, _ = build_levels(packs)
+    for lv in levels:
+        for r, (i, seg, a) in enumerate(lv.rows):  # every row's tokens and positions are its pack's slice
+            s, e = int(lv.row_start[r]), int(lv.row_start[r + 1])
+            assert (lv.ids[s:e] == packs[i].input_ids[0, a:a + e - s].numpy()).all()
+            assert (lv.positions[s:e] == packs[i].position_ids[0, a:a + e - s].numpy()).all()
+        for n in (1, 7, 16, 32, 64, 128):
+            assert np.array_equal(lv.attention_tiles(n), _greedy_tiles(lv, n)), (lv.depth, n)
