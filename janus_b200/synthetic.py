@@ -21,7 +21,7 @@ import zlib
 import numpy as np
 import torch
 
-from .config import FULL, LINEAR, SHAPES, ModelShape
+from .config import LINEAR, SHAPES, ModelShape
 from .packing import Question, pack_listwise, pack_tree
 
 LORA_TARGETS = ("q_proj", "k_proj", "v_proj", "o_proj", "in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "out_proj")

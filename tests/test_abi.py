@@ -1,6 +1,5 @@
 """The C ABI library (no GPU needed): it loads, and it exports every function include/janus_b200.h declares."""
 
-import ctypes
 import re
 from pathlib import Path
 

@@ -5,9 +5,7 @@ state is refused. A hit runs the branch levels on the same level-0 rows as the p
 plain pass's to fp32 rounding; a state level run as a different batch (the misses of a mixed batch) goes through
 cuBLAS GEMMs of another row count, so those are compared within the readout tolerance of the golden tests."""
 
-import numpy as np
 import pytest
-import torch
 
 from tests.golden_cases import case_model, load_cases
 

@@ -12,7 +12,6 @@ bf16 (its own precision noise on this random-init model). The bf16 path here is 
 
 import numpy as np
 import pytest
-import torch
 
 from tests.golden_cases import case_model, load_cases
 
