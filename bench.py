@@ -19,9 +19,12 @@ and the combine per step, each timed with CUDA events, TFLOP/s of the grouped GE
 snapshots (DecisionReadout.encode_prefixes) and each step runs the branch levels only.
 
 `--impl reference` times the reference algorithm on the host cores instead: the CPU oracle (oracle/hybrid.py, a
-restatement of the reference's readout pinned to its golden outputs) on one request of the same workload through a
-2-layer slice of the model (one DeltaNet and one attention layer over every level), its per-layer times weighted by
-the model's 24 DeltaNet and 8 attention layers.
+restatement of the reference's readout pinned to its golden outputs) on one request of the same workload, each
+step through one 4-layer block of the model (3 DeltaNet + 1 attention layer, every level; the model is 8 such
+blocks), plus one measured pass of the same request through all 32 layers as a check of that factor.
+
+Besides the batch step, the line carries `request_latency_ms`: p50/p90 over single requests of the workload run one
+at a time (batch 1), device time and end to end through the public API.
 """
 
 import argparse
@@ -43,12 +46,22 @@ REQUESTS_PER_GPU = 16
 METRIC = "decision requests/s (4B shape, 8K state, 8 questions)"
 UNIT = "requests/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one level-0 launch, from ncu captures of this build
-# (profiles/): the chunk scan (prep + state pass) of one DeltaNet layer at 16 requests x 8192 tokens, and the tree
-# attention of one layer captured at 2 requests and scaled by 8 to 16 (each request reads only its own K/V, so the
-# traffic grows in proportion to the requests). Scaled to other request counts the same way.
-NCU_LEVEL0_TRAFFIC = {"gdn_chunk_scan": (2.18e9 + 2.66e9) + (3.78e9 + 1.09e9), "tree_attention": 447.7e6 * 8}
-NCU_LEVEL0_REQUESTS = 16
+
+
+def ncu_traffic():
+    """DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one level-0 launch per kernel, as the ncu
+    summaries under profiles/ state them on a line `bench-traffic: kernel=<name> bytes=<B> requests=<R>` (the
+    capture's request count; each request reads only its own state, so the traffic scales with the requests)."""
+    import glob
+    import re
+    out = {}
+    for path in sorted(glob.glob(os.path.join(ROOT, "profiles", "*.md"))):
+        with open(path) as f:
+            for line in f:
+                m = re.match(r"\s*bench-traffic:\s*kernel=(\w+)\s+bytes=([0-9.eE+]+)\s+requests=(\d+)", line)
+                if m:
+                    out[m.group(1)] = (float(m.group(2)), int(m.group(3)), os.path.basename(path))
+    return out
 
 
 def peaks():
@@ -58,6 +71,14 @@ def peaks():
             p = json.load(f)
         return p, "measured"
     return PEAKS_FALLBACK, "fallback"
+
+
+def nearest_rank(values, q):
+    """The q-quantile by nearest rank (janus/loadtest.py:33-35); None for no values."""
+    if not values:
+        return None
+    v = sorted(values)
+    return v[min(len(v) - 1, max(0, int(np.ceil(q * len(v))) - 1))]
 
 
 def dist_env():
@@ -139,46 +160,60 @@ def run_reference(args):
         return
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    value, sample = cpu_reference_rate(args.steps, min(args.warmup, 1))
+    value, sample, detail = cpu_reference_rate(args.steps, min(args.warmup, 1), full_request=True)
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 / value if value else None, "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": detail["block_s"] * 1000.0, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": "4b-tree-8k-state-8q", "requests_per_gpu": 1, "sample": sample},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "config": {"workload": "4b-tree-8k-state-8q", "requests_per_gpu": 1, "sample": sample,
+                       "same_config": False},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample, **detail},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def cpu_reference_rate(steps=1, warmup=0):
-    """Seconds per request of the oracle for one full request of the workload (8192-token state, 8 questions)
-    through a 2-layer slice of the 4B shape (one DeltaNet and one attention layer, every level), weighted by the
-    model's layer counts (24 DeltaNet + 8 attention); returns (requests/s, description)."""
+def cpu_reference_rate(steps=1, warmup=0, full_request=False):
+    """The CPU oracle (fp32, all host threads) on one full request of the workload (8192-token state, 8 tree
+    questions). A timed step runs the request through one 4-layer block of the 4B shape (3 DeltaNet + 1 attention
+    layer, every level, embedding and head included): the model is 8 repeats of that block, so a request costs 8
+    blocks (the embedding gather and the head, a few ms, are counted 8 times). With `full_request` the whole
+    32-layer model (full vocabulary) also runs the same request once, measured, as a check of that factor.
+    Returns (requests/s from the block steps, description, details)."""
     from janus_b200 import synthetic
-    from janus_b200.config import FULL, LINEAR, SHAPES
+    from janus_b200.config import SHAPES
     from oracle import hybrid as oracle
     full = SHAPES["4b"]
-    shape = full.with_layers(2, vocab=4096)
-    shape = shape.__class__(**{**shape.__dict__, "layer_types": (LINEAR, FULL)})
+    blocks = full.layers // 4
+    shape = full.with_layers(4, vocab=4096)
     weights = synthetic.make_weights(shape, seed=0, head="scalar", device="cpu")
     model = oracle.Oracle(shape, weights)
+    del weights
     pack = synthetic.q4b_request(vocab=4096, seed=0)
     times = []
-    for i in range(max(0, warmup) + max(1, steps)):
-        model.layer_seconds = {}
+    with torch.no_grad():
+        for i in range(max(0, warmup) + max(1, steps)):
+            t0 = time.perf_counter()
+            oracle.probabilities(model.logits(pack, "tree"))
+            if i >= warmup:
+                times.append(time.perf_counter() - t0)
+    block_s = statistics.median(times)
+    detail = {"block_s": block_s, "blocks_per_request": blocks, "block_steps": len(times)}
+    sample = (f"one 4B-shape request ({pack.token_count} tokens: 8192-token state, 8 questions) through one 4-layer "
+              f"block (3 DeltaNet + 1 attention) of the CPU oracle per step, fp32, {torch.get_num_threads()} threads, "
+              f"median of {len(times)} steps; requests/s = 1 / ({blocks} x block seconds)")
+    if full_request:
+        del model
+        weights = synthetic.make_weights(full, seed=0, head="scalar", device="cpu")
+        model = oracle.Oracle(full, weights)
+        del weights
+        pack = synthetic.q4b_request(seed=0)
         t0 = time.perf_counter()
         with torch.no_grad():
             oracle.probabilities(model.logits(pack, "tree"))
-        total = time.perf_counter() - t0
-        if i >= warmup:
-            rest = total - sum(model.layer_seconds.values())
-            n_lin = sum(1 for t in full.layer_types if t == LINEAR)
-            times.append(rest + n_lin * model.layer_seconds[LINEAR] + (full.layers - n_lin) * model.layer_seconds[FULL])
-    per_request = statistics.median(times)
-    sample = (f"one 4B-shape request ({pack.token_count} tokens: 8192-token state, 8 questions) through a 2-layer "
-              f"slice (1 DeltaNet + 1 attention layer) of the CPU oracle, fp32, {torch.get_num_threads()} threads, "
-              f"per-layer times weighted 24 DeltaNet + 8 attention, median of {len(times)}")
-    return 1.0 / per_request, sample
+        detail["full_request_s"] = time.perf_counter() - t0
+        detail["full_request"] = "the same request through all 32 layers (vocab 248320), measured once"
+        detail["block_extrapolation_error"] = blocks * block_s / detail["full_request_s"] - 1.0
+    return 1.0 / (blocks * block_s), sample, detail
 
 
 def run_moe(args):
@@ -282,6 +317,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--requests", type=int, default=REQUESTS_PER_GPU)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--latency-requests", type=int, default=8, help="single requests timed one at a time")
     ap.add_argument("--layers", type=int, default=0, help="debug: fewer layers (not a valid bench number)")
     ap.add_argument("--op", default="readout", choices=["readout", "moe", "prefix"])
     ap.add_argument("--moe-tokens", type=int, default=131072)
@@ -342,13 +378,14 @@ def main():
 
     # timed device pass
     attn_flops = attention_flops(levels, shape)
-    chunked = [model._chunked(lv) for lv in levels]
+    # levels the chunk scan runs: long rows, and the leaf level's state fork as a segmented scan
+    chunked = [model._chunked(lv) or model._packed_fork(lv) for lv in levels]
     ops.TIMED.clear()
     ops.TIMED["tree_attention"] = []
     ops.TIMED["gdn_chunk_scan"] = []
     ops.TIMED["gdn_fork_recurrent"] = []
-    clocks = Clocks(local, os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else ".",
-                                        f"clocks_rank{rank}.csv"))
+    import tempfile
+    clocks = Clocks(local, os.path.join(tempfile.gettempdir(), f"janus_b200_clocks_{os.getpid()}_rank{rank}.csv"))
     barrier()
     torch.cuda.synchronize()
     launches0 = ops.LAUNCHES[0]
@@ -414,15 +451,17 @@ def main():
                     "unit": "GB/s", "frac": by / sec / b_peak, "traffic": None}
         roof["ms_per_step"] = kernel_ms[dominant]
         roof["peak_kind"] = pk_kind
-    if roof is not None and roof["kernel"] in NCU_LEVEL0_TRAFFIC and not args.layers:
+    traffic = ncu_traffic()
+    if roof is not None and roof["kernel"] in traffic and not args.layers:
         # DRAM traffic of one level-0 launch (ncu) beside the algorithmic bytes of that launch
         lv0 = levels[0]
         if roof["kernel"] == "tree_attention":
             alg0 = lv0.T * (3 * shape.heads * shape.head_dim * 2 + 2 * shape.kv_heads * shape.head_dim * 2)
         else:
             alg0 = chunk_algorithmic(levels[:1], shape, [True])[0][1]
-        roof["traffic"] = NCU_LEVEL0_TRAFFIC[roof["kernel"]] * args.requests / NCU_LEVEL0_REQUESTS
-        roof["traffic_per"] = "level-0 launch (ncu capture, profiles/)"
+        t_bytes, t_requests, t_file = traffic[roof["kernel"]]
+        roof["traffic"] = t_bytes * args.requests / t_requests
+        roof["traffic_per"] = f"level-0 launch (ncu capture at {t_requests} requests, profiles/{t_file}, scaled)"
         roof["algorithmic_bytes_per_level0_launch"] = float(alg0)
 
     # end to end through the public API: host packing -> H2D -> device pass -> D2H -> softmax
@@ -438,16 +477,35 @@ def main():
     e2e_step = max_over_ranks(statistics.median(e2e_ms))
     e2e_value = world * args.requests / (e2e_step / 1000.0)
 
+    # per-request latency: requests of the workload one at a time (batch 1), device time of the readout pass and
+    # end to end through the public API
+    lat_dev, lat_e2e = [], []
+    for j, p1 in enumerate(packs[:args.latency_requests]):
+        prep1 = model.prepare([p1])
+        if j == 0:
+            model.run(prep1)
+            model.probabilities([p1])
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        model.run(prep1)
+        b.record()
+        torch.cuda.synchronize()
+        lat_dev.append(a.elapsed_time(b))
+        t0 = time.perf_counter()
+        model.probabilities([p1])
+        lat_e2e.append((time.perf_counter() - t0) * 1000.0)
+    model.check_status()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cores = os.cpu_count() or 1
         torch.set_num_threads(cores)
-        v, sample = cpu_reference_rate(1, 0)
-        cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+        v, sample, detail = cpu_reference_rate(1, 0)
+        cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample, **detail}
 
     if rank == 0:
-        lat = sorted(step_ms)
-        p = lambda q: lat[min(len(lat) - 1, max(0, int(np.ceil(q * len(lat))) - 1))]
+        p = lambda q: nearest_rank(step_ms, q)
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
@@ -456,6 +514,10 @@ def main():
                            "questions": 8, "parallelism": f"dp{world} (replicas)",
                            "l2": "inputs larger than L2 (activations of a level are GBs)"},
                 "latency_ms": {"p50": p(0.5), "p90": p(0.9), "per": "batch step (every request of the batch completes at its end)"},
+                "request_latency_ms": {
+                    "per": f"single request (batch 1), {len(lat_dev)} requests of the workload one at a time",
+                    "device": {"p50": nearest_rank(lat_dev, 0.5), "p90": nearest_rank(lat_dev, 0.9)},
+                    "e2e": {"p50": nearest_rank(lat_e2e, 0.5), "p90": nearest_rank(lat_e2e, 0.9)}},
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "ms_per_step": e2e_step},
                 "gpu_launches": launches, "kernel_ms_per_step": kernel_ms, "op_ms_one_step": op_ms, "roofline": roof, "cpu_baseline": cpu,

@@ -154,6 +154,7 @@ int janus_b200_tree_attention_tile_tokens(int64_t D, int64_t Hq, int64_t Hkv);
 
 /* ScalarHead readout fused with the final norm: for each of n rows r = rows[i] of the fp32 residual x [*, H]:
  * h = rmsnorm(x[r]) * (1 + final_w) (eps rms_eps), logits[i] = LayerNorm(h; ln_w, ln_b, ln_eps) . w_out + b_out[0].
+ * final_w NULL: h = x[r] (rows that are already final-normed, ScalarHead.forward alone; same for the pointer heads).
  * Replaces lm.norm + ScalarHead.forward (janus/model.py:85-92, 342-350). */
 int janus_b200_head_scalar(const float* x, int64_t H, const int32_t* rows, int64_t n, const void* final_w,
                            float rms_eps, const float* ln_w, const float* ln_b, float ln_eps, const float* w_out,
@@ -162,6 +163,8 @@ int janus_b200_head_scalar(const float* x, int64_t H, const int32_t* rows, int64
 /* PointerHead readout fused with the final norm: option i (row option_rows[i], question option_question[i])
  * scores logits[i] = (LN(h_opt) Wk^T) . (LN(h_dec) Wq^T) / sqrt(R), h the final-normed rows, h_dec the row
  * decision_rows[option_question[i]]. wq, wk fp32 [R, H]. workspace: fp32, at least (n + Q) * R floats.
+ * R <= 4096, n + Q <= 2^24, Q > 0 when n > 0. The caller guarantees 0 <= option_question[i] < Q; an option outside
+ * that range reads nothing and gets a NaN logit.
  * Replaces lm.norm + PointerHead.forward (janus/model.py:71-82, 361-365). */
 int janus_b200_head_pointer(const float* x, int64_t H, const int32_t* option_rows, const int32_t* option_question,
                             int64_t n, const int32_t* decision_rows, int64_t Q, const void* final_w, float rms_eps,

@@ -9,24 +9,35 @@ namespace jb {
 
 constexpr int kHeadThreads = 256;
 constexpr int kHeadMaxH = 8192;
+constexpr int kHeadMaxRank = 4096;            // projection rank bound (the released heads use 128)
+constexpr int64_t kHeadMaxRows = 1 << 24;     // options + decision rows per call (grid size, int arithmetic)
 
-// Final RMSNorm then LayerNorm of one row into shared memory `ln` (H floats); returns nothing, ln filled.
+// Final RMSNorm then LayerNorm of one row into shared memory `ln` (H floats); returns nothing, ln filled. A null
+// final_w skips the RMSNorm (rows that are already the decoder's final-normed output).
 __device__ void norm_row(const float* __restrict__ xr, int H, const __nv_bfloat16* __restrict__ final_w, float rms_eps,
                          const float* __restrict__ ln_w, const float* __restrict__ ln_b, float ln_eps, float* ln,
                          float* red) {
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    const float v = xr[i];
-    ln[i] = v;
-    ss += v * v;
-  }
-  ss = block_sum(ss, red);
-  const float r = rsqrtf(ss / (float)H + rms_eps);
   float s = 0.f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    const float h = ln[i] * r * (1.f + bf2f(final_w[i]));
-    ln[i] = h;
-    s += h;
+  if (final_w) {
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+      const float v = xr[i];
+      ln[i] = v;
+      ss += v * v;
+    }
+    ss = block_sum(ss, red);
+    const float r = rsqrtf(ss / (float)H + rms_eps);
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+      const float h = ln[i] * r * (1.f + bf2f(final_w[i]));
+      ln[i] = h;
+      s += h;
+    }
+  } else {
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+      const float v = xr[i];
+      ln[i] = v;
+      s += v;
+    }
   }
   __syncthreads();
   s = block_sum(s, red);
@@ -83,13 +94,20 @@ __global__ void __launch_bounds__(kHeadThreads) head_project_kernel(
   }
 }
 
+// An option whose question index lies outside [0, Q) reads nothing and gets a NaN logit (the caller's contract is
+// 0 <= option_question[i] < Q; a NaN makes a broken table visible instead of reading past the projected rows).
 __global__ void head_dot_kernel(const float* __restrict__ proj, int n, const int32_t* __restrict__ option_question,
-                                int R, float inv_scale, float* __restrict__ logits) {
+                                int Q, int R, float inv_scale, float* __restrict__ logits) {
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= n) return;
+  const int qi = option_question[w];
+  if (qi < 0 || qi >= Q) {
+    if (lane == 0) logits[w] = __int_as_float(0x7fc00000);
+    return;
+  }
   const float* a = proj + (int64_t)w * R;
-  const float* b = proj + (int64_t)(n + option_question[w]) * R;
+  const float* b = proj + (int64_t)(n + qi) * R;
   float d = 0.f;
   for (int j = lane; j < R; j += 32) d += a[j] * b[j];
   d = warp_sum(d);
@@ -103,7 +121,7 @@ using namespace jb;
 extern "C" int janus_b200_head_scalar(const float* x, int64_t H, const int32_t* rows, int64_t n, const void* final_w,
                                       float rms_eps, const float* ln_w, const float* ln_b, float ln_eps,
                                       const float* w_out, const float* b_out, float* logits, void* stream) {
-  JB_REQUIRE(x && rows && final_w && ln_w && ln_b && w_out && b_out && logits, JANUS_ERR_INVALID,
+  JB_REQUIRE(x && rows && ln_w && ln_b && w_out && b_out && logits, JANUS_ERR_INVALID,
              "head_scalar: null pointer");
   JB_REQUIRE(H > 0 && H <= kHeadMaxH && n >= 0, JANUS_ERR_INVALID, "head_scalar: hidden %lld out of range", (long long)H);
   if (n == 0) return JANUS_OK;
@@ -117,9 +135,14 @@ extern "C" int janus_b200_head_pointer(const float* x, int64_t H, const int32_t*
                                        int64_t Q, const void* final_w, float rms_eps, const float* ln_w,
                                        const float* ln_b, float ln_eps, const float* wq, const float* wk, int64_t R,
                                        float* workspace, size_t workspace_bytes, float* logits, void* stream) {
-  JB_REQUIRE(x && option_rows && option_question && decision_rows && final_w && ln_w && ln_b && wq && wk && logits,
+  JB_REQUIRE(x && option_rows && option_question && decision_rows && ln_w && ln_b && wq && wk && logits,
              JANUS_ERR_INVALID, "head_pointer: null pointer");
-  JB_REQUIRE(H > 0 && H <= kHeadMaxH && n >= 0 && Q >= 0 && R > 0, JANUS_ERR_INVALID, "head_pointer: sizes");
+  JB_REQUIRE(H > 0 && H <= kHeadMaxH && n >= 0 && Q >= 0 && R > 0 && R <= kHeadMaxRank, JANUS_ERR_INVALID,
+             "head_pointer: sizes (H %lld, options %lld, questions %lld, rank %lld <= %d)", (long long)H, (long long)n,
+             (long long)Q, (long long)R, kHeadMaxRank);
+  JB_REQUIRE(n == 0 || Q > 0, JANUS_ERR_INVALID, "head_pointer: %lld options but no question", (long long)n);
+  JB_REQUIRE(n + Q <= kHeadMaxRows, JANUS_ERR_INVALID, "head_pointer: options + questions %lld > %lld",
+             (long long)(n + Q), (long long)kHeadMaxRows);
   JB_REQUIRE(workspace && workspace_bytes >= (size_t)(n + Q) * R * sizeof(float), JANUS_ERR_WORKSPACE,
              "head_pointer: workspace %zu bytes < %lld", workspace_bytes, (long long)((n + Q) * R * 4));
   if (n == 0) return JANUS_OK;
@@ -130,8 +153,8 @@ extern "C" int janus_b200_head_pointer(const float* x, int64_t H, const int32_t*
   int st = launch_status("head_pointer/project");
   if (st) return st;
   const int th = 256;
-  head_dot_kernel<<<(unsigned)((n * 32 + th - 1) / th), th, 0, s>>>(workspace, (int)n, option_question, (int)R,
-                                                                   1.f / sqrtf((float)R), logits);
+  head_dot_kernel<<<(unsigned)((n * 32 + th - 1) / th), th, 0, s>>>(workspace, (int)n, option_question, (int)Q,
+                                                                   (int)R, 1.f / sqrtf((float)R), logits);
   return launch_status("head_pointer/dot");
 }
 
@@ -183,9 +206,14 @@ extern "C" int janus_b200_head_pointer_noalloc(const float* x, int64_t H, const 
                                                float rms_eps, const float* ln_w, const float* ln_b, float ln_eps,
                                                const float* wq, const float* wk, int64_t R, float* logits,
                                                void* stream) {
-  JB_REQUIRE(x && option_rows && option_question && decision_rows && final_w && ln_w && ln_b && wq && wk && logits,
+  JB_REQUIRE(x && option_rows && option_question && decision_rows && ln_w && ln_b && wq && wk && logits,
              JANUS_ERR_INVALID, "head_pointer_noalloc: null pointer");
-  JB_REQUIRE(H > 0 && H <= kHeadMaxH && n >= 0 && Q >= 0 && R > 0, JANUS_ERR_INVALID, "head_pointer_noalloc: sizes");
+  JB_REQUIRE(H > 0 && H <= kHeadMaxH && n >= 0 && Q >= 0 && R > 0 && R <= kHeadMaxRank, JANUS_ERR_INVALID,
+             "head_pointer_noalloc: sizes (H %lld, options %lld, questions %lld, rank %lld <= %d)", (long long)H,
+             (long long)n, (long long)Q, (long long)R, kHeadMaxRank);
+  JB_REQUIRE(n == 0 || Q > 0, JANUS_ERR_INVALID, "head_pointer_noalloc: %lld options but no question", (long long)n);
+  JB_REQUIRE(n + Q <= kHeadMaxRows, JANUS_ERR_INVALID, "head_pointer_noalloc: options + questions %lld > %lld",
+             (long long)(n + Q), (long long)kHeadMaxRows);
   JB_REQUIRE((size_t)(n + Q) * (size_t)R <= kPointerScratchFloats, JANUS_ERR_WORKSPACE,
              "head_pointer_noalloc: (options %lld + decisions %lld) x rank %lld = %lld floats exceed the static "
              "scratch of %zu floats; split the call or use janus_b200_head_pointer with a workspace",
@@ -201,7 +229,7 @@ extern "C" int janus_b200_head_pointer_noalloc(const float* x, int64_t H, const 
   st = launch_status("head_pointer_noalloc/project");
   if (st) return st;
   const int th = 256;
-  head_dot_kernel<<<(unsigned)((n * 32 + th - 1) / th), th, 0, s>>>(scratch, (int)n, option_question, (int)R,
-                                                                   1.f / sqrtf((float)R), logits);
+  head_dot_kernel<<<(unsigned)((n * 32 + th - 1) / th), th, 0, s>>>(scratch, (int)n, option_question, (int)Q,
+                                                                   (int)R, 1.f / sqrtf((float)R), logits);
   return launch_status("head_pointer_noalloc/dot");
 }

@@ -192,19 +192,19 @@ class DecisionReadout:
                 and lv.fork_chunks() is not None)
 
     def _heads(self, d, x, plan, logits):
+        """The readout rows of level d through the head, their logits scattered to their slots (row and slot tables
+        come with the level plan: no host data enters the device pass)."""
         ro = self._readout
         hd, s = self.head, self.shape
         if d in ro.scalar:
-            _, slots = ro.scalar[d]
             z = ops.head_scalar(x, plan[(d, "scalar_rows")], self.final_norm, s.rms_eps, hd["norm.weight"],
                                 hd["norm.bias"], 1e-5, hd["out.weight"].reshape(-1), hd["out.bias"])
-            logits[torch.as_tensor(slots, device=x.device)] = z
+            logits.index_copy_(0, plan[(d, "scalar_slots")].long(), z)
         if d in ro.pointer:
-            slots = ro.pointer[d][3]
             z = ops.head_pointer(x, plan[(d, "opt_rows")], plan[(d, "opt_q")], plan[(d, "dec_rows")], self.final_norm,
                                  s.rms_eps, hd["norm.weight"], hd["norm.bias"], 1e-5, hd["query.weight"],
                                  hd["key.weight"])
-            logits[torch.as_tensor(slots, device=x.device)] = z
+            logits.index_copy_(0, plan[(d, "pointer_slots")].long(), z)
 
     # ------------------------------------------------------------------------------------------------ public API
 

@@ -42,6 +42,11 @@ def _ptr(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
+def _opt(t, dtype, name):
+    """An optional tensor argument: None passes as a null pointer."""
+    return None if t is None else _need(t, dtype, name)
+
+
 def _stream(t):
     return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
 
@@ -262,7 +267,7 @@ def head_scalar(x, rows, final_w, rms_eps, ln_w, ln_b, ln_eps, w_out, b_out, log
     _need(x, F32, "x"); _need(rows, I32, "rows")
     n = rows.shape[0]
     logits = torch.empty(n, dtype=F32, device=x.device) if logits is None else logits
-    _lib.check(_lib.load().janus_b200_head_scalar(_ptr(x), x.shape[1], _ptr(rows), n, _ptr(_need(final_w, BF16, "final_w")),
+    _lib.check(_lib.load().janus_b200_head_scalar(_ptr(x), x.shape[1], _ptr(rows), n, _ptr(_opt(final_w, BF16, "final_w")),
                                                   rms_eps, _ptr(_need(ln_w, F32, "ln_w")), _ptr(_need(ln_b, F32, "ln_b")),
                                                   ln_eps, _ptr(_need(w_out, F32, "w_out")), _ptr(_need(b_out, F32, "b_out")),
                                                   _ptr(logits), _stream(x)), "head_scalar")
@@ -278,7 +283,7 @@ def head_pointer(x, option_rows, option_question, decision_rows, final_w, rms_ep
     workspace = torch.empty((n + Q) * R, dtype=F32, device=x.device) if workspace is None else workspace
     _lib.check(_lib.load().janus_b200_head_pointer(
         _ptr(x), x.shape[1], _ptr(_need(option_rows, I32, "option_rows")), _ptr(_need(option_question, I32, "option_question")),
-        n, _ptr(_need(decision_rows, I32, "decision_rows")), Q, _ptr(_need(final_w, BF16, "final_w")), rms_eps,
+        n, _ptr(_need(decision_rows, I32, "decision_rows")), Q, _ptr(_opt(final_w, BF16, "final_w")), rms_eps,
         _ptr(_need(ln_w, F32, "ln_w")), _ptr(_need(ln_b, F32, "ln_b")), ln_eps, _ptr(_need(wq, F32, "wq")),
         _ptr(_need(wk, F32, "wk")), R, _ptr(workspace), workspace.numel() * 4, _ptr(logits), _stream(x)), "head_pointer")
     return logits

@@ -243,12 +243,14 @@ class DevicePlan:
                 add((d, "fc_start"), fc[0])
                 add((d, "fc_parent"), fc[1])
                 add((d, "fc_chunks"), np.arange(fc[1].shape[0] + 1, dtype=np.int32))
-        for d, (rows, _) in readout.scalar.items():
+        for d, (rows, slots) in readout.scalar.items():
             add((d, "scalar_rows"), rows)
-        for d, (orows, oq, drows, _) in readout.pointer.items():
+            add((d, "scalar_slots"), slots)
+        for d, (orows, oq, drows, slots) in readout.pointer.items():
             add((d, "opt_rows"), orows)
             add((d, "opt_q"), oq)
             add((d, "dec_rows"), drows)
+            add((d, "pointer_slots"), slots)
         host = np.concatenate(chunks) if chunks else np.zeros(0, np.int32)
         pinned = torch.from_numpy(host).pin_memory() if torch.cuda.is_available() else torch.from_numpy(host)
         self.buffer = pinned.to(device, non_blocking=True)

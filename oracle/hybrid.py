@@ -47,11 +47,21 @@ def l2norm(x, eps=1e-6):
     return x * torch.rsqrt((x * x).sum(-1, keepdim=True) + eps)
 
 
-def delta_prologue(mixed, b, a, tail, conv_w, A_log, dt_bias, key_dim, k_dim, v_dim):
+def _keep(x):
+    return x
+
+
+def bf16_round(x):
+    """x rounded to bf16 (nearest even) and back to fp32: a tensor the B200 path stores in bf16."""
+    return x.to(torch.bfloat16).float()
+
+
+def delta_prologue(mixed, b, a, tail, conv_w, A_log, dt_bias, key_dim, k_dim, v_dim, rnd=_keep):
     """The glue between a DeltaNet layer's projections and its recurrence (janus/hybrid.py:220-238, 276-301) for one
     unpadded row: causal depthwise conv (K taps) over [tail || mixed], silu, head split, l2-normalised q and k,
     beta = sigmoid(b), g = -exp(A_log) * softplus(a + dt_bias). mixed [L, C], tail [C, K-1] or None.
-    Returns q [L, Hk, Dk], k, v [L, Hv, Dv], g [L, Hv], beta [L, Hv], new tail [C, K-1] (the last K-1 conv inputs)."""
+    Returns q [L, Hk, Dk], k, v [L, Hv, Dv], g [L, Hv], beta [L, Hv], new tail [C, K-1] (the last K-1 conv inputs);
+    `rnd` is applied to q, k and v (the tensors the next op reads)."""
     L, C = mixed.shape
     K = conv_w.shape[-1]
     if tail is None:
@@ -67,7 +77,7 @@ def delta_prologue(mixed, b, a, tail, conv_w, A_log, dt_bias, key_dim, k_dim, v_
     v = v.reshape(L, -1, v_dim)
     beta = torch.sigmoid(b.float())
     g = -A_log.float().exp() * F.softplus(a.float() + dt_bias.float())
-    return q, k, v, g, beta, new_tail
+    return rnd(q), rnd(k), rnd(v), g, beta, new_tail
 
 
 def _expand_heads(x, hv):
@@ -171,9 +181,11 @@ def attention(q, k_all, v_all, n_prefix, scale):
     return out.permute(2, 0, 1, 3).reshape(L, Hq, D)
 
 
-def moe_block(x, p, shape):
+def moe_block(x, p, shape, rnd=_keep):
     """Qwen3_5MoeSparseMoeBlock (transformers qwen3_5_moe :754-791): router softmax (fp32) -> top-k -> renormalise;
-    routed SwiGLU experts weighted by the routing weights; the shared expert times sigmoid(x . w_gate)."""
+    routed SwiGLU experts weighted by the routing weights; the shared expert times sigmoid(x . w_gate). `rnd` marks
+    the tensors stored between ops: silu(gate) * up per assignment, each expert's weighted output row, the shared
+    expert's projections, and the block output."""
     logits = x @ p["gate.weight"].t()
     probs = torch.softmax(logits, dim=-1)
     top, idx = torch.topk(probs, shape.top_k, dim=-1)
@@ -184,16 +196,18 @@ def moe_block(x, p, shape):
     for e in torch.unique(idx).tolist():
         tok, slot = torch.where(idx == e)
         h = x[tok] @ gu[e].t()
-        h = F.silu(h[:, :I]) * h[:, I:]
-        out.index_add_(0, tok, (h @ dn[e].t()) * top[tok, slot, None])
-    sh = F.silu(x @ p["shared_expert.gate_proj.weight"].t()) * (x @ p["shared_expert.up_proj.weight"].t())
-    sh = sh @ p["shared_expert.down_proj.weight"].t()
-    return out + torch.sigmoid(x @ p["shared_expert_gate.weight"].t()) * sh
+        h = rnd(F.silu(h[:, :I]) * h[:, I:])
+        out.index_add_(0, tok, rnd((h @ dn[e].t()) * top[tok, slot, None]))
+    sh = rnd(F.silu(rnd(x @ p["shared_expert.gate_proj.weight"].t())) * rnd(x @ p["shared_expert.up_proj.weight"].t()))
+    sh = rnd(sh @ p["shared_expert.down_proj.weight"].t())
+    return rnd(out + torch.sigmoid(x @ p["shared_expert_gate.weight"].t()) * sh)
 
 
-def mlp(x, p):
-    """Qwen3_5MLP: down(silu(gate(x)) * up(x)) (transformers :695-708)."""
-    return (F.silu(x @ p["gate_proj.weight"].t()) * (x @ p["up_proj.weight"].t())) @ p["down_proj.weight"].t()
+def mlp(x, p, rnd=_keep):
+    """Qwen3_5MLP: down(silu(gate(x)) * up(x)) (transformers :695-708); `rnd` marks the stored tensors (the gate and
+    up projections, their SwiGLU product, the output)."""
+    h = rnd(F.silu(rnd(x @ p["gate_proj.weight"].t())) * rnd(x @ p["up_proj.weight"].t()))
+    return rnd(h @ p["down_proj.weight"].t())
 
 
 def layer_norm(x, w, b, eps=1e-5):
@@ -250,10 +264,21 @@ def tree_levels(segment_ids, parents):
 
 class Oracle:
     """The fp32 tree forward of one model. `weights`: the name -> tensor dict of janus_b200.synthetic.make_weights
-    (int4 expert stacks are dequantised here to their bf16 values)."""
+    (int4 expert stacks are dequantised here to their bf16 values).
 
-    def __init__(self, shape, weights, chunk_threshold=64):
+    `storage`: "fp32" computes and keeps every tensor in fp32 (the reference's fp32 readout). "bf16" rounds to bf16
+    exactly the tensors the B200 path stores in bf16 between its kernels (the normed GEMM inputs, every projection
+    output, q/k/v after the DeltaNet prologue and after the attention q/k preparation, the delta rule's and the
+    attention's outputs, the gated norm's output, the SwiGLU product, the MoE rows) while the residual stream, the
+    DeltaNet g/beta and states, the router logits and the heads stay fp32 as there: the reference's algorithm at the
+    storage precision of the B200 path, so the two differ only by what happens inside the kernels (accumulation
+    order, the kernels' internal bf16 operands)."""
+
+    def __init__(self, shape, weights, chunk_threshold=64, storage="fp32"):
+        if storage not in ("fp32", "bf16"):
+            raise ValueError("storage must be fp32 or bf16")
         self.shape = shape
+        self.rnd = bf16_round if storage == "bf16" else _keep
         w = {}
         for name, t in weights.items():
             if name.endswith(".scales"):
@@ -279,43 +304,44 @@ class Oracle:
         L = x.shape[0]
         cos, sin = rope_tables(positions, s.rotary_dim, s.rope_theta)
         states = []
+        r = self.rnd
         for i, kind in enumerate(s.layer_types):
             t0 = time.perf_counter()
             p = self._p(f"layers.{i}.")
-            h = rmsnorm(x, p["input_layernorm.weight"], s.rms_eps)
+            h = r(rmsnorm(x, p["input_layernorm.weight"], s.rms_eps))
             if kind == LINEAR:
                 a = {k[len("linear_attn."):]: v for k, v in p.items() if k.startswith("linear_attn.")}
-                mixed = h @ a["in_proj_qkv.weight"].t()
-                z = (h @ a["in_proj_z.weight"].t()).reshape(L, s.lin_v_heads, s.lin_v_dim)
-                b = h @ a["in_proj_b.weight"].t()
-                aa = h @ a["in_proj_a.weight"].t()
+                mixed = r(h @ a["in_proj_qkv.weight"].t())
+                z = r(h @ a["in_proj_z.weight"].t()).reshape(L, s.lin_v_heads, s.lin_v_dim)
+                b = r(h @ a["in_proj_b.weight"].t())
+                aa = r(h @ a["in_proj_a.weight"].t())
                 tail, S0 = parent_states[i] if parent_states is not None else (None, None)
                 q, k, v, g, beta, new_tail = delta_prologue(mixed, b, aa, tail, a["conv1d.weight"], a["A_log"],
-                                                            a["dt_bias"], s.key_dim, s.lin_k_dim, s.lin_v_dim)
+                                                            a["dt_bias"], s.key_dim, s.lin_k_dim, s.lin_v_dim, r)
                 rule = delta_chunked if L > self.chunk_threshold else delta_recurrent
                 core, S = rule(q, k, v, g, beta, S0)
-                core = gated_rmsnorm(core, z, a["norm.weight"], s.rms_eps).reshape(L, -1)
-                h = core @ a["out_proj.weight"].t()
+                core = r(gated_rmsnorm(r(core), z, a["norm.weight"], s.rms_eps)).reshape(L, -1)
+                h = r(core @ a["out_proj.weight"].t())
                 states.append((new_tail, S))
             else:
                 a = {k[len("self_attn."):]: v for k, v in p.items() if k.startswith("self_attn.")}
                 D = s.head_dim
-                qg = (h @ a["q_proj.weight"].t()).reshape(L, s.heads, 2 * D)
+                qg = r(h @ a["q_proj.weight"].t()).reshape(L, s.heads, 2 * D)
                 q, gate = qg[..., :D], qg[..., D:].reshape(L, -1)
-                k = (h @ a["k_proj.weight"].t()).reshape(L, s.kv_heads, D)
-                v = (h @ a["v_proj.weight"].t()).reshape(L, s.kv_heads, D)
-                q = apply_rope(rmsnorm(q, a["q_norm.weight"], s.rms_eps), cos, sin)
-                k = apply_rope(rmsnorm(k, a["k_norm.weight"], s.rms_eps), cos, sin)
+                k = r(h @ a["k_proj.weight"].t()).reshape(L, s.kv_heads, D)
+                v = r(h @ a["v_proj.weight"].t()).reshape(L, s.kv_heads, D)
+                q = r(apply_rope(rmsnorm(q, a["q_norm.weight"], s.rms_eps), cos, sin))
+                k = r(apply_rope(rmsnorm(k, a["k_norm.weight"], s.rms_eps), cos, sin))
                 if ancestor_kv is not None and ancestor_kv[i] is not None:
                     k_all = torch.cat([ancestor_kv[i][0], k]); v_all = torch.cat([ancestor_kv[i][1], v])
                 else:
                     k_all, v_all = k, v
                 o = attention(q, k_all, v_all, k_all.shape[0] - L, D ** -0.5).reshape(L, -1)
-                h = (o * torch.sigmoid(gate)) @ a["o_proj.weight"].t()
+                h = r(r(o * torch.sigmoid(gate)) @ a["o_proj.weight"].t())
                 states.append((k_all, v_all))
             x = x + h
-            h = rmsnorm(x, p["post_attention_layernorm.weight"], s.rms_eps)
-            x = x + (moe_block(h, self._p(f"layers.{i}.mlp."), s) if s.moe else mlp(h, self._p(f"layers.{i}.mlp.")))
+            h = r(rmsnorm(x, p["post_attention_layernorm.weight"], s.rms_eps))
+            x = x + (moe_block(h, self._p(f"layers.{i}.mlp."), s, r) if s.moe else mlp(h, self._p(f"layers.{i}.mlp."), r))
             self.layer_seconds[kind] = self.layer_seconds.get(kind, 0.0) + time.perf_counter() - t0
         return rmsnorm(x, self.w["norm.weight"], s.rms_eps), states
 

@@ -2,7 +2,9 @@
 
 Run in a container where the reference checkout is importable (default /root/reference, or REFERENCE_ROOT):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py            # readout_cases.json + delta_rule.npz (small cases)
+    python tests/golden/make_golden.py --full     # readout_full.json: the benchmark configurations at full depth
+    python tests/golden/make_golden.py --argmax   # argmax_4b.npz: 1000 seeded questions at 4B width
 
 For every case it builds the seeded synthetic weights (janus_b200.synthetic.make_weights), loads them into a
 transformers Qwen3_5TextModel / Qwen3_5MoeTextModel in fp32, wraps it in the reference's janus.hybrid.HybridBackbone
@@ -11,6 +13,11 @@ DecisionModel.forward readout (PointerHead for listwise, ScalarHead for tree) on
 stores the logits and the temperature-1 probabilities, plus the probabilities of the same reference readout with
 the backbone cast to bf16 and their largest deviation from the fp32 ones (the precision noise floor of the case). The int4 experts enter the reference as their dequantised
 bf16 values (HF experts hold dense stacks). It also stores per-op vectors of the reference's gated delta rule.
+
+`--full` and `--argmax` also store the probabilities of the CPU oracle (oracle/hybrid.py, test infrastructure) run
+with bf16 storage (`Oracle(..., storage="bf16")`: the reference's algorithm with every tensor the B200 path keeps
+in bf16 between kernels rounded there), the like-for-like yardstick of the B200 path at its own storage precision;
+those requests are rebuilt from their seeds by janus_b200.synthetic and checked against a stored crc of their ids.
 
 The fixtures are written once and not edited afterwards; tests compare the CPU oracle and the CUDA path to them.
 """
@@ -171,8 +178,94 @@ def delta_rule_vectors():
     return dict(q=q, k=k, v=v, g=g_, beta=beta, s0=s0, o_chunk=o_c, s_chunk=s_c, o_rec9=o_r, s_rec9=s_r)
 
 
+# The benchmark configurations at full depth. name: (shape, overrides, mode, weight seed, [(builder, kwargs)]).
+# cfg 5 (A3B) keeps its widths and all 256 experts at 4 layers: 40 layers of fp32 experts do not fit host memory.
+def _full_cases():
+    return {
+        "cfg2_08b_listwise": ("0.8b", {}, "listwise", 20, [("q08b_request", dict(seed=200))]),
+        "cfg3_4b_tree": ("4b", {}, "tree", 30, [("q4b_request", dict(seed=300))]),
+        "cfg4_08b_stress": ("0.8b", {}, "tree", 40, [("stress_request", dict(seed=400))]),
+        "cfg5_a3b_tree_4layers": ("35b-a3b", dict(layers=4), "tree", 50,
+                                  [("a3b_request", dict(seed=500, state_tokens=2048)),
+                                   ("a3b_request", dict(seed=501, state_tokens=1024))]),
+    }
+
+
+ARGMAX = dict(shape="4b", overrides=dict(layers=4, vocab=4096), mode="tree", seed=60, requests=125,
+              builder="q4b_request", kwargs=dict(vocab=4096, state_tokens=256), first_seed=600)
+
+
+def ids_crc(pack):
+    import zlib
+    return zlib.crc32(pack.input_ids[0].numpy().astype(np.int64).tobytes())
+
+
+def build_packs(specs):
+    return [getattr(synthetic, b)(**kw) for b, kw in specs]
+
+
+def oracle_probs(shape, weights, mode, packs, storage):
+    sys.path.insert(0, str(HERE.parent.parent))
+    from oracle import hybrid as oracle
+    model = oracle.Oracle(shape, weights, storage=storage)
+    with torch.no_grad():
+        return [[p.tolist() for p in oracle.probabilities(model.logits(pack, mode))] for pack in packs]
+
+
+def main_full():
+    out = HERE / "readout_full.json"
+    manifest = json.loads(out.read_text()) if out.exists() else {}
+    for name, (base, overrides, mode, seed, specs) in _full_cases().items():
+        if name in manifest:
+            continue
+        shape = shape_of(SHAPES[base], dict(overrides))
+        packs = build_packs(specs)
+        weights = synthetic.make_weights(shape, seed=seed, head="scalar" if mode == "tree" else "pointer")
+        logits = reference_logits(shape, weights, mode, packs)
+        probs = [[torch.softmax(z.float(), -1).tolist() for z in per] for per in logits]
+        logits16 = reference_logits(shape, weights, mode, packs, torch.bfloat16)
+        probs16 = [[torch.softmax(z.float(), -1).tolist() for z in per] for per in logits16]
+        dev16 = max(abs(a - b) for pp, qq in zip(probs, probs16) for p, q in zip(pp, qq) for a, b in zip(p, q))
+        po16 = oracle_probs(shape, weights, mode, packs, "bf16")
+        manifest[name] = dict(shape=base, overrides=overrides, mode=mode, seed=seed,
+                              checksum=synthetic.weight_checksum(weights),
+                              requests=[dict(builder=b, kwargs=kw, ids_crc=ids_crc(p), tokens=p.token_count)
+                                        for (b, kw), p in zip(specs, packs)],
+                              logits=[[z.float().tolist() for z in per] for per in logits], probs=probs,
+                              probs_bf16=probs16, bf16_max_dev=dev16, probs_oracle_bf16=po16)
+        print(name, "tokens", [p.token_count for p in packs], "questions", sum(len(p) for p in probs),
+              "reference bf16 vs fp32 max |dp|", dev16, flush=True)
+        out.write_text(json.dumps(manifest))
+        del weights, logits, logits16
+    print("wrote", out)
+
+
+def main_argmax():
+    a = ARGMAX
+    shape = shape_of(SHAPES[a["shape"]], dict(a["overrides"]))
+    specs = [(a["builder"], dict(a["kwargs"], seed=a["first_seed"] + j)) for j in range(a["requests"])]
+    packs = build_packs(specs)
+    weights = synthetic.make_weights(shape, seed=a["seed"], head="scalar")
+    flat = lambda per_pack: np.concatenate([np.asarray(z, dtype=np.float32) for per in per_pack for z in per])
+    logits = reference_logits(shape, weights, a["mode"], packs)
+    p32 = [[torch.softmax(z.float(), -1).numpy() for z in per] for per in logits]
+    p16 = [[torch.softmax(z.float(), -1).numpy() for z in per]
+           for per in reference_logits(shape, weights, a["mode"], packs, torch.bfloat16)]
+    po16 = oracle_probs(shape, weights, a["mode"], packs, "bf16")
+    counts = np.array([len(z) for per in p32 for z in per], dtype=np.int32)
+    np.savez_compressed(HERE / "argmax_4b.npz", spec=np.array(json.dumps(a)), counts=counts,
+                        ids_crc=np.array([ids_crc(p) for p in packs], dtype=np.int64),
+                        checksum=np.array(synthetic.weight_checksum(weights)),
+                        probs=flat(p32), probs_bf16=flat(p16), probs_oracle_bf16=flat(po16))
+    print("wrote", HERE / "argmax_4b.npz", "questions", counts.size, "options", int(counts.sum()))
+
+
 def main():
     torch.set_num_threads(os.cpu_count() or 8)
+    if "--full" in sys.argv:
+        return main_full()
+    if "--argmax" in sys.argv:
+        return main_argmax()
     manifest = {}
     for name, (base, overrides, mode, seed, factory) in _cases().items():
         shape = shape_of(base, dict(overrides))

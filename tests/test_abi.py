@@ -30,6 +30,21 @@ def test_argument_errors_need_no_gpu():
     assert "silu_mul" in _lib.last_error()
 
 
+def test_pointer_head_rejects_tables_it_cannot_serve():
+    """Options without a question, an absurd rank and a row count beyond int range are refused before any launch
+    (non-null placeholder pointers: nothing is dereferenced on the host, nothing reaches a device)."""
+    import ctypes
+    from janus_b200 import _lib
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    for fn in (lib.janus_b200_head_pointer, lib.janus_b200_head_pointer_noalloc):
+        ws = (p, 1 << 30) if fn is lib.janus_b200_head_pointer else ()
+        for n, Q, R, what in ((5, 0, 128, "no question"), (5, 1, 1 << 40, "rank"), (1 << 40, 1, 128, "options")):
+            st = fn(p, 1024, p, p, n, p, Q, p, 1e-6, p, p, 1e-5, p, p, R, *ws, p, None)
+            assert st == -1, (fn, what)
+            assert what in _lib.last_error(), _lib.last_error()
+
+
 def test_every_op_the_readout_calls_is_wrapped():
     """janus_b200.model only calls ops that janus_b200.ops defines (a CPU check of the host path's wiring)."""
     from janus_b200 import ops

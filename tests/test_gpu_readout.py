@@ -1,68 +1,112 @@
 """The full B200 readout against the reference's own probabilities (golden fixtures) and the CPU oracle.
 
-The fixtures hold, for every golden case, the reference's probabilities with its backbone in fp32 (the truth) and in
-bf16 (its own precision noise on this random-init model). The bf16 path here is held to the reference's precision:
+Per question the fixtures hold three probability vectors, all from seeded weights and requests:
 
-- aggregate: the RMS deviation of every option probability from the fp32 truth, over all golden cases, is no larger
-  than the reference's own bf16 RMS deviation over the same options;
-- per case: the largest deviation stays within max(2e-3, twice the reference's bf16 largest deviation on that case)
-  (a gross-error guard: single-option maxima move by ~1e-3 with any rounding-order change);
-- the argmax agrees wherever the reference's top-2 margin exceeds twice that per-case tolerance.
+- p_ref:  the reference (janus.hybrid.HybridBackbone + the janus.model heads) in fp32: the truth;
+- p_ref16: the same reference readout with its backbone cast to bf16 (its plain CPU path);
+- p_o16:  the CPU oracle with bf16 storage (oracle/hybrid.py `Oracle(storage="bf16")`): the reference's algorithm
+          with every tensor the B200 path keeps in bf16 between its kernels rounded at that point, the rest fp32.
+          The oracle itself is pinned to p_ref (fp32 storage: 2e-5, tests/test_oracle.py).
+
+On these random-init models the rounding of the stored bf16 tensors alone moves probabilities by up to ~1e-2 (the
+reference's own bf16 run moves them by as much or more), so the north star's 2e-3 is held where it measures the
+kernels: between the B200 path and p_o16, which round the same tensors at the same points and differ only by the
+kernels' accumulation order and internal bf16 operands.
+
+Gates per case: max |p - p_o16| <= 2e-3; argmax(p) == argmax(p_o16) where p_o16's top-2 margin exceeds 4e-3.
+Over all cases: the RMS of |p - p_ref| is no larger than the reference's own bf16 RMS |p_ref16 - p_ref|.
+Each case prints max and RMS of |p - p_ref|, |p - p_ref16|, |p_ref16 - p_ref|, |p_o16 - p_ref| and |p - p_o16|.
+
+Cases: the small golden set (tests/golden/readout_cases.json: tiny models and 4-layer slices at 0.8B/4B/A3B
+widths) and the benchmark configurations (tests/golden/readout_full.json): cfg 2 (0.8B, 24 layers, 2048-token
+state, listwise), cfg 3 (4B, 32 layers, 8192-token state, 8 tree questions), cfg 4 (0.8B, 24 layers, the
+255-option stress pack on a 4096-token state), cfg 5 at A3B widths with all 256 experts at 4 layers.
 """
 
 import numpy as np
 import pytest
 
-from tests.golden_cases import case_model, load_cases
+from tests.golden_cases import case_model, full_case_model, load_cases, load_full_cases
 
 pytestmark = pytest.mark.gpu
-CASES = load_cases()
 PROB_ATOL = 2e-3
+SMALL = load_cases()
+FULL = load_full_cases()
 _RESULTS = {}
+_REPORT = {}
 
 
-def _run(name):
-    if name not in _RESULTS:
-        from janus_b200.model import DecisionReadout
-        case = CASES[name]
-        shape, weights, mode, packs = case_model(case)
-        model = DecisionReadout(shape, weights, mode)
-        _RESULTS[name] = [[p.numpy() for p in per] for per in model.probabilities(packs)]
-    return _RESULTS[name]
+def _flat(per_pack):
+    return np.concatenate([np.asarray(p, dtype=np.float64).ravel() for per in per_pack for p in per])
 
 
-@pytest.mark.parametrize("name", sorted(CASES))
-def test_readout_matches_reference_probabilities(name):
-    case = CASES[name]
-    tol = max(PROB_ATOL, 2 * case["bf16_max_dev"])
-    worst = 0.0
-    for got_pack, ref_pack in zip(_run(name), case["probs"]):
-        for got, ref in zip(got_pack, ref_pack):
-            ref = np.array(ref)
-            worst = max(worst, float(np.abs(got - ref).max()))
-            top = np.sort(ref)[-2:]
-            if ref.size > 1 and top[1] - top[0] > 2 * tol:
-                assert got.argmax() == ref.argmax(), name
-    assert worst <= tol, f"{name}: max |p - p_ref| = {worst:.2e} > {tol:.2e}"
+def _margins(per_pack):
+    out = []
+    for per in per_pack:
+        for p in per:
+            p = np.sort(np.asarray(p, dtype=np.float64))
+            out.append(p[-1] - p[-2] if p.size > 1 else 1.0)
+    return np.array(out)
+
+
+def _argmax(per_pack):
+    return np.array([int(np.argmax(p)) for per in per_pack for p in per])
+
+
+def _cuda(shape, weights, mode, packs):
+    from janus_b200.model import DecisionReadout
+    model = DecisionReadout(shape, weights, mode)
+    return [[p.numpy() for p in per] for per in model.probabilities(packs)]
+
+
+def _check(name, got, ref, ref16, o16):
+    d = lambda a, b: (float(np.abs(_flat(a) - _flat(b)).max()), float(np.sqrt(np.mean((_flat(a) - _flat(b)) ** 2))))
+    rows = {"|p-p_ref|": d(got, ref), "|p-p_ref16|": d(got, ref16), "|p_ref16-p_ref|": d(ref16, ref),
+            "|p_o16-p_ref|": d(o16, ref), "|p-p_o16|": d(got, o16)}
+    print(f"\n{name}: " + "; ".join(f"{k} max {m:.2e} rms {r:.2e}" for k, (m, r) in rows.items()))
+    _REPORT[name] = (got, ref, ref16)
+    worst = rows["|p-p_o16|"][0]
+    assert worst <= PROB_ATOL, f"{name}: max |p - p_o16| = {worst:.2e} > {PROB_ATOL:.0e}"
+    clear = _margins(o16) > 2 * PROB_ATOL
+    assert np.array_equal(_argmax(got)[clear], _argmax(o16)[clear]), name
+
+
+@pytest.mark.parametrize("name", sorted(SMALL))
+def test_readout_small_cases(name):
+    from oracle import hybrid as oracle
+    case = SMALL[name]
+    shape, weights, mode, packs = case_model(case)
+    got = _cuda(shape, weights, mode, packs)
+    model16 = oracle.Oracle(shape, weights, storage="bf16")
+    o16 = [[p.numpy() for p in oracle.probabilities(model16.logits(pack, mode))] for pack in packs]
+    _check(name, got, case["probs"], case["probs_bf16"], o16)
+
+
+@pytest.mark.parametrize("name", sorted(FULL))
+def test_readout_benchmark_configs(name):
+    case = FULL[name]
+    shape, weights, mode, packs = full_case_model(case)
+    got = _cuda(shape, weights, mode, packs)
+    del weights
+    _check(name, got, case["probs"], case["probs_bf16"], case["probs_oracle_bf16"])
 
 
 def test_aggregate_deviation_is_within_the_reference_bf16_noise():
-    ours, theirs = [], []
-    for name in sorted(CASES):
-        case = CASES[name]
-        for got_pack, ref_pack, bf_pack in zip(_run(name), case["probs"], case["probs_bf16"]):
-            for got, ref, bf in zip(got_pack, ref_pack, bf_pack):
-                ours.append(got - np.array(ref))
-                theirs.append(np.array(bf) - np.array(ref))
-    rms = lambda xs: float(np.sqrt(np.mean(np.concatenate(xs) ** 2)))
-    print(f"RMS |p - p_fp32|: janus_b200 {rms(ours):.3e}, reference bf16 {rms(theirs):.3e}")
+    """Runs after the per-case tests (same module): over every case they ran, the B200 path is at least as close to
+    the fp32 reference as the reference's own bf16 run."""
+    if not _REPORT:
+        pytest.skip("no readout case ran")
+    ours = np.concatenate([_flat(g) - _flat(r) for g, r, _ in _REPORT.values()])
+    theirs = np.concatenate([_flat(r16) - _flat(r) for _, r, r16 in _REPORT.values()])
+    rms = lambda x: float(np.sqrt(np.mean(x ** 2)))
+    print(f"\nRMS |p - p_ref| over {len(_REPORT)} cases: janus_b200 {rms(ours):.3e}, reference bf16 {rms(theirs):.3e}")
     assert rms(ours) <= rms(theirs)
 
 
 def test_batch_composition_does_not_change_results():
     """A request's probabilities do not depend on the other requests of its batch (rows are independent)."""
     from janus_b200.model import DecisionReadout
-    case = CASES["tiny_tree"]
+    case = SMALL["tiny_tree"]
     shape, weights, mode, packs = case_model(case)
     model = DecisionReadout(shape, weights, mode)
     both = model.probabilities(packs)
