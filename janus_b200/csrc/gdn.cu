@@ -3,8 +3,9 @@
 // Prologue: a CTA covers 32 consecutive tokens x 2048 channels; each thread owns 8 channels and slides the causal
 // conv window over the tokens (registers), restarting it at a row boundary from the row's earlier tokens or the
 // parent row's conv tail, so the projection output is read once. q and k are l2-normalised per head with a shuffle
-// reduction over the lanes that hold the head. Rounding follows the reference: the conv activation is rounded once to bf16, the l2 norm is
-// computed in fp32 from that value and rounded once more (janus/hybrid.py:276-301).
+// reduction over the lanes that hold the head. Every output is rounded to bf16 once: the conv activation stays fp32
+// through the l2 norm (the reference's fp32 arithmetic, janus/hybrid.py:220-238, 276-301; its bf16 serving glue
+// rounds the activation before the norm as well, one rounding more than here).
 //
 // Fork recurrent: grid (parent row, value head). A parent's fp32 state [Dk, Dv] is read in place by every child row
 // (no per-row copy); each thread holds Dk*Dv/256 state entries (one value column, a slice of the key rows), so the
@@ -95,13 +96,13 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
 #pragma unroll
     for (int b = 0; b < kProBatch; ++b)
       xr[b] = *reinterpret_cast<const bf16x8*>(my + ((int)(tb + b - t0) & (kProRing - 1)) * kProThreads);
-    bf16x8 acc[kProBatch];  // conv + silu, rounded once to bf16 as the reference does
+    float act[kProBatch][8];  // conv + silu in fp32 (q/k normalised before their one rounding, v rounded once)
 #pragma unroll
     for (int b = 0; b < kProBatch; ++b) {
       const int64_t t = tb + b;
       if (t >= t1) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) acc[b].h[u] = __floats2bfloat162_rn(0.f, 0.f);
+        for (int u = 0; u < 8; ++u) act[b][u] = 0.f;
         continue;
       }
       const int row = rows[b];
@@ -139,7 +140,7 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
         for (int j = 0; j < K - 1; ++j) a[u] += hist[j][u] * wf[u][j];
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) acc[b].h[u] = __floats2bfloat162_rn(silu_fast(a[2 * u]), silu_fast(a[2 * u + 1]));
+      for (int u = 0; u < 8; ++u) act[b][u] = silu_fast(a[u]);
       // slide the window
 #pragma unroll
       for (int j = 0; j < K - 2; ++j)
@@ -158,10 +159,7 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
       for (int b = 0; b < kProBatch; ++b) {
         rn[b] = 0.f;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float2 f = __bfloat1622float2(acc[b].h[u]);
-          rn[b] += f.x * f.x + f.y * f.y;
-        }
+        for (int u = 0; u < 8; ++u) rn[b] += act[b][u] * act[b][u];
       }
       for (int o = lanes_per_head >> 1; o > 0; o >>= 1)
 #pragma unroll
@@ -176,14 +174,10 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
         if (is_qk) {
           float o8[8];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float2 f = __bfloat1622float2(acc[b].h[u]);
-            o8[2 * u] = f.x * rn[b];
-            o8[2 * u + 1] = f.y * rn[b];
-          }
+          for (int u = 0; u < 8; ++u) o8[u] = act[b][u] * rn[b];
           store8(dst + b * dst_stride, o8);
         } else {
-          *reinterpret_cast<bf16x8*>(dst + b * dst_stride) = acc[b];
+          store8(dst + b * dst_stride, act[b]);
         }
       }
     }

@@ -112,9 +112,10 @@ def int4_dequantize(packed, scales, dtype=torch.bfloat16):
     return w.reshape(codes.shape).to(dtype)
 
 
-def make_weights(shape: ModelShape, seed=0, head="pointer", device="cpu", layers=None, lora=True):
+def make_weights(shape: ModelShape, seed=0, head="pointer", device="cpu", layers=None, lora=True, std=None):
     """Name -> tensor. Matrices bf16 (int4 experts as (codes, scales) pairs under `<name>` and `<name>.scales`),
-    head fp32. `layers` restricts the decoder layers generated (default all)."""
+    head fp32. `layers` restricts the decoder layers generated (default all). `std`: {name suffix: standard deviation}
+    replacing the 0.02 of the matrices whose names end with the suffix (test variants only: e.g. a sharper router)."""
     out = {}
     r = shape.lora_rank if lora else 0
     for name, shp, init in parameter_shapes(shape, head, layers):
@@ -124,7 +125,8 @@ def make_weights(shape: ModelShape, seed=0, head="pointer", device="cpu", layers
             out[name + ".scales"] = scales
             continue
         if init in ("normal", "normal32"):
-            t = _normal(shp, 0.02, seed, name, device)
+            sd = next((v for k, v in (std or {}).items() if name.endswith(k)), 0.02)
+            t = _normal(shp, sd, seed, name, device)
             leaf = name.split(".")[-2] if name.endswith(".weight") else ""
             if r and init == "normal" and leaf in LORA_TARGETS:
                 a = _normal((r, shp[1]), 1.0 / r, seed, name + "#lora_A", device)

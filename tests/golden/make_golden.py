@@ -78,8 +78,8 @@ def shape_of(shape, overrides):
     return shape.with_layers(layers, **overrides)
 
 
-def hf_model(shape, weights):
-    """A transformers text model of `shape` in fp32 holding `weights` (int4 experts dequantised)."""
+def hf_model(shape, weights, dtype=torch.float32):
+    """A transformers text model of `shape` in `dtype` holding `weights` (int4 experts dequantised)."""
     from transformers import Qwen3_5MoeTextConfig, Qwen3_5TextConfig, Qwen3_5MoeTextModel, Qwen3_5TextModel
     common = dict(vocab_size=shape.vocab, hidden_size=shape.hidden, num_hidden_layers=shape.layers,
                   num_attention_heads=shape.heads, num_key_value_heads=shape.kv_heads, head_dim=shape.head_dim,
@@ -97,20 +97,29 @@ def hf_model(shape, weights):
         cfg = Qwen3_5TextConfig(intermediate_size=shape.intermediate, **common)
         cls = Qwen3_5TextModel
     cfg._attn_implementation = "sdpa"
-    torch.manual_seed(0)
-    lm = cls(cfg).float()
-    state = {}
-    for name, t in weights.items():
-        if name.startswith("head.") or name.endswith(".scales"):
-            continue
-        if name + ".scales" in weights:
-            t = synthetic.int4_dequantize(t, weights[name + ".scales"])
-        state[name] = t.float()
-    missing, unexpected = lm.load_state_dict(state, strict=False)
-    missing = [m for m in missing if "rotary" not in m]
-    if missing or unexpected:
-        raise RuntimeError(f"state dict mismatch: missing {missing[:5]} unexpected {unexpected[:5]}")
-    return lm.eval()
+    # built on the meta device and filled tensor by tensor in fp32: no random init of billions of parameters and no
+    # second full-size copy of the weights (the 4B model in fp32 is 16 GB); a bf16 model is then cast as a whole, as
+    # before (buffers included: the rotary inv_freq is rounded to bf16 by that cast)
+    with torch.device("meta"):
+        lm = cls(cfg)
+    lm = lm.to_empty(device="cpu").float()
+    lm.rotary_emb = type(lm.rotary_emb)(config=cfg)  # to_empty leaves the non-persistent inv_freq buffer empty
+    params = dict(lm.named_parameters())
+    filled = set()
+    with torch.no_grad():
+        for name, t in weights.items():
+            if name.startswith("head.") or name.endswith(".scales"):
+                continue
+            if name + ".scales" in weights:
+                t = synthetic.int4_dequantize(t, weights[name + ".scales"])
+            if name not in params:
+                raise RuntimeError(f"state dict mismatch: unexpected {name}")
+            params[name].copy_(t.reshape(params[name].shape))
+            filled.add(name)
+    missing = [n for n in params if n not in filled]
+    if missing:
+        raise RuntimeError(f"state dict mismatch: missing {missing[:5]}")
+    return lm.to(dtype).eval()
 
 
 def reference_logits(shape, weights, mode, packs, dtype=torch.float32):
@@ -118,7 +127,7 @@ def reference_logits(shape, weights, mode, packs, dtype=torch.float32):
     from janus.hybrid import HybridBackbone
     from janus.model import DecisionModel, ModelConfig, PointerHead, ScalarHead
     from janus.packing import Branch as RefBranch, PackedRequest as RefPacked
-    lm = hf_model(shape, weights).to(dtype)
+    lm = hf_model(shape, weights, dtype)
     backbone = HybridBackbone(lm, tokenizer=None, attention="sdpa", state_chunk_tokens=4096)
     model = DecisionModel.__new__(DecisionModel)
     torch.nn.Module.__init__(model)
@@ -178,10 +187,16 @@ def delta_rule_vectors():
     return dict(q=q, k=k, v=v, g=g_, beta=beta, s0=s0, o_chunk=o_c, s_chunk=s_c, o_rec9=o_r, s_rec9=s_r)
 
 
-# The benchmark configurations at full depth. name: (shape, overrides, mode, weight seed, [(builder, kwargs)]).
-# cfg 5 (A3B) keeps its widths and all 256 experts at 4 layers: 40 layers of fp32 experts do not fit host memory.
+# The benchmark configurations at full depth. name: (shape, overrides, mode, weight seed, [(builder, kwargs)]
+# [, weight std overrides]). cfg 5 (A3B) keeps its widths and all 256 experts at 4 layers: 40 layers of fp32 experts
+# do not fit host memory. Its random router is near-uniform, so bf16 rounding flips top-8 choices and moves the
+# readout by ~0.1 in any bf16 path; the "wide router" variant draws the router N(0, 0.2) (top-8 gaps ten times
+# wider) so the MoE numerics are held to the dense models' noise floor instead.
 def _full_cases():
     return {
+        "cfg5_a3b_wide_router_4layers": ("35b-a3b", dict(layers=4), "tree", 51,
+                                         [("a3b_request", dict(seed=510, state_tokens=1024))],
+                                         {"mlp.gate.weight": 0.2}),
         "cfg2_08b_listwise": ("0.8b", {}, "listwise", 20, [("q08b_request", dict(seed=200))]),
         "cfg3_4b_tree": ("4b", {}, "tree", 30, [("q4b_request", dict(seed=300))]),
         "cfg4_08b_stress": ("0.8b", {}, "tree", 40, [("stress_request", dict(seed=400))]),
@@ -215,19 +230,20 @@ def oracle_probs(shape, weights, mode, packs, storage):
 def main_full():
     out = HERE / "readout_full.json"
     manifest = json.loads(out.read_text()) if out.exists() else {}
-    for name, (base, overrides, mode, seed, specs) in _full_cases().items():
+    for name, (base, overrides, mode, seed, specs, *std) in _full_cases().items():
         if name in manifest:
             continue
+        std = std[0] if std else None
         shape = shape_of(SHAPES[base], dict(overrides))
         packs = build_packs(specs)
-        weights = synthetic.make_weights(shape, seed=seed, head="scalar" if mode == "tree" else "pointer")
+        weights = synthetic.make_weights(shape, seed=seed, head="scalar" if mode == "tree" else "pointer", std=std)
         logits = reference_logits(shape, weights, mode, packs)
         probs = [[torch.softmax(z.float(), -1).tolist() for z in per] for per in logits]
         logits16 = reference_logits(shape, weights, mode, packs, torch.bfloat16)
         probs16 = [[torch.softmax(z.float(), -1).tolist() for z in per] for per in logits16]
         dev16 = max(abs(a - b) for pp, qq in zip(probs, probs16) for p, q in zip(pp, qq) for a, b in zip(p, q))
         po16 = oracle_probs(shape, weights, mode, packs, "bf16")
-        manifest[name] = dict(shape=base, overrides=overrides, mode=mode, seed=seed,
+        manifest[name] = dict(shape=base, overrides=overrides, mode=mode, seed=seed, std=std,
                               checksum=synthetic.weight_checksum(weights),
                               requests=[dict(builder=b, kwargs=kw, ids_crc=ids_crc(p), tokens=p.token_count)
                                         for (b, kw), p in zip(specs, packs)],

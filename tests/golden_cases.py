@@ -57,7 +57,7 @@ def full_case_model(case, device="cpu"):
         assert zlib.crc32(p.input_ids[0].numpy().astype("int64").tobytes()) == r["ids_crc"], "request builder drifted"
         packs.append(p)
     weights = synthetic.make_weights(shape, seed=case["seed"], head="scalar" if case["mode"] == "tree" else "pointer",
-                                     device=device)
+                                     device=device, std=case.get("std"))
     got = synthetic.weight_checksum(weights)
     assert abs(got - case["checksum"]) <= 1e-9 * max(1.0, abs(case["checksum"])), "weight generator drifted"
     return shape, weights, case["mode"], packs
