@@ -267,6 +267,63 @@ def run_moe(args):
     }))
 
 
+def run_gemm(args):
+    """The dense projections of the 4B shape at a level-0 pass of `--gemm-tokens` rows: the tcgen05 GEMM
+    (janus_b200_gemm_bf16) against cuBLAS (torch F.linear) on the same operands, each timed with CUDA events over
+    `--steps` launches after `--warmup`; the MLP gate/up also as the SwiGLU epilogue against cuBLAS + silu_mul."""
+    import torch.nn.functional as F
+    from janus_b200 import ops
+    from janus_b200.config import SHAPES
+    device = torch.device("cuda", 0)
+    s = SHAPES["4b"]
+    T, H = args.gemm_tokens, s.hidden
+    g = torch.Generator(device=device).manual_seed(0)
+    x = {k: torch.randn(T, k, generator=g, device=device).to(torch.bfloat16) for k in (H, s.value_dim, s.intermediate)}
+    shapes = {"deltanet_proj": (s.conv_dim + s.value_dim + 2 * s.lin_v_heads, H),
+              "attn_qkv": (2 * s.heads * s.head_dim + 2 * s.kv_heads * s.head_dim, H),
+              "out_proj": (H, s.value_dim), "gate_up": (2 * s.intermediate, H), "down": (H, s.intermediate)}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        ms = []
+        for _ in range(args.steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ms.append(a.elapsed_time(b))
+        return statistics.median(ms)
+
+    pk, kind = peaks()
+    rows = {}
+    for name, (N, K) in shapes.items():
+        w = (torch.randn(N, K, generator=g, device=device) * 0.02).to(torch.bfloat16)
+        a = x[K]
+        flops = 2.0 * T * N * K
+        t_ours = timed(lambda: ops.gemm_bf16(a, w))
+        t_cublas = timed(lambda: F.linear(a, w))
+        rows[name] = {"N": N, "K": K, "ms_tcgen05": t_ours, "ms_cublas": t_cublas,
+                      "tflops_tcgen05": flops / t_ours / 1e9, "tflops_cublas": flops / t_cublas / 1e9}
+        if name == "gate_up":
+            wi = ops.swiglu_weight(w[:s.intermediate], w[s.intermediate:])
+            t_fused = timed(lambda: ops.gemm_bf16(a, wi, swiglu=True))
+            t_sep = timed(lambda: ops.silu_mul(F.linear(a, w)))
+            rows["gate_up+swiglu"] = {"ms_tcgen05_fused": t_fused, "ms_cublas_plus_silu_mul": t_sep,
+                                      "tflops_tcgen05_fused": flops / t_fused / 1e9}
+        del w
+    total_ours = sum(r["ms_tcgen05"] for n, r in rows.items() if "ms_tcgen05" in r)
+    total_cublas = sum(r["ms_cublas"] for n, r in rows.items() if "ms_cublas" in r)
+    print(json.dumps({"metric": "dense projection GEMMs of one 4B layer group at a level-0 pass", "unit": "ms",
+                      "tokens": T, "steps": args.steps, "warmup": args.warmup, "per_gemm": rows,
+                      "ms_tcgen05": total_ours, "ms_cublas": total_cublas,
+                      "peak": {"bf16_tflops": pk["bf16_tflops"], "kind": kind},
+                      "l2": "256 MiB written between launches"}))
+
+
 def run_prefix(args):
     """Repeated states (a prefix-cache hit for every request): the state level of the 16 requests is encoded once
     into snapshots; each timed step then runs the branch levels only, from the snapshots. A side line for the
@@ -319,7 +376,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--latency-requests", type=int, default=8, help="single requests timed one at a time")
     ap.add_argument("--layers", type=int, default=0, help="debug: fewer layers (not a valid bench number)")
-    ap.add_argument("--op", default="readout", choices=["readout", "moe", "prefix"])
+    ap.add_argument("--op", default="readout", choices=["readout", "moe", "prefix", "gemm"])
+    ap.add_argument("--gemm-tokens", type=int, default=131072)
     ap.add_argument("--moe-tokens", type=int, default=131072)
     args = ap.parse_args()
     if args.warmup < 3:
@@ -329,6 +387,9 @@ def main():
         return
     if args.op == "prefix":
         run_prefix(args)
+        return
+    if args.op == "gemm":
+        run_gemm(args)
         return
     if args.impl == "reference":
         run_reference(args)

@@ -171,6 +171,17 @@ int janus_b200_head_pointer(const float* x, int64_t H, const int32_t* option_row
                             const float* ln_w, const float* ln_b, float ln_eps, const float* wq, const float* wk,
                             int64_t R, float* workspace, size_t workspace_bytes, float* logits, void* stream);
 
+/* Dense bf16 GEMM on the tcgen05 tensor cores: out[M, n] = sum_k a[M, k] w[n, k] (y = x W^T, torch F.linear), fp32
+ * accumulation, one rounding to bf16. a [M, K] (row stride lda), w [N, K] (row stride ldw), both bf16, 16-byte
+ * aligned, strides multiples of 8 elements; N a multiple of 16, K of 8. epilogue 0: out [M, N] (row stride ldo);
+ * epilogue 1 (SwiGLU): w's rows come in 256-row blocks of 128 gate rows then the 128 matching up rows (N a multiple
+ * of 256), out [M, N/2] = silu(gate) * up of the fp32 accumulators. status: optional device int32 word set to 1 if a
+ * bounded device-side wait ran out.
+ * Replaces the F.linear of the merged projections (`_merge_projections`, janus/hybrid.py:1108-1133) and, with
+ * epilogue 1, the MLP's gate/up GEMM plus `_silu_mul` (janus/hybrid.py:263, 1093-1096). */
+int janus_b200_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, int64_t M, int64_t N, int64_t K,
+                         int32_t epilogue, void* out, int64_t ldo, int32_t* status, void* stream);
+
 /* MoE routing and tile plan, sync-free: softmax over fp32 router logits [S, E] (E <= 512), top-k (k <= 16),
  * renormalised weights (topk_idx int32 / topk_w fp32 [S, k]); assignments a = t*k + j sorted by expert into
  * sorted_ids [max_tiles * tile_rows] (-1 pads each expert to a multiple of tile_rows, which must be 128),

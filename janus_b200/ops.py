@@ -289,6 +289,35 @@ def head_pointer(x, option_rows, option_question, decision_rows, final_w, rms_ep
     return logits
 
 
+@_instrument("gemm_bf16", 1)
+def gemm_bf16(a, w, swiglu=False, out=None, status=None):
+    """a bf16 [M, K] (unit column stride), w bf16 [N, K] -> a w^T bf16 [M, N] on the tcgen05 GEMM; swiglu: w in
+    the interleaved gate/up order of `swiglu_weight`, result silu(gate) * up [M, N / 2]."""
+    _need(a, BF16, "a", contiguous=False)
+    _need(w, BF16, "w", contiguous=False)
+    if a.stride(1) != 1 or w.stride(1) != 1:
+        raise ValueError("gemm_bf16: a and w need unit column stride")
+    M, K = a.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError(f"gemm_bf16: a has K = {K}, w has {w.shape[1]}")
+    n_out = N // 2 if swiglu else N
+    out = torch.empty(M, n_out, dtype=BF16, device=a.device) if out is None else out
+    _need(out, BF16, "out", contiguous=False)
+    _lib.check(_lib.load().janus_b200_gemm_bf16(_ptr(a), a.stride(0), _ptr(w), w.stride(0), M, N, K, int(bool(swiglu)),
+                                                _ptr(out), out.stride(0), _ptr(status), _stream(a)), "gemm_bf16")
+    return out
+
+
+def swiglu_weight(gate, up):
+    """The gate/up weight in the order the SwiGLU epilogue reads: 256-row blocks of 128 gate rows followed by the
+    128 matching up rows. gate, up [I, H] with I a multiple of 128 -> [2I, H]."""
+    I, H = gate.shape
+    if up.shape != gate.shape or I % 128:
+        raise ValueError("swiglu_weight: gate and up [I, H] with I a multiple of 128")
+    return torch.stack([gate.reshape(I // 128, 128, H), up.reshape(I // 128, 128, H)], 1).reshape(2 * I, H).contiguous()
+
+
 MOE_TILE = 128  # rows per tile of the routing plan = the M of the grouped GEMMs' tensor-core tiles
 
 

@@ -239,6 +239,27 @@ def int4_dequantize(packed, scales, group=128):
     return w.reshape(codes.shape).to(torch.bfloat16)
 
 
+def e2m1_decode(codes):
+    """4-bit e2m1 codes (bit 3 sign, bits 2-1 exponent, bit 0 mantissa) to fp32: 0, 0.5, 1, 1.5, 2, 3, 4, 6 and their
+    negatives (janus/hybrid.py:400-405)."""
+    m = (codes & 1).float()
+    e = ((codes >> 1) & 3).float()
+    mag = torch.where(e == 0, 0.5 * m, (1.0 + 0.5 * m) * torch.exp2(e - 1.0))
+    return torch.where((codes & 8) != 0, -mag, mag)
+
+
+def nvfp4_dequantize(packed, block_scales, global_scale, block=16):
+    """NVFP4 expert weights (the reference's own MoE format, janus/hybrid.py:418-425): e2m1 codes two per byte (the
+    even element in the low nibble), one e4m3 scale per `block` consecutive inputs, an fp32 global scale per row
+    ([..., rows] or broadcastable). The value is e2m1 * (scale * global) in fp32 (the scale product first, as the
+    reference computes it), rounded once to bf16."""
+    codes = torch.stack([packed & 15, packed >> 4], dim=-1).flatten(-2)
+    s = block_scales.float() * global_scale.float()[..., None]
+    K = codes.shape[-1]
+    v = e2m1_decode(codes).view(*codes.shape[:-1], K // block, block) * s[..., None]
+    return v.reshape(codes.shape).to(torch.bfloat16)
+
+
 def tree_levels(segment_ids, parents):
     """Segments grouped by depth (janus/hybrid.py:128-153): [(segment, start, end)] per level."""
     seg = segment_ids.tolist()
@@ -281,9 +302,11 @@ class Oracle:
         self.rnd = bf16_round if storage == "bf16" else _keep
         w = {}
         for name, t in weights.items():
-            if name.endswith(".scales"):
+            if name.endswith(".scales") or name.endswith(".global"):
                 continue
-            if name + ".scales" in weights:
+            if name + ".global" in weights:  # NVFP4 experts: codes, e4m3 block scales, fp32 global per row
+                t = nvfp4_dequantize(t, weights[name + ".scales"], weights[name + ".global"])
+            elif name + ".scales" in weights:
                 t = int4_dequantize(t, weights[name + ".scales"])
             w[name] = t.float()
         self.w = w
