@@ -217,18 +217,29 @@ def cpu_reference_rate(steps=1, warmup=0, full_request=False):
 
 
 def run_moe(args):
-    """The MoE block of the A3B shape on one GPU: route -> gate/up GEMM -> down GEMM -> combine."""
+    """The MoE block of the A3B shape on one GPU: route -> gate/up GEMM -> down GEMM -> combine, experts in the
+    BASELINE's int4 group-128 format or (`--moe-format nvfp4`) the reference's NVFP4. With `--vs-reference` and the
+    reference installed under baseline/_ref, the reference's own Triton kernels (`fused_moe`,
+    janus/moe_w4a16.py:122-140, NVFP4 only) run on the same routing and weights and are timed the same way, and the
+    two outputs are compared."""
     from janus_b200 import ops
-    from janus_b200.synthetic import int4_quantized
+    from janus_b200.synthetic import int4_quantized, nvfp4_quantized
     device = torch.device("cuda", 0)
     S, E, k, H, I = args.moe_tokens, 256, 8, 2048, 512
+    fp4 = args.moe_format == "nvfp4"
     g = torch.Generator(device=device).manual_seed(0)
     x = (torch.randn(S, H, generator=g, device=device) * 0.5).to(torch.bfloat16)
     logits = torch.randn(S, E, generator=g, device=device)
     shared = torch.randn(S, H, generator=g, device=device).to(torch.bfloat16)
     sgate = torch.randn(S, generator=g, device=device)
-    gu_codes, gu_scales = int4_quantized((E, 2 * I, H), 11, "experts", device)
-    dn_codes, dn_scales = int4_quantized((E, H, I), 12, "experts", device)
+    if fp4:
+        gu = nvfp4_quantized((E, 2 * I, H), 11, "experts", device, halves=True)
+        dn = nvfp4_quantized((E, H, I), 12, "experts", device)
+        gemm = lambda a, w, plan, gated, **kw: ops.moe_grouped_nvfp4(a, *w, plan, gated, k, **kw)
+    else:
+        gu = int4_quantized((E, 2 * I, H), 11, "experts", device)
+        dn = int4_quantized((E, H, I), 12, "experts", device)
+        gemm = lambda a, w, plan, gated, **kw: ops.moe_grouped_w4a16(a, *w, plan, gated, k, **kw)
     status = torch.zeros(1, dtype=torch.int32, device=device)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)  # > L2 between steps
     names = ["moe_route", "gemm_gate_up", "gemm_down", "moe_combine"]
@@ -239,9 +250,9 @@ def run_moe(args):
         ev[0].record()
         plan = ops.moe_route(logits, k)
         ev[1].record()
-        h = ops.moe_grouped_w4a16(x, gu_codes, gu_scales, plan, True, k, status=status)
+        h = gemm(x, gu, plan, True, status=status)
         ev[2].record()
-        y2 = ops.moe_grouped_w4a16(h, dn_codes, dn_scales, plan, False, k, topk_w=plan[1], status=status)
+        y2 = gemm(h, dn, plan, False, topk_w=plan[1], status=status)
         ev[3].record()
         ops.moe_combine(y2, k, shared, sgate)
         ev[4].record()
@@ -257,14 +268,66 @@ def run_moe(args):
     pk, kind = peaks()
     gemm_ms = ms["gemm_gate_up"] + ms["gemm_down"]
     achieved = (flops["gemm_gate_up"] + flops["gemm_down"]) / (gemm_ms * 1e-3) / 1e12
-    print(json.dumps({
+    line = {
         "metric": "MoE W4A16 grouped GEMMs, A3B shape (hidden 2048, 256 experts x FFN 512, top-8)",
         "value": achieved, "unit": "TFLOP/s", "steps": args.steps, "warmup": args.warmup,
-        "config": {"tokens": S, "assignments": A, "experts": E, "top_k": k, "l2": "256 MiB written between steps"},
+        "config": {"tokens": S, "assignments": A, "experts": E, "top_k": k, "format": args.moe_format,
+                   "l2": "256 MiB written between steps"},
         "ms": ms, "tflops": {n: flops[n] / (ms[n] * 1e-3) / 1e12 for n in flops},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": achieved / pk["bf16_tflops"], "peak_kind": kind + " (burst bf16)"},
-    }))
+    }
+    if args.vs_reference:
+        line["reference_fused_moe"] = reference_fused_moe(args, x, plan, gu, dn, gemm, k, flush) if fp4 else \
+            "the reference's fused kernel reads NVFP4 only (--moe-format nvfp4)"
+    print(json.dumps(line))
+
+
+def reference_fused_moe(args, x, plan, gu, dn, gemm, k, flush):
+    """The reference's Triton NVFP4 MoE (`fused_moe` from baseline/_ref, its plan `align` included) against this
+    library's plan + two grouped GEMMs + per-token sum, on the same routing (ids and weights) and weights: device
+    milliseconds of each and the largest difference of their outputs."""
+    ref_root = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "janus")):
+        return {"unavailable": "the reference is not installed under baseline/_ref"}
+    sys.path.insert(0, ref_root)
+    try:
+        from janus.moe_w4a16 import fused_moe
+    except Exception as e:  # triton or the package missing on this box
+        return {"unavailable": f"import failed: {type(e).__name__}: {e}"}
+    from janus_b200 import ops
+    idx, w = plan[0], plan[1]
+    E = gu[0].shape[0]
+    ref_args = (gu[0], gu[1], gu[2][..., None], dn[0], dn[1], dn[2][..., None])
+
+    def ours():
+        p = ops.moe_plan(idx, E)
+        hh = gemm(x, gu, p, True)
+        y2 = gemm(hh, dn, p, False, topk_w=w.reshape(-1))
+        return ops.moe_combine(y2, k, None, None)
+
+    def theirs():
+        return fused_moe(x, idx.long(), w, *ref_args)
+
+    out = {}
+    for name, fn in (("janus_b200", ours), ("reference_triton", theirs)):
+        for _ in range(args.warmup):
+            fn()
+        ts = []
+        for _ in range(args.steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            res = fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        out[name] = {"ms": statistics.median(ts)}
+        out[name + "_result"] = res
+    d = (out.pop("janus_b200_result").float() - out.pop("reference_triton_result").float()).abs()
+    out["max_abs_diff"] = float(d.max())
+    out["speedup"] = out["reference_triton"]["ms"] / out["janus_b200"]["ms"]
+    return out
 
 
 def run_gemm(args):
@@ -379,6 +442,8 @@ def main():
     ap.add_argument("--op", default="readout", choices=["readout", "moe", "prefix", "gemm"])
     ap.add_argument("--gemm-tokens", type=int, default=131072)
     ap.add_argument("--moe-tokens", type=int, default=131072)
+    ap.add_argument("--moe-format", default="int4", choices=["int4", "nvfp4"])
+    ap.add_argument("--vs-reference", action="store_true", help="--op moe: also time the reference's Triton MoE")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -237,6 +237,19 @@ int janus_b200_moe_reduce_slots(const void* y, int64_t k, const int32_t* slot_ex
 int janus_b200_moe_combine_ep(const float* partials, const int32_t* row_index, int64_t W, const void* shared,
                               const float* shared_gate_logit, int64_t S, int64_t H, void* out, void* stream);
 
+/* The grouped GEMMs of janus_b200_moe_grouped_w4a16 on the reference's own NVFP4 expert format: codes uint8
+ * [E, rows, K/2] (two e2m1 codes per byte, even element in the low nibble), block_scales e4m3 bytes [E, rows, K/16]
+ * (one per 16 inputs), global_scales fp32 [E, rows]; the value fed to the tensor cores is e2m1 * (scale * global)
+ * formed in fp32 and rounded once to bf16, the reference's dequantised weight bit for bit. Everything else (plan,
+ * gated / down semantics, layouts, status) as janus_b200_moe_grouped_w4a16.
+ * Replaces `_w4a16_moe_kernel` / `fused_moe` (janus/moe_w4a16.py:37-140) with its NVFP4 codec
+ * (janus/hybrid.py:400-425). */
+int janus_b200_moe_grouped_nvfp4(const void* x, int64_t ldx, const uint8_t* codes, const uint8_t* block_scales,
+                                 const float* global_scales, int64_t E, int64_t N, int64_t K, int32_t gated,
+                                 const int32_t* sorted_ids, const int32_t* tile_expert, const int32_t* n_tiles,
+                                 int64_t max_tiles, int64_t topk, const float* topk_w, void* out, int64_t ldo,
+                                 int32_t* status, void* stream);
+
 /* The PointerHead readout of janus_b200_head_pointer for callers that cannot allocate device memory: it takes no
  * workspace and allocates nothing; the projected rows go to a static 1 MiB device array inside this library
  * (kept by every GPU that loads the library until the process exits). Limit: (n + Q) * R <= 262144 floats (2048

@@ -46,6 +46,9 @@ SIGNATURES = {
                                      c_void_p, c_void_p],
     "janus_b200_gemm_bf16": [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int32, c_void_p,
                              c_int64, c_void_p, c_void_p],
+    "janus_b200_moe_grouped_nvfp4": [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                     c_int32, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
+                                     c_int64, c_void_p, c_void_p],
     "janus_b200_moe_combine": [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p],
     "janus_b200_moe_plan": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
                             c_size_t, c_void_p],

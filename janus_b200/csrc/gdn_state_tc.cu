@@ -202,12 +202,14 @@ __global__ void __launch_bounds__(NT, 1) gdn_state_tc_kernel(const __grid_consta
         ok = wait_bar(&bars.vb_ready, i & 1, p.err);
         if (!ok) break;
         fence_after();
+        const uint32_t keep = s_dl != 0.f ? 1u : 0u;  // 0: the decayed state is zero, the update overwrites ST
 #pragma unroll
         for (int s = 0; s < 4; ++s)  // O2T = V'^T QK^T, 16 tokens j per step
           mma_ts(tm + cVT(st), tm + cVB + s * 8, sdesc(stage + sQK + s * 32, 16, 1024), ID_N64, s > 0);
 #pragma unroll
         for (int s = 0; s < 4; ++s)  // ST += (V' f_k)^T K, 16 tokens per step; K rows as the MN-major operand
-          mma_ts(tm + cST, tm + cVD + s * 8, sdesc(stage + sK + s * 16 * 128, kTile / 2, 1024), ID_N128, 1u);
+          mma_ts(tm + cST, tm + cVD + s * 8, sdesc(stage + sK + s * 16 * 128, kTile / 2, 1024), ID_N128,
+                 s > 0 ? 1u : keep);
         commit(&bars.st_done[st]);
         commit(&bars.empty[st]);
       }
@@ -323,9 +325,10 @@ __global__ void __launch_bounds__(NT, 1) gdn_state_tc_kernel(const __grid_consta
         tst32(la + cVB, vb);
         tst32(la + cVD, vd);
       }
-      // the state decays by e^(G_last) before the update accumulates onto it
-      {
-        const float dl = s_dl;
+      // the state decays by e^(G_last) before the update accumulates onto it; a decay that underflowed to 0 (a
+      // fast-forgetting head: G_last < -103) leaves nothing of the state, and the update MMA overwrites it instead
+      const float dl = s_dl;
+      if (dl != 0.f) {
 #pragma unroll 1
         for (int k0 = 0; k0 < DH; k0 += 64) {
           float f[64];

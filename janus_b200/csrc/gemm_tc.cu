@@ -8,8 +8,10 @@
 //           silu(gate) * up from the fp32 accumulators, rounded once: the MLP's gate/up GEMM and its SwiGLU
 //           (`_silu_mul`, janus/hybrid.py:263) in one pass, the 2N-wide intermediate never written.
 //
-// Tiles of 128 rows x 256 columns, one M=128, N=256 MMA per 16-deep k step, k-blocks of 64 (one 128-byte swizzle
-// atom of bf16). A (16 KB) and W (32 KB) of a k-block arrive by TMA (no multicast) into a 4-stage ring. Persistent
+// Tiles of 128 rows x 256 columns, one M=128, N=256 MMA per 16-deep k step. A stage holds a 128-deep k-block (two
+// 128-byte swizzle atoms of bf16) of A (32 KB) and W (64 KB), loaded by TMA (no multicast) into a 2-stage ring: the
+// MMA thread waits once per 8 MMAs (a wait costs the tensor pipe a few hundred cycles even when the phase is
+// already complete, so waiting once per 64-deep block left it idle a quarter of the time). Persistent
 // CTAs, one per SM, walk the (m-tile, n-block) items with the n-block fastest: the CTAs of a wave share one or two
 // A tiles and the whole weight matrix stays resident in L2 across waves, so A and W are read from HBM about once.
 // The fp32 accumulator is double-buffered in TMEM (2 x 256 columns), so an item's epilogue overlaps the next item's
@@ -23,11 +25,14 @@ namespace jb {
 namespace gtc {
 using namespace tcx;
 
-constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int S = 4;     // stages
+constexpr int BM = 128, BN = 256, BK = 64;  // BK: one swizzle atom
+constexpr int AT = 2;    // atoms per stage: a stage is a 128-deep k-block
+constexpr int S = 2;     // stages
 constexpr int NT = 256;  // 8 warps
-constexpr uint32_t kA = BM * BK * 2;  // 16 KB
-constexpr uint32_t kB = BN * BK * 2;  // 32 KB
+constexpr uint32_t kAtomA = BM * BK * 2;  // 16 KB
+constexpr uint32_t kAtomB = BN * BK * 2;  // 32 KB
+constexpr uint32_t kA = AT * kAtomA;
+constexpr uint32_t kB = AT * kAtomB;
 constexpr uint32_t kStage = kA + kB;
 constexpr uint32_t kOut = S * kStage;              // epilogue staging: 4 warps x 32 rows x 64 bytes
 constexpr uint32_t kSmem = kOut + 4 * 32 * 64;
@@ -52,7 +57,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_tc_kernel(const __grid_consta
   __shared__ uint32_t tmem_base;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x;
-  const int nkb = (p.K + BK - 1) / BK;
+  const int nkb = (p.K + AT * BK - 1) / (AT * BK);  // stages per item (the last one zero-filled past K)
 
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s32(&tmem_base)),
@@ -88,8 +93,11 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_tc_kernel(const __grid_consta
           if (q >= S) ok = wait_bar(&bars.empty[s], ((q / S) - 1) & 1, p.err);
           if (!ok) break;
           bar_expect_tx(&bars.full[s], kStage);
-          tma_load2(sbase + s * kStage, &p.amap, kb * BK, m0, &bars.full[s]);
-          tma_load2(sbase + s * kStage + kA, &p.bmap, kb * BK, n0, &bars.full[s]);
+#pragma unroll
+          for (int t = 0; t < AT; ++t) {
+            tma_load2(sbase + s * kStage + t * kAtomA, &p.amap, (kb * AT + t) * BK, m0, &bars.full[s]);
+            tma_load2(sbase + s * kStage + kA + t * kAtomB, &p.bmap, (kb * AT + t) * BK, n0, &bars.full[s]);
+          }
           issued = q + 1;
         }
       }
@@ -116,8 +124,11 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_tc_kernel(const __grid_consta
           fence_after();
           const uint32_t a = sbase + s * kStage, b = a + kA;
 #pragma unroll
-          for (int ks = 0; ks < BK / 16; ++ks)
-            mma(acc, sdesc(a + ks * 32, 16, 1024), sdesc(b + ks * 32, 16, 1024), ID, (kb | ks) != 0);
+          for (int ks = 0; ks < AT * BK / 16; ++ks) {
+            const uint32_t off = (ks / (BK / 16)), in = (ks % (BK / 16)) * 32;
+            mma(acc, sdesc(a + off * kAtomA + in, 16, 1024), sdesc(b + off * kAtomB + in, 16, 1024), ID,
+                (kb | ks) != 0);
+          }
           commit(&bars.empty[s]);
         }
         if (ok) commit(&bars.acc_full[ab]);

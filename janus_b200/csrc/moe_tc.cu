@@ -4,10 +4,12 @@
 //   GEMM 1 (gated):  h[sorted row] = silu(x[token] Wg^T) * (x[token] Wu^T)   B rows: 128 gate + 128 up rows
 //   GEMM 2 (down):   y[assignment] = w_assignment * (h[sorted row] Wd^T)       B rows: 128 or 256 output rows
 //
-// Weights stay int4 in HBM (two codes per byte, k = 2j in the low nibble, one bf16 scale per 128 inputs); the B
-// operand is decoded on the fly: TMA brings the packed codes of a 64-deep k-block into a ring, four converter
-// warps turn them into bf16 in registers (code * scale, rounded once to bf16: the value the reference's
-// dequantise path feeds its GEMM) and write the 128B-swizzled K-major tile the MMA reads. The activation rows are
+// Weights stay 4-bit in HBM, two codes per byte (k = 2j in the low nibble), in one of two formats: int4 with one bf16
+// scale per 128 inputs (code * scale), or the reference's NVFP4 (e2m1 codes, one e4m3 scale per 16 inputs and an
+// fp32 global scale per weight row: e2m1 * (scale * global), janus/hybrid.py:400-425). The B operand is decoded on
+// the fly: TMA brings the packed codes of a 64-deep k-block into a ring, converter warps turn them into bf16 in
+// registers (the exact fp32 value rounded once to bf16: the value the reference's dequantise path feeds its GEMM)
+// and write the 128B-swizzled K-major tile the MMA reads. The activation rows are
 // gathered with cp.async (GEMM 1 reads the token of each assignment; GEMM 2 the sorted rows), and one thread issues
 // M=128 MMAs into an fp32 accumulator in TMEM, so decode, gather and the tensor core overlap across a 3-stage ring.
 //
@@ -17,6 +19,9 @@
 // in flight at once), 12-15 epilogue (warp w reads TMEM lanes 32 (w % 4) .. +31). Every hand-off is an mbarrier
 // with a bounded wait: a wait that runs out sets the status word and the CTA winds down (loads in flight are
 // waited for, MMAs drained, TMEM released).
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+
 #include "tcgen05.cuh"
 
 namespace jb {
@@ -46,7 +51,9 @@ struct Params {
   CUtensorMap cmap;  // codes [E * NW rows][K / 2 bytes], boxes of 128 rows x 32 bytes
   const __nv_bfloat16* A;
   int64_t lda;
-  const __nv_bfloat16* scales;  // [E * NW][K / 128]
+  const __nv_bfloat16* scales;  // int4: [E * NW][K / 128]
+  const uint8_t* bscales;       // NVFP4: e4m3 [E * NW][K / 16]
+  const float* gscales;         // NVFP4: fp32 [E * NW]
   const int32_t* sorted_ids;
   const int32_t* tile_expert;
   const int32_t* n_tiles;
@@ -80,6 +87,29 @@ __device__ __forceinline__ uint4 decode8(uint32_t x, __nv_bfloat162 s2) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// 8 e2m1 codes (k = 0..7 of a 32-bit word, k even in the low nibble) -> 8 bf16 of e2m1 * s, s the fp32 block scale
+// times the global scale passed in as s * 2^14. The code's bits e1 e0 m placed as an fp16 exponent and top mantissa
+// bit give e2m1 * 2^-14 exactly (code 1, 0.5, as a denormal); times s * 2^14 that is the fp32 product e2m1 * s of the
+// reference, rounded once to bf16.
+__device__ __forceinline__ uint4 decode8_fp4(uint32_t x, float s14) {
+  const uint32_t t = x >> 4;
+  uint32_t w[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint32_t n = __byte_perm(x, t, 0x0400u | (uint32_t)p | ((uint32_t)p << 8)) & 0x000F000Fu;
+    const uint32_t hb = ((n & 0x00070007u) << 9) | ((n & 0x00080008u) << 12);
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hb));
+    w[p] = pack_bf16(f.x * s14, f.y * s14);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// block scale (e4m3) times the row's global scale, in fp32 as the reference forms it, times 2^14 (exact)
+__device__ __forceinline__ float fp4_scale14(uint8_t e4m3, float global) {
+  const __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)e4m3, __NV_E4M3);
+  return (__half2float(*reinterpret_cast<const __half*>(&h)) * global) * 16384.f;
+}
+
 __device__ __forceinline__ uint4 lds128(uint32_t a) {
   uint4 v;
   asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
@@ -95,7 +125,7 @@ __device__ __forceinline__ void cpa16(uint32_t dst, const void* src, bool ok) {
 // BN = MMA width: 256 for the gated GEMM (128 output columns: 128 gate + 128 up rows of B), 128 or 256 otherwise.
 // Persistent: CTA b takes the work items (tile, column block) b, b + grid, ...; the accumulator is double-buffered
 // in TMEM so the epilogue of one item overlaps the main loop of the next.
-template <bool GATED, int BN>
+template <bool GATED, int BN, bool FP4>
 __global__ void __launch_bounds__(NT, 1) moe_w4a16_tc_kernel(const __grid_constant__ Params p) {
   using L = Layout<BN>;
   extern __shared__ unsigned char raw[];
@@ -248,6 +278,7 @@ __global__ void __launch_bounds__(NT, 1) moe_w4a16_tc_kernel(const __grid_consta
     constexpr int U = BN / 64;
     const int grp = (warp - 4) >> 2, ct = ((warp - 4) & 3) * 32 + lane, hf = ct & 1, rr0 = ct >> 1;
     const int gk = p.K / GROUP;
+    const int fk = p.K / 16;  // NVFP4 block scales per row
     // 32-bit shared addresses: the codes of row rr0 (+ 64 j rows), and row rr0 of the B stage: row r of a 128B-swizzled
     // K-major tile starts at r * 128, its 16-byte unit u sits at (u ^ (r & 7)) * 16; r & 7 is the same for every j
     const uint32_t code0 = sbase + L::code(0) + rr0 * 32 + hf * 16;
@@ -257,34 +288,61 @@ __global__ void __launch_bounds__(NT, 1) moe_w4a16_tc_kernel(const __grid_consta
     for (int w = 0; w < 4; ++w) xo[w] = (uint32_t)(((hf * 4 + w) ^ (rr0 & 7)) << 4);
     bool ok = true;
     int q = 0;
-    const __nv_bfloat16* sp[U];  // this thread's rows' scales for the current item
-    __nv_bfloat16 s_nxt[U];      // the scales of the next k-block this group decodes
-    {
-      const int it = blockIdx.x, e = p.tile_expert[tile_of(it)], n0 = n0_of(it);
+    // int4: this thread's rows' bf16 scales; NVFP4: their e4m3 block scales (the two blocks of this thread's half of
+    // a k-block are one 16-bit load) and fp32 global scales
+    const __nv_bfloat16* sp[U];
+    const uint8_t* bp[U];
+    float gs[U];
+    __nv_bfloat16 s_nxt[U];  // int4: the scales of the next k-block this group decodes
+    uint16_t b_nxt[U];       // NVFP4: the two block scales of the next k-block
+    auto rows_of = [&](int it) {
+      const int e = p.tile_expert[tile_of(it)], n0 = n0_of(it);
 #pragma unroll
       for (int j = 0; j < U; ++j) {
-        sp[j] = p.scales + (int64_t)wrow(e, n0, rr0 + 64 * j) * gk;
-        s_nxt[j] = sp[j][0];  // the first k-block of either group is in scale group 0
+        const int64_t wr = wrow(e, n0, rr0 + 64 * j);
+        if (FP4) {
+          bp[j] = p.bscales + wr * fk + hf * 2;
+          gs[j] = p.gscales[wr];
+        } else {
+          sp[j] = p.scales + wr * gk;
+        }
       }
-    }
+    };
+    auto fetch = [&](int kb) {  // the scales of k-block kb of the current rows
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        if (FP4)
+          b_nxt[j] = *reinterpret_cast<const uint16_t*>(bp[j] + kb * (BK / 16));
+        else
+          s_nxt[j] = sp[j][kb / (GROUP / BK)];
+      }
+    };
+    rows_of(blockIdx.x);
+    float g_cur[U];
+#pragma unroll
+    for (int j = 0; j < U; ++j) g_cur[j] = FP4 ? gs[j] : 0.f;
+    fetch(grp);
     for (int it = blockIdx.x; it < n_items && ok; it += G) {
       const int nit = it + G;
-      const int e_nxt = nit < n_items ? p.tile_expert[tile_of(nit)] : 0;
       for (int kb = grp; kb < nkb; kb += 2) {
         const int qq = q + kb;
         __nv_bfloat16 s_cur[U];
+        uint16_t b_cur[U];
 #pragma unroll
-        for (int j = 0; j < U; ++j) s_cur[j] = s_nxt[j];
+        for (int j = 0; j < U; ++j) {
+          s_cur[j] = s_nxt[j];
+          b_cur[j] = b_nxt[j];
+        }
+        float g_use[U];
+#pragma unroll
+        for (int j = 0; j < U; ++j) g_use[j] = g_cur[j];
         if (kb + 2 < nkb) {  // prefetch the scales of this group's next k-block, in this item or the next
-#pragma unroll
-          for (int j = 0; j < U; ++j) s_nxt[j] = sp[j][(kb + 2) / (GROUP / BK)];
+          fetch(kb + 2);
         } else if (nit < n_items) {
-          const int n0 = n0_of(nit);
+          rows_of(nit);
+          fetch(grp);
 #pragma unroll
-          for (int j = 0; j < U; ++j) {
-            sp[j] = p.scales + (int64_t)wrow(e_nxt, n0, rr0 + 64 * j) * gk;
-            s_nxt[j] = sp[j][0];
-          }
+          for (int j = 0; j < U; ++j) g_cur[j] = FP4 ? gs[j] : 0.f;
         }
         const int c = qq % C, s = qq % S;
         ok = wait_bar(&bars.cfull[c], (qq / C) & 1, p.err);
@@ -296,11 +354,20 @@ __global__ void __launch_bounds__(NT, 1) moe_w4a16_tc_kernel(const __grid_consta
 #pragma unroll
         for (int j = 0; j < U; ++j) {
           const uint4 cw = lds128(code0 + c * L::kCode + j * (64 * 32));
-          const __nv_bfloat162 s2 = __halves2bfloat162(s_cur[j], s_cur[j]);
-          dv[j][0] = decode8(cw.x, s2);
-          dv[j][1] = decode8(cw.y, s2);
-          dv[j][2] = decode8(cw.z, s2);
-          dv[j][3] = decode8(cw.w, s2);
+          if (FP4) {  // words 0-1: the first 16-element block of this half, words 2-3 the second
+            const float s0 = fp4_scale14((uint8_t)(b_cur[j] & 0xff), g_use[j]);
+            const float s1 = fp4_scale14((uint8_t)(b_cur[j] >> 8), g_use[j]);
+            dv[j][0] = decode8_fp4(cw.x, s0);
+            dv[j][1] = decode8_fp4(cw.y, s0);
+            dv[j][2] = decode8_fp4(cw.z, s1);
+            dv[j][3] = decode8_fp4(cw.w, s1);
+          } else {
+            const __nv_bfloat162 s2 = __halves2bfloat162(s_cur[j], s_cur[j]);
+            dv[j][0] = decode8(cw.x, s2);
+            dv[j][1] = decode8(cw.y, s2);
+            dv[j][2] = decode8(cw.z, s2);
+            dv[j][3] = decode8(cw.w, s2);
+          }
         }
         if (qq >= S) ok = wait_bar(&bars.empty[s], ((qq / S) - 1) & 1, p.err);
         if (!ok) break;
@@ -427,10 +494,10 @@ int code_map(CUtensorMap* m, const void* codes, uint64_t rows, uint64_t K) {
   return JANUS_OK;
 }
 
-template <bool GATED, int BN>
+template <bool GATED, int BN, bool FP4>
 int launch(const mtc::Params& p, int64_t max_tiles, cudaStream_t s) {
   const size_t smem = mtc::Layout<BN>::bytes + 1024;
-  auto kern = mtc::moe_w4a16_tc_kernel<GATED, BN>;
+  auto kern = mtc::moe_w4a16_tc_kernel<GATED, BN, FP4>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) {
     set_error("moe_grouped_w4a16: smem attribute: %s", cudaGetErrorString(e));
@@ -449,23 +516,25 @@ int launch(const mtc::Params& p, int64_t max_tiles, cudaStream_t s) {
 
 }  // namespace
 
-extern "C" int janus_b200_moe_grouped_w4a16(const void* x, int64_t ldx, const uint8_t* codes, const void* scales,
-                                            int64_t E, int64_t N, int64_t K, int32_t gated, const int32_t* sorted_ids,
-                                            const int32_t* tile_expert, const int32_t* n_tiles, int64_t max_tiles,
-                                            int64_t topk, const float* topk_w, void* out, int64_t ldo,
-                                            int32_t* status, void* stream) {
-  JB_REQUIRE(x && codes && scales && sorted_ids && tile_expert && n_tiles && out, JANUS_ERR_INVALID,
-             "moe_grouped_w4a16: null pointer");
+// the checks and parameters shared by both weight formats; scales / bscales + gscales select the format
+static int moe_grouped(const void* x, int64_t ldx, const uint8_t* codes, const void* scales, const uint8_t* bscales,
+                       const float* gscales, int64_t E, int64_t N, int64_t K, int32_t gated, const int32_t* sorted_ids,
+                       const int32_t* tile_expert, const int32_t* n_tiles, int64_t max_tiles, int64_t topk,
+                       const float* topk_w, void* out, int64_t ldo, int32_t* status, void* stream, const char* name) {
+  const bool fp4 = bscales != nullptr;
+  JB_REQUIRE(x && codes && (fp4 ? (gscales != nullptr) : (scales != nullptr)) && sorted_ids && tile_expert && n_tiles &&
+                 out,
+             JANUS_ERR_INVALID, "%s: null pointer", name);
   JB_REQUIRE(E > 0 && N > 0 && N % 128 == 0 && K > 0 && K % mtc::GROUP == 0 && topk > 0 && max_tiles >= 0,
-             JANUS_ERR_UNSUPPORTED, "moe_grouped_w4a16: N %lld and K %lld must be multiples of 128", (long long)N,
-             (long long)K);
-  JB_REQUIRE(gated || topk_w, JANUS_ERR_INVALID, "moe_grouped_w4a16: the down projection needs routing weights");
-  JB_REQUIRE(ldx % 8 == 0 && ldo % 8 == 0 && JB_ALIGNED(x, 16) && JB_ALIGNED(codes, 16) && JB_ALIGNED(out, 16),
-             JANUS_ERR_ALIGNMENT, "moe_grouped_w4a16: x, codes and out 16-byte aligned, ldx and ldo multiples of 8");
+             JANUS_ERR_UNSUPPORTED, "%s: N %lld and K %lld must be multiples of 128", name, (long long)N, (long long)K);
+  JB_REQUIRE(gated || topk_w, JANUS_ERR_INVALID, "%s: the down projection needs routing weights", name);
+  JB_REQUIRE(ldx % 8 == 0 && ldo % 8 == 0 && JB_ALIGNED(x, 16) && JB_ALIGNED(codes, 16) && JB_ALIGNED(out, 16) &&
+                 (!fp4 || JB_ALIGNED(bscales, 2)),
+             JANUS_ERR_ALIGNMENT, "%s: x, codes and out 16-byte aligned, ldx and ldo multiples of 8", name);
   const int64_t NW = gated ? 2 * N : N;
-  JB_REQUIRE(E * NW < (1ll << 31) && K < (1 << 30), JANUS_ERR_UNSUPPORTED, "moe_grouped_w4a16: sizes");
+  JB_REQUIRE(E * NW < (1ll << 31) && K < (1 << 30), JANUS_ERR_UNSUPPORTED, "%s: sizes", name);
   const int64_t nblk = gated ? N / 128 : (N % 256 == 0 ? N / 256 : N / 128);
-  JB_REQUIRE(max_tiles * nblk < (1ll << 31), JANUS_ERR_UNSUPPORTED, "moe_grouped_w4a16: grid");
+  JB_REQUIRE(max_tiles * nblk < (1ll << 31), JANUS_ERR_UNSUPPORTED, "%s: grid", name);
   if (max_tiles == 0) return JANUS_OK;
   mtc::Params p{};
   int st = code_map(&p.cmap, codes, (uint64_t)(E * NW), (uint64_t)K);
@@ -473,6 +542,8 @@ extern "C" int janus_b200_moe_grouped_w4a16(const void* x, int64_t ldx, const ui
   p.A = (const __nv_bfloat16*)x;
   p.lda = ldx;
   p.scales = (const __nv_bfloat16*)scales;
+  p.bscales = bscales;
+  p.gscales = gscales;
   p.sorted_ids = sorted_ids;
   p.tile_expert = tile_expert;
   p.n_tiles = n_tiles;
@@ -485,7 +556,32 @@ extern "C" int janus_b200_moe_grouped_w4a16(const void* x, int64_t ldx, const ui
   p.topk = (int)topk;
   p.nblk = (int)nblk;
   cudaStream_t s = (cudaStream_t)stream;
-  if (gated) return launch<true, 256>(p, max_tiles, s);
-  if (N % 256 == 0) return launch<false, 256>(p, max_tiles, s);
-  return launch<false, 128>(p, max_tiles, s);
+  if (fp4) {
+    if (gated) return launch<true, 256, true>(p, max_tiles, s);
+    if (N % 256 == 0) return launch<false, 256, true>(p, max_tiles, s);
+    return launch<false, 128, true>(p, max_tiles, s);
+  }
+  if (gated) return launch<true, 256, false>(p, max_tiles, s);
+  if (N % 256 == 0) return launch<false, 256, false>(p, max_tiles, s);
+  return launch<false, 128, false>(p, max_tiles, s);
+}
+
+extern "C" int janus_b200_moe_grouped_w4a16(const void* x, int64_t ldx, const uint8_t* codes, const void* scales,
+                                            int64_t E, int64_t N, int64_t K, int32_t gated, const int32_t* sorted_ids,
+                                            const int32_t* tile_expert, const int32_t* n_tiles, int64_t max_tiles,
+                                            int64_t topk, const float* topk_w, void* out, int64_t ldo,
+                                            int32_t* status, void* stream) {
+  return moe_grouped(x, ldx, codes, scales, nullptr, nullptr, E, N, K, gated, sorted_ids, tile_expert, n_tiles,
+                     max_tiles, topk, topk_w, out, ldo, status, stream, "moe_grouped_w4a16");
+}
+
+extern "C" int janus_b200_moe_grouped_nvfp4(const void* x, int64_t ldx, const uint8_t* codes,
+                                            const uint8_t* block_scales, const float* global_scales, int64_t E,
+                                            int64_t N, int64_t K, int32_t gated, const int32_t* sorted_ids,
+                                            const int32_t* tile_expert, const int32_t* n_tiles, int64_t max_tiles,
+                                            int64_t topk, const float* topk_w, void* out, int64_t ldo,
+                                            int32_t* status, void* stream) {
+  JB_REQUIRE(block_scales && global_scales, JANUS_ERR_INVALID, "moe_grouped_nvfp4: null scale pointer");
+  return moe_grouped(x, ldx, codes, nullptr, block_scales, global_scales, E, N, K, gated, sorted_ids, tile_expert,
+                     n_tiles, max_tiles, topk, topk_w, out, ldo, status, stream, "moe_grouped_nvfp4");
 }

@@ -69,8 +69,16 @@ class DecisionReadout:
                 part = self.ep.shard if self.ep is not None else (lambda t: t)
                 u8 = lambda n: part(weights[n]).to(dev).contiguous()
                 bf = lambda n: part(weights[n]).to(dev, torch.bfloat16).contiguous()
-                L.gu_codes, L.gu_scales = u8(m + "experts.gate_up_proj"), bf(m + "experts.gate_up_proj.scales")
-                L.dn_codes, L.dn_scales = u8(m + "experts.down_proj"), bf(m + "experts.down_proj.scales")
+                L.fp4 = (m + "experts.gate_up_proj.global") in weights
+                if L.fp4:  # NVFP4 experts: e4m3 block scales (as bytes) and fp32 global scales per row
+                    f8 = lambda n: part(weights[n]).to(dev).view(torch.uint8).contiguous()
+                    f32 = lambda n: part(weights[n]).to(dev, torch.float32).contiguous()
+                    L.gu_codes, L.gu_scales = u8(m + "experts.gate_up_proj"), f8(m + "experts.gate_up_proj.scales")
+                    L.dn_codes, L.dn_scales = u8(m + "experts.down_proj"), f8(m + "experts.down_proj.scales")
+                    L.gu_global, L.dn_global = f32(m + "experts.gate_up_proj.global"), f32(m + "experts.down_proj.global")
+                else:
+                    L.gu_codes, L.gu_scales = u8(m + "experts.gate_up_proj"), bf(m + "experts.gate_up_proj.scales")
+                    L.dn_codes, L.dn_scales = u8(m + "experts.down_proj"), bf(m + "experts.down_proj.scales")
                 L.shared_gate_up = torch.cat([w(m + "shared_expert.gate_proj.weight"), w(m + "shared_expert.up_proj.weight")])
                 L.shared_down = w(m + "shared_expert.down_proj.weight")
                 L.shared_gate = w(m + "shared_expert_gate.weight")
@@ -151,8 +159,8 @@ class DecisionReadout:
         plan = ops.moe_route(logits, k)
         if self.ep is not None:
             return self._moe_ep(y, L, plan[0], plan[1])
-        h = ops.moe_grouped_w4a16(y, L.gu_codes, L.gu_scales, plan, True, k, status=self.status)
-        y2 = ops.moe_grouped_w4a16(h, L.dn_codes, L.dn_scales, plan, False, k, topk_w=plan[1], status=self.status)
+        h = self._experts(y, L, plan, True, k)
+        y2 = self._experts(h, L, plan, False, k, topk_w=plan[1])
         shared = F.linear(ops.silu_mul(F.linear(y, L.shared_gate_up)), L.shared_down)
         sg = torch.mm(y, L.shared_gate.t(), out_dtype=torch.float32)
         return ops.moe_combine(y2, k, shared, sg.reshape(-1))
@@ -165,9 +173,8 @@ class DecisionReadout:
         H = y.shape[1]
         if rows.shape[0]:
             plan = ops.moe_plan(slot_e, ep.local)
-            h = ops.moe_grouped_w4a16(rows, L.gu_codes, L.gu_scales, plan, True, k, status=self.status)
-            y2 = ops.moe_grouped_w4a16(h, L.dn_codes, L.dn_scales, plan, False, k, topk_w=slot_w.reshape(-1),
-                                      status=self.status)
+            h = self._experts(rows, L, plan, True, k)
+            y2 = self._experts(h, L, plan, False, k, topk_w=slot_w.reshape(-1))
             part = ops.moe_reduce_slots(y2, k, slot_e)
         else:
             part = torch.empty(0, H, dtype=torch.float32, device=y.device)
@@ -175,6 +182,14 @@ class DecisionReadout:
         sg = torch.mm(y, L.shared_gate.t(), out_dtype=torch.float32)
         back, row_index = ep.combine(part, handle)
         return ops.moe_combine_ep(back, row_index, shared, sg.reshape(-1))
+
+    def _experts(self, x, L, plan, gated, k, topk_w=None):
+        """One grouped GEMM over the layer's experts in their stored format (int4 group 128, or NVFP4)."""
+        if L.fp4:
+            codes, bs, gs = (L.gu_codes, L.gu_scales, L.gu_global) if gated else (L.dn_codes, L.dn_scales, L.dn_global)
+            return ops.moe_grouped_nvfp4(x, codes, bs, gs, plan, gated, k, topk_w=topk_w, status=self.status)
+        codes, sc = (L.gu_codes, L.gu_scales) if gated else (L.dn_codes, L.dn_scales)
+        return ops.moe_grouped_w4a16(x, codes, sc, plan, gated, k, topk_w=topk_w, status=self.status)
 
     CHUNK_MIN_TOKENS = 32  # mean row length from which a level runs the chunked rule (rows are read once per chunk)
 

@@ -367,6 +367,34 @@ def moe_grouped_w4a16(x, codes, scales, plan, gated, k, topk_w=None, out=None, s
     return out
 
 
+@_instrument("moe_grouped_nvfp4", 1)
+def moe_grouped_nvfp4(x, codes, block_scales, global_scales, plan, gated, k, topk_w=None, out=None, status=None):
+    """moe_grouped_w4a16 on NVFP4 experts: codes uint8 [E, NW, K/2] (e2m1 pairs), block_scales e4m3 [E, NW, K/16]
+    (torch.float8_e4m3fn or its uint8 bytes), global_scales fp32 [E, NW] (one per weight row)."""
+    _need(x, BF16, "x", contiguous=False)
+    if x.stride(1) != 1:
+        raise ValueError("x must have unit column stride")
+    _need(codes, torch.uint8, "codes")
+    if block_scales.dtype == torch.float8_e4m3fn:
+        block_scales = block_scales.view(torch.uint8)
+    _need(block_scales, torch.uint8, "block_scales"); _need(global_scales, F32, "global_scales")
+    E, NW, half_k = codes.shape
+    K = 2 * half_k
+    if block_scales.shape != (E, NW, K // 16) or global_scales.shape != (E, NW):
+        raise ValueError("moe_grouped_nvfp4: block_scales [E, NW, K/16] and global_scales [E, NW]")
+    N = NW // 2 if gated else NW
+    topk_idx, _, sorted_ids, tile_expert, n_tiles = plan
+    mt = tile_expert.shape[0]
+    S = topk_idx.shape[0]
+    if out is None:
+        out = torch.empty((mt * MOE_TILE if gated else S * k), N, dtype=BF16, device=x.device)
+    _lib.check(_lib.load().janus_b200_moe_grouped_nvfp4(
+        _ptr(x), x.stride(0), _ptr(codes), _ptr(block_scales), _ptr(global_scales), E, N, K, 1 if gated else 0,
+        _ptr(sorted_ids), _ptr(tile_expert), _ptr(n_tiles), mt, k, _ptr(topk_w), _ptr(out), out.stride(0),
+        _ptr(status), _stream(x)), "moe_grouped_nvfp4")
+    return out
+
+
 @_instrument("moe_combine", 1)
 def moe_combine(y, k, shared, shared_gate_logit, out=None):
     _need(y, BF16, "y")

@@ -101,6 +101,50 @@ def int4_quantized(shape, seed, name, device):
     return packed, scales
 
 
+E2M1_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
+FP4_BLOCK = 16
+
+
+def e2m1_encode(x):
+    """fp32 -> 4-bit e2m1 codes (bit 3 the sign), nearest value with ties to the even code."""
+    vals = torch.tensor(E2M1_VALUES, device=x.device)
+    mids = (vals[1:] + vals[:-1]) / 2
+    mag = x.abs()
+    code = torch.bucketize(mag, mids)  # a magnitude equal to a midpoint goes to the lower code
+    tie = (code < 7) & (mag == mids[code.clamp(max=6)]) & (code % 2 == 1)
+    code = (code + tie.to(code.dtype)).to(torch.uint8)
+    return code | ((x < 0).to(torch.uint8) << 3)
+
+
+def nvfp4_quantize(w, rows_global=None):
+    """A weight [..., rows, K] in the reference's NVFP4 layout (janus/hybrid.py:427-440, ModelOpt's rule): a global
+    fp32 scale amax / (6 * 448) over each [rows, K] matrix (or over each slice of rows given by `rows_global`, e.g.
+    the gate and up halves of a gate/up stack), per 16 inputs an e4m3 block scale block_amax / 6 / global (1 for an
+    all-zero block), codes the e2m1 rounding of w / (block scale * global), two per byte with the even element in
+    the low nibble. Returns (codes uint8 [..., rows, K/2], block scales e4m3 [..., rows, K/16], global fp32
+    [..., rows])."""
+    w = w.float()
+    *lead, R, K = w.shape
+    bounds = rows_global or [(0, R)]
+    glob = torch.empty(*lead, R, device=w.device)
+    for a, b in bounds:
+        amax = w[..., a:b, :].abs().amax(dim=(-1, -2))
+        glob[..., a:b] = (amax / (6.0 * 448.0)).clamp(min=torch.finfo(torch.float32).tiny)[..., None]
+    blocks = w.view(*lead, R, K // FP4_BLOCK, FP4_BLOCK)
+    bs = blocks.abs().amax(-1) / 6.0 / glob[..., None]
+    bs = torch.where(bs == 0, torch.ones_like(bs), bs).to(torch.float8_e4m3fn)
+    codes = e2m1_encode(blocks / (bs.float() * glob[..., None])[..., None]).reshape(w.shape)
+    return (codes[..., 0::2] | (codes[..., 1::2] << 4)).contiguous(), bs.contiguous(), glob.contiguous()
+
+
+def nvfp4_quantized(shape, seed, name, device, halves=False):
+    """A seeded NVFP4 expert stack: N(0, 0.02) weights of `shape` [E, rows, K] quantised by `nvfp4_quantize` (with
+    `halves`, the gate and up halves of a gate/up stack get their own global scales, as ModelOpt stores them)."""
+    w = _normal(shape, 0.02, seed, name, device)
+    R = shape[-2]
+    return nvfp4_quantize(w, [(0, R // 2), (R // 2, R)] if halves else None)
+
+
 def int4_dequantize(packed, scales, dtype=torch.bfloat16):
     """code * scale in fp32 (exact: a 4-bit integer times a bf16 value), rounded once to `dtype`."""
     lo = (packed & 15).to(torch.int16)
@@ -112,15 +156,22 @@ def int4_dequantize(packed, scales, dtype=torch.bfloat16):
     return w.reshape(codes.shape).to(dtype)
 
 
-def make_weights(shape: ModelShape, seed=0, head="pointer", device="cpu", layers=None, lora=True, std=None):
+def make_weights(shape: ModelShape, seed=0, head="pointer", device="cpu", layers=None, lora=True, std=None,
+                 experts="int4"):
     """Name -> tensor. Matrices bf16 (int4 experts as (codes, scales) pairs under `<name>` and `<name>.scales`),
     head fp32. `layers` restricts the decoder layers generated (default all). `std`: {name suffix: standard deviation}
-    replacing the 0.02 of the matrices whose names end with the suffix (test variants only: e.g. a sharper router)."""
+    replacing the 0.02 of the matrices whose names end with the suffix (test variants only: e.g. a sharper router).
+    `experts`: "int4" (group 128, bf16 scales: `<name>`, `<name>.scales`) or "nvfp4" (the reference's format: codes,
+    e4m3 block scales `<name>.scales`, fp32 global scales per row `<name>.global`)."""
     out = {}
     r = shape.lora_rank if lora else 0
     for name, shp, init in parameter_shapes(shape, head, layers):
         if init == "int4":
-            packed, scales = int4_quantized(shp, seed, name, device)
+            if experts == "nvfp4":
+                packed, scales, glob = nvfp4_quantized(shp, seed, name, device, halves=name.endswith("gate_up_proj"))
+                out[name + ".global"] = glob
+            else:
+                packed, scales = int4_quantized(shp, seed, name, device)
             out[name] = packed
             out[name + ".scales"] = scales
             continue

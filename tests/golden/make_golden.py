@@ -5,6 +5,7 @@ Run in a container where the reference checkout is importable (default /root/ref
     python tests/golden/make_golden.py            # readout_cases.json + delta_rule.npz (small cases)
     python tests/golden/make_golden.py --full     # readout_full.json: the benchmark configurations at full depth
     python tests/golden/make_golden.py --argmax   # argmax_4b.npz: 1000 seeded questions at 4B width
+    python tests/golden/make_golden.py --nvfp4    # nvfp4.npz: the reference's NVFP4 codec on seeded weights
 
 For every case it builds the seeded synthetic weights (janus_b200.synthetic.make_weights), loads them into a
 transformers Qwen3_5TextModel / Qwen3_5MoeTextModel in fp32, wraps it in the reference's janus.hybrid.HybridBackbone
@@ -276,8 +277,33 @@ def main_argmax():
     print("wrote", HERE / "argmax_4b.npz", "questions", counts.size, "options", int(counts.sum()))
 
 
+def main_nvfp4():
+    """The reference's NVFP4 codec (janus/hybrid.py:400-440) on a seeded [2, 128, 256] stack: its quantised codes,
+    block scales and global scale per expert, its bf16 dequantised values, and its e2m1 encoding of edge values."""
+    sys.path.insert(0, REFERENCE)
+    from janus import hybrid as ref
+    g = torch.Generator().manual_seed(77)
+    w = torch.randn(2, 128, 256, generator=g) * 0.02
+    w[1, 3, :16] = 0.0  # an all-zero block
+    out = {"w": w.numpy()}
+    for e in range(2):
+        codes, bs, gl = ref.nvfp4_quantize(w[e])
+        out[f"codes{e}"] = codes.numpy()
+        out[f"bscales{e}"] = bs.view(torch.uint8).numpy()
+        out[f"global{e}"] = np.array(float(gl), dtype=np.float32)
+        out[f"dequant{e}"] = ref._nvfp4_dequant(codes, bs, gl, torch.bfloat16).float().numpy()
+    x = torch.cat([torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0, 7.0, -0.25, -1.25, -5.0, 0.0]),
+                   torch.randn(4096, generator=g) * 3])
+    out["enc_x"] = x.numpy()
+    out["enc_codes"] = ref._e2m1_encode(x).numpy()
+    np.savez_compressed(HERE / "nvfp4.npz", **out)
+    print("wrote", HERE / "nvfp4.npz")
+
+
 def main():
     torch.set_num_threads(os.cpu_count() or 8)
+    if "--nvfp4" in sys.argv:
+        return main_nvfp4()
     if "--full" in sys.argv:
         return main_full()
     if "--argmax" in sys.argv:

@@ -144,3 +144,83 @@ def test_grouped_w4a16_run_to_run_identical(S, E, k):
         assert torch.equal(h[valid], h0[valid])
         assert torch.equal(y, y0)
     assert int(st.item()) == 0
+
+
+@pytest.mark.parametrize("fmt", ["int4", "nvfp4"])
+def test_decoded_weights_are_the_reference_values_bit_for_bit(fmt):
+    """The down GEMM of one expert on identity rows returns the decoded weight matrix itself (1 x w accumulated in
+    fp32 and rounded to bf16 is w): every decoded element equals the oracle's dequantised bf16 weight."""
+    from janus_b200 import synthetic
+    ops = _ops()
+    E, H, I = 3, 256, 512
+    if fmt == "int4":
+        codes, scales = synthetic.int4_quantized((E, H, I), 21, "dn", "cpu")
+        ref = oracle.int4_dequantize(codes, scales)
+    else:
+        codes, bs, gl = synthetic.nvfp4_quantized((E, H, I), 21, "dn", "cpu")
+        ref = oracle.nvfp4_dequantize(codes, bs, gl)
+    e = 2
+    slot = torch.full((I, 1), e, dtype=torch.int32)
+    plan = ops.moe_plan(slot.cuda(), E)
+    # the down GEMM reads sorted row r and writes assignment ids[r]: put e_a in the sorted row of assignment a
+    ids = plan[2].cpu().long()
+    pos = torch.nonzero(ids >= 0).reshape(-1)
+    assert sorted(ids[pos].tolist()) == list(range(I))
+    x = torch.zeros(ids.shape[0], I, dtype=torch.bfloat16)
+    x[pos, ids[pos]] = 1.0
+    x = x.cuda()
+    w1 = torch.ones(I, dtype=torch.float32).cuda()
+    if fmt == "int4":
+        out = ops.moe_grouped_w4a16(x, codes.cuda(), scales.cuda(), plan, False, 1, topk_w=w1)
+    else:
+        out = ops.moe_grouped_nvfp4(x, codes.cuda(), bs.cuda(), gl.cuda(), plan, False, 1, topk_w=w1)
+    np.testing.assert_array_equal(out.cpu().float().numpy(), ref[e].t().float().numpy())
+
+
+def test_grouped_nvfp4_gemms_and_combine():
+    """The A3B expert shapes in the reference's NVFP4 format (gate and up with their own global scales): both grouped
+    GEMMs and the combine against fp32 math on the oracle's dequantised weights."""
+    from janus_b200 import synthetic
+    ops = _ops()
+    S, E, k, H, I = 400, 64, 8, 2048, 512
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(S, H, generator=g).to(torch.bfloat16)
+    logits = torch.randn(S, E, generator=g)
+    gu = synthetic.nvfp4_quantized((E, 2 * I, H), 31, "gu", "cpu", halves=True)
+    dn = synthetic.nvfp4_quantized((E, H, I), 32, "dn", "cpu")
+    plan = ops.moe_route(logits.cuda(), k)
+    h = ops.moe_grouped_nvfp4(x.cuda(), *(t.cuda() for t in gu), plan, True, k)
+    y2 = ops.moe_grouped_nvfp4(h, *(t.cuda() for t in dn), plan, False, k, topk_w=plan[1])
+    out = ops.moe_combine(y2, k, None, None)
+    torch.cuda.synchronize()
+    guw = oracle.nvfp4_dequantize(*gu).float()
+    dnw = oracle.nvfp4_dequantize(*dn).float()
+    idx, wts = plan[0].cpu().long(), plan[1].cpu()
+    ref = torch.zeros(S, H)
+    for t in range(S):
+        for j in range(k):
+            e = int(idx[t, j])
+            hh = x[t].float() @ guw[e].t()
+            hh = (F.silu(hh[:I]) * hh[I:]).to(torch.bfloat16).float()
+            ref[t] += (wts[t, j] * (hh @ dnw[e].t())).to(torch.bfloat16).float()
+    scale = ref.abs().max().item()
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref.numpy(), atol=1e-2 * scale, rtol=2e-2)
+
+
+def test_nvfp4_experts_in_the_readout():
+    """A tiny MoE readout whose experts are in the reference's NVFP4 format, against the oracle at the B200 path's
+    storage precision (the same weights dequantised)."""
+    from janus_b200 import synthetic
+    from janus_b200.config import SHAPES
+    from janus_b200.model import DecisionReadout
+    shape = SHAPES["tiny-moe"]
+    weights = synthetic.make_weights(shape, seed=8, head="scalar", experts="nvfp4")
+    packs = [synthetic.tiny_request(vocab=shape.vocab, seed=s, mode="tree") for s in (3, 4)]
+    got = DecisionReadout(shape, weights, "tree").probabilities(packs)
+    model16 = oracle.Oracle(shape, weights, storage="bf16")
+    worst = 0.0
+    for pack, per in zip(packs, got):
+        for a, b in zip(per, oracle.probabilities(model16.logits(pack, "tree"))):
+            worst = max(worst, float((a - b).abs().max()))
+    print(f"\nNVFP4 tiny MoE readout: max |p - p_oracle_bf16| {worst:.2e}")
+    assert worst <= 5e-3
