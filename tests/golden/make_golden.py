@@ -123,9 +123,15 @@ def hf_model(shape, weights, dtype=torch.float32):
     return lm.to(dtype).eval()
 
 
-def reference_logits(shape, weights, mode, packs, dtype=torch.float32):
+def reference_logits(shape, weights, mode, packs, dtype=torch.float32, grouped_branches=False):
+    """The reference readout. `grouped_branches`: the plain path's branch levels through `branch_attention` (pieces
+    grouped by ancestor, bounded by PIECE_BYTES) instead of its one varlen call (`packed_attention`), whose CPU form
+    masks every query against every gathered key: at 8192-token states that is tens of GB (the same softmax over the
+    same keys either way, janus/hybrid.py:864, 958-989)."""
     sys.path.insert(0, REFERENCE)
+    from janus import hybrid as ref_hybrid
     from janus.hybrid import HybridBackbone
+    ref_hybrid.BRANCH_PACKED = not grouped_branches
     from janus.model import DecisionModel, ModelConfig, PointerHead, ScalarHead
     from janus.packing import Branch as RefBranch, PackedRequest as RefPacked
     lm = hf_model(shape, weights, dtype)
@@ -238,9 +244,9 @@ def main_full():
         shape = shape_of(SHAPES[base], dict(overrides))
         packs = build_packs(specs)
         weights = synthetic.make_weights(shape, seed=seed, head="scalar" if mode == "tree" else "pointer", std=std)
-        logits = reference_logits(shape, weights, mode, packs)
+        logits = reference_logits(shape, weights, mode, packs, grouped_branches=True)
         probs = [[torch.softmax(z.float(), -1).tolist() for z in per] for per in logits]
-        logits16 = reference_logits(shape, weights, mode, packs, torch.bfloat16)
+        logits16 = reference_logits(shape, weights, mode, packs, torch.bfloat16, grouped_branches=True)
         probs16 = [[torch.softmax(z.float(), -1).tolist() for z in per] for per in logits16]
         dev16 = max(abs(a - b) for pp, qq in zip(probs, probs16) for p, q in zip(pp, qq) for a, b in zip(p, q))
         po16 = oracle_probs(shape, weights, mode, packs, "bf16")
@@ -264,10 +270,10 @@ def main_argmax():
     packs = build_packs(specs)
     weights = synthetic.make_weights(shape, seed=a["seed"], head="scalar")
     flat = lambda per_pack: np.concatenate([np.asarray(z, dtype=np.float32) for per in per_pack for z in per])
-    logits = reference_logits(shape, weights, a["mode"], packs)
+    logits = reference_logits(shape, weights, a["mode"], packs, grouped_branches=True)
     p32 = [[torch.softmax(z.float(), -1).numpy() for z in per] for per in logits]
     p16 = [[torch.softmax(z.float(), -1).numpy() for z in per]
-           for per in reference_logits(shape, weights, a["mode"], packs, torch.bfloat16)]
+           for per in reference_logits(shape, weights, a["mode"], packs, torch.bfloat16, grouped_branches=True)]
     po16 = oracle_probs(shape, weights, a["mode"], packs, "bf16")
     counts = np.array([len(z) for per in p32 for z in per], dtype=np.int32)
     np.savez_compressed(HERE / "argmax_4b.npz", spec=np.array(json.dumps(a)), counts=counts,
