@@ -8,34 +8,19 @@
 //           silu(gate) * up from the fp32 accumulators, rounded once: the MLP's gate/up GEMM and its SwiGLU
 //           (`_silu_mul`, janus/hybrid.py:263) in one pass, the 2N-wide intermediate never written.
 //
-// Tiles of 128 rows x 256 columns, one M=128, N=256 MMA per 16-deep k step. A stage holds a 128-deep k-block (two
-// 128-byte swizzle atoms of bf16) of A (32 KB) and W (64 KB), loaded by TMA (no multicast) into a 2-stage ring: the
-// MMA thread waits once per 8 MMAs (a wait costs the tensor pipe a few hundred cycles even when the phase is
-// already complete, so waiting once per 64-deep block left it idle a quarter of the time). Persistent
-// CTAs, one per SM, walk the (m-tile, n-block) items with the n-block fastest: the CTAs of a wave share one or two
-// A tiles and the whole weight matrix stays resident in L2 across waves, so A and W are read from HBM about once.
-// The fp32 accumulator is double-buffered in TMEM (2 x 256 columns), so an item's epilogue overlaps the next item's
-// main loop. Warps: 0 TMA producer, 1 TMEM owner and MMA issuer, 2-3 idle, 4-7 epilogue (warp w reads TMEM lanes
-// 32 (w % 4) .. +31). Rows past M and columns past N are zero-filled by the loads and not stored. Every hand-off is
-// an mbarrier with a bounded wait: a wait that runs out sets the status word and the CTA winds down (loads in
-// flight waited for, MMAs drained, TMEM released).
+// Tiles of 256 rows x 256 columns per CTA pair (below), k-blocks of 64 (one 128-byte swizzle atom of bf16) in a
+// 6-stage TMA ring. Persistent pairs walk the (m-tile, n-block) items with the n-block fastest: the pairs of a wave
+// share one or two A tiles and the whole weight matrix stays resident in L2 across waves, so A and W are read from
+// HBM about once. The fp32 accumulator is double-buffered in TMEM (2 x 256 columns), so an item's epilogue overlaps
+// the next item's main loop. Warps: 0 TMA producer, 1 TMEM owner and (first CTA) MMA issuer, 2-3 idle, 4-7 epilogue
+// (warp w reads TMEM lanes 32 (w % 4) .. +31). Rows past M and columns past N are zero-filled by the loads and not
+// stored. Every hand-off is an mbarrier with a bounded wait: a wait that runs out sets the status word and the CTA
+// winds down (loads in flight waited for, MMAs drained, TMEM released).
 #include "tcgen05.cuh"
 
 namespace jb {
 namespace gtc {
 using namespace tcx;
-
-constexpr int BM = 128, BN = 256, BK = 64;  // BK: one swizzle atom
-constexpr int AT = 2;    // atoms per stage: a stage is a 128-deep k-block
-constexpr int S = 2;     // stages
-constexpr int NT = 256;  // 8 warps
-constexpr uint32_t kAtomA = BM * BK * 2;  // 16 KB
-constexpr uint32_t kAtomB = BN * BK * 2;  // 32 KB
-constexpr uint32_t kA = AT * kAtomA;
-constexpr uint32_t kB = AT * kAtomB;
-constexpr uint32_t kStage = kA + kB;
-constexpr uint32_t kOut = S * kStage;              // epilogue staging: 4 warps x 32 rows x 64 bytes
-constexpr uint32_t kSmem = kOut + 4 * 32 * 64;
 
 struct Params {
   CUtensorMap amap, bmap;  // A [M][K], W [N][K] bf16, boxes of 64 columns x 128 / 256 rows, 128B swizzle
@@ -45,73 +30,153 @@ struct Params {
   int M, N, K, nblk, n_items, swiglu;
 };
 
+}  // namespace gtc
+
+// ------------------------------------------------------------------------------------------------------------------
+// The GEMM on CTA pairs (clusters of 2, cta_group::2): a pair computes a 256 x 256 tile with M=256, N=256 MMAs
+// issued by the pair's first CTA; each CTA stages its own 128 rows of A and its own 128 of the tile's 256 W rows, so
+// a CTA's shared memory carries 8 KB of operand reads and 8 KB of TMA writes per 128 MMA cycles (128 B per cycle,
+// shared memory's rate; a single CTA with a 128 x 256 tile would carry 12 + 12 KB). Each CTA's TMEM holds the accumulator of its
+// 128 rows. Hand-offs: both CTAs' TMA loads complete on the first CTA's `full` barrier (which expects both CTAs'
+// bytes); the MMA's commits arrive on the `empty`, `acc_full` and `drain` barriers of both CTAs (multicast to the
+// pair); the epilogue warps of both CTAs arrive on the first CTA's `acc_empty`. A cluster barrier after the barrier
+// set-up and before the exit keeps every remote arrival inside the peer's lifetime. No TMA load uses multicast.
+namespace gtc2 {
+using namespace tcx;
+
+constexpr int BM = 128, BN = 256, BK = 64;  // per CTA: 128 rows of A, 128 of the 256 W rows of the tile
+constexpr int S = 6;
+constexpr int NT = 256;
+constexpr uint32_t kA = BM * BK * 2;         // 16 KB
+constexpr uint32_t kB = (BN / 2) * BK * 2;   // 16 KB
+constexpr uint32_t kStage = kA + kB;
+constexpr uint32_t kOut = S * kStage;
+constexpr uint32_t kSmem = kOut + 4 * 32 * 64;
+
 struct Bars {
   uint64_t full[S], empty[S], acc_full[2], acc_empty[2], drain;
 };
 
-__global__ void __launch_bounds__(NT, 1) gemm_bf16_tc_kernel(const __grid_constant__ Params p) {
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t n_clusters() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// the shared::cluster address of this CTA's shared variable at `saddr` in the pair's CTA `rank`
+__device__ __forceinline__ uint32_t peer_addr(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void remote_arrive(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// TMA tile load into this CTA's shared memory, completing on a barrier of the pair (cluster address); no multicast
+__device__ __forceinline__ void tma_load2_pair(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+// D (both CTAs' TMEM, 128 lanes each) (+)= A (both CTAs' shared memory) x B (both CTAs' halves)
+__device__ __forceinline__ void mma2(uint32_t tm, uint64_t da, uint64_t db, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n}\n" ::"r"(tm),
+      "l"(da), "l"(db), "r"(id), "r"(acc), "r"(0));
+}
+// completion of this CTA's MMAs issued so far, arriving on the barrier at the same offset in both CTAs of the pair
+__device__ __forceinline__ void commit2(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          s32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(NT, 1) gemm_bf16_pair_kernel(const __grid_constant__ gtc::Params p) {
   extern __shared__ unsigned char raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~(uintptr_t)1023);
   const uint32_t sbase = s32(base);
   __shared__ Bars bars;
   __shared__ uint32_t tmem_base;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int G = gridDim.x;
-  const int nkb = (p.K + AT * BK - 1) / (AT * BK);  // stages per item (the last one zero-filled past K)
+  const uint32_t rank = cluster_rank();
+  const int G = (int)n_clusters(), c = (int)cluster_id();
+  const int nkb = (p.K + BK - 1) / BK;
 
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s32(&tmem_base)),
+  if (warp == 1) {  // both CTAs' warp 1: the pair's TMEM, same columns in both
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s32(&tmem_base)),
                  "r"(2 * BN));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::);
   }
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
-      bar_init(&bars.full[s], 1);   // the producer's expect_tx, then the TMA bytes
-      bar_init(&bars.empty[s], 1);  // the stage's MMAs (commit)
+      bar_init(&bars.full[s], 1);   // the first CTA's expect_tx, then both CTAs' TMA bytes
+      bar_init(&bars.empty[s], 1);  // the stage's MMAs (commit, multicast)
     }
     for (int a = 0; a < 2; ++a) {
-      bar_init(&bars.acc_full[a], 1);   // the item's last MMAs (commit)
-      bar_init(&bars.acc_empty[a], 4);  // one arrival per epilogue warp
+      bar_init(&bars.acc_full[a], 1);   // the item's last MMAs (commit, multicast)
+      bar_init(&bars.acc_empty[a], 8);  // the 4 epilogue warps of each CTA (first CTA's barrier)
     }
     bar_init(&bars.drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   fence_before();
   __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrival
   fence_after();
   const uint32_t tm = tmem_base;
 
   if (warp == 0) {
-    // ------------------------------------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------------------------------------ TMA producers
     if (lane == 0) {
       bool ok = true;
       int q = 0, issued = 0;
-      for (int it = blockIdx.x; it < p.n_items && ok; it += G) {
-        const int m0 = (it / p.nblk) * BM, n0 = (it % p.nblk) * BN;
+      for (int it = c; it < p.n_items && ok; it += G) {
+        const int m0 = (it / p.nblk) * (2 * BM) + (int)rank * BM, n0 = (it % p.nblk) * BN + (int)rank * (BN / 2);
         for (int kb = 0; kb < nkb; ++kb, ++q) {
           const int s = q % S;
           if (q >= S) ok = wait_bar(&bars.empty[s], ((q / S) - 1) & 1, p.err);
           if (!ok) break;
-          bar_expect_tx(&bars.full[s], kStage);
-#pragma unroll
-          for (int t = 0; t < AT; ++t) {
-            tma_load2(sbase + s * kStage + t * kAtomA, &p.amap, (kb * AT + t) * BK, m0, &bars.full[s]);
-            tma_load2(sbase + s * kStage + kA + t * kAtomB, &p.bmap, (kb * AT + t) * BK, n0, &bars.full[s]);
-          }
+          if (rank == 0) bar_expect_tx(&bars.full[s], 2 * kStage);
+          const uint32_t fb = peer_addr(s32(&bars.full[s]), 0);
+          tma_load2_pair(sbase + s * kStage, &p.amap, kb * BK, m0, fb);
+          tma_load2_pair(sbase + s * kStage + kA, &p.bmap, kb * BK, n0, fb);
           issued = q + 1;
         }
       }
-      // every issued load has landed before the CTA may leave (on the normal path the MMAs consumed them all)
-      for (int j = issued - S < 0 ? 0 : issued - S; j < issued; ++j)
-        wait_bar_quiet(&bars.full[j % S], (j / S) & 1, p.err);
+      // every load landed before the CTA may leave: the first CTA's full barriers count both CTAs' bytes; the
+      // second waits for the MMAs that read its last stages
+      if (rank == 0) {
+        for (int j = issued - S < 0 ? 0 : issued - S; j < issued; ++j)
+          wait_bar_quiet(&bars.full[j % S], (j / S) & 1, p.err);
+      } else {
+        for (int j = issued - S < 0 ? 0 : issued - S; j < issued; ++j)
+          wait_bar_quiet(&bars.empty[j % S], (j / S) & 1, p.err);
+      }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t ID = idesc(BM, BN, 0, 0);
+    // ------------------------------------------------------------------------------- MMA issuer (first CTA)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t ID = idesc(2 * BM, BN, 0, 0);
       bool ok = true;
       int q = 0, i = 0;
-      for (int it = blockIdx.x; it < p.n_items && ok; it += G, ++i) {
+      for (int it = c; it < p.n_items && ok; it += G, ++i) {
         const int ab = i & 1;
         if (i >= 2) ok = wait_bar(&bars.acc_empty[ab], ((i >> 1) - 1) & 1, p.err);
         if (!ok) break;
@@ -124,31 +189,25 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_tc_kernel(const __grid_consta
           fence_after();
           const uint32_t a = sbase + s * kStage, b = a + kA;
 #pragma unroll
-          for (int ks = 0; ks < AT * BK / 16; ++ks) {
-            const uint32_t off = (ks / (BK / 16)), in = (ks % (BK / 16)) * 32;
-            mma(acc, sdesc(a + off * kAtomA + in, 16, 1024), sdesc(b + off * kAtomB + in, 16, 1024), ID,
-                (kb | ks) != 0);
-          }
-          commit(&bars.empty[s]);
+          for (int ks = 0; ks < BK / 16; ++ks)
+            mma2(acc, sdesc(a + ks * 32, 16, 1024), sdesc(b + ks * 32, 16, 1024), ID, (kb | ks) != 0);
+          commit2(&bars.empty[s]);
         }
-        if (ok) commit(&bars.acc_full[ab]);
+        if (ok) commit2(&bars.acc_full[ab]);
       }
-      commit(&bars.drain);  // completes once every MMA issued above has finished
+      commit2(&bars.drain);  // completes once every MMA issued above has finished
     }
   } else if (warp >= 4) {
-    // ------------------------------------------------------------------------------------------- epilogue
-    // thread = accumulator row (TMEM lane 32 (warp % 4) + lane). Each 32-column slice of the warp's rows goes through
-    // a small shared-memory buffer so the global stores cover 8 rows x 64 bytes per instruction instead of 32 rows x
-    // 16 bytes.
+    // ------------------------------------------------------------------------------------ epilogue (both CTAs)
     const int eq = warp & 3;
-    unsigned char* stg = base + kOut + eq * (32 * 64);  // [32 rows][64 bytes], 16-byte units swizzled by row
-    const int outc = p.swiglu ? BN / 2 : BN;            // output columns of an item
+    unsigned char* stg = base + kOut + eq * (32 * 64);
+    const int outc = p.swiglu ? BN / 2 : BN;
     const int out_n = p.swiglu ? p.N / 2 : p.N;
     bool ok = true;
     int i = 0;
-    for (int it = blockIdx.x; it < p.n_items && ok; it += G, ++i) {
+    for (int it = c; it < p.n_items && ok; it += G, ++i) {
       const int ab = i & 1;
-      const int m0 = (it / p.nblk) * BM, c0 = (it % p.nblk) * outc;
+      const int m0 = (it / p.nblk) * (2 * BM) + (int)rank * BM, c0 = (it % p.nblk) * outc;
       ok = __all_sync(kFull, wait_bar_sleep(&bars.acc_full[ab], (i >> 1) & 1, p.err));
       if (!ok) break;
       fence_after();
@@ -160,7 +219,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_tc_kernel(const __grid_consta
         for (int h2 = 0; h2 < 2; ++h2) {
           float a[16];
           tld16f(la + cc + 16 * h2, a);
-          if (p.swiglu) {  // silu(gate) * up: gate in accumulator columns 0..127, up in 128..255
+          if (p.swiglu) {
             float u[16];
             tld16f(la + 128 + cc + 16 * h2, u);
 #pragma unroll
@@ -176,7 +235,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_tc_kernel(const __grid_consta
           *reinterpret_cast<uint4*>(stg + lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4)) =
               make_uint4(o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
         __syncwarp();
-        const int col = c0 + cc + (lane & 3) * 8;  // the 8 columns this lane stores
+        const int col = c0 + cc + (lane & 3) * 8;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const int rr = k * 8 + (lane >> 2);
@@ -184,25 +243,27 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_tc_kernel(const __grid_consta
           const int row = m0 + 32 * eq + rr;
           if (row < p.M && col < out_n) *reinterpret_cast<uint4*>(p.out + (int64_t)row * p.ldo + col) = v;
         }
-        __syncwarp();  // the buffer is read before the next slice overwrites it
+        __syncwarp();
       }
       fence_before();
       __syncwarp();
-      if (lane == 0) bar_arrive(&bars.acc_empty[ab]);
+      if (lane == 0) remote_arrive(peer_addr(s32(&bars.acc_empty[ab]), 0));
     }
   }
 
-  // wind down: every MMA issued has completed before TMEM is released
+  // wind down: the pair's MMAs have completed (drain, multicast) before either CTA releases TMEM, and neither CTA
+  // leaves while the other may still arrive on its barriers
   fence_before();
   __syncthreads();
   fence_after();
   wait_bar_quiet(&bars.drain, 0, p.err);
   fence_before();
   __syncthreads();
-  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(2 * BN));
+  cluster_sync();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tm), "r"(2 * BN));
 }
 
-}  // namespace gtc
+}  // namespace gtc2
 
 // row-major [rows][cols] bf16 with row stride ld elements, boxes of 64 columns x box_rows rows, 128B swizzle,
 // zero fill past the edges
@@ -214,7 +275,7 @@ static int gemm_map(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t row
   }
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {ld * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)gtc::BK, box_rows};
+  const cuuint32_t box[2] = {(cuuint32_t)gtc2::BK, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -245,10 +306,10 @@ extern "C" int janus_b200_gemm_bf16(const void* a, int64_t lda, const void* w, i
              JANUS_ERR_ALIGNMENT, "gemm_bf16: 16-byte aligned operands, leading dimensions multiples of 8");
   if (M == 0) return JANUS_OK;
   gtc::Params p{};
-  int st = gemm_map(&p.amap, a, (uint64_t)K, (uint64_t)M, (uint64_t)lda, gtc::BM);
-  if (!st) st = gemm_map(&p.bmap, w, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, gtc::BN);
+  int st = gemm_map(&p.amap, a, (uint64_t)K, (uint64_t)M, (uint64_t)lda, gtc2::BM);
+  if (!st) st = gemm_map(&p.bmap, w, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, gtc2::BN / 2);
   if (st) return st;
-  const int64_t mt = (M + gtc::BM - 1) / gtc::BM, nblk = (N + gtc::BN - 1) / gtc::BN;
+  const int64_t mt = (M + 2 * gtc2::BM - 1) / (2 * gtc2::BM), nblk = (N + gtc2::BN - 1) / gtc2::BN;
   JB_REQUIRE(mt * nblk < (1ll << 31), JANUS_ERR_UNSUPPORTED, "gemm_bf16: too many tiles");
   p.out = (__nv_bfloat16*)out;
   p.ldo = ldo;
@@ -259,20 +320,36 @@ extern "C" int janus_b200_gemm_bf16(const void* a, int64_t lda, const void* w, i
   p.nblk = (int)nblk;
   p.n_items = (int)(mt * nblk);
   p.swiglu = epilogue;
-  const size_t smem = gtc::kSmem + 1024;
+  const size_t smem = gtc2::kSmem + 1024;
   cudaError_t e =
-      cudaFuncSetAttribute(gtc::gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      cudaFuncSetAttribute(gtc2::gemm_bf16_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) {
     set_error("gemm_bf16: smem attribute: %s", cudaGetErrorString(e));
     return JANUS_ERR_CUDA;
   }
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 1) {
     set_error("gemm_bf16: device query failed");
     return JANUS_ERR_CUDA;
   }
-  const int grid = (int)(p.n_items < sms ? p.n_items : sms);
-  gtc::gemm_bf16_tc_kernel<<<grid, gtc::NT, smem, (cudaStream_t)stream>>>(p);
+  const int pairs = (int)(p.n_items < sms / 2 ? p.n_items : sms / 2);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)(2 * pairs));
+  cfg.blockDim = dim3(gtc2::NT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, gtc2::gemm_bf16_pair_kernel, p);
+  if (e != cudaSuccess) {
+    set_error("gemm_bf16: launch: %s", cudaGetErrorString(e));
+    return JANUS_ERR_CUDA;
+  }
   return launch_status("gemm_bf16");
 }
