@@ -376,6 +376,7 @@ class Oracle:
         parents = packed.parents.tolist()
         hidden = torch.zeros(ids.shape[0], self.shape.hidden)
         seg_states = {}
+        has_children = set(parents[1:])  # only these segments' states are read again (a leaf's are dropped at once)
         for level in tree_levels(packed.segment_ids, packed.parents):
             for seg, start, end in level:
                 if seg == 0:
@@ -386,7 +387,8 @@ class Oracle:
                     ancestor_kv = [st if kind != LINEAR else None for st, kind in zip(ps, self.shape.layer_types)]
                 h, states = self.run_segment(ids[start:end], pos[start:end], parent_states, ancestor_kv)
                 hidden[start:end] = h
-                seg_states[seg] = states
+                if seg in has_children:
+                    seg_states[seg] = states
         return hidden
 
     def logits(self, packed, mode):
