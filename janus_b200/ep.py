@@ -15,9 +15,12 @@ attention and DeltaNet (data parallel) and holds the router, the shared expert a
    the gated shared expert and rounds once to bf16 (janus_b200_moe_combine_ep).
 
 The fp32 partials keep the reference's fp32 sum over the k experts (janus/moe_w4a16.py:140); only the order of
-that sum changes (per rank, then over ranks). The split sizes of the row all_to_all are read on the host (one
-small device-to-host copy per layer), so this path is not CUDA-graph capturable; every rank must run the same
-sequence of MoE layers (same levels), as all its collectives pair up by order.
+that sum changes (per rank, then over ranks). In the default form the split sizes of the row all_to_all are read on
+the host (one small device-to-host copy per layer), so it sends exactly the rows needed but is not CUDA-graph
+capturable. `ExpertParallel(..., static=True)` is the capturable form: fixed shapes, no host read and two
+collectives per layer (section `dispatch_static`), at the price of fixed-size blocks (each destination's block is
+as large as the rank's token count). Every rank must run the same sequence of MoE layers (same levels), as all its
+collectives pair up by order.
 """
 
 import torch
@@ -27,8 +30,9 @@ import torch.distributed as dist
 class ExpertParallel:
     """The expert partition of one process group and the dispatch / combine exchanges of a MoE layer."""
 
-    def __init__(self, n_experts, group=None):
+    def __init__(self, n_experts, group=None, static=False):
         self.group = group
+        self.static = static
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         if n_experts % self.world:
@@ -73,6 +77,60 @@ class ExpertParallel:
         row_index = torch.full((S, W), -1, dtype=torch.int32, device=dev)
         row_index[send_tok, send_rank] = torch.arange(send_tok.numel(), dtype=torch.int32, device=dev)
         return (recv_rows, recv_e, recv_w), (sc, rc, row_index)
+
+    def dispatch_static(self, x, topk_idx, topk_w, capacity):
+        """The capturable dispatch: one all_to_all_single with equal splits, no host read. Destination d gets a block
+        of `capacity` rows (the same on every rank and at least every rank's token count S: the level's graph bucket
+        agrees on it beforehand, `agree_capacity`); a row carries the token's H values and its k (local expert id or
+        -1, routing weight) slots as raw bits beside them, so rows and slots travel together. A token's row goes to
+        row `pos` of block d, pos counting this rank's earlier tokens that also go to d (a device cumulative sum);
+        unused rows carry only -1 slots, so the receiver's grouped GEMMs skip them.
+        Returns ((rows [W*C, H] view in x's dtype, slot_expert int32 [W*C, k], slot_w fp32 [W*C, k]), row_index
+        int32 [S, W]: where each token's row sits in the blocks, -1 where it is not sent)."""
+        S, k = topk_idx.shape
+        W, L, dev, H, C = self.world, self.local, x.device, x.shape[1], int(capacity)
+        if S > C:
+            raise ValueError(f"{S} tokens exceed the agreed capacity {C}")
+        raw = {2: torch.int16, 4: torch.int32}[x.element_size()]
+        meta = 8 * k // x.element_size()  # k int32 ids + k fp32 weights, in units of x's element size
+        dest = torch.div(topk_idx.long(), L, rounding_mode="floor")
+        hit = torch.zeros(S, W, dtype=torch.bool, device=dev)
+        if S:
+            hit.scatter_(1, dest, True)
+        pos = torch.cumsum(hit.to(torch.int64), 0) - 1
+        block = torch.arange(W, device=dev, dtype=torch.int64)[None, :] * C
+        flat = torch.where(hit, block + pos, torch.full_like(pos, W * C))  # W * C: a scratch row for non-hits
+        buf = torch.empty(W * C + 1, H + meta, dtype=raw, device=dev)
+        rows = buf[:, :H].view(x.dtype)
+        ids = buf[:, H:H + meta // 2].view(torch.int32)
+        wts = buf[:, H + meta // 2:].view(torch.float32)
+        ids.fill_(-1)
+        local_id = (topk_idx.long() - dest * L).to(torch.int32)
+        w32 = topk_w.float()
+        for d in range(W):
+            idx = flat[:, d]
+            rows.index_copy_(0, idx, x)
+            ids.index_copy_(0, idx, torch.where(dest == d, local_id, torch.full_like(local_id, -1)))
+            wts.index_copy_(0, idx, w32)
+        recv = torch.empty(W * C, H + meta, dtype=raw, device=dev)
+        dist.all_to_all_single(recv, buf[:W * C], group=self.group)
+        row_index = torch.where(hit, flat, torch.full_like(flat, -1)).to(torch.int32)
+        return ((recv[:, :H].view(x.dtype), recv[:, H:H + meta // 2].view(torch.int32).contiguous(),
+                 recv[:, H + meta // 2:].view(torch.float32).contiguous()), row_index)
+
+    def agree_capacity(self, tokens, device):
+        """The block size of the static exchange for a level: the largest token count over the group's ranks (one
+        small all_reduce, on the host side of the pass: at planning time, before a captured level runs)."""
+        t = torch.tensor([int(tokens)], dtype=torch.int64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+        return int(t.item())
+
+    def combine_static(self, partials, row_index):
+        """partials fp32 [W*S, H] in the received blocks' order -> (the owner's partials fp32 [W*S, H] in the order it
+        sent them, row_index [S, W]): one all_to_all_single with equal splits."""
+        back = torch.empty_like(partials)
+        dist.all_to_all_single(back, partials.contiguous(), group=self.group)
+        return back, row_index
 
     def combine(self, partials, handle):
         """partials fp32 [R, H] of the received rows -> (the owner's partials fp32 [n_sent, H], row_index [S, W])."""

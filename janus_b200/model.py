@@ -169,7 +169,10 @@ class DecisionReadout:
         """The expert-parallel MoE block (janus_b200/ep.py): dispatch rows to the ranks owning their experts, grouped
         GEMMs over this rank's experts, fp32 partial per received row, combine on the owner with the shared expert."""
         k, ep = self.shape.top_k, self.ep
-        (rows, slot_e, slot_w), handle = ep.dispatch(y, topk_idx, topk_w)
+        if ep.static:  # fixed shapes, no host read: the capturable exchange, blocks of the level's agreed capacity
+            (rows, slot_e, slot_w), handle = ep.dispatch_static(y, topk_idx, topk_w, self._ep_capacity)
+        else:
+            (rows, slot_e, slot_w), handle = ep.dispatch(y, topk_idx, topk_w)
         H = y.shape[1]
         if rows.shape[0]:
             plan = ops.moe_plan(slot_e, ep.local)
@@ -180,7 +183,7 @@ class DecisionReadout:
             part = torch.empty(0, H, dtype=torch.float32, device=y.device)
         shared = F.linear(ops.silu_mul(F.linear(y, L.shared_gate_up)), L.shared_down)
         sg = torch.mm(y, L.shared_gate.t(), out_dtype=torch.float32)
-        back, row_index = ep.combine(part, handle)
+        back, row_index = ep.combine_static(part, handle) if ep.static else ep.combine(part, handle)
         return ops.moe_combine_ep(back, row_index, shared, sg.reshape(-1))
 
     def _experts(self, x, L, plan, gated, k, topk_w=None):
@@ -242,6 +245,8 @@ class DecisionReadout:
         levels, readout = self.plan(packs)
         plan = DevicePlan(levels, readout, self.device, tile_tokens=(self.tile_tokens,))
         plan.prefix_history = None if prefixes is None else self._prefix_history(packs, levels, readout, prefixes)
+        if self.ep is not None and self.ep.static:  # the static exchange's block size per level, agreed by the group
+            plan.ep_capacity = {lv.depth: self.ep.agree_capacity(lv.T, self.device) for lv in levels}
         return levels, readout, plan
 
     def encode_prefixes(self, packs):
@@ -256,6 +261,8 @@ class DecisionReadout:
         self._readout = readout
         logits = torch.zeros(readout.n_slots, dtype=torch.float32, device=self.device)
         self.status.zero_()
+        self._ep_capacity = (self.ep.agree_capacity(lv.T, self.device)
+                             if self.ep is not None and self.ep.static else None)
         kept = self._level(dataclasses.replace(lv, keep=True), plan, [], logits)
         self.check_status()
         attention = [L.kind != LINEAR for L in self.layers]
@@ -308,6 +315,7 @@ class DecisionReadout:
         if prefix is not None:  # every pack's state level comes from a snapshot: start at level 1
             history.append(prefix)
         for lv in levels[len(history):]:
+            self._ep_capacity = getattr(plan, "ep_capacity", {}).get(lv.depth)
             history.append(self._level(lv, plan, history, logits))
         return logits
 

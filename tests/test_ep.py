@@ -68,9 +68,11 @@ def _rank_main(rank, world, port, scenario, queue):
         from oracle.hybrid import moe_block
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
         p = _weights()
-        ep = ExpertParallel(E)
+        static = scenario.startswith("static")
+        ep = ExpertParallel(E, static=static)
         gu, dn = ep.shard(p["experts.gate_up_proj"]), ep.shard(p["experts.down_proj"])
-        n_tok = {"basic": 37 + 11 * rank, "empty": 0 if rank == 1 else 23, "one_rank": 19}.get(scenario, 16)
+        n_tok = {"basic": 37 + 11 * rank, "empty": 0 if rank == 1 else 23, "one_rank": 19,
+                 "static": 37 + 11 * rank, "static_empty": 0 if rank == 1 else 23}.get(scenario, 16)
         x = torch.randn(n_tok, H, generator=torch.Generator().manual_seed(100 + rank))
         idx, w = _route(x, p)
         if scenario == "one_rank":  # every slot of rank 0's tokens on rank 1's experts and the reverse
@@ -78,10 +80,20 @@ def _rank_main(rank, world, port, scenario, queue):
         if scenario == "dead_peer" and rank == 1:
             queue.put((rank, "left"))
             return  # leaves before the collective; the process group is never joined again
-        (rows, se, sw), handle = ep.dispatch(x, idx, w)
-        part = _local_experts(rows, se, sw, gu, dn)
-        back, row_index = ep.combine(part, handle)
-        routed = sum_partials(back, row_index)
+        if static:
+            cap = ep.agree_capacity(n_tok, "cpu")  # the same block size on both ranks
+            (rows, se, sw), row_index = ep.dispatch_static(x, idx, w, cap)
+            assert rows.shape[0] == ep.world * cap
+            part = _local_experts(rows, se, sw, gu, dn)
+            back, row_index = ep.combine_static(part, row_index)
+            routed = sum_partials(back, row_index)
+            sent = int((row_index >= 0).sum())
+        else:
+            (rows, se, sw), handle = ep.dispatch(x, idx, w)
+            part = _local_experts(rows, se, sw, gu, dn)
+            back, row_index = ep.combine(part, handle)
+            routed = sum_partials(back, row_index)
+            sent = sum(handle[0])
         if scenario == "one_rank":
             ref = torch.zeros(n_tok, H)
             for j in range(K):
@@ -99,7 +111,7 @@ def _rank_main(rank, world, port, scenario, queue):
             err = float((got - ref).abs().max()) if n_tok else 0.0
         # one row per (token, rank owning any of its experts): deduplicated per rank, not per expert
         pairs = {(t, int(e) // ep.local) for t in range(n_tok) for e in idx[t].tolist()}
-        queue.put((rank, ("ok", err, sum(handle[0]), len(pairs))))
+        queue.put((rank, ("ok", err, sent, len(pairs))))
         dist.destroy_process_group()
     except Exception as e:  # reported to the parent, which asserts on it
         queue.put((rank, ("error", type(e).__name__, str(e)[:200], traceback.format_exc()[-400:])))
@@ -125,7 +137,7 @@ def _run(scenario, world=2, timeout=60):
     return results
 
 
-@pytest.mark.parametrize("scenario", ["basic", "empty", "one_rank"])
+@pytest.mark.parametrize("scenario", ["basic", "empty", "one_rank", "static", "static_empty"])
 def test_expert_parallel_matches_single_process(scenario):
     """Equal to the oracle's MoE block with all experts; a token is sent once per rank owning any of its experts."""
     res = _run(scenario)

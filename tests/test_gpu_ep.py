@@ -38,13 +38,16 @@ def _rank_main(rank, world, port, queue):
         for name in CASES:
             case = cases[name]
             shape, weights, mode, packs = case_model(case)
-            ep = ExpertParallel(shape.experts)
-            probs = DecisionReadout(shape, weights, mode, device=dev, ep=ep).probabilities(packs)
-            single = DecisionReadout(shape, weights, mode, device=dev).probabilities(packs)
-            ref_dev = max(float(np.abs(g.numpy() - np.array(r)).max())
-                          for gp, rp in zip(probs, case["probs"]) for g, r in zip(gp, rp))
-            single_dev = max(float((g - s).abs().max()) for gp, sp in zip(probs, single) for g, s in zip(gp, sp))
-            out[name] = (ref_dev, single_dev, case["bf16_max_dev"])
+            # each rank serves its own requests (rank 1 a shorter batch): the level sizes differ across ranks
+            mine = packs if rank == 0 else packs[:1]
+            single = DecisionReadout(shape, weights, mode, device=dev).probabilities(mine)
+            for static in (False, True):
+                ep = ExpertParallel(shape.experts, static=static)
+                probs = DecisionReadout(shape, weights, mode, device=dev, ep=ep).probabilities(mine)
+                ref_dev = max(float(np.abs(g.numpy() - np.array(r)).max())
+                              for gp, rp in zip(probs, case["probs"]) for g, r in zip(gp, rp))
+                single_dev = max(float((g - s).abs().max()) for gp, sp in zip(probs, single) for g, s in zip(gp, sp))
+                out[(name, static)] = (ref_dev, single_dev, case["bf16_max_dev"])
         queue.put((rank, ("ok", out)))
         dist.barrier()
         dist.destroy_process_group()
@@ -73,7 +76,7 @@ def test_expert_parallel_readout_matches_reference_and_single_gpu():
     for rank, r in res.items():
         assert r[0] == "ok", r
         for name, (ref_dev, single_dev, floor) in r[1].items():
-            print(f"rank {rank} {name}: |p_ep - p_ref| {ref_dev:.2e} (tolerance {max(2e-3, 2 * floor):.2e}), "
+            print(f"rank {rank} {name}: |p_ep - p_ref| {ref_dev:.2e} (tolerance {max(2e-3, 1.5 * floor):.2e}), "
                   f"|p_ep - p_1gpu| {single_dev:.2e}")
-            assert ref_dev <= max(2e-3, 2 * floor), (rank, name, ref_dev)
+            assert ref_dev <= max(2e-3, 1.5 * floor), (rank, name, ref_dev)
             assert single_dev <= 2e-3, (rank, name, single_dev)
