@@ -18,6 +18,9 @@ and the combine per step, each timed with CUDA events, TFLOP/s of the grouped GE
 `--op prefix` times the same batch with every state a prefix-cache hit: the states are encoded once into
 snapshots (DecisionReadout.encode_prefixes) and each step runs the branch levels only.
 
+`--op a3b [--ep]` runs workload 5 (the 35B-A3B shape, 40 layers, 8 requests of a 16384-token state per GPU), as
+replicas or expert parallel over the torchrun group.
+
 `--impl reference` times the reference algorithm on the host cores instead: the CPU oracle (oracle/hybrid.py, a
 restatement of the reference's readout pinned to its golden outputs) on one request of the same workload, each
 step through one 4-layer block of the model (3 DeltaNet + 1 attention layer, every level; the model is 8 such
@@ -387,6 +390,67 @@ def run_gemm(args):
                       "l2": "256 MiB written between launches"}))
 
 
+def run_a3b(args):
+    """Workload 5: the 35B-A3B shape at full depth (40 layers, 256 experts of FFN 512, top-8, int4 group-128 experts),
+    8 requests of a 16384-token state with 8 questions of 4 options per GPU. `--ep`: expert parallel over the
+    torchrun group (each rank keeps 256 / N experts; the capturable static exchange, `janus_b200/ep.py`), otherwise
+    one replica per GPU (all experts on every GPU: 16.6 GB of int4). One step = one readout of the rank's batch;
+    `value` = requests/s over all ranks, the step time the max over ranks; weights random (seeded, generated on the
+    device), requests seeded synthetic token ids."""
+    import datetime
+    import torch.distributed as dist
+    from janus_b200 import synthetic
+    from janus_b200.config import SHAPES
+    from janus_b200.ep import ExpertParallel
+    from janus_b200.model import DecisionReadout
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+    shape = SHAPES["35b-a3b"]
+    if args.layers:
+        shape = shape.with_layers(args.layers)
+    ep = ExpertParallel(shape.experts, static=True) if (args.ep and world > 1) else None
+    weights = synthetic.make_weights(shape, seed=0, head="scalar", device=device)
+    model = DecisionReadout(shape, weights, "tree", device=device, ep=ep)
+    del weights
+    torch.cuda.empty_cache()
+    n_req = args.requests if args.requests != REQUESTS_PER_GPU else 8
+    packs = [synthetic.a3b_request(seed=1000 * rank + j) for j in range(n_req)]
+    prepared = model.prepare(packs)
+    for _ in range(args.warmup):
+        model.run(prepared)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    ev = []
+    for _ in range(args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        model.run(prepared)
+        b.record()
+        ev.append((a, b))
+    torch.cuda.synchronize()
+    model.check_status()
+    total = sum(a.elapsed_time(b) for a, b in ev)
+    if world > 1:
+        t = torch.tensor([total], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total = float(t.item())
+    ms = total / args.steps
+    if rank == 0:
+        print(json.dumps({
+            "metric": "decision requests/s (35B-A3B shape, 16K state, 8 questions)", "value": world * n_req / (ms / 1e3),
+            "unit": "requests/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "config": {"workload": "a3b-tree-16k-state-8q" + (f"-{args.layers}layers-INVALID" if args.layers else ""),
+                       "requests_per_gpu": n_req, "tokens_per_gpu": sum(p.token_count for p in packs),
+                       "parallelism": f"ep{world} (static exchange)" if ep is not None else f"dp{world} (replicas)",
+                       "experts": "int4 group 128"}}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def run_prefix(args):
     """Repeated states (a prefix-cache hit for every request): the state level of the 16 requests is encoded once
     into snapshots; each timed step then runs the branch levels only, from the snapshots. A side line for the
@@ -439,7 +503,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--latency-requests", type=int, default=8, help="single requests timed one at a time")
     ap.add_argument("--layers", type=int, default=0, help="debug: fewer layers (not a valid bench number)")
-    ap.add_argument("--op", default="readout", choices=["readout", "moe", "prefix", "gemm"])
+    ap.add_argument("--op", default="readout", choices=["readout", "moe", "prefix", "gemm", "a3b"])
+    ap.add_argument("--ep", action="store_true", help="--op a3b: expert parallel over the torchrun group")
     ap.add_argument("--gemm-tokens", type=int, default=131072)
     ap.add_argument("--moe-tokens", type=int, default=131072)
     ap.add_argument("--moe-format", default="int4", choices=["int4", "nvfp4"])
@@ -455,6 +520,9 @@ def main():
         return
     if args.op == "gemm":
         run_gemm(args)
+        return
+    if args.op == "a3b":
+        run_a3b(args)
         return
     if args.impl == "reference":
         run_reference(args)
