@@ -113,6 +113,17 @@ int janus_b200_gdn_chunk_scan(const void* q, const void* k, const void* v, const
 /* Workspace bytes janus_b200_gdn_chunk_scan needs for T tokens, n_chunks chunks and Hv value heads. */
 size_t janus_b200_gdn_chunk_scan_workspace(int64_t T, int64_t n_chunks, int64_t Hv);
 
+/* The same chunked rule in one launch, for rows without segments: one CTA per (row, value head) computes chunk
+ * c+1's WY products (the prep above) while the state pass runs chunk c, handing W, U, QK and G over in shared memory
+ * (no workspace, nothing of the prep through HBM). Arguments as janus_b200_gdn_chunk_scan without segment and
+ * workspace; outputs and states bit-identical to it.
+ * Replaces fla chunk_gated_delta_rule (janus/hybrid.py:100-125, 1064-1069) on the state level's long rows. */
+int janus_b200_gdn_chunk_scan_fused(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                                    int64_t T, int64_t B, const int32_t* row_start, const int32_t* chunk_start,
+                                    int64_t n_chunks, const float* state_in, const int32_t* state_row,
+                                    float* state_out, int64_t Hk, int64_t Hv, int64_t Dk, int64_t Dv, float scale,
+                                    void* o, int32_t* status, void* stream);
+
 /* Attention q/k preparation: per head RMSNorm (1 + w) of q and k, rotary on the first `rot` dims (cos/sin of
  * positions[t] * inv_freq[i], fp32), v copied. qkv: bf16 rows of stride qkv_stride with columns
  * [per q head: query D | gate D] (Hq*2D) | k Hkv*D | v Hkv*D]. Outputs q bf16 [T, Hq, D], k, v bf16 [T, Hkv, D].

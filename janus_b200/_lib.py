@@ -27,6 +27,9 @@ SIGNATURES = {
                                   c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                   c_int64, c_float, c_void_p, c_size_t, c_void_p, c_void_p, c_void_p],
     "janus_b200_gdn_chunk_scan_workspace": [c_int64, c_int64, c_int64],
+    "janus_b200_gdn_chunk_scan_fused": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
+                                        c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                        c_int64, c_float, c_void_p, c_void_p, c_void_p],
     "janus_b200_attn_qk_prep": [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float,
                                 c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p],
     "janus_b200_tree_attention": [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p,

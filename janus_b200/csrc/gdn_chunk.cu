@@ -349,16 +349,17 @@ __global__ void __launch_bounds__(256, 3) gdn_chunk_prep_kernel(const __grid_con
   __syncthreads();
   // the beta and beta e^G factors of the tokens go on T's columns (rather than on V's and K's rows): T1, T2 bf16 in
   // the swizzled K-major layout (B operands of the U, W products)
-  for (int x = tid; x < CT * CT / 2; x += 256) {
-    const int i = x >> 5, j = (x & 31) * 2;
-    float tv[2];
+  {
+    const int j = (tid & 31) * 2, i0 = tid >> 5;  // thread: columns j, j+1 of rows i0, i0 + 8, ... (loads in flight together)
+    const float b0 = sBeta[j], b1 = sBeta[j + 1], e0 = seG[j], e1 = seG[j + 1];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const float t = sTF[i * PADF + j + u] * sBeta[j + u];
-      tv[u] = (j + u <= i) ? t : 0.f;
+    for (int it = 0; it < CT / 8; ++it) {
+      const int i = i0 + 8 * it;
+      const float2 t = *reinterpret_cast<const float2*>(&sTF[i * PADF + j]);
+      const float v0 = (j <= i) ? t.x * b0 : 0.f, v1 = (j + 1 <= i) ? t.y * b1 : 0.f;
+      *reinterpret_cast<uint32_t*>(base + kOffT1 + swz(i, j)) = tcx::pack_bf16(v0, v1);
+      *reinterpret_cast<uint32_t*>(base + kOffT2 + swz(i, j)) = tcx::pack_bf16(v0 * e0, v1 * e1);
     }
-    *reinterpret_cast<uint32_t*>(base + kOffT1 + swz(i, j)) = tcx::pack_bf16(tv[0], tv[1]);
-    *reinterpret_cast<uint32_t*>(base + kOffT2 + swz(i, j)) = tcx::pack_bf16(tv[0] * seG[j], tv[1] * seG[j + 1]);
   }
   tcx::fence_async_smem();
   tcx::fence_before();

@@ -290,12 +290,26 @@ __global__ void __launch_bounds__(NT, 1) gdn_state_tc_kernel(const __grid_consta
     for (int i = 0; i < nch && ok; ++i) {
       const int st = i & 1;
       unsigned char* stage = base + st * kStage;
-      const int64_t t0 = r0 + (int64_t)i * CT;
-      const int nt = (r1 - t0) < CT ? (int)(r1 - t0) : CT;
       ok = vand(wait_bar(&bars.full[st], (i >> 1) & 1, p.err));
       if (!ok) break;
       chunk_factors(reinterpret_cast<const float*>(stage + sG), p.scale, s_fq[st], s_fk, &s_dl, v);
       vsync();
+      // the state decays by e^(G_last) before the update accumulates onto it, while VT = S^T W^T runs (the
+      // products read the bf16 copy, not ST); a decay that underflowed to 0 (a fast-forgetting head: G_last < -103)
+      // leaves nothing of the state, and the update MMA overwrites it instead
+      const float dl = s_dl;
+      if (dl != 0.f) {
+#pragma unroll 1
+        for (int k0 = 0; k0 < DH; k0 += 64) {
+          float f[64];
+          tld64f(la + cST + k0, f);
+          uint32_t w[64];
+#pragma unroll
+          for (int e = 0; e < 64; ++e) w[e] = __float_as_uint(f[e] * dl);
+          tst32(la + cST + k0, w);
+          tst32(la + cST + k0 + 32, w + 32);
+        }
+      }
       ok = vand(wait_bar(&bars.vt_done, i & 1, p.err));
       if (!ok) break;
       fence_after();
@@ -324,21 +338,6 @@ __global__ void __launch_bounds__(NT, 1) gdn_state_tc_kernel(const __grid_consta
         }
         tst32(la + cVB, vb);
         tst32(la + cVD, vd);
-      }
-      // the state decays by e^(G_last) before the update accumulates onto it; a decay that underflowed to 0 (a
-      // fast-forgetting head: G_last < -103) leaves nothing of the state, and the update MMA overwrites it instead
-      const float dl = s_dl;
-      if (dl != 0.f) {
-#pragma unroll 1
-        for (int k0 = 0; k0 < DH; k0 += 64) {
-          float f[64];
-          tld64f(la + cST + k0, f);
-          uint32_t w[64];
-#pragma unroll
-          for (int e = 0; e < 64; ++e) w[e] = __float_as_uint(f[e] * dl);
-          tst32(la + cST + k0, w);
-          tst32(la + cST + k0 + 32, w + 32);
-        }
       }
       tst_wait();
       fence_before();

@@ -162,11 +162,16 @@ def gdn_fork_recurrent(q, k, v, g, beta, row_start, child_start, state_in, keep_
 
 @_instrument("gdn_chunk_scan", 2)
 def gdn_chunk_scan(q, k, v, g, beta, row_start, chunk_start, n_chunks, state_in, state_row, keep_state, scale,
-                   status=None, segment=None):
+                   status=None, segment=None, fused=None):
     """Long rows in 64-token chunks; row b starts from state_in[state_row[b]] (None: zeros / identity map).
     chunk_start int32 [B+1] (first chunk of each row), n_chunks = chunk_start[B]. status: optional device int32
     word set to 1 if a bounded device-side wait ran out. segment: optional int32 [T] ids of token segments that do
-    not interact, each starting from the row's initial state (rows of at most 64 tokens, no kept state)."""
+    not interact, each starting from the row's initial state (rows of at most 64 tokens, no kept state).
+    fused: True runs the one-launch form (janus_b200_gdn_chunk_scan_fused: the prep of chunk c+1 under the state
+    pass of chunk c, nothing through HBM), False or None the two-launch form (prep over all chunks in parallel into
+    a workspace, then the state pass); the two give bit-identical results. The two-launch form is the faster one on
+    every measured shape (the prep's latency chain per chunk is about 3.5x the state pass's, and only the parallel
+    prep over all chunks hides it), so it is the default."""
     if segment is not None:
         _need(segment, I32, "segment")
         if keep_state:
@@ -183,6 +188,15 @@ def gdn_chunk_scan(q, k, v, g, beta, row_start, chunk_start, n_chunks, state_in,
     for t, n in ((q, "q"), (k, "k"), (v, "v")):
         _need(t, BF16, n)
     lib = _lib.load()
+    if fused:
+        if segment is not None:
+            raise ValueError("gdn_chunk_scan: the one-launch form takes no segments")
+        _lib.check(lib.janus_b200_gdn_chunk_scan_fused(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(_need(g, F32, "g")), _ptr(_need(beta, F32, "beta")), T, B,
+            _ptr(_need(row_start, I32, "row_start")), _ptr(_need(chunk_start, I32, "chunk_start")), n_chunks,
+            _ptr(state_in), _ptr(state_row), _ptr(state_out), Hk, Hv, Dk, Dv, scale, _ptr(o), _ptr(status),
+            _stream(q)), "gdn_chunk_scan_fused")
+        return o, state_out
     nbytes = lib.janus_b200_gdn_chunk_scan_workspace(T, n_chunks, Hv)
     ws = torch.empty(max(1, nbytes), dtype=torch.uint8, device=q.device)
     _lib.check(lib.janus_b200_gdn_chunk_scan(

@@ -288,6 +288,42 @@ def test_gdn_chunk_scan_matches_recurrent_oracle():
     close(o2[a:b], ro, atol=3e-2, rtol=3e-2)
 
 
+def test_gdn_chunk_scan_one_launch_equals_two_launch():
+    """The one-launch chunk scan (prep of chunk c+1 under the state pass of chunk c, hand-over in shared memory) and
+    the two-launch form (prep into an HBM workspace, then the state pass) compute the same products with the same
+    roundings: outputs and kept states bit-identical. Rows of 0, 1, 63, 64, 65, 129, 300 and 2000 tokens, initial
+    states through state_row, fast- and slow-forgetting heads; then the same without initial states."""
+    ops = _ops()
+    Hk, Hv, D = 16, 32, 128
+    g = torch.Generator().manual_seed(17)
+    lengths = [0, 1, 63, 64, 65, 129, 300, 2000, 0, 77]
+    rs = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32))
+    T = int(rs[-1])
+    q = oracle.l2norm(torch.randn(T, Hk, D, generator=g)).to(BF).cuda()
+    k = oracle.l2norm(torch.randn(T, Hk, D, generator=g)).to(BF).cuda()
+    v = torch.randn(T, Hv, D, generator=g).to(BF).cuda()
+    A = torch.exp(torch.linspace(np.log(1e-3), np.log(16.0), Hv))
+    gg = (-A * torch.nn.functional.softplus(torch.randn(T, Hv, generator=g) + 1.0)).cuda()
+    beta = torch.sigmoid(torch.randn(T, Hv, generator=g)).cuda()
+    S0 = (torch.randn(3, Hv, D, D, generator=g) * 0.1).cuda()
+    state_row = torch.tensor([2, 1, 0, 1, 2, 0, 1, 2, 0, 1], dtype=torch.int32).cuda()
+    cs = torch.tensor(np.concatenate([[0], np.cumsum([(n + 63) // 64 for n in lengths])]).astype(np.int32)).cuda()
+    nc = int(cs[-1].item())
+    for s_in, s_row in ((S0, state_row), (None, None)):
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        o1, S1 = ops.gdn_chunk_scan(q, k, v, gg, beta, rs.cuda(), cs, nc, s_in, s_row, True, D ** -0.5,
+                                    status=status, fused=True)
+        o2, S2 = ops.gdn_chunk_scan(q, k, v, gg, beta, rs.cuda(), cs, nc, s_in, s_row, True, D ** -0.5,
+                                    status=status, fused=False)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        assert torch.equal(o1, o2), float((o1.float() - o2.float()).abs().max())
+        assert torch.equal(S1, S2), float((S1 - S2).abs().max())
+        for r, n in enumerate(lengths):  # empty rows keep their initial state
+            if n == 0:
+                assert torch.equal(S1[r], s_in[int(s_row[r])] if s_in is not None else torch.zeros_like(S1[r]))
+
+
 def test_device_wait_that_runs_out_is_reported_and_the_context_survives():
     """The bounded mbarrier wait of the tcgen05 kernels: a phase nothing completes ends in status 1 after ~1 s,
     not in a hang or a fault, and the next launch on the same context works."""
