@@ -140,7 +140,9 @@ int janus_b200_attn_qk_prep(const void* qkv, int64_t qkv_stride, int64_t T, cons
  * (level_tokens[n_levels-1] == T). tiles: [n_tiles, 2] query token ranges [start, end) of at most
  * janus_b200_tree_attention_tile_tokens(D, Hq, Hkv) tokens, each within one request (janus_b200 python builds them).
  * gate: bf16, token t head h at gate[t*gate_stride + h*gate_head_stride + d]. out bf16 [T, Hq*D]. D in
- * {32, 64, 128, 256}; 128 and 256 run on tcgen05 with TMEM accumulators, 32 and 64 on mma.sync. status: optional
+ * {32, 64, 128, 256}; 128 and 256 run on tcgen05 with TMEM accumulators (one CTA per query tile; with
+ * JANUS_B200_ATTN=pairs in the environment, on CTA pairs sharing each K/V block, the slower form on B200), 32 and 64
+ * on mma.sync. status: optional
  * device int32, zero on entry, set to 1 if a bounded device-side wait ran out (after 1 s; the output is then invalid;
  * the other CTAs see the word and give up at once); NULL: not reported.
  * Replaces branch_attention / state_attention / _piece / _merge_gate (janus/hybrid.py:806-855, 943-989) and the

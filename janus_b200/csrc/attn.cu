@@ -11,6 +11,9 @@
 // ancestor level is the union of its tokens' ranges (the caller keeps tiles inside one request, so the union is one
 // ancestor row or a few adjacent short ones); keys outside a token's own range are masked. K/V tiles of 64 keys are
 // double-buffered with cp.async in XOR-swizzled shared memory; the sigmoid output gate is applied in the epilogue.
+#include <stdlib.h>
+#include <string.h>
+
 #include "common.cuh"
 
 namespace jb {
@@ -457,7 +460,21 @@ int tree_attention_tc(const void* q, int64_t Hq, int64_t Hkv, int64_t D, int32_t
                       const void* gate, int64_t gate_stride, int64_t gate_head_stride, float scale, void* out,
                       int32_t* err, cudaStream_t stream);
 
+int tree_attention_pair(const void* q, int64_t Hq, int64_t Hkv, int64_t D, int32_t n_levels,
+                        const void* const* k_levels, const void* const* v_levels, const int64_t* level_tokens,
+                        const int32_t* const* anc_lo, const int32_t* const* anc_hi, const int32_t* row_start,
+                        const int32_t* row_of_token, const int32_t* tiles, int64_t n_tiles, const void* gate,
+                        int64_t gate_stride, int64_t gate_head_stride, float scale, void* out, int32_t* err,
+                        cudaStream_t stream);
+
 int wait_timeout_selftest(int32_t* status, cudaStream_t stream);
+
+// Which tcgen05 form runs head dims 128 and 256: single CTAs (the default, the faster one on B200) or CTA pairs
+// (JANUS_B200_ATTN=pairs in the environment at the call; for comparisons of the two)
+static bool attn_pairs() {
+  const char* v = getenv("JANUS_B200_ATTN");
+  return v && strcmp(v, "pairs") == 0;
+}
 
 }  // namespace jb
 
@@ -551,6 +568,10 @@ extern "C" int janus_b200_tree_attention(const void* q, int64_t T, int64_t Hq, i
   p.scale_log2 = scale * 1.4426950408889634f;
   if (n_tiles == 0 || T == 0) return JANUS_OK;
   cudaStream_t s = (cudaStream_t)stream;
+  if ((D == 128 || D == 256) && 128 % G == 0 && attn_pairs())
+    return tree_attention_pair(q, Hq, Hkv, D, n_levels, k_levels, v_levels, level_tokens, anc_lo, anc_hi, row_start,
+                               row_of_token, tiles, n_tiles, gate, gate_stride, gate_head_stride, scale, out, status,
+                               s);
   if ((D == 128 || D == 256) && 128 % G == 0)
     return tree_attention_tc(q, Hq, Hkv, D, n_levels, k_levels, v_levels, level_tokens, anc_lo, anc_hi, row_start,
                              row_of_token, tiles, n_tiles, gate, gate_stride, gate_head_stride, scale, out, status, s);

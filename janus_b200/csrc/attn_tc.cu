@@ -36,7 +36,8 @@ constexpr int kMaxLevels = 4;
 constexpr int kSlots = 5;                         // K/V ring slots
 constexpr uint32_t kSlotBytes = BN * 128 * 2;     // 128 keys x 128 head dims (two [128 keys][64 dims] TMA boxes)
 constexpr uint32_t kBoxBytes = BN * 128;          // one [128 keys][64 dims] box: 16 KB
-constexpr int kItemBars = 6;                      // > the K/V items in flight (at most kSlots)
+constexpr int kItemBars = 9;                      // >= the K/V items in flight (at most kSlots) + 4: the V
+                                                  // items' issuer trails the K items' by up to two items
 constexpr uint32_t kColO = 0, kColS = 256, kColQ = 384, kTmemCols = 512;
 
 struct Params {

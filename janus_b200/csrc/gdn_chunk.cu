@@ -23,6 +23,7 @@
 // The prep writes W, QK and G chunk-major ([chunk][value head][64 tokens], zeros past a row's end) and U transposed
 // ([chunk][value head][128 value columns][64 tokens], the rows the sequential pass's value threads read) for the
 // sequential pass's TMA loads.
+#include "gdn_inverse.cuh"
 #include "tcgen05.cuh"
 
 namespace jb {
@@ -234,10 +235,24 @@ __global__ void __launch_bounds__(256, 3) gdn_chunk_prep_kernel(const __grid_con
     const int qw = warp & 3, j0 = (warp >> 2) * 32;
     const int i = 32 * (qw & 1) + lane;
     const uint32_t la = tm + ((uint32_t)(32 * qw) << 16) + j0;
+    // rows 0-31 against columns 32-63 lie wholly above the diagonal: both masks are zero there (warps 4 and 6)
+    const bool none = (qw & 1) == 0 && j0 == 32;
     float d[32];
-    tcx::tld16f(la, d);
-    tcx::tld16f(la + 16, d + 16);
-    if (done) {
+    if (!none) {
+      tcx::tld16f(la, d);
+      tcx::tld16f(la + 16, d + 16);
+    }
+    if (done && none) {
+      if (qw < 2) {
+#pragma unroll
+        for (int x = 0; x < 32; x += 4) *reinterpret_cast<float4*>(&sN[i * PADF + j0 + x]) = make_float4(0, 0, 0, 0);
+      } else {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          *reinterpret_cast<uint4*>(base + kOffKQ + 8192 + swz(i, j0 + 8 * u)) = make_uint4(0, 0, 0, 0);
+        tcx::fence_async_smem();
+      }
+    } else if (done) {
       const float Gi = sG[i];
       const int si = sSeg[i];
       if (qw < 2) {
@@ -282,25 +297,7 @@ __global__ void __launch_bounds__(256, 3) gdn_chunk_prep_kernel(const __grid_con
   }
   // T = (I - N)^-1: diagonal 16x16 blocks (warps 0-3, lane c < 16 owns column c)
   if (warp < 4) {
-    const int bs = warp * 16;
-    const int cc = lane & 15;
-    float col[16];
-#pragma unroll
-    for (int r = 0; r < 16; ++r) col[r] = (r == cc) ? 1.f : 0.f;
-#pragma unroll
-    for (int r = 1; r < 16; ++r) {
-      float acc = 0.f;
-#pragma unroll
-      for (int m = 0; m < r; ++m) {  // m < r is known at compile time; the lane condition is a select
-        const float nm = sN[(bs + r) * PADF + bs + m];
-        acc += (m >= cc) ? nm * col[m] : 0.f;
-      }
-      col[r] = (cc < r) ? acc : col[r];
-    }
-    if (lane < 16) {
-#pragma unroll
-      for (int r = 0; r < 16; ++r) sTF[(bs + r) * PADF + bs + cc] = col[r];
-    }
+    diag_inverse16<PADF>(sN, sTF, warp * 16, lane);
   } else {  // zeros above the block diagonal that the full-length sums below read: T[0:16, 16:32], T[32:48, 48:64]
     for (int x = tid - 128; x < 512; x += 128) {
       const int blk = x >> 8, r = (x >> 4) & 15, cc = x & 15;

@@ -25,6 +25,7 @@
 // TMA, N, T, T diag(beta), T diag(beta e^G)). TMEM: the state pass's 384 columns and the prep's 128. Every hand-off
 // is an mbarrier with a bounded wait; a wait that runs out sets the status word and every role winds down (loads in
 // flight landed, MMAs drained, TMEM released).
+#include "gdn_inverse.cuh"
 #include "tcgen05.cuh"
 
 namespace jb {
@@ -296,8 +297,17 @@ __global__ void __launch_bounds__(NT, 1) gdn_scan_fused_kernel(const __grid_cons
       {
         const int ii = 32 * (pw & 1) + lane;
         const float Gi = sG[ii];
+        if (!(pw & 1)) {  // rows 0-31 against columns 32-63 lie wholly above the diagonal: both masks are zero
+          if (pw < 2) {
+#pragma unroll
+            for (int x = 32; x < CT; x += 4) *reinterpret_cast<float4*>(&sN[ii * PADF + x]) = make_float4(0, 0, 0, 0);
+          } else {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) *reinterpret_cast<uint4*>(stg + oQK + swz(ii, 32 + 8 * u)) = make_uint4(0, 0, 0, 0);
+          }
+        }
 #pragma unroll 1
-        for (int j0 = 0; j0 < CT; j0 += 32) {
+        for (int j0 = 0; j0 < ((pw & 1) ? CT : 32); j0 += 32) {
           float d[32];
           tld16f(la + j0, d);
           tld16f(la + j0 + 16, d + 16);
@@ -341,27 +351,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_scan_fused_kernel(const __grid_cons
         sTF[(blk * 32 + r) * PADF + blk * 32 + 16 + cc] = 0.f;
       }
       psync();  // N complete
-      {
-        const int bs = pw * 16;
-        const int cc = lane & 15;
-        float col[16];
-#pragma unroll
-        for (int r = 0; r < 16; ++r) col[r] = (r == cc) ? 1.f : 0.f;
-#pragma unroll
-        for (int r = 1; r < 16; ++r) {
-          float acc = 0.f;
-#pragma unroll
-          for (int m = 0; m < r; ++m) {
-            const float nm = sN[(bs + r) * PADF + bs + m];
-            acc += (m >= cc) ? nm * col[m] : 0.f;
-          }
-          col[r] = (cc < r) ? acc : col[r];
-        }
-        if (lane < 16) {
-#pragma unroll
-          for (int r = 0; r < 16; ++r) sTF[(bs + r) * PADF + bs + cc] = col[r];
-        }
-      }
+      diag_inverse16<PADF>(sN, sTF, pw * 16, lane);
       psync();
       // stage 1: T[2b+1, 2b] = T[2b+1, 2b+1] N[2b+1, 2b] T[2b, 2b] (16x16 blocks, tf32; warp: block b = w >> 1,
       // 8 columns (w & 1) * 8)

@@ -176,11 +176,14 @@ def test_attn_qk_prep(shape):
     close(v, f[:, Hq * 2 * D + Hkv * D:].view(T, Hkv, D), atol=0, rtol=0)
 
 
+@pytest.mark.parametrize("form", ["pairs", "single"])
 @pytest.mark.parametrize("heads", [(4, 2, 32), (16, 4, 256), (8, 2, 256), (16, 2, 256), (4, 4, 128), (8, 8, 256),
                                    (2, 1, 64)])
-def test_tree_attention_three_levels(heads):
+def test_tree_attention_three_levels(heads, form, monkeypatch):
     """A state level (2 requests), a block level and a leaf level; every query of the leaf level sees its state,
-    its block and its own leaf causally (janus/attention.py:10-23 along the path)."""
+    its block and its own leaf causally (janus/attention.py:10-23 along the path). Head dims 128 and 256 run on
+    single CTAs by default and on CTA pairs with JANUS_B200_ATTN=pairs; both are checked."""
+    monkeypatch.setenv("JANUS_B200_ATTN", form)
     ops = _ops()
     from janus_b200.plan import build_levels
     from janus_b200 import synthetic
@@ -215,6 +218,42 @@ def test_tree_attention_three_levels(heads):
             ref = oracle.attention(q[a:b].float(), k_all, v_all, k_all.shape[0] - (b - a), D ** -0.5)
             ref = ref * torch.sigmoid(gate[a:b].float())
             close(out[a:b], ref)
+
+
+@pytest.mark.parametrize("heads", [(16, 4, 256), (8, 8, 128), (16, 2, 128), (4, 4, 256)])
+def test_tree_attention_cta_pairs_match_single_ctas(heads, monkeypatch):
+    """The CTA-pair form against the single-CTA form on a three-level tree whose state rows have odd tile counts
+    (pairs that straddle two requests) and whose branch tiles pair blocks of different questions. A pair walks each
+    tile's keys plus blocks fully masked for it, and on the branch levels it may walk the union of two ancestor
+    ranges from an earlier first key, which groups the same keys into other blocks (fp32 sums in another order)."""
+    ops = _ops()
+    from janus_b200.plan import build_levels
+    from janus_b200 import synthetic
+    Hq, Hkv, D = heads
+    packs = [synthetic.q4b_request(vocab=4096, seed=s, state_tokens=n, questions=5, block_tokens=23)
+             for s, n in ((10, 1501), (11, 777), (12, 64))]
+    levels, _ = build_levels(packs)
+    g = torch.Generator().manual_seed(15)
+    K = [torch.randn(lv.T, Hkv, D, generator=g).to(BF).cuda() for lv in levels]
+    V = [torch.randn(lv.T, Hkv, D, generator=g).to(BF).cuda() for lv in levels]
+    cuda = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    for d, lv in enumerate(levels):
+        q = torch.randn(lv.T, Hq, D, generator=g).to(BF).cuda()
+        gate_buf = torch.randn(lv.T, Hq, 2 * D, generator=g).to(BF).cuda()
+        tiles = lv.attention_tiles(ops.tree_attention_tile_tokens(D, Hq, Hkv))
+        outs = {}
+        for form in ("pairs", "single"):
+            monkeypatch.setenv("JANUS_B200_ATTN", form)
+            status = torch.zeros(1, dtype=torch.int32, device="cuda")
+            outs[form] = ops.tree_attention(q, K[:d + 1], V[:d + 1], [cuda(x) for x in lv.anc_lo],
+                                            [cuda(x) for x in lv.anc_hi], cuda(lv.row_start), cuda(lv.row_of_token),
+                                            cuda(tiles), gate_buf[:, :, D:], D ** -0.5, status=status)
+            torch.cuda.synchronize()
+            assert int(status.item()) == 0, form
+        a, b = outs["pairs"].float(), outs["single"].float()
+        diff = (a - b).abs()
+        print(f"\nlevel {d}: max |pairs - single| {float(diff.max()):.2e}, equal {float((diff == 0).float().mean()):.4f}")
+        close(a, b, atol=1e-2, rtol=1e-2)
 
 
 def test_heads_match_oracle():
