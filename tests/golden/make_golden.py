@@ -123,11 +123,12 @@ def hf_model(shape, weights, dtype=torch.float32):
     return lm.to(dtype).eval()
 
 
-def reference_logits(shape, weights, mode, packs, dtype=torch.float32, grouped_branches=False):
+def reference_logits(shape, weights, mode, packs, dtype=torch.float32, grouped_branches=False, batch=None):
     """The reference readout. `grouped_branches`: the plain path's branch levels through `branch_attention` (pieces
     grouped by ancestor, bounded by PIECE_BYTES) instead of its one varlen call (`packed_attention`), whose CPU form
     masks every query against every gathered key: at 8192-token states that is tens of GB (the same softmax over the
-    same keys either way, janus/hybrid.py:864, 958-989)."""
+    same keys either way, janus/hybrid.py:864, 958-989). `batch`: requests per forward_many call (rows are
+    independent, so the split changes nothing but the peak host memory)."""
     sys.path.insert(0, REFERENCE)
     from janus import hybrid as ref_hybrid
     from janus.hybrid import HybridBackbone
@@ -156,8 +157,12 @@ def reference_logits(shape, weights, mode, packs, dtype=torch.float32, grouped_b
                       [RefBranch(b.start, b.end, b.question_index, b.option_indices, b.option_positions,
                                  b.decision_position, b.kind, b.leaves) for b in p.branches],
                       p.state_length, p.option_counts) for p in packs]
+    step = batch or len(refs)
+    out = []
     with torch.no_grad():
-        return model.forward_many(refs)
+        for i in range(0, len(refs), step):
+            out += model.forward_many(refs[i:i + step])
+    return out
 
 
 def pack_to_dict(p):
@@ -270,10 +275,11 @@ def main_argmax():
     packs = build_packs(specs)
     weights = synthetic.make_weights(shape, seed=a["seed"], head="scalar")
     flat = lambda per_pack: np.concatenate([np.asarray(z, dtype=np.float32) for per in per_pack for z in per])
-    logits = reference_logits(shape, weights, a["mode"], packs, grouped_branches=True)
+    logits = reference_logits(shape, weights, a["mode"], packs, grouped_branches=True, batch=8)
     p32 = [[torch.softmax(z.float(), -1).numpy() for z in per] for per in logits]
     p16 = [[torch.softmax(z.float(), -1).numpy() for z in per]
-           for per in reference_logits(shape, weights, a["mode"], packs, torch.bfloat16, grouped_branches=True)]
+           for per in reference_logits(shape, weights, a["mode"], packs, torch.bfloat16, grouped_branches=True,
+                                       batch=8)]
     po16 = oracle_probs(shape, weights, a["mode"], packs, "bf16")
     counts = np.array([len(z) for per in p32 for z in per], dtype=np.int32)
     np.savez_compressed(HERE / "argmax_4b.npz", spec=np.array(json.dumps(a)), counts=counts,
