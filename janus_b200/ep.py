@@ -113,7 +113,8 @@ class ExpertParallel:
             ids.index_copy_(0, idx, torch.where(dest == d, local_id, torch.full_like(local_id, -1)))
             wts.index_copy_(0, idx, w32)
         recv = torch.empty(W * C, H + meta, dtype=raw, device=dev)
-        dist.all_to_all_single(recv, buf[:W * C], group=self.group)
+        # as bytes: NCCL has no 16-bit integer type (the rows are raw bits either way)
+        dist.all_to_all_single(recv.view(torch.uint8), buf[:W * C].view(torch.uint8), group=self.group)
         row_index = torch.where(hit, flat, torch.full_like(flat, -1)).to(torch.int32)
         return ((recv[:, :H].view(x.dtype), recv[:, H:H + meta // 2].view(torch.int32).contiguous(),
                  recv[:, H + meta // 2:].view(torch.float32).contiguous()), row_index)
