@@ -91,13 +91,15 @@ constexpr uint32_t kOffVec = kOffTF + CT * PADF * 4;  // G, eG, beta, graw (fp32
 constexpr uint32_t kOffBar = kOffVec + 5 * CT * 4;
 constexpr uint32_t kPrepSmem = kOffBar + 32 + 1024;  // + alignment slack
 constexpr uint32_t kPrepTmemCols = 128;  // P1 (KK^T | QK^T) cols 0-63, then U^T cols 0-63 and W^T cols 64-127
+// after P2 the [K; Q] region holds the staged W (two [64 tokens][64 columns] boxes) and U^T ([128][64 tokens])
+constexpr uint32_t kOffWst = 0, kOffUst = 16384;
 static_assert(CT * PADF * 4 <= kOffTF - kOffNV && 32 * PADM * 4 <= 8192, "prep shared-memory regions");
 
 struct PrepParams {
   CUtensorMap qmap, kmap, vmap;       // [T][H][128] bf16 loads, boxes 64 dims x 1 head x 64 tokens
   CUtensorMap qkmap;                  // chunk-major QK store, boxes 64 x 64
-  __nv_bfloat16* Wg;                  // chunk-major [chunk][head][64 tokens][128]
-  __nv_bfloat16* Ug;
+  CUtensorMap wmap;                   // W store: chunk-major [chunk][head][64 tokens][128], boxes 64 x 64
+  CUtensorMap umap;                   // U^T store: [chunk][head][128 value columns][64 tokens], boxes 64 x 128
   const float* g;
   const float* beta;
   const int32_t* row_start;
@@ -130,6 +132,7 @@ __global__ void __launch_bounds__(256, 3) gdn_chunk_prep_kernel(const __grid_con
   float* seG = sG + CT;
   float* sBeta = sG + 2 * CT;
   float* sGraw = sG + 3 * CT;
+  float* sGl = sGraw;  // G log2(e), once the scan is done
   int32_t* sSeg = reinterpret_cast<int32_t*>(sG + 4 * CT);
   uint64_t* bar_load = reinterpret_cast<uint64_t*>(base + kOffBar);
   uint64_t* bar_mma = bar_load + 1;
@@ -222,6 +225,7 @@ __global__ void __launch_bounds__(256, 3) gdn_chunk_prep_kernel(const __grid_con
   __syncthreads();
   if (tid < CT) {
     seG[tid] = expf(sG[tid]);
+    sGl[tid] = sG[tid] * kLog2e;  // in the raw g's place (the scan has read it)
     p.Gg[(int64_t)rb + tid] = sG[tid];  // chunk-major; past the row's end G stays at G[nt - 1]
   }
   __syncthreads();
@@ -253,34 +257,43 @@ __global__ void __launch_bounds__(256, 3) gdn_chunk_prep_kernel(const __grid_con
         tcx::fence_async_smem();
       }
     } else if (done) {
-      const float Gi = sG[i];
+      // branch-free: the masks select (a divergent branch per element is slow); the segment compare only runs for a
+      // segmented scan; G log2(e) of the columns four at a time
+      const float gli = sGl[i];
       const int si = sSeg[i];
+      const bool segs = p.segment != nullptr;
+      const float4* gl4 = reinterpret_cast<const float4*>(sGl + j0);
+      const int4* sg4 = reinterpret_cast<const int4*>(sSeg + j0);
       if (qw < 2) {
         const float nb = -sBeta[i];
         float nv[32];
 #pragma unroll
-        for (int x = 0; x < 32; ++x) {  // branch-free: the mask selects (a divergent branch per element is slow)
-          const int j = j0 + x;
-          const bool m = (j < i) & (sSeg[j] == si);
-          const float val = nb * d[x] * __expf(fminf(Gi - sG[j], 0.f));
-          nv[x] = m ? val : 0.f;
+        for (int x = 0; x < 32; x += 4) {
+          const float4 g = gl4[x / 4];
+          const int4 sg = segs ? sg4[x / 4] : make_int4(si, si, si, si);
+          const float gj[4] = {g.x, g.y, g.z, g.w};
+          const int sj[4] = {sg.x, sg.y, sg.z, sg.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) nv[x + u] = n_entry(d[x + u], nb, gli, gj[u], (j0 + x + u < i) & (sj[u] == si));
         }
 #pragma unroll
         for (int x = 0; x < 32; x += 4)
           *reinterpret_cast<float4*>(&sN[i * PADF + j0 + x]) = make_float4(nv[x], nv[x + 1], nv[x + 2], nv[x + 3]);
       } else {
         uint32_t qv[16];
+        const bool il = i < nt;
 #pragma unroll
-        for (int x = 0; x < 32; x += 2) {
-          float e[2];
+        for (int x = 0; x < 32; x += 4) {
+          const float4 g = gl4[x / 4];
+          const int4 sg = segs ? sg4[x / 4] : make_int4(si, si, si, si);
+          const float gj[4] = {g.x, g.y, g.z, g.w};
+          const int sj[4] = {sg.x, sg.y, sg.z, sg.w};
+          float e[4];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int j = j0 + x + u;
-            const bool m = (j <= i) & (i < nt) & (sSeg[j] == si);
-            const float val = p.scale * d[x + u] * __expf(fminf(Gi - sG[j], 0.f));
-            e[u] = m ? val : 0.f;
-          }
+          for (int u = 0; u < 4; ++u)
+            e[u] = qk_entry(d[x + u], p.scale, gli, gj[u], (j0 + x + u <= i) & il & (sj[u] == si));
           qv[x / 2] = tcx::pack_bf16(e[0], e[1]);
+          qv[x / 2 + 1] = tcx::pack_bf16(e[2], e[3]);
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u)
@@ -383,16 +396,18 @@ __global__ void __launch_bounds__(256, 3) gdn_chunk_prep_kernel(const __grid_con
       tcx::wait_bar_quiet(bar_load, 1, p.err);  // the V load lands before the CTA may leave
     }
   }
-  // P2 epilogue: warps 0-3 U^T (lane = value column d), warps 4-7 W^T (lane = key column d), bf16 straight to the
-  // chunk-major workspace. U is kept transposed ([value column][64 tokens], the row the state pass's value thread
-  // reads): a lane writes its column's tokens contiguously. W is [token][128]: lanes d and d^1 swap one token of each
-  // pair, so every lane stores two columns of one token.
+  // P2 epilogue: warps 0-3 U^T (lane = value column d), warps 4-7 W^T (lane = key column d), bf16, staged in the
+  // [K; Q] region (every operand there has been read by P2) in the swizzled layouts of the workspace's tensor maps
+  // and written by TMA stores. U is kept transposed ([value column][64 tokens], the row the state pass's value thread
+  // reads): a lane writes its column's row. W is [token][128]: lanes d and d^1 swap one token of each pair, so every
+  // lane writes two columns of one token.
   if (live) {
     const bool done = __all_sync(0xffffffffu, tcx::wait_bar(bar_mma, 1, p.err));
+    if (!done) s_ok = 0;
     tcx::fence_after();
     const int qw = warp & 3, isw = warp >> 2;
     const int dcol = 32 * qw + lane, odd = lane & 1;
-    __nv_bfloat16* dst = isw ? p.Wg + (int64_t)rb * DH + (dcol & ~1) : p.Ug + ((int64_t)rb * 2 + dcol) * CT;
+    unsigned char* wst = base + kOffWst + (dcol >> 6) * 8192;  // the W box of this lane's column
 #pragma unroll 1
     for (int tb = 0; tb < CT; tb += 32) {
       float d[32];
@@ -402,7 +417,7 @@ __global__ void __launch_bounds__(256, 3) gdn_chunk_prep_kernel(const __grid_con
       if (done && !isw) {
 #pragma unroll
         for (int t = 0; t < 32; t += 8)
-          *reinterpret_cast<uint4*>(dst + tb + t) =
+          *reinterpret_cast<uint4*>(base + kOffUst + swz(dcol, tb + t)) =
               make_uint4(tcx::pack_bf16(d[t], d[t + 1]), tcx::pack_bf16(d[t + 2], d[t + 3]),
                          tcx::pack_bf16(d[t + 4], d[t + 5]), tcx::pack_bf16(d[t + 6], d[t + 7]));
       } else if (done) {
@@ -412,10 +427,19 @@ __global__ void __launch_bounds__(256, 3) gdn_chunk_prep_kernel(const __grid_con
           const float give = odd ? d[t] : d[t + 1];  // the partner's token
           const float got = __shfl_xor_sync(0xffffffffu, give, 1);
           const uint32_t w2 = odd ? tcx::pack_bf16(got, mine) : tcx::pack_bf16(mine, got);
-          *reinterpret_cast<uint32_t*>(dst + (int64_t)(tb + t + odd) * DH) = w2;
+          *reinterpret_cast<uint32_t*>(wst + swz(tb + t + odd, (dcol & 63) & ~1)) = w2;
         }
       }
     }
+  }
+  tcx::fence_async_smem();  // the staged tiles are read by the TMA stores
+  __syncthreads();
+  if (tid == 0 && live && s_ok) {
+    tma_store2(&p.umap, sbase + kOffUst, 0, 2 * rb);
+    tma_store2(&p.wmap, sbase + kOffWst, 0, rb);
+    tma_store2(&p.wmap, sbase + kOffWst + 8192, 64, rb);
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // written, and the staging read, before the CTA leaves
   }
   if (p2) tcx::wait_bar_quiet(bar_mma, 1, p.err);  // no MMA in flight at the dealloc (the epilogue waited already)
   tcx::fence_before();
@@ -481,6 +505,8 @@ extern "C" int janus_b200_gdn_chunk_scan(const void* q, const void* k, const voi
     if (!st) st = map3d(&pp.kmap, k, (uint64_t)T, (uint64_t)Hk);
     if (!st) st = map3d(&pp.vmap, v, (uint64_t)T, (uint64_t)Hv);
     if (!st) st = map2d(&pp.qkmap, QKg, CT, wrows, 64);
+    if (!st) st = map2d(&pp.wmap, Wg, DH, wrows, 64);
+    if (!st) st = map2d(&pp.umap, Ug, CT, 2 * wrows, 128);
     if (st) return st;
     pp.g = g;
     pp.beta = beta;
@@ -488,8 +514,6 @@ extern "C" int janus_b200_gdn_chunk_scan(const void* q, const void* k, const voi
     pp.chunk_start = chunk_start;
     pp.segment = segment;
     pp.Gg = Gg;
-    pp.Wg = Wg;
-    pp.Ug = Ug;
     pp.err = status;
     pp.B = (int)B;
     pp.Hk = (int)Hk;

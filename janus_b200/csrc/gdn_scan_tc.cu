@@ -239,6 +239,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_scan_fused_kernel(const __grid_cons
     float* seG = sG + CT;
     float* sBeta = sG + 2 * CT;
     float* sGraw = sG + 3 * CT;
+    float* sGl = sGraw;  // G log2(e), between the chunk's scan and the next chunk's raw g
     const uint32_t la = tm + ((uint32_t)(32 * pw) << 16) + cP;  // this warp's TMEM lanes, the prep's columns
     // g and beta of the chunk after the one in hand, in registers (their loads overlap a chunk's work)
     float g_next = 0.f, b_next = 0.f;
@@ -286,7 +287,10 @@ __global__ void __launch_bounds__(NT, 1) gdn_scan_fused_kernel(const __grid_cons
         sG[2 * lane + 1] = excl + b;
       }
       psync();
-      if (pt < CT) seG[pt] = expf(sG[pt]);
+      if (pt < CT) {
+        seG[pt] = expf(sG[pt]);
+        sGl[pt] = sG[pt] * kLog2e;
+      }
       ok = group_and<3>(wait_bar(&bars.p1_done, i & 1, p.err));
       if (!ok) break;
       fence_after();
@@ -296,7 +300,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_scan_fused_kernel(const __grid_cons
       // row's end zero (bf16, the stage's QK tile)
       {
         const int ii = 32 * (pw & 1) + lane;
-        const float Gi = sG[ii];
+        const float gli = sGl[ii];
         if (!(pw & 1)) {  // rows 0-31 against columns 32-63 lie wholly above the diagonal: both masks are zero
           if (pw < 2) {
 #pragma unroll
@@ -315,11 +319,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_scan_fused_kernel(const __grid_cons
             const float nb = -sBeta[ii];
             float nv[32];
 #pragma unroll
-            for (int x = 0; x < 32; ++x) {
-              const int j = j0 + x;
-              const float val = nb * d[x] * __expf(fminf(Gi - sG[j], 0.f));
-              nv[x] = j < ii ? val : 0.f;
-            }
+            for (int x = 0; x < 32; ++x) nv[x] = n_entry(d[x], nb, gli, sGl[j0 + x], j0 + x < ii);
 #pragma unroll
             for (int x = 0; x < 32; x += 4)
               *reinterpret_cast<float4*>(&sN[ii * PADF + j0 + x]) = make_float4(nv[x], nv[x + 1], nv[x + 2], nv[x + 3]);
@@ -329,11 +329,8 @@ __global__ void __launch_bounds__(NT, 1) gdn_scan_fused_kernel(const __grid_cons
             for (int x = 0; x < 32; x += 2) {
               float e[2];
 #pragma unroll
-              for (int u = 0; u < 2; ++u) {
-                const int j = j0 + x + u;
-                const float val = p.scale * d[x + u] * __expf(fminf(Gi - sG[j], 0.f));
-                e[u] = (j <= ii) & (ii < nt) ? val : 0.f;
-              }
+              for (int u = 0; u < 2; ++u)
+                e[u] = qk_entry(d[x + u], p.scale, gli, sGl[j0 + x + u], (j0 + x + u <= ii) & (ii < nt));
               qv[x / 2] = pack_bf16(e[0], e[1]);
             }
 #pragma unroll
