@@ -439,7 +439,9 @@ __global__ void __launch_bounds__(256, 3) gdn_chunk_prep_kernel(const __grid_con
     tma_store2(&p.wmap, sbase + kOffWst, 0, rb);
     tma_store2(&p.wmap, sbase + kOffWst + 8192, 64, rb);
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // written, and the staging read, before the CTA leaves
+    // the staging has been read before the CTA leaves; the writes themselves complete with the grid, before the
+    // state pass (the next launch in the stream) reads them
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
   }
   if (p2) tcx::wait_bar_quiet(bar_mma, 1, p.err);  // no MMA in flight at the dealloc (the epilogue waited already)
   tcx::fence_before();
