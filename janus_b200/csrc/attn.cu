@@ -81,6 +81,30 @@ __global__ void attn_qk_prep_kernel(const __nv_bfloat16* __restrict__ qkv, int64
     }
     ss = warp_sum(ss);
     const float r = rsqrtf(ss / (float)D + eps);
+    __nv_bfloat16* dst = isq ? q + (t * Hq + head) * D : k + (t * Hkv + (head - Hq)) * D;
+    if (nvec <= 32 && half % 8 == 0) {
+      // one vector of 8 dims per lane: the rotary partner of dim d (d +/- half) sits in lane ^ half/8, so it comes
+      // by a shuffle; cos and sin as float4 reads of the warp's table
+      float y[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, wv[8], pv[8];
+      if (lane < nvec) {
+        load8(w + lane * 8, wv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = x[i] * r * (1.f + wv[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pv[i] = __shfl_xor_sync(0xffffffffu, y[i], half >> 3);
+      if (lane * 8 < rot) {
+        const int f0 = lane * 8 < half ? lane * 8 : lane * 8 - half;
+        const float4 c0 = reinterpret_cast<const float4*>(cs + f0)[0], c1 = reinterpret_cast<const float4*>(cs + f0)[1];
+        const float4 s0 = reinterpret_cast<const float4*>(sn + f0)[0], s1 = reinterpret_cast<const float4*>(sn + f0)[1];
+        const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+        const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = lane * 8 < half ? y[i] * cv[i] - pv[i] * sv[i] : y[i] * cv[i] + pv[i] * sv[i];
+      }
+      if (lane < nvec) store8(dst + lane * 8, y);
+      continue;
+    }
     float nx[8];  // this lane's normalised dims (first 256)
     for (int c = lane; c < nvec; c += 32) {
       float y[8], wv[8];
@@ -102,7 +126,6 @@ __global__ void attn_qk_prep_kernel(const __nv_bfloat16* __restrict__ qkv, int64
       reinterpret_cast<float4*>(buf + c * 8)[1] = make_float4(y[4], y[5], y[6], y[7]);
     }
     __syncwarp();
-    __nv_bfloat16* dst = isq ? q + (t * Hq + head) * D : k + (t * Hkv + (head - Hq)) * D;
     for (int c = lane; c < nvec; c += 32) {
       float o[8];
       if (c != lane) {
