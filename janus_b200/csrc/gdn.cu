@@ -81,7 +81,17 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
   int rows_n[kProBatch];
 #pragma unroll
   for (int b = 0; b < kProBatch; ++b) rows_n[b] = row_of_token[t0 + b < t1 ? t0 + b : t1 - 1];
-  for (int64_t tb = t0; tb < t1; tb += kProBatch) {
+  // K = 4: the window rotates through its 3 registers instead of sliding (the slot of the oldest input takes the
+  // newest), so a pass of 3 batches (6 tokens, a multiple of both) fixes every register index at compile time and
+  // the per-token moves of the slide are gone; other K slide
+  constexpr int W = K - 1;
+  constexpr int kRot = (K == 4) ? 3 : 1;  // batches per pass
+  static_assert(kRot == 1 || (kProTokens % (kRot * kProBatch) == 0 && (kRot * kProBatch) % W == 0), "rotation");
+  for (int64_t tp = t0; tp < t1; tp += kRot * kProBatch) {
+#pragma unroll
+  for (int bb = 0; bb < kRot; ++bb) {
+    const int64_t tb = tp + bb * kProBatch;
+    if (tb >= t1) break;
     int rows[kProBatch];
 #pragma unroll
     for (int b = 0; b < kProBatch; ++b) rows[b] = rows_n[b];
@@ -115,13 +125,14 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
 #pragma unroll
         for (int j = 0; j < K - 1; ++j) {
           const int64_t e = i + j;  // ext index of relative position j - (K-1)
+          float* hj = hist[kRot > 1 ? (bb * kProBatch + b + j) % W : j];
           if (e >= K - 1) {
-            load8(proj + (r0 + e - (K - 1)) * proj_stride + c0, hist[j]);
+            load8(proj + (r0 + e - (K - 1)) * proj_stride + c0, hj);
           } else if (tail) {
-            load8(tail + e * C + c0, hist[j]);
+            load8(tail + e * C + c0, hj);
           } else {
 #pragma unroll
-            for (int u = 0; u < 8; ++u) hist[j][u] = 0.f;
+            for (int u = 0; u < 8; ++u) hj[u] = 0.f;
           }
         }
       }
@@ -137,20 +148,26 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
       for (int u = 0; u < 8; ++u) {
         a[u] = x[u] * wf[u][K - 1];
 #pragma unroll
-        for (int j = 0; j < K - 1; ++j) a[u] += hist[j][u] * wf[u][j];
+        for (int j = 0; j < K - 1; ++j) a[u] += hist[kRot > 1 ? (bb * kProBatch + b + j) % W : j][u] * wf[u][j];
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u) act[b][u] = silu_fast(a[u]);
-      // slide the window
+      if (kRot > 1) {  // the oldest input's slot takes the newest
 #pragma unroll
-      for (int j = 0; j < K - 2; ++j)
+        for (int u = 0; u < 8; ++u) hist[(bb * kProBatch + b) % W][u] = x[u];
+      } else {  // slide the window
 #pragma unroll
-        for (int u = 0; u < 8; ++u) hist[j][u] = hist[j + 1][u];
+        for (int j = 0; j < K - 2; ++j)
 #pragma unroll
-      for (int u = 0; u < 8; ++u) hist[K - 2][u] = x[u];
+          for (int u = 0; u < 8; ++u) hist[j][u] = hist[j + 1][u];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) hist[K - 2][u] = x[u];
+      }
       if (live && tail_out && t == r0 + L - 1) {  // the row's last K-1 conv inputs are the window now
 #pragma unroll
-        for (int j = 0; j < K - 1; ++j) store8(tail_out + ((int64_t)row * (K - 1) + j) * C + c0, hist[j]);
+        for (int j = 0; j < K - 1; ++j)
+          store8(tail_out + ((int64_t)row * (K - 1) + j) * C + c0,
+                 hist[kRot > 1 ? (bb * kProBatch + b + 1 + j) % W : j]);
       }
     }
     float rn[kProBatch];  // 1 / l2 norm of the token's head (q, k channels)
@@ -185,6 +202,7 @@ __global__ void __launch_bounds__(kProThreads, 2) gdn_prologue_kernel(
     asm volatile("" ::: "memory");  // the slots' reads and the stores above stay before their refill
 #pragma unroll
     for (int b = 0; b < kProBatch; ++b) issue(tb + kProRing + b);  // into the slots just read
+  }
   }
   asm volatile("cp.async.wait_group 0;\n" ::: "memory");  // no copy outlives the CTA
   // gates, by the first channel block: b at column C + Hv*Dv + h, a at C + Hv*Dv + Hv + h
