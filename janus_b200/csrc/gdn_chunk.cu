@@ -77,23 +77,24 @@ __device__ __forceinline__ int chunk_row(const int32_t* chunk_start, int B, int 
 
 // ------------------------------------------------------------------------------------------------ chunk prep
 
-// Shared memory of the prep (byte offsets from a 1024-aligned base), small enough for three CTAs per SM: regions are
+// Shared memory of the prep (byte offsets from a 1024-aligned base), small enough for four CTAs per SM: regions are
 // reused as their contents die. Operand tiles are in the UMMA 128B-swizzled K-major layout: [64-column atom][rows]
 // [128 bytes], the 16-byte unit u of row r at (u ^ (r & 7)) * 16.
 //   KQ [2 atoms][128 rows]: rows 0-63 the chunk's K, rows 64-127 its Q, so [K; Q] is one M=128 operand and K alone
 //      (rows 0-63) the N=64 one. Once Q is consumed, the Q half of atom 0 stages QK for its TMA store and then holds
 //      T1 = T diag(beta); the Q half of atom 1 holds the fp32 scratch M of the inverse, then T2 = T diag(beta e^G)
-//   NV fp32 N [64][PADF] for the inverse; once N is consumed, the chunk's V [2 atoms][64 rows] (a second TMA load)
-//   TF fp32 T [64][PADF]
+//   NV fp32 N [64][PADF], inverted in place into T = (I - N)^-1 block by block; once T is consumed (T1, T2 built),
+//      the chunk's V [2 atoms][64 rows] (a second TMA load)
 constexpr uint32_t kOffKQ = 0, kOffT1 = 8192, kOffM = 16384 + 8192, kOffT2 = 16384 + 8192;
-constexpr uint32_t kOffNV = 32768, kOffTF = 51200;  // 1024-byte boundaries
-constexpr uint32_t kOffVec = kOffTF + CT * PADF * 4;  // G, eG, beta, graw (fp32 [64]), seg (int [64])
+constexpr uint32_t kOffNV = 32768;  // 1024-byte boundary
+constexpr uint32_t kOffVec = kOffNV + CT * PADF * 4;  // G, eG, beta, graw (fp32 [64]), seg (int [64])
 constexpr uint32_t kOffBar = kOffVec + 5 * CT * 4;
 constexpr uint32_t kPrepSmem = kOffBar + 32 + 1024;  // + alignment slack
 constexpr uint32_t kPrepTmemCols = 128;  // P1 (KK^T | QK^T) cols 0-63, then U^T cols 0-63 and W^T cols 64-127
 // after P2 the [K; Q] region holds the staged W (two [64 tokens][64 columns] boxes) and U^T ([128][64 tokens])
 constexpr uint32_t kOffWst = 0, kOffUst = 16384;
-static_assert(CT * PADF * 4 <= kOffTF - kOffNV && 32 * PADM * 4 <= 8192, "prep shared-memory regions");
+static_assert(CT * PADF * 4 >= 2 * CT * 64 * 2 && 32 * PADM * 4 <= 8192, "prep shared-memory regions");
+static_assert(4 * (kPrepSmem + 1024) <= 228 * 1024, "four prep CTAs per SM");
 
 struct PrepParams {
   CUtensorMap qmap, kmap, vmap;       // [T][H][128] bf16 loads, boxes 64 dims x 1 head x 64 tokens
@@ -121,12 +122,12 @@ __device__ __forceinline__ void tma_store2(const CUtensorMap* map, uint32_t src,
 // byte offset of element (r, c) of a 64-column swizzled atom [rows][128 B]
 __device__ __forceinline__ uint32_t swz(int r, int c) { return r * 128 + ((((c >> 3) ^ r) & 7) << 4) + (c & 7) * 2; }
 
-__global__ void __launch_bounds__(256, 3) gdn_chunk_prep_kernel(const __grid_constant__ PrepParams p) {
+__global__ void __launch_bounds__(256, 4) gdn_chunk_prep_kernel(const __grid_constant__ PrepParams p) {
   extern __shared__ unsigned char raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~(uintptr_t)1023);
   const uint32_t sbase = tcx::s32(base);
   float* sN = reinterpret_cast<float*>(base + kOffNV);
-  float* sTF = reinterpret_cast<float*>(base + kOffTF);
+  float* sTF = sN;  // T overwrites N block by block
   float* sM = reinterpret_cast<float*>(base + kOffM);
   float* sG = reinterpret_cast<float*>(base + kOffVec);
   float* seG = sG + CT;
@@ -266,39 +267,37 @@ __global__ void __launch_bounds__(256, 3) gdn_chunk_prep_kernel(const __grid_con
       const int4* sg4 = reinterpret_cast<const int4*>(sSeg + j0);
       if (qw < 2) {
         const float nb = -sBeta[i];
-        float nv[32];
 #pragma unroll
-        for (int x = 0; x < 32; x += 4) {
+        for (int x = 0; x < 32; x += 4) {  // each group of 4 entries stored as it is made (few live registers)
           const float4 g = gl4[x / 4];
           const int4 sg = segs ? sg4[x / 4] : make_int4(si, si, si, si);
           const float gj[4] = {g.x, g.y, g.z, g.w};
           const int sj[4] = {sg.x, sg.y, sg.z, sg.w};
+          float nv[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) nv[x + u] = n_entry(d[x + u], nb, gli, gj[u], (j0 + x + u < i) & (sj[u] == si));
+          for (int u = 0; u < 4; ++u) nv[u] = n_entry(d[x + u], nb, gli, gj[u], (j0 + x + u < i) & (sj[u] == si));
+          *reinterpret_cast<float4*>(&sN[i * PADF + j0 + x]) = make_float4(nv[0], nv[1], nv[2], nv[3]);
         }
-#pragma unroll
-        for (int x = 0; x < 32; x += 4)
-          *reinterpret_cast<float4*>(&sN[i * PADF + j0 + x]) = make_float4(nv[x], nv[x + 1], nv[x + 2], nv[x + 3]);
       } else {
-        uint32_t qv[16];
         const bool il = i < nt;
 #pragma unroll
-        for (int x = 0; x < 32; x += 4) {
-          const float4 g = gl4[x / 4];
-          const int4 sg = segs ? sg4[x / 4] : make_int4(si, si, si, si);
-          const float gj[4] = {g.x, g.y, g.z, g.w};
-          const int sj[4] = {sg.x, sg.y, sg.z, sg.w};
-          float e[4];
+        for (int x = 0; x < 32; x += 8) {  // each 16-byte unit stored as it is made
+          uint32_t qv[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
-            e[u] = qk_entry(d[x + u], p.scale, gli, gj[u], (j0 + x + u <= i) & il & (sj[u] == si));
-          qv[x / 2] = tcx::pack_bf16(e[0], e[1]);
-          qv[x / 2 + 1] = tcx::pack_bf16(e[2], e[3]);
+          for (int y = 0; y < 8; y += 4) {
+            const float4 g = gl4[(x + y) / 4];
+            const int4 sg = segs ? sg4[(x + y) / 4] : make_int4(si, si, si, si);
+            const float gj[4] = {g.x, g.y, g.z, g.w};
+            const int sj[4] = {sg.x, sg.y, sg.z, sg.w};
+            float e[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              e[u] = qk_entry(d[x + y + u], p.scale, gli, gj[u], (j0 + x + y + u <= i) & il & (sj[u] == si));
+            qv[y / 2] = tcx::pack_bf16(e[0], e[1]);
+            qv[y / 2 + 1] = tcx::pack_bf16(e[2], e[3]);
+          }
+          *reinterpret_cast<uint4*>(base + kOffKQ + 8192 + swz(i, j0 + x)) = make_uint4(qv[0], qv[1], qv[2], qv[3]);
         }
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          *reinterpret_cast<uint4*>(base + kOffKQ + 8192 + swz(i, j0 + 8 * u)) =
-              make_uint4(qv[4 * u], qv[4 * u + 1], qv[4 * u + 2], qv[4 * u + 3]);
         tcx::fence_async_smem();  // the staged QK is read by the TMA store
       }
     }
@@ -308,15 +307,9 @@ __global__ void __launch_bounds__(256, 3) gdn_chunk_prep_kernel(const __grid_con
     tma_store2(&p.qkmap, sbase + kOffKQ + 8192, 0, rb);
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
   }
-  // T = (I - N)^-1: diagonal 16x16 blocks (warps 0-3, lane c < 16 owns column c)
-  if (warp < 4) {
-    diag_inverse16<PADF>(sN, sTF, warp * 16, lane);
-  } else {  // zeros above the block diagonal that the full-length sums below read: T[0:16, 16:32], T[32:48, 48:64]
-    for (int x = tid - 128; x < 512; x += 128) {
-      const int blk = x >> 8, r = (x >> 4) & 15, cc = x & 15;
-      sTF[(blk * 32 + r) * PADF + blk * 32 + 16 + cc] = 0.f;
-    }
-  }
+  // T = (I - N)^-1 in place: diagonal 16x16 blocks (warps 0-3, lane c < 16 owns column c). The zeros above the block
+  // diagonal that the full-length products below read (T[0:16, 16:32], T[32:48, 48:64]) are N's, already in place.
+  if (warp < 4) diag_inverse16<PADF>(sN, sTF, warp * 16, lane);
   __syncthreads();
   // stage 1: T[2h+1, 2h] = T[2h+1, 2h+1] N[2h+1, 2h] T[2h, 2h] (16x16 blocks), h = 0, 1, on the tensor cores in
   // tf32 (warps 0-3: block h = w >> 1, 8 columns (w & 1) * 8). The triangular zeros of N and T make full-length
@@ -345,12 +338,6 @@ __global__ void __launch_bounds__(256, 3) gdn_chunk_prep_kernel(const __grid_con
     tile_mma_tf32(cacc, &sN[(32 + 16 * mt) * PADF], PADF, &sTF[8 * ntile], PADF, 32, lane);
     store_tile(cacc, &sM[(16 * mt) * PADM + 8 * ntile], PADM, lane);
     __syncthreads();
-    if (tid == 0 && live) {  // N is consumed: the chunk's V goes into its place (the U product needs it)
-      tcx::fence_async_smem();
-      tcx::bar_expect_tx(bar_load, 2 * CT * 64 * 2);
-      tcx::tma_load3(sbase + kOffNV, &p.vmap, 0, h, (int)t0, bar_load);
-      tcx::tma_load3(sbase + kOffNV + 8192, &p.vmap, 64, h, (int)t0, bar_load);
-    }
     cacc[0] = cacc[1] = cacc[2] = cacc[3] = 0.f;
     tile_mma_tf32(cacc, &sTF[(32 + 16 * mt) * PADF + 32], PADF, &sM[8 * ntile], PADM, 32, lane);
     store_tile(cacc, &sTF[(32 + 16 * mt) * PADF + 8 * ntile], PADF, lane);
@@ -375,6 +362,11 @@ __global__ void __launch_bounds__(256, 3) gdn_chunk_prep_kernel(const __grid_con
   tcx::fence_before();
   __syncthreads();
   tcx::fence_after();
+  if (tid == 0 && live) {  // T is consumed: the chunk's V goes into its place (the U product needs it)
+    tcx::bar_expect_tx(bar_load, 2 * CT * 64 * 2);
+    tcx::tma_load3(sbase + kOffNV, &p.vmap, 0, h, (int)t0, bar_load);
+    tcx::tma_load3(sbase + kOffNV + 8192, &p.vmap, 64, h, (int)t0, bar_load);
+  }
   // P2: U^T = V^T (T diag(beta))^T and W^T = K^T (T diag(beta e^G))^T (M = 128 value / key columns, N = 64 tokens i,
   // K = 64 tokens j): A = the V / K tile read MN-major (its two 64-column atoms LBO apart), B = T1 / T2 K-major; the
   // accumulators reuse P1's TMEM columns (read out long ago)

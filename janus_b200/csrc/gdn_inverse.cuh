@@ -28,7 +28,8 @@ __device__ __forceinline__ float qk_entry(float qk, float scale, float gli, floa
 // (I - N) t = e_c by column-oriented forward substitution: once t[m] is final it is pushed into every later row,
 // t[r] += N[r][m] t[m] for r > m. The 15 steps each issue independent FMAs, so the dependent chain is 15 FMAs long
 // (a row-by-row dot product would chain all 120). Entries of t above the lane's column stay exactly zero and its
-// diagonal entry exactly one. Lanes 16-31 compute a copy and store nothing.
+// diagonal entry exactly one. Lanes 16-31 compute a copy and store nothing. T may be N itself (the block is inverted
+// in place: every lane's reads of N are done before the first write).
 template <int LD>
 __device__ __forceinline__ void diag_inverse16(const float* N, float* T, int bs, int lane) {
   const int cc = lane & 15;
@@ -41,6 +42,7 @@ __device__ __forceinline__ void diag_inverse16(const float* N, float* T, int bs,
 #pragma unroll
     for (int r = m + 1; r < 16; ++r) col[r] = fmaf(N[(bs + r) * LD + bs + m], tm, col[r]);
   }
+  __syncwarp();
   if (lane < 16) {
 #pragma unroll
     for (int r = 0; r < 16; ++r) T[(bs + r) * LD + bs + cc] = col[r];
