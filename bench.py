@@ -451,6 +451,67 @@ def run_a3b(args):
         dist.destroy_process_group()
 
 
+def run_workload(args):
+    """A BASELINE configuration other than the headline (`--workload 2`: the 0.8B shape, listwise + PointerHead, a
+    2048-token state and one choice question, batch 64; `--workload 4`: the 0.8B cardinality stress pack, a 4096-token
+    state with 32 questions, one of them 255 options, batch 1), on one GPU: requests/s at the workload's batch, then
+    per-request latency p50/p90 at batch 1 (device time and end to end through DecisionReadout.probabilities).
+    Weights random (seeded), requests seeded synthetic token ids. A side line; the headline is workload 3."""
+    from janus_b200 import synthetic
+    from janus_b200.config import SHAPES
+    from janus_b200.model import DecisionReadout
+    device = torch.device("cuda", 0)
+    wid = args.workload
+    shape_name, mode, _, batch = synthetic.WORKLOADS[wid]
+    shape = SHAPES[shape_name]
+    weights = synthetic.make_weights(shape, seed=0, head="pointer" if mode == "listwise" else "scalar", device=device)
+    model = DecisionReadout(shape, weights, mode, device=device)
+    del weights
+    torch.cuda.empty_cache()
+    packs = synthetic.workload_requests(wid, seed=7000, batch=batch)
+    prepared = model.prepare(packs)
+    for _ in range(args.warmup):
+        model.run(prepared)
+    torch.cuda.synchronize()
+    ev = []
+    for _ in range(args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        model.run(prepared)
+        b.record()
+        ev.append((a, b))
+    torch.cuda.synchronize()
+    model.check_status()
+    ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+    singles = synthetic.workload_requests(wid, seed=8000, batch=max(1, args.latency_requests))
+    dev_ms, e2e_ms = [], []
+    for pk in singles:
+        prep1 = model.prepare([pk])
+        model.run(prep1)  # warm the shapes of this request
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        model.run(prep1)
+        b.record()
+        torch.cuda.synchronize()
+        dev_ms.append(a.elapsed_time(b))
+        t0 = time.perf_counter()
+        model.probabilities([pk])
+        e2e_ms.append((time.perf_counter() - t0) * 1000.0)
+    pct = lambda xs, q: float(statistics.quantiles(xs, n=10)[q // 10 - 1]) if len(xs) >= 2 else float(xs[0])
+    print(json.dumps({
+        "metric": f"decision requests/s and p50/p90 ms per request (workload {wid})",
+        "value": batch / (ms / 1000.0), "unit": "requests/s", "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms,
+        "request_latency_ms": {"per": f"single request (batch 1), {len(singles)} requests one at a time",
+                               "device": {"p50": statistics.median(dev_ms), "p90": pct(dev_ms, 90)},
+                               "e2e": {"p50": statistics.median(e2e_ms), "p90": pct(e2e_ms, 90)}},
+        "config": {"workload": {2: "0.8b-listwise-2k-state-1q", 4: "0.8b-tree-4k-state-32q-stress"}.get(wid, str(wid)),
+                   "requests_per_step": batch, "tokens_per_step": sum(p.token_count for p in packs),
+                   "mode": mode, "data": "synthetic"},
+    }), flush=True)
+
+
 def run_prefix(args):
     """Repeated states (a prefix-cache hit for every request): the state level of the 16 requests is encoded once
     into snapshots; each timed step then runs the branch levels only, from the snapshots. A side line for the
@@ -503,7 +564,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--latency-requests", type=int, default=8, help="single requests timed one at a time")
     ap.add_argument("--layers", type=int, default=0, help="debug: fewer layers (not a valid bench number)")
-    ap.add_argument("--op", default="readout", choices=["readout", "moe", "prefix", "gemm", "a3b"])
+    ap.add_argument("--op", default="readout", choices=["readout", "moe", "prefix", "gemm", "a3b", "workload"])
+    ap.add_argument("--workload", type=int, default=2, choices=[2, 4], help="--op workload: BASELINE configuration")
     ap.add_argument("--ep", action="store_true", help="--op a3b: expert parallel over the torchrun group")
     ap.add_argument("--gemm-tokens", type=int, default=131072)
     ap.add_argument("--moe-tokens", type=int, default=131072)
@@ -523,6 +585,9 @@ def main():
         return
     if args.op == "a3b":
         run_a3b(args)
+        return
+    if args.op == "workload":
+        run_workload(args)
         return
     if args.impl == "reference":
         run_reference(args)
