@@ -206,6 +206,20 @@ int janus_b200_moe_route(const float* logits, int64_t S, int64_t E, int64_t k, i
                          float* topk_w, int32_t* sorted_ids, int32_t* tile_expert, int64_t max_tiles,
                          int32_t* n_tiles, int32_t* workspace, size_t workspace_bytes, void* stream);
 
+/* The router GEMM fused with the routing: logits = x w_router^T (x bf16 [S, H] with row stride x_stride, w_router
+ * bf16 [E, H], E <= 256) on the tensor cores, kept in TMEM (never written), then the softmax / top-k / renormalised
+ * weights of janus_b200_moe_route with the same arithmetic (k in {1, 2, 4, 6, 8}), and the same tile plan into
+ * sorted_ids / tile_expert / n_tiles. w_gate: optional bf16 [1, H], the shared expert's gate row: gate_logit fp32 [S]
+ * = x w_gate^T from the same pass. status: optional device int32 word, set to 1 if a bounded device-side wait ran
+ * out. Same workspace and max_tiles rules as janus_b200_moe_route.
+ * Replaces the router GEMM plus Qwen3_5MoeTopKRouter.forward (transformers qwen3_5_moe :754-770), the shared expert
+ * gate's GEMV (:789-790) and `align` (janus/moe_w4a16.py:89-106). */
+int janus_b200_moe_route_fused(const void* x, int64_t x_stride, int64_t S, int64_t H, const void* w_router, int64_t E,
+                               const void* w_gate, int64_t k, int64_t tile_rows, int32_t* topk_idx, float* topk_w,
+                               float* gate_logit, int32_t* sorted_ids, int32_t* tile_expert, int64_t max_tiles,
+                               int32_t* n_tiles, int32_t* workspace, size_t workspace_bytes, int32_t* status,
+                               void* stream);
+
 /* W4A16 grouped GEMM over the expert-sorted 128-row tiles of janus_b200_moe_route / janus_b200_moe_plan, on the
  * tcgen05 tensor cores. Weights: codes uint8 [E, rows, K/2] (two int4 per byte, even element in the low nibble,
  * two's complement) and bf16 scales [E, rows, K/128]; the value fed to the tensor cores is code * scale rounded

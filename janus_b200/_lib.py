@@ -44,6 +44,9 @@ SIGNATURES = {
                                 c_void_p, c_void_p],
     "janus_b200_moe_route": [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
                              c_int64, c_void_p, c_void_p, c_size_t, c_void_p],
+    "janus_b200_moe_route_fused": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64,
+                                   c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
+                                   c_size_t, c_void_p, c_void_p],
     "janus_b200_moe_grouped_w4a16": [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int32,
                                      c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64,
                                      c_void_p, c_void_p],

@@ -253,6 +253,47 @@ extern "C" int janus_b200_moe_route(const float* logits, int64_t S, int64_t E, i
   return st;
 }
 
+namespace jb {
+int moe_router_tc(const void* x, int64_t x_stride, int64_t S, int64_t H, const void* w_router, int64_t E,
+                  const void* w_gate, int64_t k, int32_t* topk_idx, float* topk_w, float* gate_logit, int32_t* counts,
+                  int32_t* status, cudaStream_t stream);
+}
+
+extern "C" int janus_b200_moe_route_fused(const void* x, int64_t x_stride, int64_t S, int64_t H, const void* w_router,
+                                          int64_t E, const void* w_gate, int64_t k, int64_t tile_rows,
+                                          int32_t* topk_idx, float* topk_w, float* gate_logit, int32_t* sorted_ids,
+                                          int32_t* tile_expert, int64_t max_tiles, int32_t* n_tiles,
+                                          int32_t* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  JB_REQUIRE(x && w_router && topk_idx && topk_w && sorted_ids && tile_expert && n_tiles && (!w_gate || gate_logit),
+             JANUS_ERR_INVALID, "moe_route_fused: null pointer");
+  JB_REQUIRE(S >= 0 && E > 0 && k > 0 && k <= E && tile_rows == BM, JANUS_ERR_INVALID,
+             "moe_route_fused: E %lld, k %lld, tile rows %lld (must be %d)", (long long)E, (long long)k,
+             (long long)tile_rows, BM);
+  const int64_t need_tiles = (S * k + E * (tile_rows - 1) + tile_rows - 1) / tile_rows;
+  JB_REQUIRE(max_tiles >= need_tiles, JANUS_ERR_INVALID, "moe_route_fused: max_tiles %lld < worst case %lld",
+             (long long)max_tiles, (long long)need_tiles);
+  JB_REQUIRE(workspace && workspace_bytes >= (size_t)(3 * E) * sizeof(int32_t), JANUS_ERR_WORKSPACE,
+             "moe_route_fused: workspace needs %lld bytes", (long long)(3 * E * 4));
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t rows = max_tiles * tile_rows;
+  route_init_kernel<<<(unsigned)std::min<int64_t>(148 * 8, (rows + 255) / 256 + 1), 256, 0, s>>>(workspace, (int)E,
+                                                                                                 sorted_ids, rows);
+  int st = launch_status("moe_route_fused/init");
+  if (st) return st;
+  st = moe_router_tc(x, x_stride, S, H, w_router, E, w_gate, k, topk_idx, topk_w, gate_logit, workspace, status, s);
+  if (st) return st;
+  route_plan_kernel<<<1, 256, E * sizeof(int32_t), s>>>(workspace, (int)E, (int)tile_rows, tile_expert, max_tiles,
+                                                        n_tiles);
+  st = launch_status("moe_route_fused/plan");
+  if (st) return st;
+  if (S > 0) {
+    route_scatter_kernel<<<(unsigned)std::min<int64_t>(148 * 8, (S * k + 255) / 256), 256, 0, s>>>(
+        topk_idx, S * k, workspace, (int)E, sorted_ids);
+    st = launch_status("moe_route_fused/scatter");
+  }
+  return st;
+}
+
 extern "C" int janus_b200_moe_combine(const void* y, int64_t k, const void* shared, const float* shared_gate_logit,
                                       int64_t S, int64_t H, void* out, void* stream) {
   JB_REQUIRE(y && out && k > 0 && S >= 0 && H > 0 && H % 8 == 0, JANUS_ERR_INVALID, "moe_combine: arguments");

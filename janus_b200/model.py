@@ -79,7 +79,9 @@ class DecisionReadout:
                 else:
                     L.gu_codes, L.gu_scales = u8(m + "experts.gate_up_proj"), bf(m + "experts.gate_up_proj.scales")
                     L.dn_codes, L.dn_scales = u8(m + "experts.down_proj"), bf(m + "experts.down_proj.scales")
-                L.shared_gate_up = torch.cat([w(m + "shared_expert.gate_proj.weight"), w(m + "shared_expert.up_proj.weight")])
+                # the shared expert's gate/up rows in the order of the tcgen05 GEMM's SwiGLU epilogue
+                L.shared_gate_up = ops.swiglu_weight(w(m + "shared_expert.gate_proj.weight"),
+                                                     w(m + "shared_expert.up_proj.weight"))
                 L.shared_down = w(m + "shared_expert.down_proj.weight")
                 L.shared_gate = w(m + "shared_expert_gate.weight")
             else:
@@ -155,17 +157,26 @@ class DecisionReadout:
         (bf16 GEMM, fp32 output) -> routing plan -> gate_up grouped GEMM (silu(gate) * up) -> down grouped GEMM times
         the routing weight -> per-token sum plus the sigmoid-gated shared expert."""
         k = self.shape.top_k
-        logits = torch.mm(y, L.router.t(), out_dtype=torch.float32)
-        plan = ops.moe_route(logits, k)
+        if L.router.shape[0] <= 256 and k in (1, 2, 4, 6, 8):
+            # the router GEMM, its softmax / top-k and the shared expert's gate logit in one tensor-core pass
+            plan, sg = ops.moe_route_fused(y, L.router, k, w_gate=L.shared_gate, status=self.status)
+        else:
+            plan = ops.moe_route(torch.mm(y, L.router.t(), out_dtype=torch.float32), k)
+            sg = torch.mm(y, L.shared_gate.t(), out_dtype=torch.float32).reshape(-1)
         if self.ep is not None:
-            return self._moe_ep(y, L, plan[0], plan[1])
+            return self._moe_ep(y, L, plan[0], plan[1], sg)
         h = self._experts(y, L, plan, True, k)
         y2 = self._experts(h, L, plan, False, k, topk_w=plan[1])
-        shared = F.linear(ops.silu_mul(F.linear(y, L.shared_gate_up)), L.shared_down)
-        sg = torch.mm(y, L.shared_gate.t(), out_dtype=torch.float32)
-        return ops.moe_combine(y2, k, shared, sg.reshape(-1))
+        shared = self._shared_expert(y, L)
+        return ops.moe_combine(y2, k, shared, sg)
 
-    def _moe_ep(self, y, L, topk_idx, topk_w):
+    def _shared_expert(self, y, L):
+        """The shared expert's SwiGLU (transformers qwen3_5_moe :778-791) on the tcgen05 GEMM: gate/up with the SwiGLU
+        epilogue (silu(gate) * up from the fp32 accumulators, rounded once), then the down projection."""
+        return ops.gemm_bf16(ops.gemm_bf16(y, L.shared_gate_up, swiglu=True, status=self.status), L.shared_down,
+                             status=self.status)
+
+    def _moe_ep(self, y, L, topk_idx, topk_w, sg):
         """The expert-parallel MoE block (janus_b200/ep.py): dispatch rows to the ranks owning their experts, grouped
         GEMMs over this rank's experts, fp32 partial per received row, combine on the owner with the shared expert."""
         k, ep = self.shape.top_k, self.ep
@@ -181,10 +192,9 @@ class DecisionReadout:
             part = ops.moe_reduce_slots(y2, k, slot_e)
         else:
             part = torch.empty(0, H, dtype=torch.float32, device=y.device)
-        shared = F.linear(ops.silu_mul(F.linear(y, L.shared_gate_up)), L.shared_down)
-        sg = torch.mm(y, L.shared_gate.t(), out_dtype=torch.float32)
+        shared = self._shared_expert(y, L)
         back, row_index = ep.combine_static(part, handle) if ep.static else ep.combine(part, handle)
-        return ops.moe_combine_ep(back, row_index, shared, sg.reshape(-1))
+        return ops.moe_combine_ep(back, row_index, shared, sg)
 
     def _experts(self, x, L, plan, gated, k, topk_w=None):
         """One grouped GEMM over the layer's experts in their stored format (int4 group 128, or NVFP4)."""

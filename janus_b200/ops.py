@@ -304,6 +304,7 @@ def head_pointer(x, option_rows, option_question, decision_rows, final_w, rms_ep
 
 
 @_instrument("gemm_bf16", 1)
+@_instrument("gemm_bf16", 1)
 def gemm_bf16(a, w, swiglu=False, out=None, status=None):
     """a bf16 [M, K] (unit column stride), w bf16 [N, K] -> a w^T bf16 [M, N] on the tcgen05 GEMM; swiglu: w in
     the interleaved gate/up order of `swiglu_weight`, result silu(gate) * up [M, N / 2]."""
@@ -356,6 +357,35 @@ def moe_route(logits, k):
                                                 _ptr(sorted_ids), _ptr(tile_expert), mt, _ptr(n_tiles), _ptr(ws),
                                                 ws.numel() * 4, _stream(logits)), "moe_route")
     return topk_idx, topk_w, sorted_ids, tile_expert, n_tiles
+
+
+@_instrument("moe_route_fused", 4)
+def moe_route_fused(x, w_router, k, w_gate=None, status=None):
+    """The router GEMM fused with the routing: x bf16 [S, H] (unit column stride), w_router bf16 [E, H] (E <= 256),
+    optional w_gate bf16 [1, H] (the shared expert's gate row) -> ((topk_idx, topk_w, sorted_ids, tile_expert,
+    n_tiles), gate_logit fp32 [S] or None), the router logits never leaving the tensor memory."""
+    _need(x, BF16, "x", contiguous=False)
+    if x.stride(1) != 1:
+        raise ValueError("x must have unit column stride")
+    _need(w_router, BF16, "w_router")
+    S, H = x.shape
+    E = w_router.shape[0]
+    if w_router.shape[1] != H or (w_gate is not None and tuple(w_gate.shape) != (1, H)):
+        raise ValueError("moe_route_fused: w_router [E, H] and w_gate [1, H] must match x [S, H]")
+    dev = x.device
+    mt = moe_max_tiles(S, E, k)
+    topk_idx = torch.empty(S, k, dtype=I32, device=dev)
+    topk_w = torch.empty(S, k, dtype=F32, device=dev)
+    sorted_ids = torch.empty(mt * MOE_TILE, dtype=I32, device=dev)
+    tile_expert = torch.empty(mt, dtype=I32, device=dev)
+    n_tiles = torch.empty(1, dtype=I32, device=dev)
+    gate = torch.empty(S, dtype=F32, device=dev) if w_gate is not None else None
+    ws = torch.empty(3 * E, dtype=I32, device=dev)
+    _lib.check(_lib.load().janus_b200_moe_route_fused(
+        _ptr(x), x.stride(0), S, H, _ptr(w_router), E, _ptr(_opt(w_gate, BF16, "w_gate")), k, MOE_TILE, _ptr(topk_idx),
+        _ptr(topk_w), _ptr(gate), _ptr(sorted_ids), _ptr(tile_expert), mt, _ptr(n_tiles), _ptr(ws), ws.numel() * 4,
+        _ptr(status), _stream(x)), "moe_route_fused")
+    return (topk_idx, topk_w, sorted_ids, tile_expert, n_tiles), gate
 
 
 @_instrument("moe_grouped_w4a16", 1)

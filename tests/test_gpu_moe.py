@@ -8,6 +8,7 @@ import torch.nn.functional as F
 from oracle import hybrid as oracle
 
 pytestmark = pytest.mark.gpu
+BF = torch.bfloat16
 
 
 def _ops():
@@ -43,6 +44,41 @@ def test_route_topk_and_plan(S, E, k):
         assert (flat[rows[rows >= 0]] == te[t]).all()
     counts = np.bincount(flat, minlength=E)
     assert n == sum((c + T - 1) // T for c in counts)
+
+
+@pytest.mark.parametrize("S,E,k,H", [(1, 8, 2, 128), (37, 8, 2, 128), (300, 256, 8, 2048), (1000, 256, 8, 2048),
+                                     (130, 40, 4, 256)])
+def test_fused_router_matches_router_gemm_and_route(S, E, k, H):
+    """The router GEMM fused with the routing against the fp32 logits x W_r^T fed to moe_route (the same top-k
+    arithmetic): the same experts wherever the logits do not tie at the k-th place within fp32 rounding, the same
+    weights for those, the shared gate logit to fp32 rounding, and a consistent tile plan."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(S + E)
+    x = torch.randn(S, H, generator=g).to(BF)
+    wr = (0.05 * torch.randn(E, H, generator=g)).to(BF)
+    wg = (0.05 * torch.randn(1, H, generator=g)).to(BF)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    (idx, w, sorted_ids, tile_expert, n_tiles), gate = ops.moe_route_fused(x.cuda(), wr.cuda(), k, w_gate=wg.cuda(),
+                                                                          status=status)
+    logits = x.double() @ wr.double().t()
+    ref_idx, ref_w, *_ = ops.moe_route(logits.float().cuda(), k)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    idx, ref_idx = idx.cpu(), ref_idx.cpu()
+    same = (idx == ref_idx).all(1)
+    assert float(same.float().mean()) >= 0.995, float(same.float().mean())
+    np.testing.assert_allclose(w.cpu()[same].numpy(), ref_w.cpu()[same].numpy(), atol=2e-6, rtol=2e-5)
+    np.testing.assert_allclose(gate.cpu().numpy(), (x.double() @ wg.double().t()).reshape(-1).numpy(),
+                               atol=1e-5, rtol=1e-5)
+    n = int(n_tiles.item())
+    T = ops.MOE_TILE
+    ids = sorted_ids.cpu().numpy()[: n * T]
+    te = tile_expert.cpu().numpy()[:n]
+    assert sorted(ids[ids >= 0].tolist()) == list(range(S * k))
+    flat = idx.numpy().reshape(-1)
+    for t in range(n):
+        rows = ids[t * T:(t + 1) * T]
+        assert (flat[rows[rows >= 0]] == te[t]).all()
 
 
 @pytest.mark.parametrize("S,E,k,H,I", [(5, 8, 2, 128, 128), (700, 16, 4, 2048, 512), (300, 256, 8, 2048, 512)])
