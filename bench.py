@@ -157,7 +157,8 @@ def chunk_algorithmic(levels, shape, which):
 
 
 def run_reference(args):
-    """The reference arm: the CPU oracle on a bounded sample of the workload, all host threads."""
+    """The reference arm: the reference's CPU readout (or the oracle's restatement of it when the reference does
+    not import) on a bounded sample of the workload, all host threads."""
     world, rank, _ = dist_env()
     if rank != 0:
         return
@@ -170,49 +171,62 @@ def run_reference(args):
             "impl": "reference",
             "config": {"workload": "4b-tree-8k-state-8q", "requests_per_gpu": 1, "sample": sample,
                        "same_config": False},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample, **detail},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "sample": sample, **detail},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def cpu_reference_rate(steps=1, warmup=0, full_request=False):
-    """The CPU oracle (fp32, all host threads) on one full request of the workload (8192-token state, 8 tree
-    questions). A timed step runs the request through one 4-layer block of the 4B shape (3 DeltaNet + 1 attention
-    layer, every level, embedding and head included): the model is 8 repeats of that block, so a request costs 8
-    blocks (the embedding gather and the head, a few ms, are counted 8 times). With `full_request` the whole
-    32-layer model (full vocabulary) also runs the same request once, measured, as a check of that factor.
-    Returns (requests/s from the block steps, description, details)."""
+def cpu_reference_rate(steps=1, warmup=0, full_request=False, kind=None):
+    """The reference's CPU readout (fp32, all host threads) on one full request of the workload (8192-token state, 8
+    tree questions). kind "reference": the reference's own code, its HybridBackbone plain CPU path over a
+    transformers Qwen3.5 model read out by its DecisionModel (oracle/reference_cpu.py; the reference installed under
+    baseline/_ref travels with the checkout); kind "port": the CPU oracle's restatement of it (oracle/hybrid.py),
+    used when the reference or transformers does not import. Default: the reference when it imports. A timed step
+    runs the request through one 4-layer block of the 4B shape (3 DeltaNet + 1 attention layer, every level,
+    embedding and head included): the model is 8 repeats of that block, so a request costs 8 blocks (the embedding
+    gather and the head, a few ms, are counted 8 times). With `full_request` the whole 32-layer model (full
+    vocabulary) also runs the same request once, measured, as a check of that factor.
+    Returns (requests/s from the block steps, description, details with the kind)."""
     from janus_b200 import synthetic
     from janus_b200.config import SHAPES
-    from oracle import hybrid as oracle
+    from oracle import reference_cpu
+    if kind is None:
+        kind = "reference" if reference_cpu.available() else "port"
     full = SHAPES["4b"]
     blocks = full.layers // 4
-    shape = full.with_layers(4, vocab=4096)
-    weights = synthetic.make_weights(shape, seed=0, head="scalar", device="cpu")
-    model = oracle.Oracle(shape, weights)
-    del weights
+
+    def readout(shape):
+        weights = synthetic.make_weights(shape, seed=0, head="scalar", device="cpu")
+        if kind == "reference":
+            model = reference_cpu.reference_readout(shape, weights, "tree", grouped_branches=True)
+            return lambda pack: model.forward_many(reference_cpu.reference_packs([pack]))
+        from oracle import hybrid as oracle
+        model = oracle.Oracle(shape, weights)
+        return lambda pack: oracle.probabilities(model.logits(pack, "tree"))
+
+    run = readout(full.with_layers(4, vocab=4096))
     pack = synthetic.q4b_request(vocab=4096, seed=0)
     times = []
     with torch.no_grad():
         for i in range(max(0, warmup) + max(1, steps)):
             t0 = time.perf_counter()
-            oracle.probabilities(model.logits(pack, "tree"))
+            run(pack)
             if i >= warmup:
                 times.append(time.perf_counter() - t0)
     block_s = statistics.median(times)
-    detail = {"block_s": block_s, "blocks_per_request": blocks, "block_steps": len(times)}
+    detail = {"block_s": block_s, "blocks_per_request": blocks, "block_steps": len(times), "kind": kind}
+    what = ("the reference's own CPU readout (janus HybridBackbone + DecisionModel over transformers Qwen3.5)"
+            if kind == "reference" else "the CPU oracle (a restatement of the reference)")
     sample = (f"one 4B-shape request ({pack.token_count} tokens: 8192-token state, 8 questions) through one 4-layer "
-              f"block (3 DeltaNet + 1 attention) of the CPU oracle per step, fp32, {torch.get_num_threads()} threads, "
+              f"block (3 DeltaNet + 1 attention) of {what} per step, fp32, {torch.get_num_threads()} threads, "
               f"median of {len(times)} steps; requests/s = 1 / ({blocks} x block seconds)")
     if full_request:
-        del model
-        weights = synthetic.make_weights(full, seed=0, head="scalar", device="cpu")
-        model = oracle.Oracle(full, weights)
-        del weights
+        del run
+        run = readout(full)
         pack = synthetic.q4b_request(seed=0)
         t0 = time.perf_counter()
         with torch.no_grad():
-            oracle.probabilities(model.logits(pack, "tree"))
+            run(pack)
         detail["full_request_s"] = time.perf_counter() - t0
         detail["full_request"] = "the same request through all 32 layers (vocab 248320), measured once"
         detail["block_extrapolation_error"] = blocks * block_s / detail["full_request_s"] - 1.0
@@ -761,7 +775,7 @@ def main():
         cores = os.cpu_count() or 1
         torch.set_num_threads(cores)
         v, sample, detail = cpu_reference_rate(1, 0)
-        cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample, **detail}
+        cpu = {"value": v, "unit": UNIT, "cores": cores, "sample": sample, **detail}
 
     if rank == 0:
         p = lambda q: nearest_rank(step_ms, q)
