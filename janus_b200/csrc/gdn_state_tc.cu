@@ -76,8 +76,9 @@ struct Params {
 };
 
 struct Bars {
-  // st_done per chunk parity: the output warps trail the value-column warps by up to a chunk
-  uint64_t full[2], empty[2], sb_ready, vt_done, vb_ready, st_done[2], drain;
+  // st_done per chunk parity: the output warps trail the value-column warps by up to a chunk; s_upd: the state
+  // update of the current chunk is done (the value-column warps' hand-off, committed before O2T is issued)
+  uint64_t full[2], empty[2], sb_ready, vt_done, vb_ready, st_done[2], s_upd, drain;
 };
 
 // G -> (fq, fk) per token and the chunk's decay, in shared memory; by the 64 first value-column threads
@@ -140,6 +141,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_state_tc_kernel(const __grid_consta
     bar_init(&bars.vb_ready, 128);
     bar_init(&bars.st_done[0], 1);
     bar_init(&bars.st_done[1], 1);
+    bar_init(&bars.s_upd, 1);
     bar_init(&bars.drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -203,13 +205,15 @@ __global__ void __launch_bounds__(NT, 1) gdn_state_tc_kernel(const __grid_consta
         if (!ok) break;
         fence_after();
         const uint32_t keep = s_dl != 0.f ? 1u : 0u;  // 0: the decayed state is zero, the update overwrites ST
-#pragma unroll
-        for (int s = 0; s < 4; ++s)  // O2T = V'^T QK^T, 16 tokens j per step
-          mma_ts(tm + cVT(st), tm + cVB + s * 8, sdesc(stage + sQK + s * 32, 16, 1024), ID_N64, s > 0);
+        // the state update first (the next chunk waits on it), then the output's O2T (only the output warps do)
 #pragma unroll
         for (int s = 0; s < 4; ++s)  // ST += (V' f_k)^T K, 16 tokens per step; K rows as the MN-major operand
           mma_ts(tm + cST, tm + cVD + s * 8, sdesc(stage + sK + s * 16 * 128, kTile / 2, 1024), ID_N128,
                  s > 0 ? 1u : keep);
+        commit(&bars.s_upd);
+#pragma unroll
+        for (int s = 0; s < 4; ++s)  // O2T = V'^T QK^T, 16 tokens j per step
+          mma_ts(tm + cVT(st), tm + cVB + s * 8, sdesc(stage + sQK + s * 32, 16, 1024), ID_N64, s > 0);
         commit(&bars.st_done[st]);
         commit(&bars.empty[st]);
       }
@@ -342,7 +346,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_state_tc_kernel(const __grid_consta
       tst_wait();
       fence_before();
       bar_arrive(&bars.vb_ready);
-      ok = vand(wait_bar(&bars.st_done[st], (i >> 1) & 1, p.err));
+      ok = vand(wait_bar(&bars.s_upd, i & 1, p.err));
       if (!ok) break;
       fence_after();
       // the next chunk's bf16 state first: it releases the next chunk's products
@@ -359,7 +363,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_state_tc_kernel(const __grid_consta
       fence_before();
       bar_arrive(&bars.sb_ready);
     }
-    // the final state (the last update is complete: st_done of the last chunk was waited for above)
+    // the final state (the last update is complete: s_upd of the last chunk was waited for above)
     if (p.state_out && ok) {
       float* so = p.state_out + ((int64_t)row * p.Hv + h) * DH * DH;
 #pragma unroll 1
