@@ -695,35 +695,45 @@ def main():
     op_ms = {name: round(sum(s.elapsed_time(e) for s, e in rec), 2) for name, rec in ops.TIMED.items() if rec}
     ops.TIMED.clear()
 
-    # the roofline of the dominant kernel of the library
+    # the roofline of each of the library's timed kernels; the line's `roofline` is the dominant one's
     pk, pk_kind = peaks()
+
+    def kernel_roofline(name):
+        if name == "tree_attention":
+            flops_step = n_attn_layers * sum(attn_flops)
+            launches_per_step = len(per_attn) // args.steps
+            achieved = flops_step / (kernel_ms[name] / 1000.0) / 1e12
+            peak = pk["bf16_tflops_sustained"]
+            return {"kernel": "tree_attention", "bound": "tensor", "achieved": achieved, "peak": peak,
+                    "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                    "peak_kind": f"{pk_kind} bf16 sustained",
+                    "algorithmic_per_launch": flops_step / max(1, launches_per_step),
+                    "launches_per_step": launches_per_step, "ms_per_step": kernel_ms[name]}
+        if name in ("gdn_chunk_scan", "gdn_fork_recurrent"):
+            alg = chunk_algorithmic(levels, shape, chunked if name == "gdn_chunk_scan" else [not c for c in chunked])
+            fl = sum(f for f, _ in alg) * n_lin_layers
+            by = sum(b for _, b in alg) * n_lin_layers
+            sec = kernel_ms[name] / 1000.0
+            t_peak = pk["bf16_tflops_sustained"] * 1e12
+            b_peak = pk["hbm_gbs"] * 1e9
+            if fl / t_peak > by / b_peak:
+                r = {"kernel": name, "bound": "tensor", "achieved": fl / sec / 1e12, "peak": t_peak / 1e12,
+                     "unit": "TFLOP/s", "frac": fl / sec / t_peak, "traffic": None}
+            else:
+                r = {"kernel": name, "bound": "hbm", "achieved": by / sec / 1e9, "peak": b_peak / 1e9,
+                     "unit": "GB/s", "frac": by / sec / b_peak, "traffic": None}
+            r["ms_per_step"] = kernel_ms[name]
+            r["peak_kind"] = pk_kind
+            return r
+        return None
+
     dominant = max(kernel_ms, key=kernel_ms.get) if kernel_ms else None
-    roof = None
-    if dominant == "tree_attention":
-        flops_step = n_attn_layers * sum(attn_flops)
-        launches_per_step = len(per_attn) // args.steps
-        achieved = flops_step / (kernel_ms[dominant] / 1000.0) / 1e12
-        peak = pk["bf16_tflops_sustained"]
-        roof = {"kernel": "tree_attention", "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "traffic": None, "peak_kind": f"{pk_kind} bf16 sustained",
-                "algorithmic_per_launch": flops_step / max(1, launches_per_step), "launches_per_step": launches_per_step,
-                "ms_per_step": kernel_ms[dominant]}
-    elif dominant in ("gdn_chunk_scan", "gdn_fork_recurrent"):
-        alg = chunk_algorithmic(levels, shape, chunked if dominant == "gdn_chunk_scan" else [not c for c in chunked])
-        fl = sum(f for f, _ in alg) * n_lin_layers
-        by = sum(b for _, b in alg) * n_lin_layers
-        sec = kernel_ms[dominant] / 1000.0
-        t_peak = pk["bf16_tflops_sustained"] * 1e12
-        b_peak = pk["hbm_gbs"] * 1e9
-        bound = "tensor" if fl / t_peak > by / b_peak else "hbm"
-        if bound == "tensor":
-            roof = {"kernel": dominant, "bound": "tensor", "achieved": fl / sec / 1e12, "peak": t_peak / 1e12,
-                    "unit": "TFLOP/s", "frac": fl / sec / t_peak, "traffic": None}
-        else:
-            roof = {"kernel": dominant, "bound": "hbm", "achieved": by / sec / 1e9, "peak": b_peak / 1e9,
-                    "unit": "GB/s", "frac": by / sec / b_peak, "traffic": None}
-        roof["ms_per_step"] = kernel_ms[dominant]
-        roof["peak_kind"] = pk_kind
+    roof = kernel_roofline(dominant) if dominant else None
+    roofline_kernels = {}
+    for name in kernel_ms:
+        r = kernel_roofline(name)
+        if r is not None:
+            roofline_kernels[name] = {k: r[k] for k in ("bound", "achieved", "peak", "unit", "frac", "ms_per_step")}
     traffic = ncu_traffic()
     if roof is not None and roof["kernel"] in traffic and not args.layers:
         # DRAM traffic of one level-0 launch (ncu) beside the algorithmic bytes of that launch
@@ -793,7 +803,8 @@ def main():
                     "e2e": {"p50": nearest_rank(lat_e2e, 0.5), "p90": nearest_rank(lat_e2e, 0.9)}},
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "ms_per_step": e2e_step},
-                "gpu_launches": launches, "kernel_ms_per_step": kernel_ms, "op_ms_one_step": op_ms, "roofline": roof, "cpu_baseline": cpu,
+                "gpu_launches": launches, "kernel_ms_per_step": kernel_ms, "op_ms_one_step": op_ms, "roofline": roof,
+                "roofline_kernels": roofline_kernels, "cpu_baseline": cpu,
                 "clocks": clock}
         print(json.dumps(line), flush=True)
     if pg is not None:
