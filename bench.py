@@ -364,19 +364,22 @@ def run_gemm(args):
               "out_proj": (H, s.value_dim), "gate_up": (2 * s.intermediate, H), "down": (H, s.intermediate)}
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
 
-    def timed(fn):
+    def timed(*fns):
+        """Median ms of each of `fns`, the calls interleaved step by step so that they see the same clocks."""
         for _ in range(args.warmup):
-            fn()
-        ms = []
+            for fn in fns:
+                fn()
+        ms = [[] for _ in fns]
         for _ in range(args.steps):
-            flush.zero_()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            fn()
-            b.record()
-            torch.cuda.synchronize()
-            ms.append(a.elapsed_time(b))
-        return statistics.median(ms)
+            for fn, out in zip(fns, ms):
+                flush.zero_()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                fn()
+                b.record()
+                torch.cuda.synchronize()
+                out.append(a.elapsed_time(b))
+        return [statistics.median(m) for m in ms]
 
     pk, kind = peaks()
     rows = {}
@@ -384,14 +387,12 @@ def run_gemm(args):
         w = (torch.randn(N, K, generator=g, device=device) * 0.02).to(torch.bfloat16)
         a = x[K]
         flops = 2.0 * T * N * K
-        t_ours = timed(lambda: ops.gemm_bf16(a, w))
-        t_cublas = timed(lambda: F.linear(a, w))
+        t_ours, t_cublas = timed(lambda: ops.gemm_bf16(a, w), lambda: F.linear(a, w))
         rows[name] = {"N": N, "K": K, "ms_tcgen05": t_ours, "ms_cublas": t_cublas,
                       "tflops_tcgen05": flops / t_ours / 1e9, "tflops_cublas": flops / t_cublas / 1e9}
         if name == "gate_up":
             wi = ops.swiglu_weight(w[:s.intermediate], w[s.intermediate:])
-            t_fused = timed(lambda: ops.gemm_bf16(a, wi, swiglu=True))
-            t_sep = timed(lambda: ops.silu_mul(F.linear(a, w)))
+            t_fused, t_sep = timed(lambda: ops.gemm_bf16(a, wi, swiglu=True), lambda: ops.silu_mul(F.linear(a, w)))
             rows["gate_up+swiglu"] = {"ms_tcgen05_fused": t_fused, "ms_cublas_plus_silu_mul": t_sep,
                                       "tflops_tcgen05_fused": flops / t_fused / 1e9}
         del w
@@ -657,6 +658,8 @@ def main():
     ops.TIMED["tree_attention"] = []
     ops.TIMED["gdn_chunk_scan"] = []
     ops.TIMED["gdn_fork_recurrent"] = []
+    ops.TIMED["gemm_bf16"] = []
+    ops.FLOPS.clear()
     import tempfile
     clocks = Clocks(local, os.path.join(tempfile.gettempdir(), f"janus_b200_clocks_{os.getpid()}_rank{rank}.csv"))
     barrier()
@@ -674,6 +677,7 @@ def main():
     barrier()
     clock = clocks.stop()
     launches = (ops.LAUNCHES[0] - launches0) // args.steps
+    gemm_flops_step = ops.FLOPS.get("gemm_bf16", 0.0) / args.steps
     step_ms = [s.elapsed_time(e) for s, e in step_events]
     total_ms = max_over_ranks(sum(step_ms))
     ms_per_step = total_ms / args.steps
@@ -685,6 +689,7 @@ def main():
     n_lin_layers = shape.layers - n_attn_layers
     attn_launch = ops.TIMED["tree_attention"]
     per_attn = [s.elapsed_time(e) for s, e in attn_launch]
+    gemm_launches = list(ops.TIMED["gemm_bf16"])
     ops.TIMED.clear()
 
     # where one (extra, untimed) step's device time goes, per library op; the rest is cuBLAS GEMMs and torch glue
@@ -709,6 +714,12 @@ def main():
                     "peak_kind": f"{pk_kind} bf16 sustained",
                     "algorithmic_per_launch": flops_step / max(1, launches_per_step),
                     "launches_per_step": launches_per_step, "ms_per_step": kernel_ms[name]}
+        if name == "gemm_bf16":  # the tcgen05 dense GEMM: the MLP's gate/up with the SwiGLU epilogue (2 M N K each)
+            achieved = gemm_flops_step / (kernel_ms[name] / 1000.0) / 1e12
+            peak = pk["bf16_tflops_sustained"]
+            return {"kernel": "gemm_bf16", "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak, "traffic": None, "peak_kind": f"{pk_kind} bf16 sustained",
+                    "launches_per_step": len(gemm_launches) // args.steps, "ms_per_step": kernel_ms[name]}
         if name in ("gdn_chunk_scan", "gdn_fork_recurrent"):
             alg = chunk_algorithmic(levels, shape, chunked if name == "gdn_chunk_scan" else [not c for c in chunked])
             fl = sum(f for f, _ in alg) * n_lin_layers
@@ -735,11 +746,15 @@ def main():
         if r is not None:
             roofline_kernels[name] = {k: r[k] for k in ("bound", "achieved", "peak", "unit", "frac", "ms_per_step")}
     traffic = ncu_traffic()
-    if roof is not None and roof["kernel"] in traffic and not args.layers:
+    if (roof is not None and roof["kernel"] in traffic and not args.layers
+            and not (roof["kernel"] == "gemm_bf16" and not shape.intermediate)):
         # DRAM traffic of one level-0 launch (ncu) beside the algorithmic bytes of that launch
         lv0 = levels[0]
         if roof["kernel"] == "tree_attention":
             alg0 = lv0.T * (3 * shape.heads * shape.head_dim * 2 + 2 * shape.kv_heads * shape.head_dim * 2)
+        elif roof["kernel"] == "gemm_bf16":  # the MLP's gate/up + SwiGLU: y in, weights, the I-wide product out
+            I = shape.intermediate
+            alg0 = lv0.T * shape.hidden * 2 + 2 * I * shape.hidden * 2 + lv0.T * I * 2
         else:
             alg0 = chunk_algorithmic(levels[:1], shape, [True])[0][1]
         t_bytes, t_requests, t_file = traffic[roof["kernel"]]

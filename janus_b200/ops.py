@@ -16,6 +16,7 @@ BF16, F32, I32 = torch.bfloat16, torch.float32, torch.int32
 LAUNCHES = [0]
 TIMED = {}
 OPS = []  # names of the instrumented ops
+FLOPS = {}  # op name -> tensor-core FLOPs issued so far (the dense GEMM: 2 M N K per call)
 
 
 def _instrument(name, kernels=1):
@@ -304,7 +305,6 @@ def head_pointer(x, option_rows, option_question, decision_rows, final_w, rms_ep
 
 
 @_instrument("gemm_bf16", 1)
-@_instrument("gemm_bf16", 1)
 def gemm_bf16(a, w, swiglu=False, out=None, status=None):
     """a bf16 [M, K] (unit column stride), w bf16 [N, K] -> a w^T bf16 [M, N] on the tcgen05 GEMM; swiglu: w in
     the interleaved gate/up order of `swiglu_weight`, result silu(gate) * up [M, N / 2]."""
@@ -317,6 +317,7 @@ def gemm_bf16(a, w, swiglu=False, out=None, status=None):
     if w.shape[1] != K:
         raise ValueError(f"gemm_bf16: a has K = {K}, w has {w.shape[1]}")
     n_out = N // 2 if swiglu else N
+    FLOPS["gemm_bf16"] = FLOPS.get("gemm_bf16", 0.0) + 2.0 * M * N * K
     out = torch.empty(M, n_out, dtype=BF16, device=a.device) if out is None else out
     _need(out, BF16, "out", contiguous=False)
     _lib.check(_lib.load().janus_b200_gemm_bf16(_ptr(a), a.stride(0), _ptr(w), w.stride(0), M, N, K, int(bool(swiglu)),

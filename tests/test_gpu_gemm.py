@@ -61,3 +61,26 @@ def test_gemm_swiglu(M, I, K):
     assert out.shape == (M, I)
     want = torch.nn.functional.silu(_ref(a, gate)) * _ref(a, up)
     _close(out, want)
+
+
+@pytest.mark.parametrize("M,N,K,swiglu", [(5000, 12352, 2560, False), (16384, 2560, 1024, False),
+                                          (3000, 1024, 2560, True), (100, 768, 512, False)])
+def test_gemm_tall_and_pair_tiles_agree(M, N, K, swiglu, monkeypatch):
+    """The tall-tile form (512 x 256 per CTA pair, the default) and the 256 x 256 form (JANUS_B200_GEMM=pair) issue
+    the same MMAs in the same k order for every output element: bit-identical results, several items per pair."""
+    from janus_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    a = torch.randn(M, K, generator=g, device="cuda").to(BF)
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).to(BF)
+    if swiglu:
+        w = ops.swiglu_weight(w[:N // 2], w[N // 2:])
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    monkeypatch.delenv("JANUS_B200_GEMM", raising=False)
+    tall = ops.gemm_bf16(a, w, swiglu=swiglu, status=status)
+    monkeypatch.setenv("JANUS_B200_GEMM", "pair")
+    pair = ops.gemm_bf16(a, w, swiglu=swiglu, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(tall, pair)
+    if not swiglu:
+        _close(tall, _ref(a, w))
