@@ -85,7 +85,12 @@ class DecisionReadout:
                 L.shared_down = w(m + "shared_expert.down_proj.weight")
                 L.shared_gate = w(m + "shared_expert_gate.weight")
             else:
-                L.gate_up = torch.cat([w(m + "gate_proj.weight"), w(m + "up_proj.weight")])
+                gate, up = w(m + "gate_proj.weight"), w(m + "up_proj.weight")
+                if gate.shape[0] % 128 == 0:  # the tcgen05 GEMM's SwiGLU epilogue takes 128-row gate/up blocks
+                    L.gate_up, L.gate_up_swiglu = None, ops.swiglu_weight(gate, up)
+                else:
+                    L.gate_up, L.gate_up_swiglu = torch.cat([gate, up]), None
+                del gate, up
                 L.down = w(m + "down_proj.weight")
             self.layers.append(L)
         f32 = lambda n: w(n, torch.float32)
@@ -147,10 +152,18 @@ class DecisionReadout:
                 h = F.linear(o, L.o)
                 kept.append((kk, vv) if lv.keep else None)
             y = ops.add_rmsnorm(x, h, L.post_norm, eps)
-            pending = self._moe(y, L) if s.moe else F.linear(ops.silu_mul(F.linear(y, L.gate_up)), L.down)
+            pending = self._moe(y, L) if s.moe else F.linear(self._swiglu(y, L), L.down)
         ops.add_rmsnorm(x, pending, self.final_norm, eps)  # the last residual add (its normed output is unused)
         self._heads(d, x, plan, logits)
         return kept
+
+    def _swiglu(self, y, L):
+        """The dense MLP's silu(gate(y)) * up(y) (`_silu_mul`, janus/hybrid.py:263): one tcgen05 GEMM whose epilogue
+        applies the SwiGLU to the fp32 accumulators and writes the I-wide product once; widths that are not multiples
+        of 128 take the merged GEMM and the silu_mul kernel."""
+        if L.gate_up_swiglu is not None:
+            return ops.gemm_bf16(y, L.gate_up_swiglu, swiglu=True, status=self.status)
+        return ops.silu_mul(F.linear(y, L.gate_up))
 
     def _moe(self, y, L):
         """Qwen3_5MoeSparseMoeBlock (transformers qwen3_5_moe :773-791) on the W4A16 experts: router logits in fp32
