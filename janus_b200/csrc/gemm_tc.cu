@@ -33,6 +33,7 @@ struct Params {
   int64_t ldo;
   int32_t* err;
   int M, N, K, nblk, n_items, swiglu;
+  int mt, band;  // tall form: m-tiles, n-blocks per band (items walk a band's n-blocks for every m-tile, band by band)
 };
 
 }  // namespace gtc
@@ -307,6 +308,15 @@ struct Bars {
   uint64_t full[S], empty[S], acc_full, acc_empty[2], drain;
 };
 
+// item -> (m-tile, n-block): the n-blocks come in bands of p.band (the last one narrower); a band's items run its
+// n-blocks fastest for every m-tile before the next band starts, so the band's weight rows stay in L2 while A streams
+__device__ __forceinline__ void item_tile(const gtc::Params& p, int it, int& mi, int& ni) {
+  const int per_band = p.mt * p.band, b = it / per_band, r = it - b * per_band;
+  const int w = min(p.band, p.nblk - b * p.band);
+  mi = r / w;
+  ni = b * p.band + (r - mi * w);
+}
+
 __global__ void __launch_bounds__(NT, 1) gemm_bf16_tall_kernel(const __grid_constant__ gtc::Params p) {
   extern __shared__ unsigned char raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~(uintptr_t)1023);
@@ -345,7 +355,9 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_tall_kernel(const __grid_cons
       bool ok = true;
       int q = 0, issued = 0;
       for (int it = c; it < p.n_items && ok; it += G) {
-        const int m0 = (it / p.nblk) * (4 * BM) + (int)rank * (2 * BM), n0 = (it % p.nblk) * BN + (int)rank * (BN / 2);
+        int mi, ni;
+        item_tile(p, it, mi, ni);
+        const int m0 = mi * (4 * BM) + (int)rank * (2 * BM), n0 = ni * BN + (int)rank * (BN / 2);
         for (int kb = 0; kb < nkb; ++kb, ++q) {
           const int s = q % S;
           if (q >= S) ok = wait_bar(&bars.empty[s], ((q / S) - 1) & 1, p.err);
@@ -432,9 +444,11 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_tall_kernel(const __grid_cons
       ok = __all_sync(kFull, wait_bar_sleep(&bars.acc_full, i & 1, p.err));
       if (!ok) break;
       fence_after();
+      int mi, ni;
+      item_tile(p, it, mi, ni);
 #pragma unroll 1
       for (int g = 0; g < 2; ++g) {
-        const int m0 = (it / p.nblk) * (4 * BM) + (int)rank * (2 * BM) + g * BM, c0 = (it % p.nblk) * outc;
+        const int m0 = mi * (4 * BM) + (int)rank * (2 * BM) + g * BM, c0 = ni * outc;
         const uint32_t la = tm + ((uint32_t)(32 * eq) << 16) + g * BN;
 #pragma unroll 1
         for (int cc = h * half; cc < (h + 1) * half; cc += 32) {
@@ -547,6 +561,12 @@ extern "C" int janus_b200_gemm_bf16(const void* a, int64_t lda, const void* w, i
   p.K = (int)K;
   p.nblk = (int)nblk;
   p.n_items = (int)(mt * nblk);
+  p.mt = (int)mt;
+  // bands of at most 48 MB of weight rows: one band's rows plus the A tiles and outputs that stream past between
+  // two uses of a weight tile stay within L2 (126 MB), at the price of reading A once per band
+  const int64_t w_bytes = N * K * 2, band_cap = 48ll << 20;
+  const int64_t nbands = tall ? (w_bytes + band_cap - 1) / band_cap : 1;
+  p.band = (int)((nblk + nbands - 1) / nbands);
   p.swiglu = epilogue;
   const size_t smem = (tall ? gtc4::kSmem : gtc2::kSmem) + 1024;
   void (*kernel)(const gtc::Params) = tall ? gtc4::gemm_bf16_tall_kernel : gtc2::gemm_bf16_pair_kernel;
