@@ -189,7 +189,8 @@ int janus_b200_head_pointer(const float* x, int64_t H, const int32_t* option_row
  * aligned, strides multiples of 8 elements; N a multiple of 16, K of 8. epilogue 0: out [M, N] (row stride ldo);
  * epilogue 1 (SwiGLU): w's rows come in 256-row blocks of 128 gate rows then the 128 matching up rows (N a multiple
  * of 256), out [M, N/2] = silu(gate) * up of the fp32 accumulators. status: optional device int32 word set to 1 if a
- * bounded device-side wait ran out.
+ * bounded device-side wait ran out. Runs 512 x 256 tiles per CTA pair; the environment variable JANUS_B200_GEMM=pair
+ * selects 256 x 256 tiles instead (bit-identical results).
  * Replaces the F.linear of the merged projections (`_merge_projections`, janus/hybrid.py:1108-1133) and, with
  * epilogue 1, the MLP's gate/up GEMM plus `_silu_mul` (janus/hybrid.py:263, 1093-1096). */
 int janus_b200_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, int64_t M, int64_t N, int64_t K,
