@@ -278,9 +278,10 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair_kernel(const __grid_cons
 // computes a 512 x 256 tile. Per CTA and 64-deep k-block that is 48 KB of TMA loads for 1024 MMA cycles (48 B per
 // cycle) against the 256-row form's 32 KB per 512 cycles (64 B per cycle): the L2-to-shared-memory path, which
 // bounds the 256-row form at about two thirds of the tensor peak, carries a quarter fewer bytes per FLOP. The
-// accumulators are single-buffered. The 8 epilogue warps (two per TMEM lane quarter, splitting the columns) drain
-// accumulator 0 and release it, then accumulator 1; the next item starts skewed: its first 4 staged k-blocks go into
-// accumulator 0 while accumulator 1 drains, then into accumulator 1, and only then are their stages released.
+// accumulators are single-buffered. The 8 epilogue warps (two per TMEM lane quarter, splitting the columns) read
+// accumulator 0 into registers as bf16 pairs and release it before storing, then accumulator 1; the next item starts
+// skewed: its first 4 staged k-blocks go into accumulator 0 while accumulator 1 is read, then into accumulator 1, and
+// only then are their stages released; the stores run under the next item's MMAs.
 // Meanwhile the 4-stage ring holds the next k-blocks. Hand-offs and the wind-down as in the 256-row form. No TMA
 // load uses multicast.
 namespace gtc4 {
@@ -315,6 +316,54 @@ __device__ __forceinline__ void item_tile(const gtc::Params& p, int it, int& mi,
   const int w = min(p.band, p.nblk - b * p.band);
   mi = r / w;
   ni = b * p.band + (r - mi * w);
+}
+
+// One accumulator's share of an epilogue warp (32 TMEM lanes x 128 accumulator columns): TMEM -> bf16 pairs in
+// registers (plain: 128 output columns, 64 registers; SwiGLU: 64 output columns from 64 gate and 64 up columns, 32
+// registers), then the accumulator is released to the next item's MMAs, and only then go the stores (staged through
+// the warp's 2 KB of shared memory for 16-byte row segments), so the stores run under the next item's MMAs.
+template <bool SW>
+__device__ __forceinline__ void drain_acc(const gtc::Params& p, uint32_t la, int h, int eq, int lane, int m0, int c0,
+                                          int out_n, unsigned char* stg, uint64_t* acc_empty) {
+  constexpr int kChunks = SW ? 2 : 4;  // 32-column output chunks of this warp
+  constexpr int kHalf = 32 * kChunks;  // output columns of this warp
+  uint32_t pk[kChunks][16];
+#pragma unroll
+  for (int ch = 0; ch < kChunks; ++ch) {
+    const int cc = h * kHalf + 32 * ch;
+    float a[32];
+    tld32f(la + cc, a);
+    if (SW) {
+      float u[32];
+      tld32f(la + 128 + cc, u);
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        pk[ch][k] = pack_bf16(silu_fast(a[2 * k]) * u[2 * k], silu_fast(a[2 * k + 1]) * u[2 * k + 1]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 16; ++k) pk[ch][k] = pack_bf16(a[2 * k], a[2 * k + 1]);
+    }
+  }
+  fence_before();
+  __syncwarp();
+  if (lane == 0) remote_arrive(peer_addr(s32(acc_empty), 0));
+#pragma unroll
+  for (int ch = 0; ch < kChunks; ++ch) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      *reinterpret_cast<uint4*>(stg + lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4)) =
+          make_uint4(pk[ch][4 * u], pk[ch][4 * u + 1], pk[ch][4 * u + 2], pk[ch][4 * u + 3]);
+    __syncwarp();
+    const int col = c0 + h * kHalf + 32 * ch + (lane & 3) * 8;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int rr = k * 8 + (lane >> 2);
+      const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 64 + (((lane & 3) ^ ((rr >> 1) & 3)) << 4));
+      const int row = m0 + 32 * eq + rr;
+      if (row < p.M && col < out_n) *reinterpret_cast<uint4*>(p.out + (int64_t)row * p.ldo + col) = v;
+    }
+    __syncwarp();
+  }
 }
 
 __global__ void __launch_bounds__(NT, 1) gemm_bf16_tall_kernel(const __grid_constant__ gtc::Params p) {
@@ -436,7 +485,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_tall_kernel(const __grid_cons
     // split between the two warps of a TMEM lane quarter by columns (warp group h takes the h-th half of the outputs)
     const int eq = warp & 3, h = (warp - 4) >> 2;
     unsigned char* stg = base + kOut + (warp - 4) * (32 * 64);
-    const int outc = p.swiglu ? BN / 2 : BN, half = outc / 2;
+    const int outc = p.swiglu ? BN / 2 : BN;
     const int out_n = p.swiglu ? p.N / 2 : p.N;
     bool ok = true;
     int i = 0;
@@ -450,42 +499,10 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_tall_kernel(const __grid_cons
       for (int g = 0; g < 2; ++g) {
         const int m0 = mi * (4 * BM) + (int)rank * (2 * BM) + g * BM, c0 = ni * outc;
         const uint32_t la = tm + ((uint32_t)(32 * eq) << 16) + g * BN;
-#pragma unroll 1
-        for (int cc = h * half; cc < (h + 1) * half; cc += 32) {
-          uint32_t o[16];
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            float a[16];
-            tld16f(la + cc + 16 * h2, a);
-            if (p.swiglu) {
-              float u[16];
-              tld16f(la + 128 + cc + 16 * h2, u);
-#pragma unroll
-              for (int k = 0; k < 8; ++k)
-                o[8 * h2 + k] = pack_bf16(silu_fast(a[2 * k]) * u[2 * k], silu_fast(a[2 * k + 1]) * u[2 * k + 1]);
-            } else {
-#pragma unroll
-              for (int k = 0; k < 8; ++k) o[8 * h2 + k] = pack_bf16(a[2 * k], a[2 * k + 1]);
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            *reinterpret_cast<uint4*>(stg + lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4)) =
-                make_uint4(o[4 * u], o[4 * u + 1], o[4 * u + 2], o[4 * u + 3]);
-          __syncwarp();
-          const int col = c0 + cc + (lane & 3) * 8;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int rr = k * 8 + (lane >> 2);
-            const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 64 + (((lane & 3) ^ ((rr >> 1) & 3)) << 4));
-            const int row = m0 + 32 * eq + rr;
-            if (row < p.M && col < out_n) *reinterpret_cast<uint4*>(p.out + (int64_t)row * p.ldo + col) = v;
-          }
-          __syncwarp();
-        }
-        fence_before();
-        __syncwarp();
-        if (lane == 0) remote_arrive(peer_addr(s32(&bars.acc_empty[g]), 0));
+        if (p.swiglu)
+          drain_acc<true>(p, la, h, eq, lane, m0, c0, out_n, stg, &bars.acc_empty[g]);
+        else
+          drain_acc<false>(p, la, h, eq, lane, m0, c0, out_n, stg, &bars.acc_empty[g]);
       }
     }
   }
