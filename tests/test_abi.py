@@ -50,3 +50,28 @@ def test_every_op_the_readout_calls_is_wrapped():
     from janus_b200 import ops
     used = set(re.findall(r"\bops\.(\w+)\(", (ROOT / "janus_b200" / "model.py").read_text()))
     assert used and all(callable(getattr(ops, n, None)) for n in used), used - set(dir(ops))
+
+
+def test_gemm_rejects_shapes_and_layouts_it_cannot_serve():
+    """The dense GEMM refuses an unknown epilogue, N or K off the tile granularity, a SwiGLU width that does not split
+    into 128-row gate/up blocks, misaligned operands and an output stride too small, before any CUDA call
+    (placeholder pointers: nothing is dereferenced on the host)."""
+    import ctypes
+    from janus_b200 import _lib
+    lib = _lib.load()
+    p = ctypes.c_void_p(256)
+    odd = ctypes.c_void_p(258)
+    cases = [  # a, lda, w, ldw, M, N, K, epilogue, out, ldo, expected words in the error
+        (p, 64, p, 64, 128, 256, 64, 2, p, 256, "epilogue"),
+        (p, 64, p, 64, 128, 200, 64, 0, p, 256, "multiple of 16"),
+        (p, 60, p, 60, 128, 256, 60, 0, p, 256, "multiple of 16"),
+        (p, 64, p, 64, 128, 384, 64, 1, p, 192, "256 for swiglu"),
+        (odd, 64, p, 64, 128, 256, 64, 0, p, 256, "aligned"),
+        (p, 64, p, 64, 128, 256, 64, 1, p, 64, "aligned"),
+        (p, 64, p, 64, -1, 256, 64, 0, p, 256, "sizes"),
+        (None, 64, p, 64, 128, 256, 64, 0, p, 256, "null"),
+    ]
+    for a, lda, w, ldw, M, N, K, ep, out, ldo, words in cases:
+        st = lib.janus_b200_gemm_bf16(a, lda, w, ldw, M, N, K, ep, out, ldo, None, None)
+        assert st < 0, (M, N, K, ep, ldo)
+        assert words in _lib.last_error(), (words, _lib.last_error())
