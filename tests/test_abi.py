@@ -75,3 +75,21 @@ def test_gemm_rejects_shapes_and_layouts_it_cannot_serve():
         st = lib.janus_b200_gemm_bf16(a, lda, w, ldw, M, N, K, ep, out, ldo, None, None)
         assert st < 0, (M, N, K, ep, ldo)
         assert words in _lib.last_error(), (words, _lib.last_error())
+
+
+def test_swiglu_weight_interleaves_128_row_blocks():
+    """The SwiGLU epilogue's weight order (host-side, no GPU): 256-row blocks of 128 gate rows then the matching 128
+    up rows; widths that are not multiples of 128 are refused."""
+    import pytest
+    import torch
+    from janus_b200 import ops
+    I, H = 384, 8
+    gate = torch.arange(I * H, dtype=torch.float32).reshape(I, H).to(torch.bfloat16)
+    up = -gate - 1
+    w = ops.swiglu_weight(gate, up)
+    assert w.shape == (2 * I, H) and w.is_contiguous()
+    for b in range(I // 128):
+        assert torch.equal(w[256 * b:256 * b + 128], gate[128 * b:128 * (b + 1)])
+        assert torch.equal(w[256 * b + 128:256 * (b + 1)], up[128 * b:128 * (b + 1)])
+    with pytest.raises(ValueError):
+        ops.swiglu_weight(gate[:200], up[:200])
